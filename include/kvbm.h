@@ -1,0 +1,151 @@
+/*
+ * kvbm.h - C ABI of the B200 (sm_100a) block-granular attention-mass kernels.
+ *
+ *   mass[j] = sum over (b, h_q, query i, key c in block j) of
+ *             softmax_c(q[b,h_q,i] . k[b,h_q/G,c] * scale),   G = H_q / H_kv
+ *
+ * computed in two passes (row log-sum-exp, then column sums of the softmax)
+ * without materialising the [B, H, N, N] matrix.
+ *
+ * Every entry point takes plain pointers and sizes; no C++ or torch types
+ * cross this boundary.  All device pointers must belong to the CUDA device
+ * that is current on the calling thread, and `stream` is a cudaStream_t of
+ * that device (NULL = legacy default stream).  Launches are asynchronous on
+ * `stream`; nothing here synchronises the host.  The caller owns every
+ * buffer, including the workspace.  Status codes are returned, nothing is
+ * thrown across the ABI.
+ *
+ * Reference interfaces replaced (kv-block-mass, file:line):
+ *   kvbm_block_mass      <- block_mass_triton(q, k, attn_mask, causal, block_size,
+ *                           scale, BLOCK_M, BLOCK_N, causal_skip)
+ *                           src/kvblockmass/triton_kernel.py:148-196, whose
+ *                           kernel launch is at :183-195; and the CUDA branch of
+ *                           the dispatcher block_mass, src/kvblockmass/reference.py:129-135
+ *   kvbm_validate        <- the wrapper's argument checks, triton_kernel.py:159-164
+ *                           (GQA ValueError, reference.py:29-30)
+ *   kvbm_workspace_bytes <- the wrapper's device allocations, triton_kernel.py:166-180
+ *   kvbm_num_blocks      <- num_blocks = ceil(N / block_size), reference.py:89
+ */
+#ifndef KVBM_H
+#define KVBM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KVBM_ABI_VERSION 1
+
+/* Element type of q and k.  The mass output is float32, or float64 for
+ * KVBM_F64 inputs (reference.py:77: fp64 stays fp64, everything else
+ * accumulates in fp32). */
+enum kvbm_dtype {
+  KVBM_F32 = 0,
+  KVBM_BF16 = 1,
+  KVBM_F16 = 2,
+  KVBM_F64 = 3
+};
+
+enum kvbm_status {
+  KVBM_OK = 0,
+  KVBM_ERR_GQA = 1,         /* H_q % H_kv != 0 (reference raises ValueError) */
+  KVBM_ERR_SHAPE = 2,       /* a size is out of range or inconsistent        */
+  KVBM_ERR_DTYPE = 3,       /* unknown dtype                                  */
+  KVBM_ERR_HEAD_DIM = 4,    /* head dim D not supported for this dtype        */
+  KVBM_ERR_BLOCK_SIZE = 5,  /* block_size < 1                                  */
+  KVBM_ERR_UNITS = 6,       /* unit range not inside [0, B*H_kv]              */
+  KVBM_ERR_NULL = 7,        /* a required pointer is NULL                     */
+  KVBM_ERR_WORKSPACE = 8,   /* workspace missing, too small or misaligned     */
+  KVBM_ERR_CUDA = 9,        /* a CUDA runtime call or launch failed           */
+  KVBM_ERR_DEVICE = 10,     /* current device is not an sm_100 GPU            */
+  KVBM_ERR_TIMEOUT = 11,    /* a device-side wait ran out its iteration limit */
+  KVBM_ERR_SCRATCH = 12     /* problem exceeds a fixed-size scratch area      */
+};
+
+/* Attention-mass problem.  Strides are in ELEMENTS for the dims [B, H, N, D]
+ * of q ([B, H_q, N, D]) and k ([B, H_kv, N, D]); any strides are accepted.
+ *
+ * Masks are byte arrays, nonzero = keep, NULL = absent; they combine with
+ * `causal` by logical AND (reference.py:83-87):
+ *   key_mask   [B|1, N]     column mask: key_mask[b*key_mask_bstride + c]
+ *                           (an [N] attn_mask of the reference is bstride 0)
+ *   query_mask [B|1, N]     row mask: a row whose entry is 0 keeps no key
+ *                           and contributes exactly 0 (extension)
+ *   pair_mask  [B|1, N, N]  pair mask: pair_mask[b*bstride + i*rstride + c]
+ *                           (an [N, N] attn_mask of the reference is bstride 0)
+ *
+ * `units`: the problem splits into B*H_kv independent (batch, kv-head) units,
+ * u = b*H_kv + g, each owning q-heads [g*G, (g+1)*G).  One call computes the
+ * mass of units [unit_begin, unit_end); the full problem is [0, B*H_kv).
+ * Mass is a sum over units, so shards of one problem add up exactly.
+ */
+typedef struct kvbm_problem {
+  const void* q;
+  int64_t q_stride[4];
+  const void* k;
+  int64_t k_stride[4];
+  int32_t dtype;
+  int32_t B, Hq, Hkv, N, D;
+  const uint8_t* key_mask;
+  int64_t key_mask_bstride;
+  const uint8_t* query_mask;
+  int64_t query_mask_bstride;
+  const uint8_t* pair_mask;
+  int64_t pair_mask_bstride;
+  int64_t pair_mask_rstride;
+  double scale;          /* score scale; the reference's default is 1/sqrt(D) */
+  int32_t block_size;    /* KV block (bucket) size; the last bucket may be ragged */
+  int32_t causal;        /* keep key c for query i only if c <= i           */
+  int32_t causal_skip;   /* 1: never visit tiles above the causal diagonal  */
+  int32_t unit_begin;
+  int32_t unit_end;
+} kvbm_problem;
+
+/* ABI version of the loaded library (KVBM_ABI_VERSION it was built with). */
+int kvbm_abi_version(void);
+
+/* Static description of a status code. */
+const char* kvbm_status_string(int status);
+
+/* Host-only argument validation; touches no GPU.  Returns KVBM_OK or the
+ * first failing check. */
+int kvbm_validate(const kvbm_problem* p);
+
+/* ceil(N / block_size), the length of the mass vector. */
+int64_t kvbm_num_blocks(int32_t N, int32_t block_size);
+
+/* Bytes of device workspace kvbm_block_mass needs for `p` (0 on invalid
+ * input).  Host-only; the size depends on the device's kernel path but not
+ * on pointer values. */
+size_t kvbm_workspace_bytes(const kvbm_problem* p);
+
+/* Which kernel family will run `p` on the current device:
+ * 0 = SIMT (fp32 FFMA / fp64 DFMA, any mask, D <= 256),
+ * 1 = tcgen05 tensor cores with TMA and TMEM (bf16/fp16, D in {64, 128}),
+ * negative = a kvbm_status error code, negated. */
+int kvbm_kernel_path(const kvbm_problem* p);
+
+/* Kernel launches one kvbm_block_mass call of `p` makes (host-only). */
+int kvbm_launches_per_call(const kvbm_problem* p);
+
+/* Compute the mass of units [p->unit_begin, p->unit_end) into
+ * `mass_out` (device, num_blocks elements of float32, or float64 for
+ * KVBM_F64 inputs; overwritten, not accumulated).  `workspace` is device
+ * memory of at least kvbm_workspace_bytes(p) bytes, 256-byte aligned; its
+ * contents on entry do not matter.  Results are deterministic: the same
+ * inputs give the same bits, and causal_skip on/off give the same bits. */
+int kvbm_block_mass(const kvbm_problem* p, void* mass_out, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/* Reads and clears the device-side error word of the current device (set
+ * when a bounded wait inside a tcgen05 kernel gave up).  Synchronises
+ * `stream`.  Returns KVBM_OK, KVBM_ERR_TIMEOUT or KVBM_ERR_CUDA. */
+int kvbm_check_device_errors(void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVBM_H */

@@ -1,0 +1,182 @@
+// C ABI entry points (include/kvbm.h): validation, kernel-path choice,
+// workspace layout and the two-pass + reduce launch sequence.
+#include <cuda_runtime.h>
+#include <stdio.h>
+
+#include "kvbm_internal.cuh"
+
+namespace kvbm {
+
+namespace {
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+constexpr int kMaxDevices = 64;
+// Lazily filled per-device attribute cache: 0 unknown, 1 sm_100, 2 other.
+int g_dev_kind[kMaxDevices] = {0};
+
+int device_kind(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return 2;
+  if (g_dev_kind[dev] == 0) {
+    int major = 0, minor = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+      return 2;
+    g_dev_kind[dev] = (major == 10 && minor == 0) ? 1 : 2;
+  }
+  return g_dev_kind[dev];
+}
+
+}  // namespace
+
+int validate(const kvbm_problem* p) {
+  if (p == nullptr) return KVBM_ERR_NULL;
+  if (p->dtype < KVBM_F32 || p->dtype > KVBM_F64) return KVBM_ERR_DTYPE;
+  if (p->B < 1 || p->Hq < 1 || p->Hkv < 1 || p->N < 1 || p->D < 1) return KVBM_ERR_SHAPE;
+  if (p->Hq % p->Hkv != 0) return KVBM_ERR_GQA;
+  if (p->block_size < 1) return KVBM_ERR_BLOCK_SIZE;
+  const int dmax = (p->dtype == KVBM_F64) ? 128 : 256;
+  if (p->D > dmax) return KVBM_ERR_HEAD_DIM;
+  const long long units = (long long)p->B * p->Hkv;
+  if (p->unit_begin < 0 || p->unit_end > units || p->unit_begin >= p->unit_end)
+    return KVBM_ERR_UNITS;
+  if ((long long)p->B * p->Hq > 65535) return KVBM_ERR_SHAPE;  // grid.y of pass 1
+  if (p->q == nullptr || p->k == nullptr) return KVBM_ERR_NULL;
+  for (int i = 0; i < 4; ++i)
+    if (p->q_stride[i] < 0 || p->k_stride[i] < 0) return KVBM_ERR_SHAPE;
+  if (p->pair_mask && p->pair_mask_rstride < 0) return KVBM_ERR_SHAPE;
+  if (!(p->scale == p->scale)) return KVBM_ERR_SHAPE;  // NaN scale
+  return KVBM_OK;
+}
+
+// Path 1 (tcgen05) needs a 16-bit dtype, D in {64, 128}, a unit-stride head
+// dim, 16-byte aligned base pointers and row/head/batch strides (TMA rules),
+// and no pair mask; everything else runs the SIMT kernels.
+int select_path(const kvbm_problem* p, int device) {
+  if (device >= 0 && device_kind(device) != 1) return 0;
+  if (p->dtype != KVBM_BF16 && p->dtype != KVBM_F16) return 0;
+  if (p->D != 64 && p->D != 128) return 0;
+  if (p->pair_mask != nullptr) return 0;
+  const int64_t* qs = p->q_stride;
+  const int64_t* ks = p->k_stride;
+  if (qs[3] != 1 || ks[3] != 1) return 0;
+  for (int i = 0; i < 3; ++i)
+    if ((qs[i] * 2) % 16 != 0 || (ks[i] * 2) % 16 != 0) return 0;
+  if (((uintptr_t)p->q % 16) != 0 || ((uintptr_t)p->k % 16) != 0) return 0;
+  return tc_path_enabled() ? 1 : 0;
+}
+
+WsLayout layout_for(const kvbm_problem* p, int path) {
+  WsLayout L;
+  L.path = path;
+  L.acc_bytes = (p->dtype == KVBM_F64) ? 8 : 4;
+  L.qchunk = path == 1 ? kTcQChunk : kSimtQChunk;
+  L.key_tile = path == 1 ? kTcTile : kSimtBN;
+  L.nchunk = (p->N + L.qchunk - 1) / L.qchunk;
+  const size_t U = (size_t)(p->unit_end - p->unit_begin);
+  const size_t G = (size_t)(p->Hq / p->Hkv);
+  L.lse_off = 0;
+  L.lse_bytes = U * G * (size_t)p->N * L.acc_bytes;
+  L.part_off = align_up(L.lse_off + L.lse_bytes, 256);
+  L.part_bytes = U * (size_t)L.nchunk * (size_t)p->N * L.acc_bytes;
+  L.total = align_up(L.part_off + L.part_bytes, 256);
+  return L;
+}
+
+}  // namespace kvbm
+
+using namespace kvbm;
+
+extern "C" {
+
+int kvbm_abi_version(void) { return KVBM_ABI_VERSION; }
+
+const char* kvbm_status_string(int status) {
+  switch (status) {
+    case KVBM_OK: return "ok";
+    case KVBM_ERR_GQA: return "GQA requires H_q % H_kv == 0";
+    case KVBM_ERR_SHAPE: return "invalid or inconsistent sizes/strides";
+    case KVBM_ERR_DTYPE: return "unsupported dtype (expected float32, bfloat16, float16 or float64)";
+    case KVBM_ERR_HEAD_DIM: return "head dim D not supported (D <= 256; D <= 128 for float64)";
+    case KVBM_ERR_BLOCK_SIZE: return "block_size must be >= 1";
+    case KVBM_ERR_UNITS: return "unit range must satisfy 0 <= unit_begin < unit_end <= B*H_kv";
+    case KVBM_ERR_NULL: return "required pointer is NULL";
+    case KVBM_ERR_WORKSPACE: return "workspace missing, too small or not 256-byte aligned";
+    case KVBM_ERR_CUDA: return "CUDA runtime error";
+    case KVBM_ERR_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
+    case KVBM_ERR_TIMEOUT: return "a device-side wait exceeded its iteration limit";
+    case KVBM_ERR_SCRATCH: return "problem exceeds the fixed scratch area";
+    default: return "unknown status";
+  }
+}
+
+int kvbm_validate(const kvbm_problem* p) { return validate(p); }
+
+int64_t kvbm_num_blocks(int32_t N, int32_t block_size) {
+  if (N < 0 || block_size < 1) return 0;
+  return ((int64_t)N + block_size - 1) / block_size;
+}
+
+size_t kvbm_workspace_bytes(const kvbm_problem* p) {
+  if (validate(p) != KVBM_OK) return 0;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    dev = -1;
+  }
+  const int path = select_path(p, dev);
+  // Size for the larger of the two layouts when the device is unknown, so a
+  // workspace sized on the host is valid for whichever path runs.
+  if (dev < 0) {
+    const WsLayout a = layout_for(p, 0), b = layout_for(p, 1);
+    return a.total > b.total ? a.total : b.total;
+  }
+  return layout_for(p, path).total;
+}
+
+int kvbm_kernel_path(const kvbm_problem* p) {
+  const int st = validate(p);
+  if (st != KVBM_OK) return -st;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    dev = -1;
+  }
+  return select_path(p, dev);
+}
+
+int kvbm_launches_per_call(const kvbm_problem* p) {
+  if (validate(p) != KVBM_OK) return 0;
+  return 3;  // pass 1 (lse2), pass 2 (per-key partials), bucket reduce
+}
+
+int kvbm_block_mass(const kvbm_problem* p, void* mass_out, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  int st = validate(p);
+  if (st != KVBM_OK) return st;
+  if (mass_out == nullptr) return KVBM_ERR_NULL;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return KVBM_ERR_CUDA;
+  }
+  if (device_kind(dev) != 1) return KVBM_ERR_DEVICE;
+  const int path = select_path(p, dev);
+  const WsLayout L = layout_for(p, path);
+  if (workspace == nullptr || workspace_bytes < L.total || ((uintptr_t)workspace % 256) != 0)
+    return KVBM_ERR_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = (path == 1) ? launch_tc(p, L, mass_out, workspace, s)
+                   : launch_simt(p, L, mass_out, workspace, s);
+  if (st != KVBM_OK) return st;
+  return launch_reduce(p, L, mass_out, workspace, s);
+}
+
+int kvbm_check_device_errors(void* stream) {
+  int err = 0;
+  const int st = read_and_clear_device_error(static_cast<cudaStream_t>(stream), &err);
+  if (st != KVBM_OK) return st;
+  return err ? KVBM_ERR_TIMEOUT : KVBM_OK;
+}
+
+}  // extern "C"

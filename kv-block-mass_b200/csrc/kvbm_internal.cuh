@@ -1,0 +1,52 @@
+// Internal declarations shared by the block-mass kernels and the C ABI layer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kvbm.h"
+
+namespace kvbm {
+
+// log2(e): scores are kept in the base-2 domain, t = (q.k) * scale * log2(e),
+// so softmax(s)_c = 2^(t_c - lse2) with lse2 = log2(sum_c 2^t_c).
+constexpr double kLog2e = 1.4426950408889634073599246810018921;
+
+// ---- SIMT tiles (fp32 FFMA / fp64 DFMA path) ----
+constexpr int kSimtBM = 64;        // query rows per tile
+constexpr int kSimtBN = 64;        // key columns per tile
+constexpr int kSimtThreads = 256;  // 16 x 16 threads, 4 x 4 scores each
+constexpr int kSimtQChunk = 512;   // query rows per mass-pass CTA
+
+// ---- tcgen05 tiles (bf16 / fp16 path) ----
+constexpr int kTcTile = 128;       // rows of an MMA tile (M) and key/query tile (N)
+constexpr int kTcQChunk = 2048;    // query rows per mass-pass CTA
+
+// Where each array lives inside the caller's workspace.
+struct WsLayout {
+  size_t lse_off = 0, lse_bytes = 0;     // [U_sel * G * N] lse2 (Acc)
+  size_t part_off = 0, part_bytes = 0;   // [U_sel * nchunk * N] per-key partials (Acc)
+  size_t total = 0;
+  int path = 0;        // 0 SIMT, 1 tcgen05
+  int qchunk = 0;      // query rows per mass-pass CTA
+  int key_tile = 0;    // keys per mass-pass CTA
+  int nchunk = 0;      // ceil(N / qchunk)
+  int acc_bytes = 4;   // 4 (float) or 8 (double)
+};
+
+// Host helpers (kvbm_api.cu).
+bool tc_path_enabled();  // kvbm_tc.cu
+int validate(const kvbm_problem* p);
+int select_path(const kvbm_problem* p, int device);
+WsLayout layout_for(const kvbm_problem* p, int path);
+
+// Launchers (return a kvbm_status).
+int launch_simt(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws, cudaStream_t s);
+int launch_tc(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws, cudaStream_t s);
+int launch_reduce(const kvbm_problem* p, const WsLayout& L, void* mass_out, const void* ws,
+                  cudaStream_t s);
+
+// Device error word: set when a bounded wait in a tcgen05 kernel gives up.
+int read_and_clear_device_error(cudaStream_t s, int* err);
+
+}  // namespace kvbm

@@ -1,0 +1,381 @@
+// SIMT block-mass kernels: fp32 FFMA (fp32 / bf16 / fp16 inputs) and fp64 DFMA
+// (fp64 inputs), any head dim up to 256, every mask kind.
+//
+// Pass 1 (row log-sum-exp) restates the online max/denominator loop of the
+// reference's Triton kernel (kv-block-mass src/kvblockmass/triton_kernel.py:69-104)
+// and the streaming softmax of src/kvblockmass/reference.py:108-119; pass 2
+// recomputes each score tile and sums softmax weights per key column
+// (triton_kernel.py:106-145, reference.py:121-124), but writes one partial per
+// (unit, query chunk, key) into the workspace instead of float atomics, so a
+// separate fixed-order reduce makes every result deterministic.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <math.h>
+
+#include "kvbm_internal.cuh"
+
+namespace kvbm {
+namespace {
+
+constexpr int BM = kSimtBM;
+constexpr int BN = kSimtBN;
+constexpr int NT = kSimtThreads;
+
+template <typename Acc>
+struct Args {
+  const void* q;
+  long long qs0, qs1, qs2, qs3;
+  const void* k;
+  long long ks0, ks1, ks2, ks3;
+  int N, D, G, Hkv, ub;
+  const uint8_t* kmask;
+  long long kmb;
+  const uint8_t* qmask;
+  long long qmb;
+  const uint8_t* pmask;
+  long long pmb, pmr;
+  Acc C;  // scale * log2(e)
+  int causal, skip;
+  Acc* lse;   // [U_sel*G, N]
+  Acc* part;  // [U_sel, nchunk, N]
+  int qchunk, nchunk;
+};
+
+template <typename In, typename Acc>
+__device__ __forceinline__ Acc load_as(const void* base, long long off);
+template <>
+__device__ __forceinline__ float load_as<float, float>(const void* b, long long o) {
+  return static_cast<const float*>(b)[o];
+}
+template <>
+__device__ __forceinline__ float load_as<__nv_bfloat16, float>(const void* b, long long o) {
+  return __bfloat162float(static_cast<const __nv_bfloat16*>(b)[o]);
+}
+template <>
+__device__ __forceinline__ float load_as<__half, float>(const void* b, long long o) {
+  return __half2float(static_cast<const __half*>(b)[o]);
+}
+template <>
+__device__ __forceinline__ double load_as<double, double>(const void* b, long long o) {
+  return static_cast<const double*>(b)[o];
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ double fast_exp2(double x) { return exp2(x); }
+__device__ __forceinline__ float acc_log2(float x) { return log2f(x); }
+__device__ __forceinline__ double acc_log2(double x) { return log2(x); }
+
+template <typename Acc>
+__device__ __forceinline__ Acc neg_inf();
+template <>
+__device__ __forceinline__ float neg_inf<float>() { return -INFINITY; }
+template <>
+__device__ __forceinline__ double neg_inf<double>() { return -(double)INFINITY; }
+
+// keep(b, row, col): causal & key mask & query mask & pair mask (reference.py:83-87).
+template <typename Acc>
+__device__ __forceinline__ bool keep_at(const Args<Acc>& a, int b, int row, int col) {
+  if (row >= a.N || col >= a.N) return false;
+  if (a.causal && col > row) return false;
+  if (a.kmask && !a.kmask[b * a.kmb + col]) return false;
+  if (a.qmask && !a.qmask[b * a.qmb + row]) return false;
+  if (a.pmask && !a.pmask[b * a.pmb + (long long)row * a.pmr + col]) return false;
+  return true;
+}
+
+// Stage a [rows x D] slab of a [*, N, D] operand into smem as S[d * 64 + r]
+// (transposed so that each thread reads 4 consecutive rows with one vector load).
+template <typename In, typename Acc>
+__device__ __forceinline__ void stage_tile(Acc* S, const void* base, long long off0, long long rs,
+                                           long long ds, int r0, int rlim, int D) {
+  for (int idx = threadIdx.x; idx < 64 * D; idx += NT) {
+    const int r = idx / D;
+    const int d = idx - r * D;
+    const int row = r0 + r;
+    Acc v = Acc(0);
+    if (row < rlim) v = load_as<In, Acc>(base, off0 + row * rs + d * ds);
+    S[d * 64 + r] = v;
+  }
+}
+
+template <typename Acc>
+__device__ __forceinline__ void load4(const Acc* p, Acc (&v)[4]) {
+  if constexpr (sizeof(Acc) == 4) {
+    const float4 t = *reinterpret_cast<const float4*>(p);
+    v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+  } else {
+    const double2 t0 = *reinterpret_cast<const double2*>(p);
+    const double2 t1 = *reinterpret_cast<const double2*>(p + 2);
+    v[0] = t0.x; v[1] = t0.y; v[2] = t1.x; v[3] = t1.y;
+  }
+}
+
+// S[4][4] = Qs[rows ty*4.., :] . Ks[cols tx*4.., :]
+template <typename Acc>
+__device__ __forceinline__ void tile_scores(const Acc* Qs, const Acc* Ks, int D, int tx, int ty,
+                                            Acc (&acc)[4][4]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = Acc(0);
+#pragma unroll 4
+  for (int d = 0; d < D; ++d) {
+    Acc qa[4], kb[4];
+    load4(Qs + d * 64 + ty * 4, qa);
+    load4(Ks + d * 64 + tx * 4, kb);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = fma(qa[i], kb[j], acc[i][j]);
+  }
+}
+
+// ---------------------------------------------------------------- pass 1: lse2
+template <typename In, typename Acc>
+__global__ void __launch_bounds__(NT) simt_lse_kernel(Args<Acc> a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  Acc* Qs = reinterpret_cast<Acc*>(smem_raw);  // [D][64]
+  Acc* Ks = Qs + a.D * 64;                      // [D][64]
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int ntile = (a.N + BM - 1) / BM;
+  const int r0 = (ntile - 1 - (int)blockIdx.x) * BM;  // long (late) rows first
+  const int hidx = blockIdx.y;                         // (u - ub) * G + hh
+  const int u = a.ub + hidx / a.G, hh = hidx % a.G;
+  const int b = u / a.Hkv, g = u % a.Hkv, h = g * a.G + hh;
+
+  stage_tile<In, Acc>(Qs, a.q, b * a.qs0 + h * a.qs1, a.qs2, a.qs3, r0, a.N, a.D);
+
+  const int n_end = (a.causal && a.skip) ? min(a.N, r0 + BM) : a.N;
+  Acc m[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) { m[i] = neg_inf<Acc>(); l[i] = Acc(0); }
+
+  for (int n0 = 0; n0 < n_end; n0 += BN) {
+    __syncthreads();
+    stage_tile<In, Acc>(Ks, a.k, b * a.ks0 + g * a.ks1, a.ks2, a.ks3, n0, a.N, a.D);
+    __syncthreads();
+    Acc acc[4][4];
+    tile_scores(Qs, Ks, a.D, tx, ty, acc);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int row = r0 + ty * 4 + i;
+      Acc t[4];
+      Acc tmax = neg_inf<Acc>();
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int col = n0 + tx * 4 + j;
+        t[j] = keep_at(a, b, row, col) ? acc[i][j] * a.C : neg_inf<Acc>();
+        tmax = t[j] > tmax ? t[j] : tmax;
+      }
+      // Rescale only when the running max grows: a tile that is fully masked
+      // leaves (m, l) bit-identical, which keeps causal_skip on/off identical.
+      if (tmax > m[i]) {
+        l[i] = l[i] * fast_exp2(m[i] - tmax);
+        m[i] = tmax;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (t[j] != neg_inf<Acc>()) l[i] += fast_exp2(t[j] - m[i]);
+    }
+  }
+  // Merge the 16 per-thread partial (m, l) of each row (lanes sharing ty).
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+#pragma unroll
+    for (int off = 1; off < 16; off <<= 1) {
+      const Acc mo = __shfl_xor_sync(0xffffffffu, m[i], off);
+      const Acc lo = __shfl_xor_sync(0xffffffffu, l[i], off);
+      const Acc mn = mo > m[i] ? mo : m[i];
+      if (mn != neg_inf<Acc>()) {
+        l[i] = l[i] * fast_exp2(m[i] - mn) + lo * fast_exp2(mo - mn);
+        m[i] = mn;
+      }
+    }
+  }
+  if (tx == 0) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int row = r0 + ty * 4 + i;
+      if (row < a.N) {
+        // Rows that keep no key get +inf: 2^(t - inf) = 0, so they contribute 0.
+        a.lse[(long long)hidx * a.N + row] =
+            (m[i] == neg_inf<Acc>()) ? -neg_inf<Acc>() : m[i] + acc_log2(l[i]);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- pass 2: mass
+template <typename In, typename Acc>
+__global__ void __launch_bounds__(NT) simt_mass_kernel(Args<Acc> a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  Acc* Ks = reinterpret_cast<Acc*>(smem_raw);  // [D][64]
+  Acc* Qs = Ks + a.D * 64;                      // [D][64]
+  Acc* Ls = Qs + a.D * 64;                      // [64]
+  Acc* red = Ls + 64;                           // [16][64]
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int c0 = blockIdx.x * BN;
+  const int y = blockIdx.y;
+  const int uu = blockIdx.z;
+  const int u = a.ub + uu;
+  const int b = u / a.Hkv, g = u % a.Hkv;
+  const int qa = y * a.qchunk;
+  const int qb = min(a.N, qa + a.qchunk);
+  // Causal: rows < c0 keep no key of this tile.  With causal_skip the CTA
+  // starts at the first row tile that reaches c0 (tile boundaries stay those
+  // of the unskipped loop, so the same non-zero terms add in the same order).
+  int rs = qa;
+  if (a.causal && a.skip) {
+    if (qb - 1 < c0) return;  // whole chunk above the diagonal: nothing to add
+    if (c0 > qa) rs = qa + ((c0 - qa) / BM) * BM;
+  }
+  stage_tile<In, Acc>(Ks, a.k, b * a.ks0 + g * a.ks1, a.ks2, a.ks3, c0, a.N, a.D);
+  Acc cs[4] = {Acc(0), Acc(0), Acc(0), Acc(0)};
+  for (int hh = 0; hh < a.G; ++hh) {
+    const int h = g * a.G + hh;
+    const Acc* lse_h = a.lse + (long long)(uu * a.G + hh) * a.N;
+    for (int r0 = rs; r0 < qb; r0 += BM) {
+      __syncthreads();
+      stage_tile<In, Acc>(Qs, a.q, b * a.qs0 + h * a.qs1, a.qs2, a.qs3, r0, qb, a.D);
+      if (tid < BM) Ls[tid] = (r0 + tid < qb) ? lse_h[r0 + tid] : Acc(0);
+      __syncthreads();
+      Acc acc[4][4];
+      tile_scores(Qs, Ks, a.D, tx, ty, acc);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int row = r0 + ty * 4 + i;
+        if (row >= qb) continue;
+        const Acc L = Ls[ty * 4 + i];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int col = c0 + tx * 4 + j;
+          if (keep_at(a, b, row, col)) cs[j] += fast_exp2(acc[i][j] * a.C - L);
+        }
+      }
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < 4; ++j) red[ty * 64 + tx * 4 + j] = cs[j];
+  __syncthreads();
+  if (tid < BN) {
+    Acc s = Acc(0);
+#pragma unroll
+    for (int r = 0; r < 16; ++r) s += red[r * 64 + tid];
+    const int col = c0 + tid;
+    if (col < a.N) a.part[((long long)uu * a.nchunk + y) * a.N + col] = s;
+  }
+}
+
+template <typename In, typename Acc>
+int launch_typed(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s) {
+  Args<Acc> a;
+  a.q = p->q;
+  a.qs0 = p->q_stride[0]; a.qs1 = p->q_stride[1]; a.qs2 = p->q_stride[2]; a.qs3 = p->q_stride[3];
+  a.k = p->k;
+  a.ks0 = p->k_stride[0]; a.ks1 = p->k_stride[1]; a.ks2 = p->k_stride[2]; a.ks3 = p->k_stride[3];
+  a.N = p->N; a.D = p->D; a.G = p->Hq / p->Hkv; a.Hkv = p->Hkv; a.ub = p->unit_begin;
+  a.kmask = p->key_mask; a.kmb = p->key_mask_bstride;
+  a.qmask = p->query_mask; a.qmb = p->query_mask_bstride;
+  a.pmask = p->pair_mask; a.pmb = p->pair_mask_bstride; a.pmr = p->pair_mask_rstride;
+  a.C = static_cast<Acc>(p->scale * kLog2e);
+  a.causal = p->causal != 0;
+  a.skip = p->causal_skip != 0;
+  a.lse = reinterpret_cast<Acc*>(static_cast<char*>(ws) + L.lse_off);
+  a.part = reinterpret_cast<Acc*>(static_cast<char*>(ws) + L.part_off);
+  a.qchunk = L.qchunk;
+  a.nchunk = L.nchunk;
+
+  const int U = p->unit_end - p->unit_begin;
+  const size_t smem1 = size_t(2) * p->D * 64 * sizeof(Acc);
+  const size_t smem2 = smem1 + (64 + 16 * 64) * sizeof(Acc);
+  auto k1 = simt_lse_kernel<In, Acc>;
+  auto k2 = simt_mass_kernel<In, Acc>;
+  if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1) != cudaSuccess ||
+      cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2) != cudaSuccess)
+    return KVBM_ERR_CUDA;
+  dim3 g1((p->N + BM - 1) / BM, U * a.G);
+  k1<<<g1, NT, smem1, s>>>(a);
+  if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
+  dim3 g2((p->N + BN - 1) / BN, L.nchunk, U);
+  k2<<<g2, NT, smem2, s>>>(a);
+  if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
+  return KVBM_OK;
+}
+
+// ---------------------------------------------------------------- bucket reduce
+// mass[j] = sum over (unit, query chunk, key c in bucket j) of the partials,
+// accumulated in fp64 in a fixed order (deterministic).  With causal, a chunk
+// whose last row lies before the key tile start holds no kept pair and is not
+// read (its CTA either returned early or wrote exact zeros).
+template <typename Acc, typename Out>
+__global__ void __launch_bounds__(256) reduce_kernel(const Acc* part, Out* mass, int N, int bs,
+                                                     int U, int nchunk, int qchunk, int key_tile,
+                                                     int causal) {
+  __shared__ double warp_sums[8];
+  const int j = blockIdx.x;
+  const int cb = j * bs;
+  const int ce = min(N, cb + bs);
+  const int nk = ce - cb;
+  const long long total = (long long)U * nchunk * nk;
+  double s = 0.0;
+  for (long long idx = threadIdx.x; idx < total; idx += blockDim.x) {
+    const int c = cb + (int)(idx % nk);
+    const long long rest = idx / nk;
+    const int y = (int)(rest % nchunk);
+    const long long uu = rest / nchunk;
+    if (causal) {
+      const int c0 = (c / key_tile) * key_tile;
+      if ((long long)(y + 1) * qchunk - 1 < c0) continue;
+    }
+    s += (double)part[(uu * nchunk + y) * N + c];
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if ((threadIdx.x & 31) == 0) warp_sums[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += warp_sums[w];
+    mass[j] = static_cast<Out>(t);
+  }
+}
+
+}  // namespace
+
+int launch_simt(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws,
+                cudaStream_t s) {
+  (void)mass_out;
+  switch (p->dtype) {
+    case KVBM_F32: return launch_typed<float, float>(p, L, ws, s);
+    case KVBM_BF16: return launch_typed<__nv_bfloat16, float>(p, L, ws, s);
+    case KVBM_F16: return launch_typed<__half, float>(p, L, ws, s);
+    case KVBM_F64: return launch_typed<double, double>(p, L, ws, s);
+    default: return KVBM_ERR_DTYPE;
+  }
+}
+
+int launch_reduce(const kvbm_problem* p, const WsLayout& L, void* mass_out, const void* ws,
+                  cudaStream_t s) {
+  const int nb = (int)kvbm_num_blocks(p->N, p->block_size);
+  const int U = p->unit_end - p->unit_begin;
+  const char* base = static_cast<const char*>(ws) + L.part_off;
+  if (p->dtype == KVBM_F64) {
+    reduce_kernel<double, double><<<nb, 256, 0, s>>>(reinterpret_cast<const double*>(base),
+                                                     static_cast<double*>(mass_out), p->N,
+                                                     p->block_size, U, L.nchunk, L.qchunk,
+                                                     L.key_tile, p->causal != 0);
+  } else {
+    reduce_kernel<float, float><<<nb, 256, 0, s>>>(reinterpret_cast<const float*>(base),
+                                                   static_cast<float*>(mass_out), p->N,
+                                                   p->block_size, U, L.nchunk, L.qchunk,
+                                                   L.key_tile, p->causal != 0);
+  }
+  return cudaGetLastError() == cudaSuccess ? KVBM_OK : KVBM_ERR_CUDA;
+}
+
+}  // namespace kvbm

@@ -1,0 +1,36 @@
+"""kvblockmass_b200: block-granular attention mass on B200 (sm_100a).
+
+    mass[j] = sum over (b, h_q, query i, key c in block j) of softmax_c(q_i . k_c * scale)
+
+A drop-in for the GPU path of kv-block-mass (``block_mass`` /
+``block_mass_triton``), computed by hand-written CUDA kernels behind the C ABI
+of ``include/kvbm.h`` (``libkvbm.so``, loaded with ctypes).
+"""
+
+__version__ = "0.1.0"
+
+from .ops import (  # noqa: F401
+    block_mass,
+    block_mass_b200,
+    block_mass_triton,
+    kernel_path,
+    launches_per_call,
+    make_problem,
+    workspace_bytes,
+)
+from .workloads import WORKLOADS, Workload, make_inputs, pairs  # noqa: F401
+
+__all__ = [
+    "block_mass_b200",
+    "block_mass_triton",
+    "block_mass",
+    "kernel_path",
+    "make_problem",
+    "workspace_bytes",
+    "launches_per_call",
+    "WORKLOADS",
+    "Workload",
+    "make_inputs",
+    "pairs",
+    "__version__",
+]

@@ -1,0 +1,115 @@
+"""ctypes binding of ``libkvbm.so`` (C ABI declared in ``include/kvbm.h``).
+
+The library is built in-tree by ``kv-block-mass_b200/build.py``.  There is no
+fallback: if the library is missing or fails to load, every entry point raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libkvbm.so"
+
+KVBM_F32, KVBM_BF16, KVBM_F16, KVBM_F64 = 0, 1, 2, 3
+
+KVBM_OK = 0
+KVBM_ERR_GQA = 1
+KVBM_ERR_SHAPE = 2
+KVBM_ERR_DTYPE = 3
+KVBM_ERR_HEAD_DIM = 4
+KVBM_ERR_BLOCK_SIZE = 5
+KVBM_ERR_UNITS = 6
+KVBM_ERR_NULL = 7
+KVBM_ERR_WORKSPACE = 8
+KVBM_ERR_CUDA = 9
+KVBM_ERR_DEVICE = 10
+KVBM_ERR_TIMEOUT = 11
+KVBM_ERR_SCRATCH = 12
+
+# Symbols include/kvbm.h declares; tests check the library exports each one.
+EXPORTED = [
+    "kvbm_abi_version",
+    "kvbm_status_string",
+    "kvbm_validate",
+    "kvbm_num_blocks",
+    "kvbm_workspace_bytes",
+    "kvbm_kernel_path",
+    "kvbm_launches_per_call",
+    "kvbm_block_mass",
+    "kvbm_check_device_errors",
+]
+
+
+class Problem(ctypes.Structure):
+    """Mirror of ``struct kvbm_problem``."""
+
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("q_stride", ctypes.c_int64 * 4),
+        ("k", ctypes.c_void_p),
+        ("k_stride", ctypes.c_int64 * 4),
+        ("dtype", ctypes.c_int32),
+        ("B", ctypes.c_int32),
+        ("Hq", ctypes.c_int32),
+        ("Hkv", ctypes.c_int32),
+        ("N", ctypes.c_int32),
+        ("D", ctypes.c_int32),
+        ("key_mask", ctypes.c_void_p),
+        ("key_mask_bstride", ctypes.c_int64),
+        ("query_mask", ctypes.c_void_p),
+        ("query_mask_bstride", ctypes.c_int64),
+        ("pair_mask", ctypes.c_void_p),
+        ("pair_mask_bstride", ctypes.c_int64),
+        ("pair_mask_rstride", ctypes.c_int64),
+        ("scale", ctypes.c_double),
+        ("block_size", ctypes.c_int32),
+        ("causal", ctypes.c_int32),
+        ("causal_skip", ctypes.c_int32),
+        ("unit_begin", ctypes.c_int32),
+        ("unit_end", ctypes.c_int32),
+    ]
+
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load ``libkvbm.so`` once and declare its signatures."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise RuntimeError(
+            f"{LIB_PATH} is missing: build it with `python kv-block-mass_b200/build.py` "
+            "(there is no CPU fallback for the block-mass kernels)")
+    lib = ctypes.CDLL(os.fspath(LIB_PATH))
+    P = ctypes.POINTER(Problem)
+    lib.kvbm_abi_version.restype = ctypes.c_int
+    lib.kvbm_abi_version.argtypes = []
+    lib.kvbm_status_string.restype = ctypes.c_char_p
+    lib.kvbm_status_string.argtypes = [ctypes.c_int]
+    lib.kvbm_validate.restype = ctypes.c_int
+    lib.kvbm_validate.argtypes = [P]
+    lib.kvbm_num_blocks.restype = ctypes.c_int64
+    lib.kvbm_num_blocks.argtypes = [ctypes.c_int32, ctypes.c_int32]
+    lib.kvbm_workspace_bytes.restype = ctypes.c_size_t
+    lib.kvbm_workspace_bytes.argtypes = [P]
+    lib.kvbm_kernel_path.restype = ctypes.c_int
+    lib.kvbm_kernel_path.argtypes = [P]
+    lib.kvbm_launches_per_call.restype = ctypes.c_int
+    lib.kvbm_launches_per_call.argtypes = [P]
+    lib.kvbm_block_mass.restype = ctypes.c_int
+    lib.kvbm_block_mass.argtypes = [P, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                    ctypes.c_void_p]
+    lib.kvbm_check_device_errors.restype = ctypes.c_int
+    lib.kvbm_check_device_errors.argtypes = [ctypes.c_void_p]
+    if lib.kvbm_abi_version() != 1:
+        raise RuntimeError(f"libkvbm ABI {lib.kvbm_abi_version()} != 1")
+    _lib = lib
+    return lib
+
+
+def status_string(code: int) -> str:
+    return load().kvbm_status_string(int(code)).decode()

@@ -1,0 +1,236 @@
+"""Python entry points for the B200 block-mass kernels.
+
+Drop-in for the reference's GPU path (kv-block-mass):
+
+* ``block_mass_b200`` accepts every argument of ``block_mass_reference``
+  (``src/kvblockmass/reference.py:35-45``) and of ``block_mass_triton``
+  (``src/kvblockmass/triton_kernel.py:148-158``); ``BLOCK_M``/``BLOCK_N``/
+  ``query_chunk`` are accepted and ignored (tiling is the kernel's choice),
+  ``device`` moves CPU inputs to that CUDA device first (``reference.py:74-76``).
+* ``block_mass_triton`` keeps the reference kernel wrapper's exact signature.
+* ``block_mass`` is the dispatcher of ``reference.py:129-135`` for CUDA tensors.
+
+Errors follow the reference: ``H_q % H_kv != 0`` raises ``ValueError`` with
+the reference's message (``reference.py:29-30``, ``triton_kernel.py:161-162``).
+There is no CPU path: CPU tensors without a CUDA ``device`` raise ``ValueError``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+__all__ = ["block_mass_b200", "block_mass_triton", "block_mass", "kernel_path", "make_problem",
+           "workspace_bytes", "launches_per_call"]
+
+_DTYPES = {
+    torch.float32: _lib.KVBM_F32,
+    torch.bfloat16: _lib.KVBM_BF16,
+    torch.float16: _lib.KVBM_F16,
+    torch.float64: _lib.KVBM_F64,
+}
+
+_VALUE_ERRORS = {
+    _lib.KVBM_ERR_GQA, _lib.KVBM_ERR_SHAPE, _lib.KVBM_ERR_DTYPE, _lib.KVBM_ERR_HEAD_DIM,
+    _lib.KVBM_ERR_BLOCK_SIZE, _lib.KVBM_ERR_UNITS, _lib.KVBM_ERR_NULL, _lib.KVBM_ERR_SCRATCH,
+}
+
+
+def _raise(code: int, prob: "_lib.Problem"):
+    if code == _lib.KVBM_ERR_GQA:
+        raise ValueError(f"GQA requires H_q % H_kv == 0, got H_q={prob.Hq}, H_kv={prob.Hkv}")
+    msg = f"kvbm error {code}: {_lib.status_string(code)}"
+    if code in _VALUE_ERRORS:
+        raise ValueError(msg)
+    raise RuntimeError(msg)
+
+
+def _as_mask(m: torch.Tensor, device) -> torch.Tensor:
+    m = m.to(device=device)
+    if m.dtype != torch.bool:
+        m = m != 0
+    return m
+
+
+class _Prepared:
+    """A filled ``kvbm_problem`` plus the tensors it points into (kept alive)."""
+
+    def __init__(self, prob, keep, out_dtype, nb):
+        self.prob = prob
+        self.keep = keep
+        self.out_dtype = out_dtype
+        self.nb = nb
+
+
+def make_problem(q, k, attn_mask=None, causal=False, block_size=64, scale=None,
+                 causal_skip=True, query_mask=None, units=None) -> _Prepared:
+    """Validate arguments and build the C ``kvbm_problem`` for ``q``/``k``.
+
+    Mask shapes (True = keep; combined with ``causal`` by AND):
+    ``attn_mask``: ``[N]`` key mask, ``[N, N]`` pair mask (the reference's two
+    forms), ``[B|1, 1, N]`` per-batch key mask, ``[B|1, N, N]`` per-batch pair
+    mask; ``query_mask``: ``[N]`` or ``[B, N]`` rows to keep (a dropped row
+    contributes exactly 0, as a pair-mask row that keeps nothing would).
+    """
+    if not (isinstance(q, torch.Tensor) and isinstance(k, torch.Tensor)):
+        raise TypeError("q and k must be torch tensors")
+    if q.dim() != 4 or k.dim() != 4:
+        raise ValueError(f"q and k must be 4-D [B, H, N, D], got {tuple(q.shape)} and {tuple(k.shape)}")
+    B, Hq, N, D = q.shape
+    if k.shape[0] != B or k.shape[2] != N or k.shape[3] != D:
+        raise ValueError(f"k shape {tuple(k.shape)} does not match q shape {tuple(q.shape)}")
+    Hkv = k.shape[1]
+    if Hkv == 0 or Hq % Hkv != 0:
+        raise ValueError(f"GQA requires H_q % H_kv == 0, got H_q={Hq}, H_kv={Hkv}")
+    if q.device != k.device:
+        raise ValueError(f"q and k are on different devices ({q.device}, {k.device})")
+    if q.dtype != k.dtype:
+        common = torch.promote_types(q.dtype, k.dtype)
+        q, k = q.to(common), k.to(common)
+    if q.dtype not in _DTYPES:
+        raise ValueError(f"unsupported dtype {q.dtype}; expected float32, bfloat16, float16 or float64")
+    if N == 0:
+        raise ValueError("N must be >= 1")
+    if block_size is None or int(block_size) < 1:
+        raise ValueError("block_size must be >= 1")
+    if scale is None:
+        scale = 1.0 / D ** 0.5
+    dev = q.device
+    keep = [q, k]
+    prob = _lib.Problem()
+    prob.q = q.data_ptr()
+    prob.k = k.data_ptr()
+    for i in range(4):
+        prob.q_stride[i] = q.stride(i)
+        prob.k_stride[i] = k.stride(i)
+    prob.dtype = _DTYPES[q.dtype]
+    prob.B, prob.Hq, prob.Hkv, prob.N, prob.D = B, Hq, Hkv, N, D
+
+    if attn_mask is not None:
+        m = _as_mask(attn_mask, dev)
+        if m.dim() == 1:
+            if m.shape[0] != N:
+                raise ValueError(f"attn_mask of shape {tuple(m.shape)} does not match N={N}")
+            m = m.contiguous()
+            prob.key_mask, prob.key_mask_bstride = m.data_ptr(), 0
+        elif m.dim() == 2:
+            if tuple(m.shape) != (N, N):
+                raise ValueError(f"attn_mask of shape {tuple(m.shape)} is not [N, N] with N={N}")
+            if m.stride(1) != 1:
+                m = m.contiguous()
+            prob.pair_mask, prob.pair_mask_bstride, prob.pair_mask_rstride = m.data_ptr(), 0, m.stride(0)
+        elif m.dim() == 3:
+            if m.shape[0] not in (1, B) or m.shape[1] not in (1, N) or m.shape[2] != N:
+                raise ValueError(f"attn_mask of shape {tuple(m.shape)} is not [B|1, 1|N, N]")
+            if m.stride(2) != 1:
+                m = m.contiguous()
+            bstride = m.stride(0) if m.shape[0] > 1 else 0
+            if m.shape[1] == 1:
+                prob.key_mask, prob.key_mask_bstride = m.data_ptr(), bstride
+            else:
+                prob.pair_mask = m.data_ptr()
+                prob.pair_mask_bstride, prob.pair_mask_rstride = bstride, m.stride(1)
+        else:
+            raise ValueError(f"attn_mask must be 1-D, 2-D or 3-D, got {m.dim()}-D")
+        keep.append(m)
+    if query_mask is not None:
+        qm = _as_mask(query_mask, dev)
+        if qm.dim() == 1:
+            qm = qm.reshape(1, -1)
+        if qm.dim() != 2 or qm.shape[0] not in (1, B) or qm.shape[1] != N:
+            raise ValueError(f"query_mask of shape {tuple(qm.shape)} is not [N] or [B, N]")
+        qm = qm.contiguous()
+        prob.query_mask = qm.data_ptr()
+        prob.query_mask_bstride = qm.stride(0) if qm.shape[0] > 1 else 0
+        keep.append(qm)
+
+    prob.scale = float(scale)
+    prob.block_size = int(block_size)
+    prob.causal = int(bool(causal))
+    prob.causal_skip = int(bool(causal_skip))
+    ub, ue = (0, B * Hkv) if units is None else (int(units[0]), int(units[1]))
+    prob.unit_begin, prob.unit_end = ub, ue
+    code = _lib.load().kvbm_validate(ctypes.byref(prob))
+    if code != _lib.KVBM_OK:
+        _raise(code, prob)
+    nb = (N + int(block_size) - 1) // int(block_size)
+    out_dtype = torch.float64 if q.dtype == torch.float64 else torch.float32
+    return _Prepared(prob, keep, out_dtype, nb)
+
+
+def workspace_bytes(prep: _Prepared) -> int:
+    return int(_lib.load().kvbm_workspace_bytes(ctypes.byref(prep.prob)))
+
+
+def kernel_path(prep: _Prepared) -> int:
+    """0 = SIMT kernels, 1 = tcgen05 tensor-core kernels (on the current device)."""
+    return int(_lib.load().kvbm_kernel_path(ctypes.byref(prep.prob)))
+
+
+def launches_per_call(prep: _Prepared) -> int:
+    return int(_lib.load().kvbm_launches_per_call(ctypes.byref(prep.prob)))
+
+
+def run_prepared(prep: _Prepared, out: torch.Tensor | None = None,
+                 workspace: torch.Tensor | None = None,
+                 stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """Launch the kernels of a prepared problem on ``stream`` (default: current)."""
+    q = prep.keep[0]
+    dev = q.device
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws_need = int(lib.kvbm_workspace_bytes(ctypes.byref(prep.prob)))
+        if workspace is None or workspace.numel() < ws_need:
+            workspace = torch.empty(max(ws_need, 256), dtype=torch.uint8, device=dev)
+        if out is None:
+            out = torch.empty(prep.nb, dtype=prep.out_dtype, device=dev)
+        elif out.dtype != prep.out_dtype or out.numel() != prep.nb or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous {prep.out_dtype} tensor of {prep.nb} elements")
+        s = stream if stream is not None else torch.cuda.current_stream(dev)
+        code = lib.kvbm_block_mass(ctypes.byref(prep.prob), out.data_ptr(), workspace.data_ptr(),
+                                   workspace.numel(), s.cuda_stream)
+    if code != _lib.KVBM_OK:
+        _raise(code, prep.prob)
+    return out
+
+
+def block_mass_b200(q, k, attn_mask=None, causal=False, block_size=64, scale=None,
+                    causal_skip=True, query_mask=None, *, BLOCK_M=None, BLOCK_N=None,
+                    query_chunk=None, device=None, units=None, out=None, workspace=None):
+    """Block-pooled column sums of the softmax attention matrix on a B200.
+
+    Returns ``mass [ceil(N / block_size)]`` (float32; float64 for float64
+    inputs) on the CUDA device of ``q``.  ``units=(begin, end)`` restricts the
+    sum to the (batch, kv-head) units ``[begin, end)`` of ``B * H_kv`` (used by
+    the multi-GPU shards); ``out``/``workspace`` let callers reuse buffers.
+    """
+    del BLOCK_M, BLOCK_N, query_chunk  # tiling is fixed by the kernels
+    if device is not None:
+        dev = torch.device(device)
+        if dev.type != "cuda":
+            raise ValueError(f"block_mass_b200 computes on CUDA devices only, got device={device}")
+        q, k = q.to(dev), k.to(dev)
+    if not (q.is_cuda and k.is_cuda):
+        raise ValueError("block_mass_b200 needs CUDA tensors (there is no CPU path); "
+                         "pass device='cuda' or use the reference's block_mass_reference")
+    prep = make_problem(q, k, attn_mask=attn_mask, causal=causal, block_size=block_size,
+                        scale=scale, causal_skip=causal_skip, query_mask=query_mask, units=units)
+    return run_prepared(prep, out=out, workspace=workspace)
+
+
+def block_mass_triton(q, k, attn_mask=None, causal=False, block_size=64, scale=None,
+                      BLOCK_M=64, BLOCK_N=64, causal_skip=True):
+    """Same signature as the reference's ``block_mass_triton`` (``triton_kernel.py:148-158``)."""
+    return block_mass_b200(q, k, attn_mask=attn_mask, causal=causal, block_size=block_size,
+                           scale=scale, causal_skip=causal_skip, BLOCK_M=BLOCK_M, BLOCK_N=BLOCK_N)
+
+
+def block_mass(q, k, **kwargs):
+    """Dispatcher of ``reference.py:129-135``: CUDA tensors run the B200 kernels."""
+    if q.is_cuda or kwargs.get("device") not in (None, "cpu"):
+        return block_mass_b200(q, k, **kwargs)
+    raise ValueError("kvblockmass_b200.block_mass handles CUDA tensors; CPU tensors belong to "
+                     "the reference's block_mass_reference")

@@ -1,0 +1,141 @@
+"""C-ABI library checks that need no GPU: load, exports, host-side validation."""
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+import torch
+
+from kvblockmass_b200 import _lib
+from kvblockmass_b200.ops import make_problem
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADERS = sorted((ROOT / "include").glob("*.h"))
+
+
+def declared_functions():
+    names = []
+    for h in HEADERS:
+        text = h.read_text()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names += re.findall(r"\b(kvbm_\w+)\s*\(", text)
+    return sorted(set(names))
+
+
+def test_library_loads():
+    lib = _lib.load()
+    assert lib.kvbm_abi_version() == 1
+
+
+def test_every_declared_symbol_is_exported():
+    decl = declared_functions()
+    assert "kvbm_block_mass" in decl
+    lib = _lib.load()
+    for name in decl:
+        assert hasattr(lib, name), f"{name} declared in include/*.h but not exported"
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)],
+                         capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (kvbm_\w+)", out))
+    assert set(decl) <= exported
+    assert set(_lib.EXPORTED) <= exported
+
+
+def _problem(**kw):
+    p = _lib.Problem()
+    p.q = 16
+    p.k = 16
+    B, Hq, Hkv, N, D = kw.get("shape", (1, 8, 2, 128, 64))
+    p.B, p.Hq, p.Hkv, p.N, p.D = B, Hq, Hkv, N, D
+    for i, s in enumerate((Hq * N * D, N * D, D, 1)):
+        p.q_stride[i] = s
+    for i, s in enumerate((Hkv * N * D, N * D, D, 1)):
+        p.k_stride[i] = s
+    p.dtype = kw.get("dtype", _lib.KVBM_F32)
+    p.scale = 0.125
+    p.block_size = kw.get("block_size", 64)
+    p.causal = 1
+    p.causal_skip = 1
+    p.unit_begin, p.unit_end = kw.get("units", (0, B * Hkv))
+    return p
+
+
+@pytest.mark.parametrize("kw,code", [
+    ({}, _lib.KVBM_OK),
+    ({"shape": (1, 6, 4, 8, 4)}, _lib.KVBM_ERR_GQA),
+    ({"shape": (1, 8, 2, 0, 64)}, _lib.KVBM_ERR_SHAPE),
+    ({"dtype": 7}, _lib.KVBM_ERR_DTYPE),
+    ({"shape": (1, 8, 2, 128, 300)}, _lib.KVBM_ERR_HEAD_DIM),
+    ({"shape": (1, 8, 2, 128, 200), "dtype": _lib.KVBM_F64}, _lib.KVBM_ERR_HEAD_DIM),
+    ({"block_size": 0}, _lib.KVBM_ERR_BLOCK_SIZE),
+    ({"units": (0, 3)}, _lib.KVBM_ERR_UNITS),
+    ({"units": (1, 1)}, _lib.KVBM_ERR_UNITS),
+])
+def test_validate_codes(kw, code):
+    lib = _lib.load()
+    assert lib.kvbm_validate(ctypes.byref(_problem(**kw))) == code
+    assert _lib.status_string(code)
+
+
+def test_num_blocks_and_workspace():
+    lib = _lib.load()
+    assert lib.kvbm_num_blocks(100, 64) == 2       # KVBM-05: ragged last block
+    assert lib.kvbm_num_blocks(2048, 64) == 32
+    assert lib.kvbm_num_blocks(16, 64) == 1
+    p = _problem()
+    ws = lib.kvbm_workspace_bytes(ctypes.byref(p))
+    # lse2 [U*G*N] + per-key partials [U*nchunk*N], fp32
+    assert ws >= (2 * 4 * 128 + 2 * 1 * 128) * 4
+    assert ws % 256 == 0
+    assert lib.kvbm_workspace_bytes(ctypes.byref(_problem(shape=(1, 6, 4, 8, 4)))) == 0
+    assert lib.kvbm_launches_per_call(ctypes.byref(p)) == 3
+
+
+def test_block_mass_without_device_fails_cleanly():
+    """No GPU here: the compute entry point reports an error, it never falls back."""
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    lib = _lib.load()
+    p = _problem()
+    code = lib.kvbm_block_mass(ctypes.byref(p), ctypes.c_void_p(256), ctypes.c_void_p(256), 1 << 20, None)
+    assert code in (_lib.KVBM_ERR_CUDA, _lib.KVBM_ERR_DEVICE)
+
+
+def test_python_wrapper_errors_match_reference():
+    """ValueError with the reference's message for GQA (reference.py:29-30, KVBM-06)."""
+    q = torch.randn(1, 6, 8, 4)
+    k = torch.randn(1, 4, 8, 4)
+    with pytest.raises(ValueError, match=r"GQA requires H_q % H_kv == 0, got H_q=6, H_kv=4"):
+        make_problem(q, k, block_size=4)
+    with pytest.raises(ValueError):
+        make_problem(torch.randn(1, 2, 8, 4), torch.randn(1, 1, 9, 4))
+    with pytest.raises(ValueError):
+        make_problem(torch.randn(1, 2, 8, 4), torch.randn(1, 1, 8, 4), attn_mask=torch.ones(7, dtype=torch.bool))
+
+
+def test_cpu_tensors_are_rejected():
+    from kvblockmass_b200 import block_mass, block_mass_b200
+
+    q = torch.randn(1, 2, 8, 4)
+    k = torch.randn(1, 1, 8, 4)
+    with pytest.raises(ValueError, match="CUDA"):
+        block_mass_b200(q, k)
+    with pytest.raises(ValueError):
+        block_mass(q, k)
+
+
+def test_signatures_are_drop_in():
+    """Every argument of the reference's entry points is accepted."""
+    import inspect
+
+    from kvblockmass_b200 import block_mass_b200, block_mass_triton
+
+    ref_reference = ["q", "k", "attn_mask", "causal", "block_size", "scale", "query_chunk", "device",
+                     "causal_skip"]                       # reference.py:35-45
+    ref_triton = ["q", "k", "attn_mask", "causal", "block_size", "scale", "BLOCK_M", "BLOCK_N",
+                  "causal_skip"]                          # triton_kernel.py:148-158
+    params = inspect.signature(block_mass_b200).parameters
+    for name in ref_reference + ref_triton:
+        assert name in params, name
+    assert list(inspect.signature(block_mass_triton).parameters) == ref_triton

@@ -1,0 +1,239 @@
+"""GPU parity: the CUDA kernels (through the C ABI) against the reference's
+golden outputs and the CPU oracle.
+
+Tolerances (max relative error per bucket, |a-b| / max(|b|, 1e-6)):
+  * fp64 inputs: 1e-9 against the reference's fp64 output;
+  * fp32 inputs: 2e-5 against the reference's fp32 output;
+  * bf16/fp16 inputs: 1e-3 against the reference fed the same values upcast
+    to fp32.
+Sum rule sum(mass) = B * H_q * (#rows that keep a key) to 1e-5 relative;
+causal_skip on/off and repeated runs bit-identical (torch.equal).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden
+from _helpers import case_inputs, checksum_ok, max_rel
+from oracle import block_mass_np as orc
+
+import kvblockmass_b200 as kb
+from kvblockmass_b200.workloads import WORKLOADS, make_inputs
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float64: 1e-9, torch.float32: 2e-5, torch.bfloat16: 1e-3, torch.float16: 1e-3}
+
+
+def run(q, k, **kw):
+    out = kb.block_mass_b200(q, k, **kw)
+    torch.cuda.synchronize()
+    return out
+
+
+def oracle_for(q, k, **kw):
+    """CPU oracle on the exact values the kernel saw (upcast to fp32/fp64)."""
+    qn = q.detach().cpu()
+    kn = k.detach().cpu()
+    if qn.dtype in (torch.bfloat16, torch.float16):
+        qn, kn = qn.float(), kn.float()
+    km = kw.pop("attn_mask", None)
+    qm = kw.pop("query_mask", None)
+    return orc.block_mass_stream(qn.numpy(), kn.numpy(),
+                                 attn_mask=None if km is None else km.cpu().numpy(),
+                                 query_mask=None if qm is None else qm.cpu().numpy(), **kw)
+
+
+# ------------------------------------------------------------ golden: small cases
+@pytest.mark.parametrize("idx", range(22))
+@pytest.mark.parametrize("dtype", [torch.float64, torch.float32, torch.bfloat16])
+def test_small_cases(cuda_device, small_cases, idx, dtype):
+    c = small_cases[idx]
+    q, k, mask = case_inputs(c)
+    qd, kd = q.to(dtype).to(cuda_device), k.to(dtype).to(cuda_device)
+    md = None if mask is None else mask.to(cuda_device)
+    got = run(qd, kd, attn_mask=md, causal=c["causal"], block_size=c["block_size"])
+    assert got.dtype == (torch.float64 if dtype == torch.float64 else torch.float32)
+    assert got.shape == (len(c["mass_ref_fp64"]),)
+    assert torch.isfinite(got).all()
+    if dtype == torch.float64:
+        want = c["mass_ref_fp64"]
+    elif dtype == torch.float32:
+        want = c["mass_ref_fp32"]
+    else:
+        want = oracle_for(qd, kd, attn_mask=md, causal=c["causal"], block_size=c["block_size"])
+    assert max_rel(got.cpu().numpy(), want) < TOL[dtype], c["name"]
+    # sum rule against the reference's fp64 total
+    total = float(np.sum(c["mass_ref_fp64"]))
+    assert abs(float(got.double().sum()) - total) <= 1e-5 * max(total, 1.0)
+
+
+# ------------------------------------------------------------ golden: workloads
+@pytest.mark.parametrize("name", ["cpu_ref_n2048", "gqa_n8192_fp32"])
+def test_fp32_workloads_vs_reference(cuda_device, name):
+    g = load_golden(name)
+    w = WORKLOADS[name]
+    q, k, _, _ = make_inputs(w)
+    assert checksum_ok(q, g["q_checksum"]) and checksum_ok(k, g["k_checksum"])
+    qd, kd = q.to(cuda_device), k.to(cuda_device)
+    a = run(qd, kd, causal=w.causal, block_size=w.block_size)
+    b = run(qd, kd, causal=w.causal, block_size=w.block_size, causal_skip=False)
+    c = run(qd, kd, causal=w.causal, block_size=w.block_size)
+    assert torch.equal(a, b), "causal_skip on/off must be bit-identical"
+    assert torch.equal(a, c), "repeated runs must be bit-identical"
+    assert max_rel(a.cpu().numpy(), g["mass_ref_fp32"]) < 2e-5
+    assert max_rel(a.cpu().numpy(), g["mass_ref_fp64"]) < 2e-5
+    expect = w.B * w.Hq * w.N
+    assert abs(float(a.double().sum()) - expect) <= 1e-5 * expect
+
+
+@pytest.mark.parametrize("name", ["llama3_8b_n32k", "batched_masked_n16k"])
+def test_bf16_workloads_vs_reference(cuda_device, name):
+    g = load_golden(name)
+    if g is None:
+        pytest.skip(f"golden fixture {name}.json not generated")
+    w = WORKLOADS[name]
+    q, k, km, qm = make_inputs(w)
+    assert checksum_ok(q, g["q_checksum"]) and checksum_ok(k, g["k_checksum"])
+    qd, kd = q.to(cuda_device), k.to(cuda_device)
+    kmd = None if km is None else km.to(cuda_device)
+    qmd = None if qm is None else qm.to(cuda_device)
+    a = run(qd, kd, attn_mask=kmd, query_mask=qmd, causal=w.causal, block_size=w.block_size)
+    assert max_rel(a.cpu().numpy(), g["mass_ref_fp32"]) < 1e-3
+    alive = w.B * w.N if qm is None else int(qm.sum())
+    expect = w.Hq * alive
+    assert abs(float(a.double().sum()) - expect) <= 1e-5 * expect
+    if w.causal:
+        b = run(qd, kd, attn_mask=kmd, query_mask=qmd, causal=w.causal, block_size=w.block_size,
+                causal_skip=False)
+        assert torch.equal(a, b)
+
+
+def test_dead_rows_contribute_exactly_zero(cuda_device):
+    """Rows that keep nothing add exactly 0: masking them equals dropping them."""
+    w = WORKLOADS["batched_masked_n16k"]
+    q, k, km, qm = make_inputs(w, N=1024)
+    qd, kd, kmd, qmd = q.to(cuda_device), k.to(cuda_device), km.to(cuda_device), qm.to(cuda_device)
+    a = run(qd, kd, attn_mask=kmd, query_mask=qmd, block_size=w.block_size)
+    # the same rows removed through an [B, N, N] pair mask
+    pair = (km[None, None, :] & qm[:, :, None]).to(cuda_device)
+    b = run(qd, kd, attn_mask=pair, block_size=w.block_size)
+    assert max_rel(a.cpu().numpy(), b.cpu().numpy()) < 1e-5
+    want = oracle_for(qd, kd, attn_mask=km, query_mask=qm, block_size=w.block_size)
+    assert max_rel(a.cpu().numpy(), want) < 1e-3
+    expect = w.Hq * int(qm.sum())
+    assert abs(float(a.double().sum()) - expect) <= 1e-5 * expect
+
+
+# ------------------------------------------------------------ masks and shapes
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("kind", ["keys", "pairs", "batch_keys", "batch_pairs", "query"])
+@pytest.mark.parametrize("causal", [False, True])
+def test_mask_kinds(cuda_device, dtype, kind, causal):
+    g = torch.Generator().manual_seed(101)
+    B, Hq, Hkv, N, D = 2, 4, 2, 333, 64
+    q = torch.randn(B, Hq, N, D, generator=g).to(dtype)
+    k = torch.randn(B, Hkv, N, D, generator=g).to(dtype)
+    kw = {}
+    if kind == "keys":
+        kw["attn_mask"] = torch.rand(N, generator=g) > 0.25
+    elif kind == "pairs":
+        kw["attn_mask"] = torch.rand(N, N, generator=g) > 0.4
+    elif kind == "batch_keys":
+        kw["attn_mask"] = torch.rand(B, 1, N, generator=g) > 0.25
+    elif kind == "batch_pairs":
+        kw["attn_mask"] = torch.rand(B, N, N, generator=g) > 0.4
+    else:
+        kw["query_mask"] = torch.rand(B, N, generator=g) > 0.3
+    dev = {n: v.to(cuda_device) for n, v in kw.items()}
+    got = run(q.to(cuda_device), k.to(cuda_device), causal=causal, block_size=48, **dev)
+    want = oracle_for(q, k, causal=causal, block_size=48, **kw)
+    assert max_rel(got.cpu().numpy(), want) < TOL[dtype]
+
+
+@pytest.mark.parametrize("N", [1, 2, 63, 64, 65, 127, 128, 129, 255, 257, 1000])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_ragged_lengths(cuda_device, N, dtype):
+    g = torch.Generator().manual_seed(N)
+    q = torch.randn(1, 4, N, 128, generator=g).to(dtype)
+    k = torch.randn(1, 2, N, 128, generator=g).to(dtype)
+    for causal in (True, False):
+        got = run(q.to(cuda_device), k.to(cuda_device), causal=causal, block_size=64)
+        want = oracle_for(q, k, causal=causal, block_size=64)
+        assert max_rel(got.cpu().numpy(), want) < TOL[dtype], (N, causal)
+
+
+@pytest.mark.parametrize("D", [8, 16, 32, 64, 96, 128, 256])
+def test_head_dims(cuda_device, D):
+    g = torch.Generator().manual_seed(D)
+    q = torch.randn(1, 2, 300, D, generator=g)
+    k = torch.randn(1, 1, 300, D, generator=g)
+    for dtype in (torch.float32, torch.bfloat16):
+        got = run(q.to(dtype).to(cuda_device), k.to(dtype).to(cuda_device), causal=True, block_size=32)
+        want = oracle_for(q.to(dtype), k.to(dtype), causal=True, block_size=32)
+        assert max_rel(got.cpu().numpy(), want) < TOL[dtype]
+
+
+def test_strided_inputs_match_contiguous(cuda_device):
+    """q/k as views of [B, N, H, D] storage (the common KV layout) give the same bits."""
+    g = torch.Generator().manual_seed(3)
+    for dtype in (torch.float32, torch.bfloat16):
+        qs = torch.randn(2, 500, 8, 128, generator=g).to(dtype).to(cuda_device)
+        ks = torch.randn(2, 500, 2, 128, generator=g).to(dtype).to(cuda_device)
+        qv, kv = qs.transpose(1, 2), ks.transpose(1, 2)
+        a = run(qv, kv, causal=True, block_size=64)
+        b = run(qv.contiguous(), kv.contiguous(), causal=True, block_size=64)
+        assert torch.equal(a, b)
+
+
+def test_units_shard_and_sum(cuda_device):
+    """Mass is a sum over (batch, kv-head) units: shards add up to the whole."""
+    g = torch.Generator().manual_seed(9)
+    q = torch.randn(2, 8, 700, 64, generator=g).to(torch.bfloat16).to(cuda_device)
+    k = torch.randn(2, 2, 700, 64, generator=g).to(torch.bfloat16).to(cuda_device)
+    full = run(q, k, causal=True, block_size=64)
+    parts = [run(q, k, causal=True, block_size=64, units=(u, u + 1)) for u in range(4)]
+    assert max_rel(sum(p.double() for p in parts).cpu().numpy(), full.double().cpu().numpy()) < 1e-6
+    u2 = run(q, k, causal=True, block_size=64, units=(1, 3))
+    assert max_rel(u2.cpu().numpy(), (parts[1].double() + parts[2].double()).cpu().numpy()) < 1e-6
+
+
+def test_drop_in_entry_points(cuda_device):
+    g = torch.Generator().manual_seed(31)
+    q = torch.randn(2, 4, 256, 32, generator=g, dtype=torch.float64).float()
+    k = torch.randn(2, 2, 256, 32, generator=g, dtype=torch.float64).float()
+    want = oracle_for(q, k, causal=True, block_size=64)
+    qd, kd = q.to(cuda_device), k.to(cuda_device)
+    for fn in (lambda: kb.block_mass_triton(qd, kd, causal=True, block_size=64),
+               lambda: kb.block_mass(qd, kd, causal=True, block_size=64),
+               lambda: kb.block_mass_b200(q, k, causal=True, block_size=64, device="cuda",
+                                          query_chunk=128)):
+        got = fn()
+        assert got.is_cuda
+        assert max_rel(got.cpu().numpy(), want) < 2e-5
+
+
+def test_peak_memory_n4096(cuda_device):
+    """O(N) workspace: N=4096 must not allocate anything like an [N, N] matrix
+    (the reference's bound, tests/test_triton.py:85-103)."""
+    g = torch.Generator().manual_seed(47)
+    q = torch.randn(1, 8, 4096, 64, generator=g).to(cuda_device)
+    k = torch.randn(1, 2, 4096, 64, generator=g).to(cuda_device)
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    torch.cuda.reset_peak_memory_stats()
+    base = torch.cuda.memory_allocated()
+    run(q, k, causal=True, block_size=64)
+    peak = (torch.cuda.max_memory_allocated() - base) / 2**20
+    assert peak < 64, f"peak {peak:.1f} MiB"
+
+
+def test_determinism_bf16(cuda_device):
+    g = torch.Generator().manual_seed(77)
+    q = torch.randn(1, 8, 3000, 128, generator=g).to(torch.bfloat16).to(cuda_device)
+    k = torch.randn(1, 2, 3000, 128, generator=g).to(torch.bfloat16).to(cuda_device)
+    a = run(q, k, causal=True, block_size=64)
+    b = run(q, k, causal=True, block_size=64, causal_skip=False)
+    c = run(q, k, causal=True, block_size=64)
+    assert torch.equal(a, b) and torch.equal(a, c)
