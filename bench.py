@@ -1,0 +1,427 @@
+#!/usr/bin/env python
+"""Benchmark: causal block-mass QK pairs/sec on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload NAME]
+
+A step is one pass of the hot path (pass 1 row log-sum-exp, pass 2 per-key
+partials, bucket reduce) over one synthetic batch of the Llama-3-8B attention
+shape (B=1, H_q=32, H_kv=8, D=128, N=32768, block 64, causal, bf16), with
+inputs resident in HBM.  With N GPUs (torchrun, one rank per GPU) every rank
+owns one batch entry of that shape (weak scaling: per-GPU work is fixed) and
+the per-rank mass vectors are combined by one NCCL reduce to rank 0 inside
+each step.
+
+Reported beside the device-timed value:
+  e2e           the same metric through the public API (block_mass_b200 on
+                pinned host tensors, device="cuda"), H2D of q/k and D2H of the
+                mass inside the timed region;
+  roofline      the dominant kernel's algorithmic tensor FLOP/s against the
+                measured bf16 peak, and its exp rate against the MUFU ex2
+                rate measured live on this GPU (the binding unit);
+  cpu_baseline  the CPU oracle (a numpy restatement of the reference's
+                streaming algorithm) on a bounded sample, all host cores.
+`--impl reference` times only that CPU restatement (rank 0), as the
+reference arm.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "kv-block-mass_b200"))
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "causal block-mass QK pairs/sec at Llama-3-8B shape N=32k; % tensor/MUFU peak"
+UNIT = "QK pairs/s"
+DEFAULT_WORKLOAD = "llama3_8b_n32k"
+L2_BYTES = 126 * 2**20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
+    ap.add_argument("--cpu-seconds", type=float, default=8.0,
+                    help="target CPU time of the bounded CPU-baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    return ap.parse_args()
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d.get("hbm_gbs"), "bf16_tflops": d.get("bf16_tflops"),
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def traffic_record(workload: str):
+    """DRAM bytes per launch of each kernel from a committed ncu summary, if any."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    return d.get(workload)
+
+
+# ----------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling in the background (rank 0)."""
+
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus: list[int]):
+        self.gpus = gpus
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-i", ",".join(map(str, self.gpus)), "-lms", "50"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        self.t_start = time.time()
+        return self
+
+    def mark(self):
+        return time.time()
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self, t0: float, t1: float):
+        if self.proc is None or self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 10:
+                continue
+            try:
+                ts = time.mktime(time.strptime(parts[0].split(".")[0], "%Y/%m/%d %H:%M:%S"))
+                frac = float("0." + parts[0].split(".")[1]) if "." in parts[0] else 0.0
+                rows.append((ts + frac, parts))
+            except (ValueError, IndexError):
+                continue
+        inside = [r for r in rows if t0 - 0.06 <= r[0] <= t1 + 0.06]
+        window = "timed region"
+        if len(inside) < 3:
+            inside = [r for r in rows if r[0] >= t0 - 2.0]
+            window = "timed region +/- neighbouring steady-state steps (short timed region)"
+        os.unlink(self.file.name)
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = [float(r[1][2]) for r in inside if r[1][2].replace(".", "").isdigit()]
+        mx = [float(r[1][3]) for r in inside if r[1][3].replace(".", "").isdigit()]
+        pw = [float(r[1][4]) for r in inside if r[1][4].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in inside for n, v in zip(names, r[1][6:10]) if v.strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(pw) if pw else None, "reasons": reasons, "samples": len(inside),
+                "window": window}
+
+
+# ------------------------------------------------------------------- CPU sample
+def cpu_sample(w, seconds: float):
+    """Time the CPU oracle on a bounded sample of workload ``w`` (all host cores).
+
+    The sample is the q-heads of the first (batch, kv-head) unit over a range of
+    query rows [r0, N) at the end of the sequence (the longest causal rows),
+    sized from a one-chunk calibration to take about ``seconds``.
+    """
+    from threadpoolctl import threadpool_limits
+
+    from kvblockmass_b200.workloads import make_inputs
+    from oracle.block_mass_np import block_mass_stream, sample_pairs
+
+    cores = os.cpu_count() or 1
+    q, k, km, qm = make_inputs(w)
+    G = w.Hq // w.Hkv
+    qn = q[:1, :G].float().numpy()
+    kn = k[:1, :1].float().numpy()
+    kmn = None if km is None else km.numpy()
+    qmn = None if qm is None else qm[:1].numpy()
+    chunk = 256
+
+    def run(rows):
+        with threadpool_limits(limits=1):
+            t0 = time.perf_counter()
+            block_mass_stream(qn, kn, attn_mask=kmn, query_mask=qmn, causal=w.causal,
+                              block_size=w.block_size, rows=rows, threads=cores, split_rows=True)
+            return time.perf_counter() - t0
+
+    n = w.N
+    t1 = run((n - chunk, n))
+    pairs1 = sample_pairs(G, 1, n, (n - chunk, n), w.causal)
+    want_pairs = pairs1 * max(1.0, seconds / max(t1, 1e-3))
+    r0 = n - chunk
+    while r0 > 0 and sample_pairs(G, 1, n, (r0, n), w.causal) < want_pairs:
+        r0 -= chunk
+    r0 = max(r0, 0)
+    t = run((r0, n))
+    pairs = sample_pairs(G, 1, n, (r0, n), w.causal)
+    return {
+        "value": pairs / t, "unit": UNIT, "cores": cores, "kind": "port",
+        "sample": (f"oracle/block_mass_np.py (numpy restatement of reference.py:35-126) on "
+                   f"unit (b=0, kv-head 0) = {G} q-heads x query rows [{r0}, {n}) of {w.name}: "
+                   f"{pairs:.3e} pairs in {t:.2f} s"),
+        "seconds": t, "pairs": pairs,
+    }
+
+
+def reference_arm(args, w):
+    """--impl reference: the CPU restatement of the reference's algorithm, rank 0 only."""
+    steps, warm = args.steps, args.warmup
+    per_step = max(1.0, min(8.0, 150.0 / max(1, steps + warm)))
+    for _ in range(warm):
+        cpu_sample(w, per_step)
+    rates, secs, last = [], [], None
+    for _ in range(steps):
+        last = cpu_sample(w, per_step)
+        rates.append(last["value"])
+        secs.append(last["seconds"])
+    value = statistics.median(rates)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
+        "warmup": warm, "ms_per_step": statistics.median(secs) * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "impl": "reference",
+        "config": workload_config(w, args.gpus),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": last["cores"], "kind": "port",
+                         "sample": last["sample"] + " (each step one such sample; value = median rate)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": ("the reference is pure Python (torch CPU + Triton); its CPU path is timed through "
+                 "the committed numpy restatement of src/kvblockmass/reference.py:35-126"),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(w, world: int):
+    return {
+        "workload": w.name, "B_per_rank": w.B, "global_batch": w.B * world, "Hq": w.Hq, "Hkv": w.Hkv,
+        "D": w.D, "seq_len": w.N, "block_size": w.block_size, "causal": w.causal,
+        "parallelism": f"units{world}" if world > 1 else "single",
+        "shard": "each rank owns B_per_rank batch entries (B*H_kv units); NCCL reduce of mass to rank 0",
+        "inputs_exceed_l2": True, "l2_flush": "none (q+k per step exceed the 126 MB L2)",
+    }
+
+
+# ------------------------------------------------------------------- B200 arm
+def b200_arm(args, w):
+    import torch.distributed as dist
+
+    import kvblockmass_b200 as kb
+    from kvblockmass_b200 import _lib, ops
+    from kvblockmass_b200.workloads import make_inputs, pairs
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    lib = _lib.load()
+
+    # Inputs: rank r owns batch entry r of the weak-scaled problem (seed offset by rank).
+    from dataclasses import replace
+    wr = replace(w, seed=w.seed + 1000 * rank) if rank else w
+    q_cpu, k_cpu, km, qm = make_inputs(wr)
+    q_pin, k_pin = q_cpu.pin_memory(), k_cpu.pin_memory()
+    q = q_pin.to(dev)
+    k = k_pin.to(dev)
+    kmd = None if km is None else km.to(dev)
+    qmd = None if qm is None else qm.to(dev)
+    prep = ops.make_problem(q, k, attn_mask=kmd, query_mask=qmd, causal=w.causal, block_size=w.block_size)
+    path = ops.kernel_path(prep)
+    ws = torch.empty(max(ops.workspace_bytes(prep), 256), dtype=torch.uint8, device=dev)
+    out = torch.empty(prep.nb, dtype=prep.out_dtype, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    pairs_rank = pairs(w)
+    launches = ops.launches_per_call(prep)
+
+    def step(events=None):
+        if events is None:
+            code = lib.kvbm_block_mass(ctypes.byref(prep.prob), out.data_ptr(), ws.data_ptr(), ws.numel(),
+                                       stream.cuda_stream)
+        else:
+            arr = (ctypes.c_void_p * 4)(*[e.cuda_event for e in events])
+            code = lib.kvbm_block_mass_events(ctypes.byref(prep.prob), out.data_ptr(), ws.data_ptr(),
+                                              ws.numel(), stream.cuda_stream, arr)
+        if code != 0:
+            raise RuntimeError(f"kvbm_block_mass failed: {_lib.status_string(code)}")
+        if world > 1:
+            dist.reduce(out, dst=0, op=dist.ReduceOp.SUM)
+
+    # Warm-up (also creates the NCCL communicator).
+    for _ in range(max(args.warmup, 0)):
+        step()
+    torch.cuda.synchronize()
+    if lib.kvbm_check_device_errors(stream.cuda_stream) != 0:
+        raise RuntimeError("a device-side wait timed out during warm-up")
+
+    # Timed region: K steps, CUDA events on the launching stream, per-pass events inside.
+    K = args.steps
+    pass_events = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(list(range(torch.cuda.device_count())) if world > 1 else [local]) \
+        if rank == 0 else None
+    if sampler:
+        sampler.__enter__()
+        time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_wall0 = time.time()
+    e_start.record(stream)
+    for i in range(K):
+        step(pass_events[i])
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    if world > 1:
+        dist.barrier()
+    ms_local = e_start.elapsed_time(e_end)
+    ms_t = torch.tensor([ms_local], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_total = float(ms_t.item())
+    p1 = [ev[0].elapsed_time(ev[1]) for ev in pass_events]
+    p2 = [ev[1].elapsed_time(ev[2]) for ev in pass_events]
+    p3 = [ev[2].elapsed_time(ev[3]) for ev in pass_events]
+    if lib.kvbm_check_device_errors(stream.cuda_stream) != 0:
+        raise RuntimeError("a device-side wait timed out in the timed region")
+
+    # End to end through the public API: pinned host q/k in, mass back on the host.
+    e2e = None
+    if not args.no_e2e:
+        Ke = args.e2e_steps or max(3, min(K, 10))
+        kb.block_mass_b200(q_pin, k_pin, attn_mask=kmd, query_mask=qmd, causal=w.causal,
+                           block_size=w.block_size, device=dev).cpu()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(Ke):
+            m = kb.block_mass_b200(q_pin, k_pin, attn_mask=kmd, query_mask=qmd, causal=w.causal,
+                                   block_size=w.block_size, device=dev)
+            if world > 1:
+                dist.reduce(m, dst=0, op=dist.ReduceOp.SUM)
+            m_host = m.cpu()
+        a1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = torch.tensor([a0.elapsed_time(a1)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+        e2e = {"value": pairs_rank * world * Ke / (float(e_ms.item()) * 1e-3), "unit": UNIT,
+               "h2d_bytes_per_step": int(q_pin.numel() * q_pin.element_size() + k_pin.numel() * k_pin.element_size()),
+               "d2h_bytes_per_step": int(m_host.numel() * m_host.element_size()),
+               "steps": Ke, "api": "kvblockmass_b200.block_mass_b200(pinned host q/k, device='cuda').cpu()"}
+
+    # Roofline: calibration of the MUFU ex2 rate on this GPU, then the dominant kernel.
+    ex2 = ctypes.c_double(0.0)
+    if lib.kvbm_measure_ex2_rate(stream.cuda_stream, ctypes.byref(ex2)) != 0:
+        ex2.value = float("nan")
+    clocks = None
+    if sampler:
+        sampler.__exit__(None, None, None)
+        clocks = sampler.summary(t_wall0, t_wall1)
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peaks = measured_peaks()
+    t1, t2, t3 = statistics.mean(p1), statistics.mean(p2), statistics.mean(p3)
+    dom_name, dom_ms = ("pass2_mass", t2) if t2 >= t1 else ("pass1_lse", t1)
+    flops = pairs_rank * 2 * w.D                      # algorithmic tensor FLOPs per launch
+    achieved_tflops = flops / (dom_ms * 1e-3) / 1e12
+    exp_rate = pairs_rank / (dom_ms * 1e-3)           # one ex2 per pair per pass
+    tensor_peak = peaks["bf16_tflops"]
+    bound_time = max(flops / (tensor_peak * 1e12), pairs_rank / ex2.value)
+    binding = "mufu_ex2" if pairs_rank / ex2.value >= flops / (tensor_peak * 1e12) else "tensor"
+    tr = traffic_record(w.name)
+    traffic = None
+    if tr and dom_name in tr:
+        traffic = tr[dom_name]
+    value = pairs_rank * world * K / (ms_total * 1e-3)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": ms_total / K, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": workload_config(w, world),
+        "kernel_path": "tcgen05" if path == 1 else "simt",
+        "kernel_ms": {"pass1_lse": t1, "pass2_mass": t2, "reduce": t3},
+        "roofline": {
+            "bound": "tensor", "achieved": achieved_tflops, "peak": tensor_peak, "unit": "TFLOP/s",
+            "frac": achieved_tflops / tensor_peak, "traffic": traffic, "kernel": dom_name,
+            "peak_source": f"{peaks['source']} bf16_tflops (burst) of MEASURED_PEAKS.json",
+            "binding_unit": binding,
+            "mufu": {"achieved_ex2_per_s": exp_rate, "peak_ex2_per_s": ex2.value,
+                     "frac": exp_rate / ex2.value, "peak_source": "measured live (kvbm_measure_ex2_rate)"},
+            "frac_of_binding": (bound_time / (dom_ms * 1e-3)),
+            "algorithmic_per_launch": {"pairs": pairs_rank, "tensor_flops": flops, "ex2": pairs_rank},
+        },
+        "gpu_launches": K * launches,
+        "clocks": clocks,
+    }
+    if e2e:
+        line["e2e"] = e2e
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = {k: v for k, v in cpu_sample(w, args.cpu_seconds).items()
+                                if k not in ("seconds", "pairs")}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    from kvblockmass_b200.workloads import WORKLOADS
+
+    w = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) != 0:
+            return 0
+        reference_arm(args, w)
+        return 0
+    b200_arm(args, w)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

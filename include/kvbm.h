@@ -139,6 +139,22 @@ int kvbm_launches_per_call(const kvbm_problem* p);
 int kvbm_block_mass(const kvbm_problem* p, void* mass_out, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/* kvbm_block_mass that also records up to four CUDA events (cudaEvent_t,
+ * each may be NULL) on `stream`: events[0] before pass 1, events[1] between
+ * pass 1 and pass 2, events[2] between pass 2 and the bucket reduce,
+ * events[3] after the reduce.  Per-kernel timing for benchmarks; it replaces
+ * the CUDA-event timing of the reference's bench (bench/bench_block_mass.py:37-54)
+ * at kernel rather than call granularity. */
+int kvbm_block_mass_events(const kvbm_problem* p, void* mass_out, void* workspace,
+                           size_t workspace_bytes, void* stream, void* const* events);
+
+/* Measures the current device's MUFU ex2.approx.f32 throughput (results per
+ * second, all SMs) with a calibration kernel, timed with CUDA events on
+ * `stream`; synchronises `stream`.  The exp/sum warps of both passes are
+ * bound by this rate, so benchmarks report it as the roofline denominator.
+ * No counterpart in the reference. */
+int kvbm_measure_ex2_rate(void* stream, double* ex2_per_second);
+
 /* Reads and clears the device-side error word of the current device (set
  * when a bounded wait inside a tcgen05 kernel gave up).  Synchronises
  * `stream`.  Returns KVBM_OK, KVBM_ERR_TIMEOUT or KVBM_ERR_CUDA. */

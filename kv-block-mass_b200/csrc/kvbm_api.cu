@@ -57,6 +57,7 @@ int select_path(const kvbm_problem* p, int device) {
   if (p->dtype != KVBM_BF16 && p->dtype != KVBM_F16) return 0;
   if (p->D != 64 && p->D != 128) return 0;
   if (p->pair_mask != nullptr) return 0;
+  if (!(p->scale > 0.0)) return 0;  // the exp/sum warps assume a positive scale
   const int64_t* qs = p->q_stride;
   const int64_t* ks = p->k_stride;
   if (qs[3] != 1 || ks[3] != 1) return 0;
@@ -75,8 +76,11 @@ WsLayout layout_for(const kvbm_problem* p, int path) {
   L.nchunk = (p->N + L.qchunk - 1) / L.qchunk;
   const size_t U = (size_t)(p->unit_end - p->unit_begin);
   const size_t G = (size_t)(p->Hq / p->Hkv);
+  // The tensor-core path pads each head's lse2 row to whole 128-row tiles
+  // (padding rows hold +inf) so that pass 2 can bulk-copy full tiles.
+  const size_t n_lse = path == 1 ? (size_t)(p->N + kTcTile - 1) / kTcTile * kTcTile : (size_t)p->N;
   L.lse_off = 0;
-  L.lse_bytes = U * G * (size_t)p->N * L.acc_bytes;
+  L.lse_bytes = U * G * n_lse * L.acc_bytes;
   L.part_off = align_up(L.lse_off + L.lse_bytes, 256);
   L.part_bytes = U * (size_t)L.nchunk * (size_t)p->N * L.acc_bytes;
   L.total = align_up(L.part_off + L.part_bytes, 256);
@@ -152,6 +156,11 @@ int kvbm_launches_per_call(const kvbm_problem* p) {
 
 int kvbm_block_mass(const kvbm_problem* p, void* mass_out, void* workspace,
                     size_t workspace_bytes, void* stream) {
+  return kvbm_block_mass_events(p, mass_out, workspace, workspace_bytes, stream, nullptr);
+}
+
+int kvbm_block_mass_events(const kvbm_problem* p, void* mass_out, void* workspace,
+                           size_t workspace_bytes, void* stream, void* const* events) {
   int st = validate(p);
   if (st != KVBM_OK) return st;
   if (mass_out == nullptr) return KVBM_ERR_NULL;
@@ -166,10 +175,19 @@ int kvbm_block_mass(const kvbm_problem* p, void* mass_out, void* workspace,
   if (workspace == nullptr || workspace_bytes < L.total || ((uintptr_t)workspace % 256) != 0)
     return KVBM_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  st = (path == 1) ? launch_tc(p, L, mass_out, workspace, s)
-                   : launch_simt(p, L, mass_out, workspace, s);
+  auto mark = [&](int i) {
+    if (events != nullptr && events[i] != nullptr)
+      return cudaEventRecord(static_cast<cudaEvent_t>(events[i]), s) == cudaSuccess;
+    return true;
+  };
+  if (!mark(0)) return KVBM_ERR_CUDA;
+  st = (path == 1) ? launch_tc(p, L, mass_out, workspace, s, events != nullptr ? events[1] : nullptr)
+                   : launch_simt(p, L, mass_out, workspace, s, events != nullptr ? events[1] : nullptr);
   if (st != KVBM_OK) return st;
-  return launch_reduce(p, L, mass_out, workspace, s);
+  if (!mark(2)) return KVBM_ERR_CUDA;
+  st = launch_reduce(p, L, mass_out, workspace, s);
+  if (st != KVBM_OK) return st;
+  return mark(3) ? KVBM_OK : KVBM_ERR_CUDA;
 }
 
 int kvbm_check_device_errors(void* stream) {

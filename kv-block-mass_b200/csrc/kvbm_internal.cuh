@@ -41,8 +41,11 @@ int select_path(const kvbm_problem* p, int device);
 WsLayout layout_for(const kvbm_problem* p, int path);
 
 // Launchers (return a kvbm_status).
-int launch_simt(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws, cudaStream_t s);
-int launch_tc(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws, cudaStream_t s);
+// `mid_event` (a cudaEvent_t or null) is recorded between pass 1 and pass 2.
+int launch_simt(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws, cudaStream_t s,
+                void* mid_event);
+int launch_tc(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws, cudaStream_t s,
+              void* mid_event);
 int launch_reduce(const kvbm_problem* p, const WsLayout& L, void* mass_out, const void* ws,
                   cudaStream_t s);
 

@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(NT) simt_mass_kernel(Args<Acc> a) {
 }
 
 template <typename In, typename Acc>
-int launch_typed(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s) {
+int launch_typed(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s, void* mid_event) {
   Args<Acc> a;
   a.q = p->q;
   a.qs0 = p->q_stride[0]; a.qs1 = p->q_stride[1]; a.qs2 = p->q_stride[2]; a.qs3 = p->q_stride[3];
@@ -301,6 +301,8 @@ int launch_typed(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_
   dim3 g1((p->N + BM - 1) / BM, U * a.G);
   k1<<<g1, NT, smem1, s>>>(a);
   if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
+  if (mid_event != nullptr && cudaEventRecord(static_cast<cudaEvent_t>(mid_event), s) != cudaSuccess)
+    return KVBM_ERR_CUDA;
   dim3 g2((p->N + BN - 1) / BN, L.nchunk, U);
   k2<<<g2, NT, smem2, s>>>(a);
   if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
@@ -348,13 +350,13 @@ __global__ void __launch_bounds__(256) reduce_kernel(const Acc* part, Out* mass,
 }  // namespace
 
 int launch_simt(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws,
-                cudaStream_t s) {
+                cudaStream_t s, void* mid_event) {
   (void)mass_out;
   switch (p->dtype) {
-    case KVBM_F32: return launch_typed<float, float>(p, L, ws, s);
-    case KVBM_BF16: return launch_typed<__nv_bfloat16, float>(p, L, ws, s);
-    case KVBM_F16: return launch_typed<__half, float>(p, L, ws, s);
-    case KVBM_F64: return launch_typed<double, double>(p, L, ws, s);
+    case KVBM_F32: return launch_typed<float, float>(p, L, ws, s, mid_event);
+    case KVBM_BF16: return launch_typed<__nv_bfloat16, float>(p, L, ws, s, mid_event);
+    case KVBM_F16: return launch_typed<__half, float>(p, L, ws, s, mid_event);
+    case KVBM_F64: return launch_typed<double, double>(p, L, ws, s, mid_event);
     default: return KVBM_ERR_DTYPE;
   }
 }

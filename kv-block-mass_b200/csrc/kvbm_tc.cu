@@ -1,0 +1,546 @@
+// tcgen05 (sm_100a tensor core) block-mass kernels for bf16 / fp16 inputs
+// with head dim 64 or 128.
+//
+// Both passes stream 128 x 128 score tiles through TMEM:
+//   warp 0     TMA producer (one elected lane): Q/K tiles -> 128B-swizzled smem
+//   warp 1     MMA issuer (one lane) + TMEM owner: tcgen05.mma kind::f16, fp32
+//              accumulators in two 128-column TMEM buffers
+//   warps 2-5  exp/sum warpgroup: tcgen05.ld, one thread per accumulator row
+//
+// Pass 1 (row log-sum-exp) follows the reference Triton kernel's pass 1
+// (kv-block-mass src/kvblockmass/triton_kernel.py:69-104): S = Q K^T with
+// query rows as the MMA's M; each thread owns a query row and keeps its
+// online max / denominator in registers.  Causal tiles stop at the query
+// tile's last row (triton_kernel.py:57-60).
+//
+// Pass 2 (mass) recomputes the scores transposed, S^T = K Q^T with key rows as
+// M, so each thread owns one key and sums 2^(t - lse2) over every query of
+// every head of its GQA group (triton_kernel.py:106-145, reference.py:121-124)
+// in registers.  One partial per (unit, query chunk, key) goes to the
+// workspace; the SIMT reduce (kvbm_simt.cu) adds them in a fixed order.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include "kvbm_internal.cuh"
+#include "kvbm_sm100.cuh"
+
+namespace kvbm {
+
+namespace {
+using namespace sm100;
+
+constexpr int TILE = kTcTile;       // 128
+constexpr int kThreads = 192;       // 6 warps
+constexpr int kStages = 2;          // K (pass 1) / Q (pass 2) ring depth
+constexpr int kTmemCols = 256;      // two 128-column fp32 accumulators
+constexpr int kMinSmem = 100 * 1024;  // caps residency at 2 CTAs/SM (TMEM: 2 x 256 columns)
+
+struct TcArgs {
+  int N, Npad, G, Hkv, ub;
+  float C;                 // scale * log2(e), > 0
+  int causal, skip;
+  const uint8_t* kmask;    // [B|1, N] or null
+  long long kmb;
+  const uint8_t* qmask;    // [B|1, N] or null
+  long long qmb;
+  float* lse;              // [U_sel * G, Npad]
+  float* part;             // [U_sel, nchunk, N]
+  int qchunk, nchunk;
+};
+
+template <int D>
+struct Cfg {
+  static constexpr int kBlocks = D / 64;          // 128-byte K-blocks per row
+  static constexpr int kBlockBytes = TILE * 128;  // 16 KB
+  static constexpr int kTileBytes = TILE * D * 2;
+  static constexpr int kSteps = D / 16;           // K=16 MMAs per tile
+};
+
+__device__ __forceinline__ uint8_t* align1k(uint8_t* p) {
+  const uint32_t a = smem_u32(p);
+  return p + ((1024u - (a & 1023u)) & 1023u);
+}
+
+// Issue the MMAs of one 128 x 128 tile: D[tmem] = A[128 x D] * B[128 x D]^T.
+template <int D>
+__device__ __forceinline__ void issue_tile_mma(uint32_t d_tmem, uint32_t a_smem, uint32_t b_smem,
+                                               uint32_t idesc) {
+#pragma unroll
+  for (int kk = 0; kk < Cfg<D>::kSteps; ++kk) {
+    const uint32_t koff = (kk >> 2) * Cfg<D>::kBlockBytes + (kk & 3) * 32;
+    mma_f16(d_tmem, sw128_desc(a_smem + koff), sw128_desc(b_smem + koff), idesc, kk > 0 ? 1u : 0u);
+  }
+}
+
+__device__ __forceinline__ void load_row128(uint32_t taddr, float (&v)[128]) {
+  tmem_ld32(taddr + 0, *reinterpret_cast<float(*)[32]>(&v[0]));
+  tmem_ld32(taddr + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+  tmem_ld32(taddr + 64, *reinterpret_cast<float(*)[32]>(&v[64]));
+  tmem_ld32(taddr + 96, *reinterpret_cast<float(*)[32]>(&v[96]));
+  tmem_ld_wait();
+}
+
+// ============================================================ pass 1: lse2
+// grid (U_sel * G, ceil(N / 128)); blockIdx.y counts query tiles from the
+// last (longest under causal_skip) to the first.
+template <int D, bool kBF16, bool kKeyMask>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_lse_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk, TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1k(smem_raw);
+  constexpr int TB = Cfg<D>::kTileBytes;
+  uint8_t* q_tile = smem;
+  uint8_t* k_ring = smem + TB;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TB * (1 + kStages));
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + kStages;
+  uint64_t* s_full = k_empty + kStages;
+  uint64_t* s_empty = s_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hidx = blockIdx.x;
+  const int u = a.ub + hidx / a.G, hh = hidx % a.G;
+  const int b = u / a.Hkv, g = u % a.Hkv, h = g * a.G + hh;
+  const int ntiles = (a.N + TILE - 1) / TILE;
+  const int qt = ntiles - 1 - (int)blockIdx.y;
+  const int r0 = qt * TILE;
+  const int nkt = (a.causal && a.skip) ? min(ntiles, qt + 1) : ntiles;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 128);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tq);
+      prefetch_tmap(&tk);
+      mbar_arrive_expect_tx(q_full, TB);
+#pragma unroll
+      for (int kb = 0; kb < Cfg<D>::kBlocks; ++kb)
+        tma_load_4d(q_tile + kb * Cfg<D>::kBlockBytes, &tq, q_full, kb * 64, r0, h, b);
+      int issued = 0;
+      for (int j = 0; j < nkt; ++j) {
+        const int s = j % kStages, n = j / kStages;
+        if (n > 0 && !mbar_wait(&k_empty[s], (n - 1) & 1, abort_flag)) break;
+        uint8_t* dst = k_ring + s * TB;
+        mbar_arrive_expect_tx(&k_full[s], TB);
+#pragma unroll
+        for (int kb = 0; kb < Cfg<D>::kBlocks; ++kb)
+          tma_load_4d(dst + kb * Cfg<D>::kBlockBytes, &tk, &k_full[s], kb * 64, j * TILE, g, b);
+        issued = j + 1;
+      }
+      // Do not leave while our copies are in flight.
+      mbar_wait(q_full, 0, abort_flag);
+      for (int j = max(0, issued - kStages); j < issued; ++j)
+        mbar_wait(&k_full[j % kStages], (j / kStages) & 1, abort_flag);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(TILE, TILE, kBF16);
+      const uint32_t qs = smem_u32(q_tile), ks = smem_u32(k_ring);
+      int issued = 0;
+      if (mbar_wait(q_full, 0, abort_flag)) {
+        for (int j = 0; j < nkt; ++j) {
+          const int s = j % kStages, buf = j & 1;
+          if (!mbar_wait(&k_full[s], (j / kStages) & 1, abort_flag)) break;
+          if (j >= 2 && !mbar_wait(&s_empty[buf], ((j >> 1) - 1) & 1, abort_flag)) break;
+          tc_fence_after();
+          issue_tile_mma<D>(tmem + buf * TILE, qs, ks + s * TB, idesc);
+          mma_commit(&k_empty[s]);
+          mma_commit(&s_full[buf]);
+          issued = j + 1;
+        }
+      }
+      if (issued > 0) mbar_wait(&s_full[(issued - 1) & 1], ((issued - 1) >> 1) & 1, abort_flag);
+    }
+  } else {
+    // exp/sum warpgroup: thread owns query row r0 + rl.
+    const int sub = warp & 3;
+    const int rl = sub * 32 + lane;
+    const int row = r0 + rl;
+    const uint32_t trow = tmem + ((uint32_t)(sub * 32) << 16);
+    const uint8_t* kmask = kKeyMask ? a.kmask + b * a.kmb : nullptr;
+    float m = -INFINITY, l = 0.f;
+    for (int j = 0; j < nkt; ++j) {
+      const int buf = j & 1;
+      const bool ok = mbar_wait(&s_full[buf], (j >> 1) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      float v[128];
+      load_row128(trow + buf * TILE, v);
+      tc_fence_before();
+      mbar_arrive(&s_empty[buf]);
+
+      const int c0 = j * TILE;
+      uint32_t kw[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
+      if (kKeyMask) {
+#pragma unroll
+        for (int qd = 0; qd < 4; ++qd) {
+          const int col = c0 + qd * 32 + lane;
+          kw[qd] = __ballot_sync(0xffffffffu, col < a.N && kmask[col] != 0);
+        }
+      }
+      const bool need_mask = kKeyMask || (c0 + TILE > a.N) || (a.causal && c0 + TILE - 1 > r0);
+      if (need_mask) {
+        const int lim_causal = a.causal ? row - c0 : TILE - 1;  // keep col_local <= row - c0
+        const int lim_n = a.N - 1 - c0;                         // keep col_local <= N-1-c0
+        const int lim = min(lim_causal, lim_n);
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          const bool keep = (c <= lim) && ((kw[c >> 5] >> (c & 31)) & 1u);
+          v[c] = keep ? v[c] : -INFINITY;
+        }
+      }
+      float tmax = v[0];
+#pragma unroll
+      for (int c = 1; c < 128; ++c) tmax = fmaxf(tmax, v[c]);
+      if (tmax != -INFINITY) {
+        const float mt = tmax * a.C;
+        if (mt > m) {
+          l = l * ex2(m - mt);
+          m = mt;
+        }
+        const float nm = -m;
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+        for (int c = 0; c < 128; c += 4) {
+          s0 += ex2(fmaf(v[c + 0], a.C, nm));
+          s1 += ex2(fmaf(v[c + 1], a.C, nm));
+          s2 += ex2(fmaf(v[c + 2], a.C, nm));
+          s3 += ex2(fmaf(v[c + 3], a.C, nm));
+        }
+        l += (s0 + s1) + (s2 + s3);
+      }
+    }
+    bool dead = (m == -INFINITY) || row >= a.N;
+    if (!dead && a.qmask != nullptr) dead = a.qmask[b * a.qmb + row] == 0;
+    // Rows that keep no key (and padding rows) get +inf: 2^(t - inf) = 0.
+    a.lse[(long long)(hidx) * a.Npad + row] = dead ? INFINITY : m + log2f(l);
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ============================================================ pass 2: mass
+// grid (U_sel, nchunk, ceil(N / 128)): one CTA owns 128 keys of one
+// (batch, kv-head) unit and one chunk of query rows, for every head of the
+// GQA group.
+template <int D, bool kBF16, bool kKeyMask>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_mass_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk, TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1k(smem_raw);
+  constexpr int TB = Cfg<D>::kTileBytes;
+  constexpr int LB = TILE * 4;  // lse2 bytes of one query tile
+  uint8_t* k_tile = smem;
+  uint8_t* q_ring = smem + TB;
+  float* l_ring = reinterpret_cast<float*>(smem + TB * (1 + kStages));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TB * (1 + kStages) + LB * kStages);
+  uint64_t* k_full = bars;
+  uint64_t* q_full = bars + 1;
+  uint64_t* q_empty = q_full + kStages;
+  uint64_t* s_full = q_empty + kStages;
+  uint64_t* s_empty = s_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int uu = blockIdx.x, y = blockIdx.y, kt = blockIdx.z;
+  const int u = a.ub + uu;
+  const int b = u / a.Hkv, g = u % a.Hkv;
+  const int c0 = kt * TILE;
+  const int qa = y * a.qchunk;
+  const int qb = min(a.N, qa + a.qchunk);
+  int rs = qa;
+  if (a.causal && a.skip) {
+    if (qb - 1 < c0) return;  // chunk entirely above the diagonal: nothing kept
+    rs = max(qa, c0);
+  }
+  const int nqt = (qb - rs + TILE - 1) / TILE;
+  const int J = a.G * nqt;
+
+  if (threadIdx.x == 0) {
+    mbar_init(k_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&q_full[s], 1);
+      mbar_init(&q_empty[s], 1 + 128);  // MMA commit + every exp thread done with lse2
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 128);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tq);
+      prefetch_tmap(&tk);
+      mbar_arrive_expect_tx(k_full, TB);
+#pragma unroll
+      for (int kb = 0; kb < Cfg<D>::kBlocks; ++kb)
+        tma_load_4d(k_tile + kb * Cfg<D>::kBlockBytes, &tk, k_full, kb * 64, c0, g, b);
+      int issued = 0;
+      for (int j = 0; j < J; ++j) {
+        const int s = j % kStages, n = j / kStages;
+        if (n > 0 && !mbar_wait(&q_empty[s], (n - 1) & 1, abort_flag)) break;
+        const int hh = j / nqt;
+        const int r = rs + (j - hh * nqt) * TILE;
+        const int h = g * a.G + hh;
+        mbar_arrive_expect_tx(&q_full[s], TB + LB);
+#pragma unroll
+        for (int kb = 0; kb < Cfg<D>::kBlocks; ++kb)
+          tma_load_4d(q_ring + s * TB + kb * Cfg<D>::kBlockBytes, &tq, &q_full[s], kb * 64, r, h, b);
+        bulk_load(l_ring + s * TILE, a.lse + (long long)(uu * a.G + hh) * a.Npad + r, LB, &q_full[s]);
+        issued = j + 1;
+      }
+      mbar_wait(k_full, 0, abort_flag);
+      for (int j = max(0, issued - kStages); j < issued; ++j)
+        mbar_wait(&q_full[j % kStages], (j / kStages) & 1, abort_flag);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(TILE, TILE, kBF16);
+      const uint32_t ks = smem_u32(k_tile), qs = smem_u32(q_ring);
+      int issued = 0;
+      if (mbar_wait(k_full, 0, abort_flag)) {
+        for (int j = 0; j < J; ++j) {
+          const int s = j % kStages, buf = j & 1;
+          if (!mbar_wait(&q_full[s], (j / kStages) & 1, abort_flag)) break;
+          if (j >= 2 && !mbar_wait(&s_empty[buf], ((j >> 1) - 1) & 1, abort_flag)) break;
+          tc_fence_after();
+          issue_tile_mma<D>(tmem + buf * TILE, ks, qs + s * TB, idesc);
+          mma_commit(&q_empty[s]);
+          mma_commit(&s_full[buf]);
+          issued = j + 1;
+        }
+      }
+      if (issued > 0) mbar_wait(&s_full[(issued - 1) & 1], ((issued - 1) >> 1) & 1, abort_flag);
+    }
+  } else {
+    // exp/sum warpgroup: thread owns key c0 + rl.
+    const int sub = warp & 3;
+    const int rl = sub * 32 + lane;
+    const int key = c0 + rl;
+    const uint32_t trow = tmem + ((uint32_t)(sub * 32) << 16);
+    const float C = a.C;
+    float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+    for (int j = 0; j < J; ++j) {
+      const int buf = j & 1, s = j % kStages;
+      bool ok = mbar_wait(&s_full[buf], (j >> 1) & 1, abort_flag);
+      ok = ok && mbar_wait(&q_full[s], (j / kStages) & 1, abort_flag);  // lse2 bytes landed
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      float v[128];
+      load_row128(trow + buf * TILE, v);
+      tc_fence_before();
+      mbar_arrive(&s_empty[buf]);
+
+      const int hh = j / nqt;
+      const int r = rs + (j - hh * nqt) * TILE;
+      const float* L = l_ring + s * TILE;
+      if (!a.causal || r > c0) {
+        // every (key, query) pair of the tile is kept
+#pragma unroll
+        for (int c = 0; c < 128; c += 4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(L + c);
+          acc0 += ex2(fmaf(v[c + 0], C, -l4.x));
+          acc1 += ex2(fmaf(v[c + 1], C, -l4.y));
+          acc2 += ex2(fmaf(v[c + 2], C, -l4.z));
+          acc3 += ex2(fmaf(v[c + 3], C, -l4.w));
+        }
+      } else if (r == c0) {
+        // diagonal tile: key c0+rl is kept by query r+c iff c >= rl
+#pragma unroll
+        for (int c = 0; c < 128; c += 4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(L + c);
+          acc0 += (c + 0 >= rl) ? ex2(fmaf(v[c + 0], C, -l4.x)) : 0.f;
+          acc1 += (c + 1 >= rl) ? ex2(fmaf(v[c + 1], C, -l4.y)) : 0.f;
+          acc2 += (c + 2 >= rl) ? ex2(fmaf(v[c + 2], C, -l4.z)) : 0.f;
+          acc3 += (c + 3 >= rl) ? ex2(fmaf(v[c + 3], C, -l4.w)) : 0.f;
+        }
+      }
+      // r < c0 (only without causal_skip): every pair is above the diagonal, adds 0.
+      mbar_arrive(&q_empty[s]);
+    }
+    if (key < a.N) {
+      float total = (acc0 + acc1) + (acc2 + acc3);
+      if (kKeyMask && a.kmask[b * a.kmb + key] == 0) total = 0.f;
+      a.part[((long long)uu * a.nchunk + y) * a.N + key] = total;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ============================================================ host side
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                   CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    else
+      cudaGetLastError();
+  }
+  return fn;
+}
+
+// 4-D map over a [B, H, N, D] operand with unit-stride D: box 64 x 128 x 1 x 1,
+// 128-byte swizzle, zero fill outside [N) so ragged tiles read zeros.
+bool make_map(CUtensorMap* map, const void* base, bool bf16, int B, int H, int N, int D,
+              const int64_t* st) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)N, (cuuint64_t)H, (cuuint64_t)B};
+  // Size-1 dims get a harmless nonzero stride (TMA wants multiples of 16 bytes).
+  const uint64_t row = (uint64_t)st[2] * 2;
+  uint64_t hs = (uint64_t)st[1] * 2, bs = (uint64_t)st[0] * 2;
+  if (H == 1) hs = row * (uint64_t)N;
+  if (B == 1) bs = hs * (uint64_t)H;
+  const cuuint64_t strides[3] = {row, hs, bs};
+  const cuuint32_t box[4] = {64, (cuuint32_t)TILE, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                        const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int D>
+constexpr size_t smem_lse() {
+  return 1024 + (size_t)Cfg<D>::kTileBytes * (1 + kStages) + 8 * (1 + 2 * kStages + 4) + 16;
+}
+template <int D>
+constexpr size_t smem_mass() {
+  return 1024 + (size_t)Cfg<D>::kTileBytes * (1 + kStages) + TILE * 4 * kStages + 8 * (1 + 2 * kStages + 4) + 16;
+}
+
+template <int D, bool kBF16, bool kKeyMask>
+int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s, void* mid_event) {
+  CUtensorMap tq, tk;
+  if (!make_map(&tq, p->q, kBF16, p->B, p->Hq, p->N, D, p->q_stride) ||
+      !make_map(&tk, p->k, kBF16, p->B, p->Hkv, p->N, D, p->k_stride))
+    return KVBM_ERR_CUDA;
+  TcArgs a;
+  a.N = p->N;
+  a.Npad = (p->N + TILE - 1) / TILE * TILE;
+  a.G = p->Hq / p->Hkv;
+  a.Hkv = p->Hkv;
+  a.ub = p->unit_begin;
+  a.C = (float)(p->scale * kLog2e);
+  a.causal = p->causal != 0;
+  a.skip = p->causal_skip != 0;
+  a.kmask = p->key_mask;
+  a.kmb = p->key_mask_bstride;
+  a.qmask = p->query_mask;
+  a.qmb = p->query_mask_bstride;
+  a.lse = reinterpret_cast<float*>(static_cast<char*>(ws) + L.lse_off);
+  a.part = reinterpret_cast<float*>(static_cast<char*>(ws) + L.part_off);
+  a.qchunk = L.qchunk;
+  a.nchunk = L.nchunk;
+  const int U = p->unit_end - p->unit_begin;
+  const int ntiles = a.Npad / TILE;
+
+  const size_t sm1 = smem_lse<D>() > (size_t)kMinSmem ? smem_lse<D>() : (size_t)kMinSmem;
+  const size_t sm2 = smem_mass<D>() > (size_t)kMinSmem ? smem_mass<D>() : (size_t)kMinSmem;
+  auto k1 = tc_lse_kernel<D, kBF16, kKeyMask>;
+  auto k2 = tc_mass_kernel<D, kBF16, kKeyMask>;
+  if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1) != cudaSuccess ||
+      cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2) != cudaSuccess)
+    return KVBM_ERR_CUDA;
+  k1<<<dim3(U * a.G, ntiles), kThreads, sm1, s>>>(tq, tk, a);
+  if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
+  if (mid_event != nullptr && cudaEventRecord(static_cast<cudaEvent_t>(mid_event), s) != cudaSuccess)
+    return KVBM_ERR_CUDA;
+  k2<<<dim3(U, L.nchunk, ntiles), kThreads, sm2, s>>>(tq, tk, a);
+  if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
+  return KVBM_OK;
+}
+
+template <int D>
+int launch_d(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s, void* ev) {
+  const bool bf16 = p->dtype == KVBM_BF16;
+  const bool km = p->key_mask != nullptr;
+  if (bf16)
+    return km ? launch_variant<D, true, true>(p, L, ws, s, ev) : launch_variant<D, true, false>(p, L, ws, s, ev);
+  return km ? launch_variant<D, false, true>(p, L, ws, s, ev) : launch_variant<D, false, false>(p, L, ws, s, ev);
+}
+
+}  // namespace
+
+bool tc_path_enabled() { return encode_fn() != nullptr; }
+
+int launch_tc(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws, cudaStream_t s,
+              void* mid_event) {
+  (void)mass_out;
+  if (p->D == 64) return launch_d<64>(p, L, ws, s, mid_event);
+  if (p->D == 128) return launch_d<128>(p, L, ws, s, mid_event);
+  return KVBM_ERR_HEAD_DIM;
+}
+
+int read_and_clear_device_error(cudaStream_t s, int* err) {
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbolAsync(&v, sm100::g_kvbm_device_error, sizeof(v), 0, cudaMemcpyDeviceToHost, s) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return KVBM_ERR_CUDA;
+  *err = v != 0;
+  if (v != 0) {
+    const unsigned int zero = 0;
+    if (cudaMemcpyToSymbolAsync(sm100::g_kvbm_device_error, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+      return KVBM_ERR_CUDA;
+  }
+  return KVBM_OK;
+}
+
+}  // namespace kvbm

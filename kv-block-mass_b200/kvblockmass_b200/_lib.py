@@ -38,6 +38,8 @@ EXPORTED = [
     "kvbm_kernel_path",
     "kvbm_launches_per_call",
     "kvbm_block_mass",
+    "kvbm_block_mass_events",
+    "kvbm_measure_ex2_rate",
     "kvbm_check_device_errors",
 ]
 
@@ -103,6 +105,11 @@ def load() -> ctypes.CDLL:
     lib.kvbm_block_mass.restype = ctypes.c_int
     lib.kvbm_block_mass.argtypes = [P, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
                                     ctypes.c_void_p]
+    lib.kvbm_block_mass_events.restype = ctypes.c_int
+    lib.kvbm_block_mass_events.argtypes = [P, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                           ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
+    lib.kvbm_measure_ex2_rate.restype = ctypes.c_int
+    lib.kvbm_measure_ex2_rate.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_double)]
     lib.kvbm_check_device_errors.restype = ctypes.c_int
     lib.kvbm_check_device_errors.argtypes = [ctypes.c_void_p]
     if lib.kvbm_abi_version() != 1:

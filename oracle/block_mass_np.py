@@ -142,6 +142,7 @@ def block_mass_stream(
     heads: slice | None = None,
     rows: tuple[int, int] | None = None,
     threads: int = 1,
+    split_rows: bool = False,
 ):
     """Block mass ``[ceil(N / block_size)]`` of ``q [B,H_q,N,D]``, ``k [B,H_kv,N,D]``.
 
@@ -151,7 +152,8 @@ def block_mass_stream(
     query rows, aligned to ``query_chunk``) restrict the sum to a sample of the
     workload; the CPU baseline uses them to time a bounded part of a large
     shape.  ``threads`` > 1 splits (batch, head) work over a thread pool
-    (numpy releases the GIL inside its kernels).
+    (numpy releases the GIL inside its kernels); ``split_rows`` also splits
+    each (batch, head) into its query chunks.
 
     The result dtype is float64 for float64 inputs and float32 otherwise
     (``reference.py:77``).
@@ -177,10 +179,10 @@ def block_mass_stream(
     hsel = range(Hq)[heads] if heads is not None else range(Hq)
     r0, r1 = rows if rows is not None else (0, N)
 
-    def one(bh):
-        b, h = bh
+    def one(item):
+        b, h, lo, hi = item
         part = np.zeros(nb, dtype=np.float64 if acc is np.float64 else np.float32)
-        for start in range(r0, r1, query_chunk):
+        for start in range(lo, hi, query_chunk):
             stop = min(start + query_chunk, N)
             n_lim = stop if (causal and causal_skip) else N
             keep = _keep_rows(b, start, stop, n_lim, causal, key, pair, qm)
@@ -189,7 +191,11 @@ def block_mass_stream(
             part += np.bincount(col_block[:n_lim], weights=c, minlength=nb).astype(part.dtype)
         return part
 
-    work = [(b, h) for b in range(B) for h in hsel]
+    if split_rows:
+        work = [(b, h, s, min(s + query_chunk, r1)) for b in range(B) for h in hsel
+                for s in range(r0, r1, query_chunk)]
+    else:
+        work = [(b, h, r0, r1) for b in range(B) for h in hsel]
     mass = np.zeros(nb, dtype=np.float64 if acc is np.float64 else np.float32)
     if threads > 1 and len(work) > 1:
         with ThreadPoolExecutor(max_workers=threads) as ex:
