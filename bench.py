@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
+    ap.add_argument("--seq-len", type=int, default=None,
+                    help="override N of the workload (small cases for profiler captures)")
     ap.add_argument("--cpu-seconds", type=float, default=8.0,
                     help="target CPU time of the bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -297,6 +299,12 @@ def b200_arm(args, w):
     # Timed region: K steps, CUDA events on the launching stream, per-pass events inside.
     K = args.steps
     pass_events = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
+    # torch creates the CUDA event lazily at its first record(); record each once
+    # so that the raw handles exist before the library records them in-call.
+    for evs in pass_events:
+        for e in evs:
+            e.record(stream)
+    torch.cuda.synchronize()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(list(range(torch.cuda.device_count())) if world > 1 else [local]) \
         if rank == 0 else None
@@ -414,6 +422,9 @@ def main():
     from kvblockmass_b200.workloads import WORKLOADS
 
     w = WORKLOADS[args.workload]
+    if args.seq_len:
+        from dataclasses import replace
+        w = replace(w, N=args.seq_len, name=f"{w.name}@N={args.seq_len}")
     if args.impl == "reference":
         if int(os.environ.get("RANK", "0")) != 0:
             return 0

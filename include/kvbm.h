@@ -60,8 +60,7 @@ enum kvbm_status {
   KVBM_ERR_WORKSPACE = 8,   /* workspace missing, too small or misaligned     */
   KVBM_ERR_CUDA = 9,        /* a CUDA runtime call or launch failed           */
   KVBM_ERR_DEVICE = 10,     /* current device is not an sm_100 GPU            */
-  KVBM_ERR_TIMEOUT = 11,    /* a device-side wait ran out its iteration limit */
-  KVBM_ERR_SCRATCH = 12     /* problem exceeds a fixed-size scratch area      */
+  KVBM_ERR_TIMEOUT = 11     /* a device-side wait ran out its iteration limit */
 };
 
 /* Attention-mass problem.  Strides are in ELEMENTS for the dims [B, H, N, D]

@@ -26,7 +26,6 @@ KVBM_ERR_WORKSPACE = 8
 KVBM_ERR_CUDA = 9
 KVBM_ERR_DEVICE = 10
 KVBM_ERR_TIMEOUT = 11
-KVBM_ERR_SCRATCH = 12
 
 # Symbols include/kvbm.h declares; tests check the library exports each one.
 EXPORTED = [

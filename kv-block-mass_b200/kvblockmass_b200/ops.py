@@ -35,7 +35,7 @@ _DTYPES = {
 
 _VALUE_ERRORS = {
     _lib.KVBM_ERR_GQA, _lib.KVBM_ERR_SHAPE, _lib.KVBM_ERR_DTYPE, _lib.KVBM_ERR_HEAD_DIM,
-    _lib.KVBM_ERR_BLOCK_SIZE, _lib.KVBM_ERR_UNITS, _lib.KVBM_ERR_NULL, _lib.KVBM_ERR_SCRATCH,
+    _lib.KVBM_ERR_BLOCK_SIZE, _lib.KVBM_ERR_UNITS, _lib.KVBM_ERR_NULL,
 }
 
 
