@@ -60,7 +60,8 @@ enum kvbm_status {
   KVBM_ERR_WORKSPACE = 8,   /* workspace missing, too small or misaligned     */
   KVBM_ERR_CUDA = 9,        /* a CUDA runtime call or launch failed           */
   KVBM_ERR_DEVICE = 10,     /* current device is not an sm_100 GPU            */
-  KVBM_ERR_TIMEOUT = 11     /* a device-side wait ran out its iteration limit */
+  KVBM_ERR_TIMEOUT = 11,    /* a device-side wait ran out its iteration limit */
+  KVBM_ERR_SCRATCH = 12     /* problem needs more scratch than the fixed area  */
 };
 
 /* Attention-mass problem.  Strides are in ELEMENTS for the dims [B, H, N, D]
@@ -153,6 +154,40 @@ int kvbm_block_mass_events(const kvbm_problem* p, void* mass_out, void* workspac
  * bound by this rate, so benchmarks report it as the roofline denominator.
  * No counterpart in the reference. */
 int kvbm_measure_ex2_rate(void* stream, double* ex2_per_second);
+
+/* kvbm_block_mass for callers that cannot allocate device memory.  It has
+ * no counterpart in the reference.
+ *
+ * Who needs it: a serving engine that reserves all free device memory for its
+ * own KV-cache pool at start-up has none left for a cudaMalloc, and cannot
+ * afford cudaMalloc/cudaFree in its step loop because they synchronise the
+ * device and stall its other streams.  A C/FFI host may hold only the input and
+ * output pointers another framework gave it.  Such callers still pass q, k, the
+ * masks and `mass_out`; the scratch the two passes need (the per-row lse2 values
+ * and per-key partial sums) comes from a fixed device array inside this
+ * library instead of a caller workspace.
+ *
+ * Limit: the array holds kvbm_static_scratch_bytes() bytes (64 MiB).  Every
+ * GPU that loads the library holds it until the process exits.  A problem
+ * whose workspace (kvbm_workspace_bytes) is larger is rejected with
+ * KVBM_ERR_SCRATCH before anything is launched.  Split such a problem into
+ * unit ranges (unit_begin/unit_end) that fit.
+ *
+ * No allocation: the call makes no cudaMalloc, cudaFree or other allocating
+ * call.  The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture.
+ *
+ * Sharing: every call on a device uses the same array.  The array keeps the
+ * last call's contents, and each call overwrites what it reads, so nothing has
+ * to be cleared between calls.  Calls that can overlap on the GPU (different
+ * streams without ordering between them) race on the array and give wrong
+ * results; order them on one stream or with events. */
+int kvbm_block_mass_static(const kvbm_problem* p, void* mass_out, void* stream);
+
+/* Size in bytes of the fixed scratch array used by kvbm_block_mass_static.
+ * No counterpart in the reference. */
+size_t kvbm_static_scratch_bytes(void);
 
 /* Reads and clears the device-side error word of the current device (set
  * when a bounded wait inside a tcgen05 kernel gave up).  Synchronises

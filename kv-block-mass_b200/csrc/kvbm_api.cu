@@ -109,6 +109,9 @@ const char* kvbm_status_string(int status) {
     case KVBM_ERR_CUDA: return "CUDA runtime error";
     case KVBM_ERR_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
     case KVBM_ERR_TIMEOUT: return "a device-side wait exceeded its iteration limit";
+    case KVBM_ERR_SCRATCH:
+      return "problem needs more scratch than the fixed area of kvbm_block_mass_static "
+             "(see kvbm_static_scratch_bytes); split it into unit ranges";
     default: return "unknown status";
   }
 }

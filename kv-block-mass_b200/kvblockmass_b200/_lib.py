@@ -26,6 +26,7 @@ KVBM_ERR_WORKSPACE = 8
 KVBM_ERR_CUDA = 9
 KVBM_ERR_DEVICE = 10
 KVBM_ERR_TIMEOUT = 11
+KVBM_ERR_SCRATCH = 12
 
 # Symbols include/kvbm.h declares; tests check the library exports each one.
 EXPORTED = [
@@ -40,6 +41,8 @@ EXPORTED = [
     "kvbm_block_mass_events",
     "kvbm_measure_ex2_rate",
     "kvbm_check_device_errors",
+    "kvbm_block_mass_static",
+    "kvbm_static_scratch_bytes",
 ]
 
 
@@ -109,6 +112,11 @@ def load() -> ctypes.CDLL:
                                            ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
     lib.kvbm_measure_ex2_rate.restype = ctypes.c_int
     lib.kvbm_measure_ex2_rate.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_double)]
+    # No-allocation variant: scratch from a fixed device array inside the library.
+    lib.kvbm_block_mass_static.restype = ctypes.c_int
+    lib.kvbm_block_mass_static.argtypes = [P, ctypes.c_void_p, ctypes.c_void_p]
+    lib.kvbm_static_scratch_bytes.restype = ctypes.c_size_t
+    lib.kvbm_static_scratch_bytes.argtypes = []
     lib.kvbm_check_device_errors.restype = ctypes.c_int
     lib.kvbm_check_device_errors.argtypes = [ctypes.c_void_p]
     if lib.kvbm_abi_version() != 1:
