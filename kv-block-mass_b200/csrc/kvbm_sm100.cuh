@@ -185,5 +185,58 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// ---- packed fp32 pairs (sm_100 f32x2 instructions) ----
+__device__ __forceinline__ unsigned long long pk(float2 v) { return *reinterpret_cast<unsigned long long*>(&v); }
+__device__ __forceinline__ float2 upk(unsigned long long u) { return *reinterpret_cast<float2*>(&u); }
+
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(pk(a)), "l"(pk(b)), "l"(pk(c)));
+  return upk(d);
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pk(a)), "l"(pk(b)));
+  return upk(d);
+}
+// Flush-to-zero add: denormal inputs count as 0 (matches ex2.approx.ftz).
+__device__ __forceinline__ float2 fadd2_ftz(float2 a, float2 b) {
+  unsigned long long d;
+  asm("add.rn.ftz.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pk(a)), "l"(pk(b)));
+  return upk(d);
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for two arguments on the FMA pipe (no MUFU): x = j + f with
+// j = rint(x) (the 1.5 * 2^23 shift rounds to nearest), f in [-1/2, 1/2];
+// p(f) ~= 2^f is the degree-4 minimax polynomial for relative error on that
+// interval (max 2.7e-6, kv-block-mass_b200/csrc/gen_exp2_poly.py), and 2^j is
+// added into the exponent field.  x is clamped at -126.75 so that every
+// result below 2^-126 is a positive denormal (never a wrapped exponent); a
+// flush-to-zero accumulate adds those as exact zeros, like ex2.approx.ftz.
+__device__ __forceinline__ float2 exp2_fma2(float2 x) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -126.75f);
+  x.y = fmaxf(x.y, -126.75f);
+  const float2 t = fadd2(x, make_float2(kShift, kShift));
+  const float2 j = fadd2(t, make_float2(-kShift, -kShift));
+  const float2 f = ffma2(j, make_float2(-1.f, -1.f), x);
+  float2 p = ffma2(f, make_float2(0.009570102207362652f, 0.009570102207362652f),
+                   make_float2(0.05591785907745361f, 0.05591785907745361f));
+  p = ffma2(p, f, make_float2(0.240247443318367f, 0.240247443318367f));
+  p = ffma2(p, f, make_float2(0.6931217908859253f, 0.6931217908859253f));
+  p = ffma2(p, f, make_float2(0.9999992847442627f, 0.9999992847442627f));
+  // bits(t) = bits(1.5 * 2^23) + j and 0x4B400000 << 23 == 0 (mod 2^32), so
+  // (bits(t) << 23) is j << 23: the exponent increment of 2^j.
+  const uint32_t rx = __float_as_uint(p.x) + (__float_as_uint(t.x) << 23);
+  const uint32_t ry = __float_as_uint(p.y) + (__float_as_uint(t.y) << 23);
+  return make_float2(__uint_as_float(rx), __uint_as_float(ry));
+}
+
 }  // namespace sm100
 }  // namespace kvbm

@@ -47,7 +47,17 @@ struct TcArgs {
   float* lse;              // [U_sel * G, Npad]
   float* part;             // [U_sel, nchunk, N]
   int qchunk, nchunk;
+  int per_unit;            // pass-2 CTAs per unit (sum of keys_in_chunk over chunks)
 };
+
+// Key tiles of query chunk y that hold a kept pair: with causal_skip only
+// those up to the chunk's last row, otherwise all of them.
+__host__ __device__ inline int keys_in_chunk(const TcArgs& a, int y) {
+  const int ntiles = a.Npad / TILE;
+  if (!(a.causal && a.skip)) return ntiles;
+  const int lim = (y + 1) * (a.qchunk / TILE);
+  return lim < ntiles ? lim : ntiles;
+}
 
 template <int D>
 struct Cfg {
@@ -81,11 +91,92 @@ __device__ __forceinline__ void load_row128(uint32_t taddr, float (&v)[128]) {
   tmem_ld_wait();
 }
 
+// Of the 32 four-column groups of a row, kEmuGroups take their exp2 from the
+// FMA-pipe polynomial (exp2_fma2) and the rest from MUFU ex2.approx: one ex2
+// per score element is the binding unit of both passes, and the FMA pipe has
+// room to absorb part of it.  The groups are spread evenly so that the
+// scheduler can interleave both kinds.
+#ifndef KVBM_EMU_GROUPS
+#define KVBM_EMU_GROUPS 8
+#endif
+constexpr int kEmuGroups = KVBM_EMU_GROUPS;
+static_assert(kEmuGroups >= 0 && kEmuGroups <= 32, "emulated groups out of range");
+
+__host__ __device__ constexpr bool emu_group(int g) {
+  return ((g + 1) * kEmuGroups) / 32 != (g * kEmuGroups) / 32;  // Bresenham spread
+}
+
+// Sum over the row of 2^(v*C + nm), nm = -(running max); masked entries hold -inf.
+__device__ __forceinline__ float row_sum_exp2(const float (&v)[128], float C, float nm) {
+  const float2 C2 = make_float2(C, C), N2 = make_float2(nm, nm);
+  float2 a0 = make_float2(0.f, 0.f), a1 = a0;
+#pragma unroll
+  for (int g = 0; g < 32; ++g) {
+    const int c = 4 * g;
+    const float2 x0 = ffma2(make_float2(v[c], v[c + 1]), C2, N2);
+    const float2 x1 = ffma2(make_float2(v[c + 2], v[c + 3]), C2, N2);
+    if (emu_group(g)) {
+      a0 = fadd2_ftz(a0, exp2_fma2(x0));
+      a1 = fadd2_ftz(a1, exp2_fma2(x1));
+    } else {
+      a0 = fadd2_ftz(a0, make_float2(ex2(x0.x), ex2(x0.y)));
+      a1 = fadd2_ftz(a1, make_float2(ex2(x1.x), ex2(x1.y)));
+    }
+  }
+  a0 = fadd2(a0, a1);
+  return a0.x + a0.y;
+}
+
+// Sum over the row of 2^(v[c]*C + nL[c]) with per-column nL = -lse2 (query
+// columns); `keep_from` masks columns c < keep_from (diagonal tile) to 0.
+template <bool kDiag>
+__device__ __forceinline__ float2 col_sum_exp2(const float (&v)[128], float C, const float* nL, int keep_from,
+                                               float2 acc) {
+  const float2 C2 = make_float2(C, C);
+  float2 a1 = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int g = 0; g < 32; ++g) {
+    const int c = 4 * g;
+    const float4 l4 = *reinterpret_cast<const float4*>(nL + c);
+    float2 v0 = make_float2(v[c], v[c + 1]), v1 = make_float2(v[c + 2], v[c + 3]);
+    if (kDiag) {
+      v0.x = (c + 0 >= keep_from) ? v0.x : -INFINITY;
+      v0.y = (c + 1 >= keep_from) ? v0.y : -INFINITY;
+      v1.x = (c + 2 >= keep_from) ? v1.x : -INFINITY;
+      v1.y = (c + 3 >= keep_from) ? v1.y : -INFINITY;
+    }
+    const float2 x0 = ffma2(v0, C2, make_float2(l4.x, l4.y));
+    const float2 x1 = ffma2(v1, C2, make_float2(l4.z, l4.w));
+    if (emu_group(g)) {
+      acc = fadd2_ftz(acc, exp2_fma2(x0));
+      a1 = fadd2_ftz(a1, exp2_fma2(x1));
+    } else {
+      acc = fadd2_ftz(acc, make_float2(ex2(x0.x), ex2(x0.y)));
+      a1 = fadd2_ftz(a1, make_float2(ex2(x1.x), ex2(x1.y)));
+    }
+  }
+  return fadd2(acc, a1);
+}
+
+__device__ __forceinline__ float row_max128(const float (&v)[128]) {
+  float m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = fmaxf(v[i], v[i + 8]);
+#pragma unroll
+  for (int c = 16; c < 128; c += 16)
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+      m[i] = fmax3(m[i], v[c + i], v[c + i + 8]);
+      m[i + 1] = fmax3(m[i + 1], v[c + i + 1], v[c + i + 9]);
+    }
+  return fmax3(fmax3(m[0], m[1], m[2]), fmax3(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
+}
+
 // ============================================================ pass 1: lse2
 // grid (U_sel * G, ceil(N / 128)); blockIdx.y counts query tiles from the
 // last (longest under causal_skip) to the first.
 template <int D, bool kBF16, bool kKeyMask>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     tc_lse_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk, TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1k(smem_raw);
@@ -213,31 +304,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           v[c] = keep ? v[c] : -INFINITY;
         }
       }
-      float tmax = v[0];
-#pragma unroll
-      for (int c = 1; c < 128; ++c) tmax = fmaxf(tmax, v[c]);
+      const float tmax = row_max128(v);
       if (tmax != -INFINITY) {
         const float mt = tmax * a.C;
+        // Rescale only when the running max grows: a fully masked tile leaves
+        // (m, l) bit-identical, which keeps causal_skip on/off identical.
         if (mt > m) {
           l = l * ex2(m - mt);
           m = mt;
         }
-        const float nm = -m;
-        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll
-        for (int c = 0; c < 128; c += 4) {
-          s0 += ex2(fmaf(v[c + 0], a.C, nm));
-          s1 += ex2(fmaf(v[c + 1], a.C, nm));
-          s2 += ex2(fmaf(v[c + 2], a.C, nm));
-          s3 += ex2(fmaf(v[c + 3], a.C, nm));
-        }
-        l += (s0 + s1) + (s2 + s3);
+        l += row_sum_exp2(v, a.C, -m);
       }
     }
     bool dead = (m == -INFINITY) || row >= a.N;
     if (!dead && a.qmask != nullptr) dead = a.qmask[b * a.qmb + row] == 0;
-    // Rows that keep no key (and padding rows) get +inf: 2^(t - inf) = 0.
-    a.lse[(long long)(hidx) * a.Npad + row] = dead ? INFINITY : m + log2f(l);
+    // Stored negated (pass 2 adds it): rows that keep no key, and padding
+    // rows, get -inf, so 2^(t - lse2) = 0 for them.
+    a.lse[(long long)(hidx) * a.Npad + row] = dead ? -INFINITY : -(m + log2f(l));
   }
 
   __syncthreads();
@@ -248,11 +331,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ============================================================ pass 2: mass
-// grid (U_sel, nchunk, ceil(N / 128)): one CTA owns 128 keys of one
-// (batch, kv-head) unit and one chunk of query rows, for every head of the
-// GQA group.
+// One CTA owns 128 keys of one (batch, kv-head) unit and one chunk of query
+// rows, for every head of the GQA group.  The 1-D grid enumerates only the
+// (unit, chunk, key tile) triples that keep a pair: per unit, chunks run from
+// the last (most key tiles under causal_skip) to the first, and all key tiles
+// of a chunk are adjacent, so the CTAs resident at one time share that
+// chunk's query tiles in L2.
 template <int D, bool kBF16, bool kKeyMask>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     tc_mass_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk, TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1k(smem_raw);
@@ -271,7 +357,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int uu = blockIdx.x, y = blockIdx.y, kt = blockIdx.z;
+  const int uu = (int)blockIdx.x / a.per_unit;
+  int y = a.nchunk - 1, kt = (int)blockIdx.x - uu * a.per_unit;
+  while (kt >= keys_in_chunk(a, y)) {
+    kt -= keys_in_chunk(a, y);
+    --y;
+  }
   const int u = a.ub + uu;
   const int b = u / a.Hkv, g = u % a.Hkv;
   const int c0 = kt * TILE;
@@ -359,7 +450,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int key = c0 + rl;
     const uint32_t trow = tmem + ((uint32_t)(sub * 32) << 16);
     const float C = a.C;
-    float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+    float2 acc = make_float2(0.f, 0.f);
     for (int j = 0; j < J; ++j) {
       const int buf = j & 1, s = j % kStages;
       bool ok = mbar_wait(&s_full[buf], (j >> 1) & 1, abort_flag);
@@ -373,33 +464,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       const int hh = j / nqt;
       const int r = rs + (j - hh * nqt) * TILE;
-      const float* L = l_ring + s * TILE;
+      const float* nL = l_ring + s * TILE;  // -lse2 of the tile's 128 query rows
       if (!a.causal || r > c0) {
-        // every (key, query) pair of the tile is kept
-#pragma unroll
-        for (int c = 0; c < 128; c += 4) {
-          const float4 l4 = *reinterpret_cast<const float4*>(L + c);
-          acc0 += ex2(fmaf(v[c + 0], C, -l4.x));
-          acc1 += ex2(fmaf(v[c + 1], C, -l4.y));
-          acc2 += ex2(fmaf(v[c + 2], C, -l4.z));
-          acc3 += ex2(fmaf(v[c + 3], C, -l4.w));
-        }
+        acc = col_sum_exp2<false>(v, C, nL, 0, acc);          // every pair kept
       } else if (r == c0) {
-        // diagonal tile: key c0+rl is kept by query r+c iff c >= rl
-#pragma unroll
-        for (int c = 0; c < 128; c += 4) {
-          const float4 l4 = *reinterpret_cast<const float4*>(L + c);
-          acc0 += (c + 0 >= rl) ? ex2(fmaf(v[c + 0], C, -l4.x)) : 0.f;
-          acc1 += (c + 1 >= rl) ? ex2(fmaf(v[c + 1], C, -l4.y)) : 0.f;
-          acc2 += (c + 2 >= rl) ? ex2(fmaf(v[c + 2], C, -l4.z)) : 0.f;
-          acc3 += (c + 3 >= rl) ? ex2(fmaf(v[c + 3], C, -l4.w)) : 0.f;
-        }
+        acc = col_sum_exp2<true>(v, C, nL, rl, acc);          // diagonal: query r+c keeps key c0+rl iff c >= rl
       }
       // r < c0 (only without causal_skip): every pair is above the diagonal, adds 0.
       mbar_arrive(&q_empty[s]);
     }
     if (key < a.N) {
-      float total = (acc0 + acc1) + (acc2 + acc3);
+      float total = acc.x + acc.y;
       if (kKeyMask && a.kmask[b * a.kmb + key] == 0) total = 0.f;
       a.part[((long long)uu * a.nchunk + y) * a.N + key] = total;
     }
@@ -486,6 +561,8 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
   a.part = reinterpret_cast<float*>(static_cast<char*>(ws) + L.part_off);
   a.qchunk = L.qchunk;
   a.nchunk = L.nchunk;
+  a.per_unit = 0;
+  for (int y = 0; y < a.nchunk; ++y) a.per_unit += keys_in_chunk(a, y);
   const int U = p->unit_end - p->unit_begin;
   const int ntiles = a.Npad / TILE;
 
@@ -500,7 +577,7 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
   if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
   if (mid_event != nullptr && cudaEventRecord(static_cast<cudaEvent_t>(mid_event), s) != cudaSuccess)
     return KVBM_ERR_CUDA;
-  k2<<<dim3(U, L.nchunk, ntiles), kThreads, sm2, s>>>(tq, tk, a);
+  k2<<<dim3(U * a.per_unit), kThreads, sm2, s>>>(tq, tk, a);
   if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
   return KVBM_OK;
 }
