@@ -5,19 +5,23 @@
 //   warp 0     TMA producer (one elected lane): Q/K tiles -> 128B-swizzled smem
 //   warp 1     MMA issuer (one lane) + TMEM owner: tcgen05.mma kind::f16, fp32
 //              accumulators in two 128-column TMEM buffers
-//   warps 2-5  exp/sum warpgroup: tcgen05.ld, one thread per accumulator row
+//   warps 2-9  exp/sum: two warpgroups, each reading one 64-column half of
+//              every accumulator row with tcgen05.ld (one thread per row
+//              and half), so four exp warps share each SM sub-partition
 //
 // Pass 1 (row log-sum-exp) follows the reference Triton kernel's pass 1
 // (kv-block-mass src/kvblockmass/triton_kernel.py:69-104): S = Q K^T with
-// query rows as the MMA's M; each thread owns a query row and keeps its
-// online max / denominator in registers.  Causal tiles stop at the query
-// tile's last row (triton_kernel.py:57-60).
+// query rows as the MMA's M.  Each thread keeps an online max / denominator
+// over its column half of every key tile in registers; the two halves of a
+// row merge once, at the end.  Causal tiles stop at the query tile's last
+// row (triton_kernel.py:57-60).
 //
 // Pass 2 (mass) recomputes the scores transposed, S^T = K Q^T with key rows as
-// M, so each thread owns one key and sums 2^(t - lse2) over every query of
-// every head of its GQA group (triton_kernel.py:106-145, reference.py:121-124)
-// in registers.  One partial per (unit, query chunk, key) goes to the
-// workspace; the SIMT reduce (kvbm_simt.cu) adds them in a fixed order.
+// M, so each thread owns one key (and one half of the query columns) and
+// sums 2^(t - lse2) over every query of every head of its GQA group
+// (triton_kernel.py:106-145, reference.py:121-124) in registers.  One partial
+// per (unit, query chunk, key) goes to the workspace; the SIMT reduce
+// (kvbm_simt.cu) adds them in a fixed order.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -31,10 +35,13 @@ namespace {
 using namespace sm100;
 
 constexpr int TILE = kTcTile;       // 128
-constexpr int kThreads = 192;       // 6 warps
+constexpr int HALF = TILE / 2;      // columns per exp warpgroup
+constexpr int kExpThreads = 256;    // two warpgroups
+constexpr int kThreads = 64 + kExpThreads;  // + TMA warp + MMA warp
 constexpr int kStages = 2;          // K (pass 1) / Q (pass 2) ring depth
 constexpr int kTmemCols = 256;      // two 128-column fp32 accumulators
 constexpr int kMinSmem = 100 * 1024;  // caps residency at 2 CTAs/SM (TMEM: 2 x 256 columns)
+constexpr int kExpBarrier = 1;      // named barrier of the 256 exp threads
 
 struct TcArgs {
   int N, Npad, G, Hkv, ub;
@@ -44,7 +51,7 @@ struct TcArgs {
   long long kmb;
   const uint8_t* qmask;    // [B|1, N] or null
   long long qmb;
-  float* lse;              // [U_sel * G, Npad]
+  float* lse;              // [U_sel * G, Npad], stored negated (-lse2)
   float* part;             // [U_sel, nchunk, N]
   int qchunk, nchunk;
   int per_unit;            // pass-2 CTAs per unit (sum of keys_in_chunk over chunks)
@@ -72,6 +79,10 @@ __device__ __forceinline__ uint8_t* align1k(uint8_t* p) {
   return p + ((1024u - (a & 1023u)) & 1023u);
 }
 
+__device__ __forceinline__ void exp_bar_sync() {
+  asm volatile("bar.sync %0, %1;" ::"n"(kExpBarrier), "n"(kExpThreads) : "memory");
+}
+
 // Issue the MMAs of one 128 x 128 tile: D[tmem] = A[128 x D] * B[128 x D]^T.
 template <int D>
 __device__ __forceinline__ void issue_tile_mma(uint32_t d_tmem, uint32_t a_smem, uint32_t b_smem,
@@ -83,35 +94,34 @@ __device__ __forceinline__ void issue_tile_mma(uint32_t d_tmem, uint32_t a_smem,
   }
 }
 
-__device__ __forceinline__ void load_row128(uint32_t taddr, float (&v)[128]) {
+__device__ __forceinline__ void load_half(uint32_t taddr, float (&v)[HALF]) {
   tmem_ld32(taddr + 0, *reinterpret_cast<float(*)[32]>(&v[0]));
   tmem_ld32(taddr + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
-  tmem_ld32(taddr + 64, *reinterpret_cast<float(*)[32]>(&v[64]));
-  tmem_ld32(taddr + 96, *reinterpret_cast<float(*)[32]>(&v[96]));
   tmem_ld_wait();
 }
 
-// Of the 32 four-column groups of a row, kEmuGroups take their exp2 from the
-// FMA-pipe polynomial (exp2_fma2) and the rest from MUFU ex2.approx: one ex2
-// per score element is the binding unit of both passes, and the FMA pipe has
-// room to absorb part of it.  The groups are spread evenly so that the
+// Of the 16 four-column groups of a half row, kEmuGroups take their exp2 from
+// the FMA-pipe polynomial (exp2_fma2) and the rest from MUFU ex2.approx: one
+// ex2 per score element is the binding unit of both passes, and the FMA pipe
+// has room to absorb part of it.  The groups are spread evenly so that the
 // scheduler can interleave both kinds.
 #ifndef KVBM_EMU_GROUPS
-#define KVBM_EMU_GROUPS 8
+#define KVBM_EMU_GROUPS 4
 #endif
+constexpr int kGroups = HALF / 4;
 constexpr int kEmuGroups = KVBM_EMU_GROUPS;
-static_assert(kEmuGroups >= 0 && kEmuGroups <= 32, "emulated groups out of range");
+static_assert(kEmuGroups >= 0 && kEmuGroups <= kGroups, "emulated groups out of range");
 
 __host__ __device__ constexpr bool emu_group(int g) {
-  return ((g + 1) * kEmuGroups) / 32 != (g * kEmuGroups) / 32;  // Bresenham spread
+  return ((g + 1) * kEmuGroups) / kGroups != (g * kEmuGroups) / kGroups;  // Bresenham spread
 }
 
-// Sum over the row of 2^(v*C + nm), nm = -(running max); masked entries hold -inf.
-__device__ __forceinline__ float row_sum_exp2(const float (&v)[128], float C, float nm) {
+// Sum over the half row of 2^(v*C + nm), nm = -(running max); masked entries hold -inf.
+__device__ __forceinline__ float row_sum_exp2(const float (&v)[HALF], float C, float nm) {
   const float2 C2 = make_float2(C, C), N2 = make_float2(nm, nm);
   float2 a0 = make_float2(0.f, 0.f), a1 = a0;
 #pragma unroll
-  for (int g = 0; g < 32; ++g) {
+  for (int g = 0; g < kGroups; ++g) {
     const int c = 4 * g;
     const float2 x0 = ffma2(make_float2(v[c], v[c + 1]), C2, N2);
     const float2 x1 = ffma2(make_float2(v[c + 2], v[c + 3]), C2, N2);
@@ -127,15 +137,15 @@ __device__ __forceinline__ float row_sum_exp2(const float (&v)[128], float C, fl
   return a0.x + a0.y;
 }
 
-// Sum over the row of 2^(v[c]*C + nL[c]) with per-column nL = -lse2 (query
-// columns); `keep_from` masks columns c < keep_from (diagonal tile) to 0.
+// acc += 2^(v[c]*C + nL[c]) over the half row, per-column nL = -lse2 (query
+// columns); with kDiag, columns c < keep_from are masked to 0.
 template <bool kDiag>
-__device__ __forceinline__ float2 col_sum_exp2(const float (&v)[128], float C, const float* nL, int keep_from,
+__device__ __forceinline__ float2 col_sum_exp2(const float (&v)[HALF], float C, const float* nL, int keep_from,
                                                float2 acc) {
   const float2 C2 = make_float2(C, C);
   float2 a1 = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int g = 0; g < 32; ++g) {
+  for (int g = 0; g < kGroups; ++g) {
     const int c = 4 * g;
     const float4 l4 = *reinterpret_cast<const float4*>(nL + c);
     float2 v0 = make_float2(v[c], v[c + 1]), v1 = make_float2(v[c + 2], v[c + 3]);
@@ -158,18 +168,26 @@ __device__ __forceinline__ float2 col_sum_exp2(const float (&v)[128], float C, c
   return fadd2(acc, a1);
 }
 
-__device__ __forceinline__ float row_max128(const float (&v)[128]) {
+__device__ __forceinline__ float row_max64(const float (&v)[HALF]) {
   float m[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) m[i] = fmaxf(v[i], v[i + 8]);
 #pragma unroll
-  for (int c = 16; c < 128; c += 16)
+  for (int c = 16; c < HALF; c += 16)
 #pragma unroll
     for (int i = 0; i < 8; i += 2) {
       m[i] = fmax3(m[i], v[c + i], v[c + i + 8]);
       m[i + 1] = fmax3(m[i + 1], v[c + i + 1], v[c + i + 9]);
     }
   return fmax3(fmax3(m[0], m[1], m[2]), fmax3(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
+}
+
+// Merge two online-softmax states (m, l) in the base-2 domain.
+__device__ __forceinline__ void merge_ml(float& m, float& l, float mo, float lo) {
+  const float mn = fmaxf(m, mo);
+  if (mn == -INFINITY) return;  // both halves saw only masked entries
+  l = l * ex2(m - mn) + lo * ex2(mo - mn);
+  m = mn;
 }
 
 // ============================================================ pass 1: lse2
@@ -183,7 +201,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   constexpr int TB = Cfg<D>::kTileBytes;
   uint8_t* q_tile = smem;
   uint8_t* k_ring = smem + TB;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TB * (1 + kStages));
+  float2* merge = reinterpret_cast<float2*>(smem + TB * (1 + kStages));  // [128] (m, l) of the upper halves
+  uint64_t* bars = reinterpret_cast<uint64_t*>(merge + TILE);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = k_full + kStages;
@@ -209,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 128);
+      mbar_init(&s_empty[i], kExpThreads);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -267,11 +286,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (issued > 0) mbar_wait(&s_full[(issued - 1) & 1], ((issued - 1) >> 1) & 1, abort_flag);
     }
   } else {
-    // exp/sum warpgroup: thread owns query row r0 + rl.
+    // exp/sum warps: thread owns query row r0 + rl, columns [hf*64, hf*64 + 64) of each tile.
     const int sub = warp & 3;
+    const int hf = (warp - 2) >> 2;
     const int rl = sub * 32 + lane;
     const int row = r0 + rl;
-    const uint32_t trow = tmem + ((uint32_t)(sub * 32) << 16);
+    const uint32_t trow = tmem + ((uint32_t)(sub * 32) << 16) + hf * HALF;
     const uint8_t* kmask = kKeyMask ? a.kmask + b * a.kmb : nullptr;
     float m = -INFINITY, l = 0.f;
     for (int j = 0; j < nkt; ++j) {
@@ -279,32 +299,31 @@ __global__ void __launch_bounds__(kThreads, 2)
       const bool ok = mbar_wait(&s_full[buf], (j >> 1) & 1, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      float v[128];
-      load_row128(trow + buf * TILE, v);
+      float v[HALF];
+      load_half(trow + buf * TILE, v);
       tc_fence_before();
       mbar_arrive(&s_empty[buf]);
 
-      const int c0 = j * TILE;
-      uint32_t kw[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
+      const int c0 = j * TILE + hf * HALF;  // first key of this thread's half
+      uint32_t kw[2] = {0xffffffffu, 0xffffffffu};
       if (kKeyMask) {
 #pragma unroll
-        for (int qd = 0; qd < 4; ++qd) {
+        for (int qd = 0; qd < 2; ++qd) {
           const int col = c0 + qd * 32 + lane;
           kw[qd] = __ballot_sync(0xffffffffu, col < a.N && kmask[col] != 0);
         }
       }
-      const bool need_mask = kKeyMask || (c0 + TILE > a.N) || (a.causal && c0 + TILE - 1 > r0);
+      const bool need_mask = kKeyMask || (c0 + HALF > a.N) || (a.causal && c0 + HALF - 1 > r0);
       if (need_mask) {
-        const int lim_causal = a.causal ? row - c0 : TILE - 1;  // keep col_local <= row - c0
-        const int lim_n = a.N - 1 - c0;                         // keep col_local <= N-1-c0
-        const int lim = min(lim_causal, lim_n);
+        const int lim_causal = a.causal ? row - c0 : HALF - 1;  // keep col_local <= row - c0
+        const int lim = min(lim_causal, a.N - 1 - c0);          // and col < N
 #pragma unroll
-        for (int c = 0; c < 128; ++c) {
+        for (int c = 0; c < HALF; ++c) {
           const bool keep = (c <= lim) && ((kw[c >> 5] >> (c & 31)) & 1u);
           v[c] = keep ? v[c] : -INFINITY;
         }
       }
-      const float tmax = row_max128(v);
+      const float tmax = row_max64(v);
       if (tmax != -INFINITY) {
         const float mt = tmax * a.C;
         // Rescale only when the running max grows: a fully masked tile leaves
@@ -316,11 +335,18 @@ __global__ void __launch_bounds__(kThreads, 2)
         l += row_sum_exp2(v, a.C, -m);
       }
     }
-    bool dead = (m == -INFINITY) || row >= a.N;
-    if (!dead && a.qmask != nullptr) dead = a.qmask[b * a.qmb + row] == 0;
-    // Stored negated (pass 2 adds it): rows that keep no key, and padding
-    // rows, get -inf, so 2^(t - lse2) = 0 for them.
-    a.lse[(long long)(hidx) * a.Npad + row] = dead ? -INFINITY : -(m + log2f(l));
+    // Merge the two column halves of each row (fixed order: lower half first).
+    if (hf == 1) merge[rl] = make_float2(m, l);
+    exp_bar_sync();
+    if (hf == 0) {
+      const float2 o = merge[rl];
+      merge_ml(m, l, o.x, o.y);
+      bool dead = (m == -INFINITY) || row >= a.N;
+      if (!dead && a.qmask != nullptr) dead = a.qmask[b * a.qmb + row] == 0;
+      // Stored negated (pass 2 adds it): rows that keep no key, and padding
+      // rows, get -inf, so 2^(t - lse2) = 0 for them.
+      a.lse[(long long)(hidx) * a.Npad + row] = dead ? -INFINITY : -(m + log2f(l));
+    }
   }
 
   __syncthreads();
@@ -347,7 +373,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint8_t* k_tile = smem;
   uint8_t* q_ring = smem + TB;
   float* l_ring = reinterpret_cast<float*>(smem + TB * (1 + kStages));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TB * (1 + kStages) + LB * kStages);
+  float2* merge = reinterpret_cast<float2*>(smem + TB * (1 + kStages) + LB * kStages);  // [128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(merge + TILE);
   uint64_t* k_full = bars;
   uint64_t* q_full = bars + 1;
   uint64_t* q_empty = q_full + kStages;
@@ -380,11 +407,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_init(k_full, 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&q_full[s], 1);
-      mbar_init(&q_empty[s], 1 + 128);  // MMA commit + every exp thread done with lse2
+      mbar_init(&q_empty[s], 1 + kExpThreads);  // MMA commit + every exp thread done with lse2
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 128);
+      mbar_init(&s_empty[i], kExpThreads);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -444,11 +471,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (issued > 0) mbar_wait(&s_full[(issued - 1) & 1], ((issued - 1) >> 1) & 1, abort_flag);
     }
   } else {
-    // exp/sum warpgroup: thread owns key c0 + rl.
+    // exp/sum warps: thread owns key c0 + rl and query columns [hf*64, hf*64 + 64) of each tile.
     const int sub = warp & 3;
+    const int hf = (warp - 2) >> 2;
     const int rl = sub * 32 + lane;
     const int key = c0 + rl;
-    const uint32_t trow = tmem + ((uint32_t)(sub * 32) << 16);
+    const uint32_t trow = tmem + ((uint32_t)(sub * 32) << 16) + hf * HALF;
     const float C = a.C;
     float2 acc = make_float2(0.f, 0.f);
     for (int j = 0; j < J; ++j) {
@@ -457,24 +485,29 @@ __global__ void __launch_bounds__(kThreads, 2)
       ok = ok && mbar_wait(&q_full[s], (j / kStages) & 1, abort_flag);  // lse2 bytes landed
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      float v[128];
-      load_row128(trow + buf * TILE, v);
+      float v[HALF];
+      load_half(trow + buf * TILE, v);
       tc_fence_before();
       mbar_arrive(&s_empty[buf]);
 
       const int hh = j / nqt;
       const int r = rs + (j - hh * nqt) * TILE;
-      const float* nL = l_ring + s * TILE;  // -lse2 of the tile's 128 query rows
+      const float* nL = l_ring + s * TILE + hf * HALF;  // -lse2 of this half's 64 query rows
       if (!a.causal || r > c0) {
-        acc = col_sum_exp2<false>(v, C, nL, 0, acc);          // every pair kept
+        acc = col_sum_exp2<false>(v, C, nL, 0, acc);  // every pair kept
       } else if (r == c0) {
-        acc = col_sum_exp2<true>(v, C, nL, rl, acc);          // diagonal: query r+c keeps key c0+rl iff c >= rl
+        // diagonal: query r + hf*64 + c keeps key c0 + rl iff hf*64 + c >= rl
+        acc = col_sum_exp2<true>(v, C, nL, rl - hf * HALF, acc);
       }
       // r < c0 (only without causal_skip): every pair is above the diagonal, adds 0.
       mbar_arrive(&q_empty[s]);
     }
-    if (key < a.N) {
-      float total = acc.x + acc.y;
+    // Merge the two query halves of each key (fixed order: lower half first).
+    if (hf == 1) merge[rl] = acc;
+    exp_bar_sync();
+    if (hf == 0 && key < a.N) {
+      const float2 o = merge[rl];
+      float total = (acc.x + acc.y) + (o.x + o.y);
       if (kKeyMask && a.kmask[b * a.kmb + key] == 0) total = 0.f;
       a.part[((long long)uu * a.nchunk + y) * a.N + key] = total;
     }
@@ -529,13 +562,15 @@ bool make_map(CUtensorMap* map, const void* base, bool bf16, int B, int H, int N
   return r == CUDA_SUCCESS;
 }
 
+constexpr size_t kBarBytes = 8 * (1 + 2 * kStages + 4) + 16;  // mbarriers + TMEM slot + abort flag
+
 template <int D>
 constexpr size_t smem_lse() {
-  return 1024 + (size_t)Cfg<D>::kTileBytes * (1 + kStages) + 8 * (1 + 2 * kStages + 4) + 16;
+  return 1024 + (size_t)Cfg<D>::kTileBytes * (1 + kStages) + TILE * 8 + kBarBytes;
 }
 template <int D>
 constexpr size_t smem_mass() {
-  return 1024 + (size_t)Cfg<D>::kTileBytes * (1 + kStages) + TILE * 4 * kStages + 8 * (1 + 2 * kStages + 4) + 16;
+  return 1024 + (size_t)Cfg<D>::kTileBytes * (1 + kStages) + TILE * 4 * kStages + TILE * 8 + kBarBytes;
 }
 
 template <int D, bool kBF16, bool kKeyMask>
