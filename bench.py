@@ -65,6 +65,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
+                    help="weak: every rank owns a full batch entry of the workload; strong: the "
+                         "workload's (batch, kv-head) units are split across the ranks")
     return ap.parse_args()
 
 
@@ -231,12 +234,20 @@ def reference_arm(args, w):
     print(json.dumps(line), flush=True)
 
 
-def workload_config(w, world: int):
+def workload_config(w, world: int, scaling: str = "weak"):
+    if scaling == "weak":
+        shard = "each rank owns B_per_rank batch entries (B*H_kv units); NCCL reduce of mass to rank 0"
+        gb = w.B * world
+    else:
+        shard = (f"the {w.B * w.Hkv} (batch, kv-head) units split contiguously over {world} ranks, "
+                 "inputs drawn per unit on each rank's GPU; NCCL reduce of mass to rank 0")
+        gb = w.B
     return {
-        "workload": w.name, "B_per_rank": w.B, "global_batch": w.B * world, "Hq": w.Hq, "Hkv": w.Hkv,
+        "workload": w.name, "B_per_rank": w.B if scaling == "weak" else None, "global_batch": gb,
+        "Hq": w.Hq, "Hkv": w.Hkv,
         "D": w.D, "seq_len": w.N, "block_size": w.block_size, "causal": w.causal,
         "parallelism": f"units{world}" if world > 1 else "single",
-        "shard": "each rank owns B_per_rank batch entries (B*H_kv units); NCCL reduce of mass to rank 0",
+        "shard": shard,
         "inputs_exceed_l2": True, "l2_flush": "none (q+k per step exceed the 126 MB L2)",
     }
 
@@ -259,10 +270,27 @@ def b200_arm(args, w):
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     lib = _lib.load()
 
-    # Inputs: rank r owns batch entry r of the weak-scaled problem (seed offset by rank).
-    from dataclasses import replace
-    wr = replace(w, seed=w.seed + 1000 * rank) if rank else w
-    q_cpu, k_cpu, km, qm = make_inputs(wr)
+    if args.scaling == "weak":
+        # Rank r owns batch entry r of the weak-scaled problem (seed offset by rank).
+        from dataclasses import replace
+        wr = replace(w, seed=w.seed + 1000 * rank) if rank else w
+        q_cpu, k_cpu, km, qm = make_inputs(wr)
+        pairs_total_per_step = pairs(w) * world
+    else:
+        # Rank r owns a contiguous range of the workload's (batch, kv-head) units and
+        # draws only those, on its own GPU (per-unit seeded protocol).
+        from kvblockmass_b200.distributed import partition_units
+        from kvblockmass_b200.workloads import make_unit_inputs
+        if w.key_mask_frac > 0 or w.dead_tail_rows > 0:
+            raise SystemExit("--scaling strong supports unmasked workloads only")
+        ub, ue = partition_units(w.B * w.Hkv, world)[rank]
+        if ue <= ub:
+            raise SystemExit(f"rank {rank} has no units: use at most {w.B * w.Hkv} GPUs")
+        qd, kd = make_unit_inputs(w, ub, ue, device=dev)
+        q_cpu, k_cpu = qd.cpu(), kd.cpu()
+        del qd, kd
+        km = qm = None
+        pairs_total_per_step = pairs(w)
     q_pin, k_pin = q_cpu.pin_memory(), k_cpu.pin_memory()
     q = q_pin.to(dev)
     k = k_pin.to(dev)
@@ -273,7 +301,8 @@ def b200_arm(args, w):
     ws = torch.empty(max(ops.workspace_bytes(prep), 256), dtype=torch.uint8, device=dev)
     out = torch.empty(prep.nb, dtype=prep.out_dtype, device=dev)
     stream = torch.cuda.current_stream(dev)
-    pairs_rank = pairs(w)
+    per_head = w.N * (w.N + 1) // 2 if w.causal else w.N * w.N
+    pairs_rank = q.shape[0] * q.shape[1] * per_head
     launches = ops.launches_per_call(prep)
 
     def step(events=None):
@@ -288,6 +317,12 @@ def b200_arm(args, w):
             raise RuntimeError(f"kvbm_block_mass failed: {_lib.status_string(code)}")
         if world > 1:
             dist.reduce(out, dst=0, op=dist.ReduceOp.SUM)
+
+    # MUFU ex2 rate of this GPU, measured before any heavy work so that the
+    # peak is the unthrottled one (the roofline denominator of the exp unit).
+    ex2 = ctypes.c_double(0.0)
+    if lib.kvbm_measure_ex2_rate(stream.cuda_stream, ctypes.byref(ex2)) != 0:
+        ex2.value = float("nan")
 
     # Warm-up (also creates the NCCL communicator).
     for _ in range(max(args.warmup, 0)):
@@ -356,15 +391,11 @@ def b200_arm(args, w):
         e_ms = torch.tensor([a0.elapsed_time(a1)], device=dev, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
-        e2e = {"value": pairs_rank * world * Ke / (float(e_ms.item()) * 1e-3), "unit": UNIT,
+        e2e = {"value": pairs_total_per_step * Ke / (float(e_ms.item()) * 1e-3), "unit": UNIT,
                "h2d_bytes_per_step": int(q_pin.numel() * q_pin.element_size() + k_pin.numel() * k_pin.element_size()),
                "d2h_bytes_per_step": int(m_host.numel() * m_host.element_size()),
                "steps": Ke, "api": "kvblockmass_b200.block_mass_b200(pinned host q/k, device='cuda').cpu()"}
 
-    # Roofline: calibration of the MUFU ex2 rate on this GPU, then the dominant kernel.
-    ex2 = ctypes.c_double(0.0)
-    if lib.kvbm_measure_ex2_rate(stream.cuda_stream, ctypes.byref(ex2)) != 0:
-        ex2.value = float("nan")
     clocks = None
     if sampler:
         sampler.__exit__(None, None, None)
@@ -388,12 +419,12 @@ def b200_arm(args, w):
     traffic = None
     if tr and dom_name in tr:
         traffic = tr[dom_name]
-    value = pairs_rank * world * K / (ms_total * 1e-3)
+    value = pairs_total_per_step * K / (ms_total * 1e-3)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": ms_total / K, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": workload_config(w, world),
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": workload_config(w, world, args.scaling),
         "kernel_path": "tcgen05" if path == 1 else "simt",
         "kernel_ms": {"pass1_lse": t1, "pass2_mass": t2, "reduce": t3},
         "roofline": {

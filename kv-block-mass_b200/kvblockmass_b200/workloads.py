@@ -21,7 +21,7 @@ from dataclasses import dataclass, field
 
 import torch
 
-__all__ = ["Workload", "WORKLOADS", "make_inputs", "pairs"]
+__all__ = ["Workload", "WORKLOADS", "make_inputs", "make_unit_inputs", "pairs"]
 
 
 @dataclass(frozen=True)
@@ -116,3 +116,40 @@ def make_inputs(w: Workload, N: int | None = None, device: str | torch.device = 
         key_mask = key_mask.to(device) if key_mask is not None else None
         query_mask = query_mask.to(device) if query_mask is not None else None
     return q, k, key_mask, query_mask
+
+
+def make_unit_inputs(w: Workload, unit_begin: int, unit_end: int, device="cpu", N: int | None = None):
+    """Inputs of the (batch, kv-head) units ``[unit_begin, unit_end)`` only.
+
+    Per-unit protocol for shards of large shapes, so that a rank draws just
+    the q/k it owns (on its own device): unit ``u`` draws its ``G`` q-heads and
+    then its kv-head from a generator seeded ``seed * 1_000_003 + u``.  The
+    per-q-head scales and the sink rows are drawn from a generator seeded
+    ``seed`` and shared by every unit.  Same shapes and distributions as
+    ``make_inputs``; different values.  The units must lie in one batch
+    entry.  Returns ``(q [1, (u1-u0)*G, N, D], k [1, u1-u0, N, D])`` in
+    ``w.dtype``.
+    """
+    n = w.N if N is None else N
+    G = w.G
+    if unit_begin // w.Hkv != (unit_end - 1) // w.Hkv:
+        raise ValueError("units must belong to one batch entry")
+    dev = torch.device(device)
+    shared = torch.Generator().manual_seed(w.seed)
+    head_scale = (torch.rand(w.Hq, generator=shared) * 1.5 + 0.5) if w.head_scale else None
+    sink_rows = None
+    if w.sink_frac > 0:
+        sink_rows = torch.randperm(n, generator=shared)[: max(1, int(n * w.sink_frac))].to(dev)
+    qs, ks = [], []
+    for u in range(unit_begin, unit_end):
+        g = torch.Generator(device=dev).manual_seed(w.seed * 1_000_003 + u)
+        q = torch.randn(1, G, n, w.D, generator=g, device=dev, dtype=torch.float32)
+        k = torch.randn(1, 1, n, w.D, generator=g, device=dev, dtype=torch.float32)
+        if head_scale is not None:
+            h0 = (u % w.Hkv) * G
+            q.mul_(head_scale[h0:h0 + G].to(dev).view(1, G, 1, 1))
+        if sink_rows is not None:
+            k[:, :, sink_rows, :] *= w.sink_gain
+        qs.append(q.to(w.dtype))
+        ks.append(k.to(w.dtype))
+    return torch.cat(qs, dim=1), torch.cat(ks, dim=1)
