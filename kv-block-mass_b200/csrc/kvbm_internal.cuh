@@ -20,7 +20,10 @@ constexpr int kSimtQChunk = 512;   // query rows per mass-pass CTA
 
 // ---- tcgen05 tiles (bf16 / fp16 path) ----
 constexpr int kTcTile = 128;       // rows of an MMA tile (M) and key/query tile (N)
-constexpr int kTcQChunk = 2048;    // query rows per mass-pass CTA
+#ifndef KVBM_TC_QCHUNK
+#define KVBM_TC_QCHUNK 2048
+#endif
+constexpr int kTcQChunk = KVBM_TC_QCHUNK;  // query rows per mass-pass CTA
 
 // Where each array lives inside the caller's workspace.
 struct WsLayout {

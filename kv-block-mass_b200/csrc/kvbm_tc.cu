@@ -38,7 +38,11 @@ constexpr int TILE = kTcTile;       // 128
 constexpr int HALF = TILE / 2;      // columns per exp warpgroup
 constexpr int kExpThreads = 256;    // two warpgroups
 constexpr int kThreads = 64 + kExpThreads;  // + TMA warp + MMA warp
-constexpr int kStages = 2;          // K (pass 1) / Q (pass 2) ring depth
+#ifndef KVBM_STAGES
+#define KVBM_STAGES 2
+#endif
+constexpr int kStages = KVBM_STAGES;  // K (pass 1) / Q (pass 2) ring depth
+constexpr int kLStages = 4;         // lse2 ring depth (pass 2)
 constexpr int kTmemCols = 256;      // two 128-column fp32 accumulators
 constexpr int kMinSmem = 100 * 1024;  // caps residency at 2 CTAs/SM (TMEM: 2 x 256 columns)
 constexpr int kExpBarrier = 1;      // named barrier of the 256 exp threads
@@ -106,7 +110,7 @@ __device__ __forceinline__ void load_half(uint32_t taddr, float (&v)[HALF]) {
 // has room to absorb part of it.  The groups are spread evenly so that the
 // scheduler can interleave both kinds.
 #ifndef KVBM_EMU_GROUPS
-#define KVBM_EMU_GROUPS 4
+#define KVBM_EMU_GROUPS 2
 #endif
 constexpr int kGroups = HALF / 4;
 constexpr int kEmuGroups = KVBM_EMU_GROUPS;
@@ -373,14 +377,16 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint8_t* k_tile = smem;
   uint8_t* q_ring = smem + TB;
   float* l_ring = reinterpret_cast<float*>(smem + TB * (1 + kStages));
-  float2* merge = reinterpret_cast<float2*>(smem + TB * (1 + kStages) + LB * kStages);  // [128]
+  float2* merge = reinterpret_cast<float2*>(smem + TB * (1 + kStages) + LB * kLStages);  // [128]
   uint64_t* bars = reinterpret_cast<uint64_t*>(merge + TILE);
   uint64_t* k_full = bars;
   uint64_t* q_full = bars + 1;
   uint64_t* q_empty = q_full + kStages;
   uint64_t* s_full = q_empty + kStages;
   uint64_t* s_empty = s_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_empty + 2);
+  uint64_t* l_full = s_empty + 2;
+  uint64_t* l_empty = l_full + kLStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(l_empty + kLStages);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -407,11 +413,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_init(k_full, 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&q_full[s], 1);
-      mbar_init(&q_empty[s], 1 + kExpThreads);  // MMA commit + every exp thread done with lse2
+      mbar_init(&q_empty[s], 1);  // MMA commit: the Q tile is no longer read
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], kExpThreads);
+    }
+    for (int t = 0; t < kLStages; ++t) {
+      mbar_init(&l_full[t], 1);
+      mbar_init(&l_empty[t], kExpThreads);  // every exp thread done with the tile's lse2
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -436,20 +446,26 @@ __global__ void __launch_bounds__(kThreads, 2)
       int issued = 0;
       for (int j = 0; j < J; ++j) {
         const int s = j % kStages, n = j / kStages;
+        const int t = j % kLStages, nl = j / kLStages;
         if (n > 0 && !mbar_wait(&q_empty[s], (n - 1) & 1, abort_flag)) break;
+        if (nl > 0 && !mbar_wait(&l_empty[t], (nl - 1) & 1, abort_flag)) break;
         const int hh = j / nqt;
         const int r = rs + (j - hh * nqt) * TILE;
         const int h = g * a.G + hh;
-        mbar_arrive_expect_tx(&q_full[s], TB + LB);
+        mbar_arrive_expect_tx(&q_full[s], TB);
 #pragma unroll
         for (int kb = 0; kb < Cfg<D>::kBlocks; ++kb)
           tma_load_4d(q_ring + s * TB + kb * Cfg<D>::kBlockBytes, &tq, &q_full[s], kb * 64, r, h, b);
-        bulk_load(l_ring + s * TILE, a.lse + (long long)(uu * a.G + hh) * a.Npad + r, LB, &q_full[s]);
+        mbar_arrive_expect_tx(&l_full[t], LB);
+        bulk_load(l_ring + t * TILE, a.lse + (long long)(uu * a.G + hh) * a.Npad + r, LB, &l_full[t]);
         issued = j + 1;
       }
+      // Do not leave while our copies are in flight.
       mbar_wait(k_full, 0, abort_flag);
       for (int j = max(0, issued - kStages); j < issued; ++j)
         mbar_wait(&q_full[j % kStages], (j / kStages) & 1, abort_flag);
+      for (int j = max(0, issued - kLStages); j < issued; ++j)
+        mbar_wait(&l_full[j % kLStages], (j / kLStages) & 1, abort_flag);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -480,9 +496,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     const float C = a.C;
     float2 acc = make_float2(0.f, 0.f);
     for (int j = 0; j < J; ++j) {
-      const int buf = j & 1, s = j % kStages;
+      const int buf = j & 1, t = j % kLStages;
       bool ok = mbar_wait(&s_full[buf], (j >> 1) & 1, abort_flag);
-      ok = ok && mbar_wait(&q_full[s], (j / kStages) & 1, abort_flag);  // lse2 bytes landed
+      ok = ok && mbar_wait(&l_full[t], (j / kLStages) & 1, abort_flag);  // lse2 bytes landed
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
       float v[HALF];
@@ -492,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
       const int hh = j / nqt;
       const int r = rs + (j - hh * nqt) * TILE;
-      const float* nL = l_ring + s * TILE + hf * HALF;  // -lse2 of this half's 64 query rows
+      const float* nL = l_ring + t * TILE + hf * HALF;  // -lse2 of this half's 64 query rows
       if (!a.causal || r > c0) {
         acc = col_sum_exp2<false>(v, C, nL, 0, acc);  // every pair kept
       } else if (r == c0) {
@@ -500,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         acc = col_sum_exp2<true>(v, C, nL, rl - hf * HALF, acc);
       }
       // r < c0 (only without causal_skip): every pair is above the diagonal, adds 0.
-      mbar_arrive(&q_empty[s]);
+      mbar_arrive(&l_empty[t]);
     }
     // Merge the two query halves of each key (fixed order: lower half first).
     if (hf == 1) merge[rl] = acc;
@@ -570,7 +586,8 @@ constexpr size_t smem_lse() {
 }
 template <int D>
 constexpr size_t smem_mass() {
-  return 1024 + (size_t)Cfg<D>::kTileBytes * (1 + kStages) + TILE * 4 * kStages + TILE * 8 + kBarBytes;
+  return 1024 + (size_t)Cfg<D>::kTileBytes * (1 + kStages) + TILE * 4 * kLStages + TILE * 8 + kBarBytes +
+         16 * kLStages;
 }
 
 template <int D, bool kBF16, bool kKeyMask>
