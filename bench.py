@@ -369,6 +369,38 @@ def b200_arm(args, w):
     if lib.kvbm_check_device_errors(stream.cuda_stream) != 0:
         raise RuntimeError("a device-side wait timed out in the timed region")
 
+    # Caller-provided LSE (pass 1 skipped): the path an attention forward can feed.
+    lse_input = None
+    if not args.no_e2e:
+        lse_buf = torch.empty(q.shape[0], q.shape[1], q.shape[2], dtype=torch.float32, device=dev)
+        # the LSE of these inputs, from the library's own pass 1 (the values an attention
+        # forward would return): run once, read back negated base-2 lse2, convert to natural log
+        ops.run_prepared(prep, out=out, workspace=ws)
+        torch.cuda.synchronize()
+        if path == 1:
+            npad = (w.N + 127) // 128 * 128
+            nl = ws[: q.shape[0] * q.shape[1] * npad * 4].view(torch.float32).view(q.shape[0], q.shape[1], npad)
+            lse_buf.copy_(-nl[:, :, : w.N] / 1.4426950408889634)
+        else:
+            nl = ws[: q.shape[0] * q.shape[1] * w.N * 4].view(torch.float32).view(q.shape[0], q.shape[1], w.N)
+            lse_buf.copy_(nl / 1.4426950408889634)
+        st3 = (ctypes.c_int64 * 3)(*lse_buf.stride())
+        for _ in range(2):
+            lib.kvbm_block_mass_lse(ctypes.byref(prep.prob), lse_buf.data_ptr(), st3, out.data_ptr(),
+                                    ws.data_ptr(), ws.numel(), stream.cuda_stream)
+        torch.cuda.synchronize()
+        l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        l0.record(stream)
+        for _ in range(K):
+            lib.kvbm_block_mass_lse(ctypes.byref(prep.prob), lse_buf.data_ptr(), st3, out.data_ptr(),
+                                    ws.data_ptr(), ws.numel(), stream.cuda_stream)
+        l1.record(stream)
+        torch.cuda.synchronize()
+        lse_input = {"value": pairs_rank * K / (l0.elapsed_time(l1) * 1e-3), "unit": UNIT,
+                     "ms_per_step": l0.elapsed_time(l1) / K, "per_gpu": True,
+                     "api": "kvbm_block_mass_lse (row LSE supplied, as an attention forward returns it)"}
+        del lse_buf
+
     # End to end through the public API: pinned host q/k in, mass back on the host.
     e2e = None
     if not args.no_e2e:
@@ -442,6 +474,8 @@ def b200_arm(args, w):
     }
     if e2e:
         line["e2e"] = e2e
+    if lse_input:
+        line["lse_input"] = lse_input
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = {k: v for k, v in cpu_sample(w, args.cpu_seconds).items()
                                 if k not in ("seconds", "pairs")}

@@ -139,6 +139,19 @@ int kvbm_launches_per_call(const kvbm_problem* p);
 int kvbm_block_mass(const kvbm_problem* p, void* mass_out, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/* kvbm_block_mass for callers that already hold each query row's
+ * log-sum-exp, as an attention forward pass returns it (for example the
+ * softmax LSE of a FlashAttention forward): lse[b*s0 + h*s1 + i*s2] =
+ * log(sum over kept keys c of exp(scale * q[b,h,i] . k[b,h/G,c])), natural
+ * log, fp32, with the same scale and masks as `p`.  Pass 1 is skipped: the
+ * LSE is copied into the workspace and only pass 2 and the bucket reduce run,
+ * about half the work.  A non-finite LSE marks a row that keeps no key (it
+ * contributes 0).  lse_stride = {s0, s1, s2} in elements.  It extends the
+ * reference's entry points (there the row statistics are always recomputed,
+ * triton_kernel.py:69-104); workspace and output as kvbm_block_mass. */
+int kvbm_block_mass_lse(const kvbm_problem* p, const float* lse, const int64_t* lse_stride, void* mass_out,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
 /* kvbm_block_mass that also records up to four CUDA events (cudaEvent_t,
  * each may be NULL) on `stream`: events[0] before pass 1, events[1] between
  * pass 1 and pass 2, events[2] between pass 2 and the bucket reduce,

@@ -87,6 +87,30 @@ WsLayout layout_for(const kvbm_problem* p, int path) {
   return L;
 }
 
+// Launch sequence shared by the entry points: (pass 1 | lse import), pass 2,
+// bucket reduce, with optional events around them.
+int run_passes(const kvbm_problem* p, const WsLayout& L, int path, void* mass_out, void* ws, cudaStream_t s,
+               void* const* events, const float* lse, const int64_t* lse_stride) {
+  auto mark = [&](int i) {
+    if (events != nullptr && events[i] != nullptr)
+      return cudaEventRecord(static_cast<cudaEvent_t>(events[i]), s) == cudaSuccess;
+    return true;
+  };
+  if (!mark(0)) return KVBM_ERR_CUDA;
+  LaunchOpts o;
+  o.mid_event = events != nullptr ? events[1] : nullptr;
+  o.run_pass1 = lse == nullptr;
+  int st = KVBM_OK;
+  if (lse != nullptr) st = launch_lse_import(p, L, lse, lse_stride, ws, s);
+  if (st != KVBM_OK) return st;
+  st = (path == 1) ? launch_tc(p, L, mass_out, ws, s, o) : launch_simt(p, L, mass_out, ws, s, o);
+  if (st != KVBM_OK) return st;
+  if (!mark(2)) return KVBM_ERR_CUDA;
+  st = launch_reduce(p, L, mass_out, ws, s);
+  if (st != KVBM_OK) return st;
+  return mark(3) ? KVBM_OK : KVBM_ERR_CUDA;
+}
+
 }  // namespace kvbm
 
 using namespace kvbm;
@@ -153,7 +177,7 @@ int kvbm_kernel_path(const kvbm_problem* p) {
 
 int kvbm_launches_per_call(const kvbm_problem* p) {
   if (validate(p) != KVBM_OK) return 0;
-  return 3;  // pass 1 (lse2), pass 2 (per-key partials), bucket reduce
+  return 3;  // pass 1 (lse2) or the lse import, pass 2 (per-key partials), bucket reduce
 }
 
 int kvbm_block_mass(const kvbm_problem* p, void* mass_out, void* workspace,
@@ -177,19 +201,28 @@ int kvbm_block_mass_events(const kvbm_problem* p, void* mass_out, void* workspac
   if (workspace == nullptr || workspace_bytes < L.total || ((uintptr_t)workspace % 256) != 0)
     return KVBM_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  auto mark = [&](int i) {
-    if (events != nullptr && events[i] != nullptr)
-      return cudaEventRecord(static_cast<cudaEvent_t>(events[i]), s) == cudaSuccess;
-    return true;
-  };
-  if (!mark(0)) return KVBM_ERR_CUDA;
-  st = (path == 1) ? launch_tc(p, L, mass_out, workspace, s, events != nullptr ? events[1] : nullptr)
-                   : launch_simt(p, L, mass_out, workspace, s, events != nullptr ? events[1] : nullptr);
+  return run_passes(p, L, path, mass_out, workspace, s, events, nullptr, nullptr);
+}
+
+int kvbm_block_mass_lse(const kvbm_problem* p, const float* lse, const int64_t* lse_stride, void* mass_out,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  int st = validate(p);
   if (st != KVBM_OK) return st;
-  if (!mark(2)) return KVBM_ERR_CUDA;
-  st = launch_reduce(p, L, mass_out, workspace, s);
-  if (st != KVBM_OK) return st;
-  return mark(3) ? KVBM_OK : KVBM_ERR_CUDA;
+  if (mass_out == nullptr || lse == nullptr || lse_stride == nullptr) return KVBM_ERR_NULL;
+  for (int i = 0; i < 3; ++i)
+    if (lse_stride[i] < 0) return KVBM_ERR_SHAPE;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return KVBM_ERR_CUDA;
+  }
+  if (device_kind(dev) != 1) return KVBM_ERR_DEVICE;
+  const int path = select_path(p, dev);
+  const WsLayout L = layout_for(p, path);
+  if (workspace == nullptr || workspace_bytes < L.total || ((uintptr_t)workspace % 256) != 0)
+    return KVBM_ERR_WORKSPACE;
+  return run_passes(p, L, path, mass_out, workspace, static_cast<cudaStream_t>(stream), nullptr, lse,
+                    lse_stride);
 }
 
 int kvbm_check_device_errors(void* stream) {

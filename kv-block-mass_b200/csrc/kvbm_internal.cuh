@@ -44,11 +44,17 @@ int select_path(const kvbm_problem* p, int device);
 WsLayout layout_for(const kvbm_problem* p, int path);
 
 // Launchers (return a kvbm_status).
-// `mid_event` (a cudaEvent_t or null) is recorded between pass 1 and pass 2.
+struct LaunchOpts {
+  void* mid_event = nullptr;  // cudaEvent_t recorded between pass 1 and pass 2 (or null)
+  bool run_pass1 = true;      // false: lse2 is already in the workspace (kvbm_block_mass_lse)
+};
 int launch_simt(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws, cudaStream_t s,
-                void* mid_event);
+                const LaunchOpts& o);
 int launch_tc(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws, cudaStream_t s,
-              void* mid_event);
+              const LaunchOpts& o);
+// Writes a caller's natural-log row LSE into the workspace's lse2 layout of `L.path`.
+int launch_lse_import(const kvbm_problem* p, const WsLayout& L, const float* lse, const int64_t* lse_stride,
+                      void* ws, cudaStream_t s);
 int launch_reduce(const kvbm_problem* p, const WsLayout& L, void* mass_out, const void* ws,
                   cudaStream_t s);
 

@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(NT) simt_mass_kernel(Args<Acc> a) {
 }
 
 template <typename In, typename Acc>
-int launch_typed(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s, void* mid_event) {
+int launch_typed(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s, const LaunchOpts& o) {
   Args<Acc> a;
   a.q = p->q;
   a.qs0 = p->q_stride[0]; a.qs1 = p->q_stride[1]; a.qs2 = p->q_stride[2]; a.qs3 = p->q_stride[3];
@@ -299,9 +299,11 @@ int launch_typed(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_
       cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2) != cudaSuccess)
     return KVBM_ERR_CUDA;
   dim3 g1((p->N + BM - 1) / BM, U * a.G);
-  k1<<<g1, NT, smem1, s>>>(a);
-  if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
-  if (mid_event != nullptr && cudaEventRecord(static_cast<cudaEvent_t>(mid_event), s) != cudaSuccess)
+  if (o.run_pass1) {
+    k1<<<g1, NT, smem1, s>>>(a);
+    if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
+  }
+  if (o.mid_event != nullptr && cudaEventRecord(static_cast<cudaEvent_t>(o.mid_event), s) != cudaSuccess)
     return KVBM_ERR_CUDA;
   dim3 g2((p->N + BN - 1) / BN, L.nchunk, U);
   k2<<<g2, NT, smem2, s>>>(a);
@@ -350,15 +352,68 @@ __global__ void __launch_bounds__(256) reduce_kernel(const Acc* part, Out* mass,
 }  // namespace
 
 int launch_simt(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws,
-                cudaStream_t s, void* mid_event) {
+                cudaStream_t s, const LaunchOpts& o) {
   (void)mass_out;
   switch (p->dtype) {
-    case KVBM_F32: return launch_typed<float, float>(p, L, ws, s, mid_event);
-    case KVBM_BF16: return launch_typed<__nv_bfloat16, float>(p, L, ws, s, mid_event);
-    case KVBM_F16: return launch_typed<__half, float>(p, L, ws, s, mid_event);
-    case KVBM_F64: return launch_typed<double, double>(p, L, ws, s, mid_event);
+    case KVBM_F32: return launch_typed<float, float>(p, L, ws, s, o);
+    case KVBM_BF16: return launch_typed<__nv_bfloat16, float>(p, L, ws, s, o);
+    case KVBM_F16: return launch_typed<__half, float>(p, L, ws, s, o);
+    case KVBM_F64: return launch_typed<double, double>(p, L, ws, s, o);
     default: return KVBM_ERR_DTYPE;
   }
+}
+
+// Caller-provided row LSE (natural log of sum_c exp(scale * q.k_c) over kept
+// keys, as an attention forward returns it) -> the lse2 layout of the path:
+// SIMT keeps +lse2 in the accumulation type with +inf for rows that keep no
+// key; the tensor-core path keeps -lse2 (fp32) over whole 128-row tiles with
+// -inf for rows that keep no key and for padding rows.  A non-finite input or
+// a dropped query_mask row counts as a row that keeps no key.
+template <typename Acc, bool kNegated>
+__global__ void lse_import_kernel(const float* lse, long long s0, long long s1, long long s2, Acc* out, int N,
+                                  int Nrow, int G, int Hkv, int ub, long long rows_total, const uint8_t* qmask,
+                                  long long qmb) {
+  const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (idx >= rows_total) return;
+  const int i = (int)(idx % Nrow);
+  const long long hidx = idx / Nrow;  // (u - ub) * G + hh
+  const int u = ub + (int)(hidx / G), hh = (int)(hidx % G);
+  const int b = u / Hkv, h = (u % Hkv) * G + hh;
+  bool dead = i >= N;
+  double v = 0.0;
+  if (!dead) {
+    v = (double)lse[b * s0 + h * s1 + (long long)i * s2];
+    dead = !isfinite(v) || (qmask != nullptr && qmask[b * qmb + i] == 0);
+  }
+  const double l2 = v * kLog2e;
+  Acc r;
+  if (kNegated) r = dead ? (Acc)(-INFINITY) : (Acc)(-l2);
+  else r = dead ? (Acc)INFINITY : (Acc)l2;
+  out[idx] = r;
+}
+
+int launch_lse_import(const kvbm_problem* p, const WsLayout& L, const float* lse, const int64_t* st, void* ws,
+                      cudaStream_t s) {
+  const int U = p->unit_end - p->unit_begin, G = p->Hq / p->Hkv;
+  const int Nrow = L.path == 1 ? (p->N + kTcTile - 1) / kTcTile * kTcTile : p->N;
+  const long long rows = (long long)U * G * Nrow;
+  const int threads = 256;
+  const long long blocks = (rows + threads - 1) / threads;
+  char* base = static_cast<char*>(ws) + L.lse_off;
+  if (L.path == 1) {
+    lse_import_kernel<float, true><<<(unsigned)blocks, threads, 0, s>>>(
+        lse, st[0], st[1], st[2], reinterpret_cast<float*>(base), p->N, Nrow, G, p->Hkv, p->unit_begin, rows,
+        p->query_mask, p->query_mask_bstride);
+  } else if (p->dtype == KVBM_F64) {
+    lse_import_kernel<double, false><<<(unsigned)blocks, threads, 0, s>>>(
+        lse, st[0], st[1], st[2], reinterpret_cast<double*>(base), p->N, Nrow, G, p->Hkv, p->unit_begin, rows,
+        p->query_mask, p->query_mask_bstride);
+  } else {
+    lse_import_kernel<float, false><<<(unsigned)blocks, threads, 0, s>>>(
+        lse, st[0], st[1], st[2], reinterpret_cast<float*>(base), p->N, Nrow, G, p->Hkv, p->unit_begin, rows,
+        p->query_mask, p->query_mask_bstride);
+  }
+  return cudaGetLastError() == cudaSuccess ? KVBM_OK : KVBM_ERR_CUDA;
 }
 
 int launch_reduce(const kvbm_problem* p, const WsLayout& L, void* mass_out, const void* ws,

@@ -591,7 +591,7 @@ constexpr size_t smem_mass() {
 }
 
 template <int D, bool kBF16, bool kKeyMask>
-int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s, void* mid_event) {
+int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s, const LaunchOpts& o) {
   CUtensorMap tq, tk;
   if (!make_map(&tq, p->q, kBF16, p->B, p->Hq, p->N, D, p->q_stride) ||
       !make_map(&tk, p->k, kBF16, p->B, p->Hkv, p->N, D, p->k_stride))
@@ -625,9 +625,11 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
   if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1) != cudaSuccess ||
       cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2) != cudaSuccess)
     return KVBM_ERR_CUDA;
-  k1<<<dim3(U * a.G, ntiles), kThreads, sm1, s>>>(tq, tk, a);
-  if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
-  if (mid_event != nullptr && cudaEventRecord(static_cast<cudaEvent_t>(mid_event), s) != cudaSuccess)
+  if (o.run_pass1) {
+    k1<<<dim3(U * a.G, ntiles), kThreads, sm1, s>>>(tq, tk, a);
+    if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
+  }
+  if (o.mid_event != nullptr && cudaEventRecord(static_cast<cudaEvent_t>(o.mid_event), s) != cudaSuccess)
     return KVBM_ERR_CUDA;
   k2<<<dim3(U * a.per_unit), kThreads, sm2, s>>>(tq, tk, a);
   if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
@@ -635,7 +637,7 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
 }
 
 template <int D>
-int launch_d(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s, void* ev) {
+int launch_d(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s, const LaunchOpts& ev) {
   const bool bf16 = p->dtype == KVBM_BF16;
   const bool km = p->key_mask != nullptr;
   if (bf16)
@@ -648,10 +650,10 @@ int launch_d(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s,
 bool tc_path_enabled() { return encode_fn() != nullptr; }
 
 int launch_tc(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws, cudaStream_t s,
-              void* mid_event) {
+              const LaunchOpts& o) {
   (void)mass_out;
-  if (p->D == 64) return launch_d<64>(p, L, ws, s, mid_event);
-  if (p->D == 128) return launch_d<128>(p, L, ws, s, mid_event);
+  if (p->D == 64) return launch_d<64>(p, L, ws, s, o);
+  if (p->D == 128) return launch_d<128>(p, L, ws, s, o);
   return KVBM_ERR_HEAD_DIM;
 }
 

@@ -39,6 +39,7 @@ EXPORTED = [
     "kvbm_launches_per_call",
     "kvbm_block_mass",
     "kvbm_block_mass_events",
+    "kvbm_block_mass_lse",
     "kvbm_measure_ex2_rate",
     "kvbm_check_device_errors",
     "kvbm_block_mass_static",
@@ -110,6 +111,9 @@ def load() -> ctypes.CDLL:
     lib.kvbm_block_mass_events.restype = ctypes.c_int
     lib.kvbm_block_mass_events.argtypes = [P, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
                                            ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
+    lib.kvbm_block_mass_lse.restype = ctypes.c_int
+    lib.kvbm_block_mass_lse.argtypes = [P, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64), ctypes.c_void_p,
+                                        ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
     lib.kvbm_measure_ex2_rate.restype = ctypes.c_int
     lib.kvbm_measure_ex2_rate.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_double)]
     # No-allocation variant: scratch from a fixed device array inside the library.

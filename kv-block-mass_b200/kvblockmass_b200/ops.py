@@ -176,8 +176,12 @@ def launches_per_call(prep: _Prepared) -> int:
 
 def run_prepared(prep: _Prepared, out: torch.Tensor | None = None,
                  workspace: torch.Tensor | None = None,
-                 stream: torch.cuda.Stream | None = None) -> torch.Tensor:
-    """Launch the kernels of a prepared problem on ``stream`` (default: current)."""
+                 stream: torch.cuda.Stream | None = None,
+                 lse: torch.Tensor | None = None) -> torch.Tensor:
+    """Launch the kernels of a prepared problem on ``stream`` (default: current).
+
+    With ``lse`` ([B, H_q, N] natural-log row log-sum-exp) pass 1 is skipped.
+    """
     q = prep.keep[0]
     dev = q.device
     lib = _lib.load()
@@ -190,8 +194,18 @@ def run_prepared(prep: _Prepared, out: torch.Tensor | None = None,
         elif out.dtype != prep.out_dtype or out.numel() != prep.nb or not out.is_contiguous():
             raise ValueError(f"out must be a contiguous {prep.out_dtype} tensor of {prep.nb} elements")
         s = stream if stream is not None else torch.cuda.current_stream(dev)
-        code = lib.kvbm_block_mass(ctypes.byref(prep.prob), out.data_ptr(), workspace.data_ptr(),
-                                   workspace.numel(), s.cuda_stream)
+        if lse is None:
+            code = lib.kvbm_block_mass(ctypes.byref(prep.prob), out.data_ptr(), workspace.data_ptr(),
+                                       workspace.numel(), s.cuda_stream)
+        else:
+            B, Hq, N = prep.prob.B, prep.prob.Hq, prep.prob.N
+            if tuple(lse.shape) != (B, Hq, N):
+                raise ValueError(f"lse must be [B, H_q, N] = {(B, Hq, N)}, got {tuple(lse.shape)}")
+            lse = lse.to(device=dev, dtype=torch.float32)
+            prep.keep.append(lse)
+            st = (ctypes.c_int64 * 3)(*lse.stride())
+            code = lib.kvbm_block_mass_lse(ctypes.byref(prep.prob), lse.data_ptr(), st, out.data_ptr(),
+                                           workspace.data_ptr(), workspace.numel(), s.cuda_stream)
     if code != _lib.KVBM_OK:
         _raise(code, prep.prob)
     return out
@@ -199,13 +213,16 @@ def run_prepared(prep: _Prepared, out: torch.Tensor | None = None,
 
 def block_mass_b200(q, k, attn_mask=None, causal=False, block_size=64, scale=None,
                     causal_skip=True, query_mask=None, *, BLOCK_M=None, BLOCK_N=None,
-                    query_chunk=None, device=None, units=None, out=None, workspace=None):
+                    query_chunk=None, device=None, units=None, out=None, workspace=None, lse=None):
     """Block-pooled column sums of the softmax attention matrix on a B200.
 
     Returns ``mass [ceil(N / block_size)]`` (float32; float64 for float64
     inputs) on the CUDA device of ``q``.  ``units=(begin, end)`` restricts the
     sum to the (batch, kv-head) units ``[begin, end)`` of ``B * H_kv`` (used by
     the multi-GPU shards); ``out``/``workspace`` let callers reuse buffers.
+    ``lse`` ([B, H_q, N], natural log of sum_c exp(scale * q.k_c) over the kept
+    keys, e.g. the softmax LSE an attention forward returns) skips the row
+    statistics pass: about half the work.
     """
     del BLOCK_M, BLOCK_N, query_chunk  # tiling is fixed by the kernels
     if device is not None:
@@ -218,7 +235,7 @@ def block_mass_b200(q, k, attn_mask=None, causal=False, block_size=64, scale=Non
                          "pass device='cuda' or use the reference's block_mass_reference")
     prep = make_problem(q, k, attn_mask=attn_mask, causal=causal, block_size=block_size,
                         scale=scale, causal_skip=causal_skip, query_mask=query_mask, units=units)
-    return run_prepared(prep, out=out, workspace=workspace)
+    return run_prepared(prep, out=out, workspace=workspace, lse=lse)
 
 
 def block_mass_triton(q, k, attn_mask=None, causal=False, block_size=64, scale=None,
