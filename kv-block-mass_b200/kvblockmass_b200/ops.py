@@ -229,6 +229,11 @@ def block_mass_b200(q, k, attn_mask=None, causal=False, block_size=64, scale=Non
         dev = torch.device(device)
         if dev.type != "cuda":
             raise ValueError(f"block_mass_b200 computes on CUDA devices only, got device={device}")
+        if (not q.is_cuda and not k.is_cuda and q.is_pinned() and k.is_pinned() and units is None
+                and lse is None and out is None and q.dim() == 4 and k.dim() == 4):
+            return _from_pinned_host(q, k, dev, attn_mask=attn_mask, causal=causal, block_size=block_size,
+                                     scale=scale, causal_skip=causal_skip, query_mask=query_mask,
+                                     workspace=workspace)
         q, k = q.to(dev), k.to(dev)
     if not (q.is_cuda and k.is_cuda):
         raise ValueError("block_mass_b200 needs CUDA tensors (there is no CPU path); "
@@ -236,6 +241,64 @@ def block_mass_b200(q, k, attn_mask=None, causal=False, block_size=64, scale=Non
     prep = make_problem(q, k, attn_mask=attn_mask, causal=causal, block_size=block_size,
                         scale=scale, causal_skip=causal_skip, query_mask=query_mask, units=units)
     return run_prepared(prep, out=out, workspace=workspace, lse=lse)
+
+
+_COPY_STREAMS: dict = {}
+
+
+def _copy_stream(dev: torch.device) -> torch.cuda.Stream:
+    if dev not in _COPY_STREAMS:
+        _COPY_STREAMS[dev] = torch.cuda.Stream(device=dev)
+    return _COPY_STREAMS[dev]
+
+
+def _from_pinned_host(q, k, dev, attn_mask, causal, block_size, scale, causal_skip, query_mask, workspace,
+                      target_units: int = 2):
+    """Pinned host q/k: overlap the host-to-device copy with the kernels.
+
+    The (batch, kv-head) units are cut into contiguous segments; a side
+    stream copies segment i + 1 while segment i runs on the caller's stream,
+    and the per-segment mass vectors are added in segment order (deterministic;
+    the grouping of the final sum differs from one call over all units, so the
+    bits can differ from it in the last place).
+    """
+    from .distributed import unit_segments
+
+    B, Hq, N, D = q.shape
+    Hkv = k.shape[1]
+    if Hkv == 0 or Hq % Hkv != 0:
+        raise ValueError(f"GQA requires H_q % H_kv == 0, got H_q={Hq}, H_kv={Hkv}")
+    G = Hq // Hkv
+    with torch.cuda.device(dev):
+        qd = torch.empty(q.shape, dtype=q.dtype, device=dev)
+        kd = torch.empty(k.shape, dtype=k.dtype, device=dev)
+        compute = torch.cuda.current_stream(dev)
+        copy = _copy_stream(dev)
+        copy.wait_stream(compute)  # qd/kd may reuse memory the compute stream still reads
+        am = None if attn_mask is None else attn_mask.to(dev, non_blocking=True)
+        qm = None if query_mask is None else query_mask.to(dev, non_blocking=True)
+        U = B * Hkv
+        step = max(1, min(target_units, U))
+        bounds = [(u, min(U, u + step)) for u in range(0, U, step)]
+        parts = []
+        for ub, ue in bounds:
+            with torch.cuda.stream(copy):
+                for b, g0, g1 in unit_segments(ub, ue, Hkv):
+                    qd[b, g0 * G:g1 * G].copy_(q[b, g0 * G:g1 * G], non_blocking=True)
+                    kd[b, g0:g1].copy_(k[b, g0:g1], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(copy)
+            compute.wait_event(ev)
+            prep = make_problem(qd, kd, attn_mask=am, causal=causal, block_size=block_size, scale=scale,
+                                causal_skip=causal_skip, query_mask=qm, units=(ub, ue))
+            parts.append(run_prepared(prep, workspace=workspace))
+        # qd/kd were written on the copy stream: tell the allocator before they are freed
+        qd.record_stream(copy)
+        kd.record_stream(copy)
+        total = parts[0].clone()
+        for m in parts[1:]:
+            total += m
+        return total
 
 
 def block_mass_triton(q, k, attn_mask=None, causal=False, block_size=64, scale=None,

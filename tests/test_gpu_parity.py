@@ -271,3 +271,23 @@ def test_llama3_70b_prefix_vs_oracle(cuda_device):
     got = run(q, k, causal=True, block_size=w.block_size)
     want = oracle_for(q, k, causal=True, block_size=w.block_size)
     assert max_rel(got.cpu().numpy(), want) < 1e-3
+
+
+@pytest.mark.parametrize("shape", [(1, 32, 8, 3000, 128), (3, 8, 2, 777, 64)])
+def test_pinned_host_inputs_pipelined(cuda_device, shape):
+    """Pinned host inputs with device='cuda' copy unit segments on a side stream
+    while earlier segments compute; the result equals the device-input call."""
+    B, Hq, Hkv, N, D = shape
+    g = torch.Generator().manual_seed(17)
+    q = torch.randn(B, Hq, N, D, generator=g).to(torch.bfloat16).pin_memory()
+    k = torch.randn(B, Hkv, N, D, generator=g).to(torch.bfloat16).pin_memory()
+    km = torch.rand(N, generator=g) > 0.1
+    qm = torch.rand(B, N, generator=g) > 0.1
+    a = kb.block_mass_b200(q, k, attn_mask=km, query_mask=qm, causal=True, block_size=64, device=cuda_device)
+    b = run(q.to(cuda_device), k.to(cuda_device), attn_mask=km.to(cuda_device), query_mask=qm.to(cuda_device),
+            causal=True, block_size=64)
+    torch.cuda.synchronize()
+    assert a.is_cuda
+    assert max_rel(a.cpu().numpy(), b.cpu().numpy()) < 1e-6
+    c = kb.block_mass_b200(q, k, attn_mask=km, query_mask=qm, causal=True, block_size=64, device=cuda_device)
+    assert torch.equal(a, c)
