@@ -38,6 +38,14 @@ extern "C" {
 
 #define KVBM_ABI_VERSION 1
 
+/* Only the entry points below are exported from libkvbm.so (it is built with
+ * hidden default visibility). */
+#if defined(__GNUC__)
+#define KVBM_API __attribute__((visibility("default")))
+#else
+#define KVBM_API
+#endif
+
 /* Element type of q and k.  The mass output is float32, or float64 for
  * KVBM_F64 inputs (reference.py:77: fp64 stays fp64, everything else
  * accumulates in fp32). */
@@ -104,31 +112,31 @@ typedef struct kvbm_problem {
 } kvbm_problem;
 
 /* ABI version of the loaded library (KVBM_ABI_VERSION it was built with). */
-int kvbm_abi_version(void);
+KVBM_API int kvbm_abi_version(void);
 
 /* Static description of a status code. */
-const char* kvbm_status_string(int status);
+KVBM_API const char* kvbm_status_string(int status);
 
 /* Host-only argument validation; touches no GPU.  Returns KVBM_OK or the
  * first failing check. */
-int kvbm_validate(const kvbm_problem* p);
+KVBM_API int kvbm_validate(const kvbm_problem* p);
 
 /* ceil(N / block_size), the length of the mass vector. */
-int64_t kvbm_num_blocks(int32_t N, int32_t block_size);
+KVBM_API int64_t kvbm_num_blocks(int32_t N, int32_t block_size);
 
 /* Bytes of device workspace kvbm_block_mass needs for `p` (0 on invalid
  * input).  Host-only; the size depends on the device's kernel path but not
  * on pointer values. */
-size_t kvbm_workspace_bytes(const kvbm_problem* p);
+KVBM_API size_t kvbm_workspace_bytes(const kvbm_problem* p);
 
 /* Which kernel family will run `p` on the current device:
  * 0 = SIMT (fp32 FFMA / fp64 DFMA, any mask, D <= 256),
  * 1 = tcgen05 tensor cores with TMA and TMEM (bf16/fp16, D in {64, 128}),
  * negative = a kvbm_status error code, negated. */
-int kvbm_kernel_path(const kvbm_problem* p);
+KVBM_API int kvbm_kernel_path(const kvbm_problem* p);
 
 /* Kernel launches one kvbm_block_mass call of `p` makes (host-only). */
-int kvbm_launches_per_call(const kvbm_problem* p);
+KVBM_API int kvbm_launches_per_call(const kvbm_problem* p);
 
 /* Compute the mass of units [p->unit_begin, p->unit_end) into
  * `mass_out` (device, num_blocks elements of float32, or float64 for
@@ -136,7 +144,7 @@ int kvbm_launches_per_call(const kvbm_problem* p);
  * memory of at least kvbm_workspace_bytes(p) bytes, 256-byte aligned; its
  * contents on entry do not matter.  Results are deterministic: the same
  * inputs give the same bits, and causal_skip on/off give the same bits. */
-int kvbm_block_mass(const kvbm_problem* p, void* mass_out, void* workspace,
+KVBM_API int kvbm_block_mass(const kvbm_problem* p, void* mass_out, void* workspace,
                     size_t workspace_bytes, void* stream);
 
 /* kvbm_block_mass for callers that already hold each query row's
@@ -149,7 +157,7 @@ int kvbm_block_mass(const kvbm_problem* p, void* mass_out, void* workspace,
  * contributes 0).  lse_stride = {s0, s1, s2} in elements.  It extends the
  * reference's entry points (there the row statistics are always recomputed,
  * triton_kernel.py:69-104); workspace and output as kvbm_block_mass. */
-int kvbm_block_mass_lse(const kvbm_problem* p, const float* lse, const int64_t* lse_stride, void* mass_out,
+KVBM_API int kvbm_block_mass_lse(const kvbm_problem* p, const float* lse, const int64_t* lse_stride, void* mass_out,
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /* kvbm_block_mass that also records up to four CUDA events (cudaEvent_t,
@@ -158,7 +166,7 @@ int kvbm_block_mass_lse(const kvbm_problem* p, const float* lse, const int64_t* 
  * events[3] after the reduce.  Per-kernel timing for benchmarks; it replaces
  * the CUDA-event timing of the reference's bench (bench/bench_block_mass.py:37-54)
  * at kernel rather than call granularity. */
-int kvbm_block_mass_events(const kvbm_problem* p, void* mass_out, void* workspace,
+KVBM_API int kvbm_block_mass_events(const kvbm_problem* p, void* mass_out, void* workspace,
                            size_t workspace_bytes, void* stream, void* const* events);
 
 /* Measures the current device's MUFU ex2.approx.f32 throughput (results per
@@ -166,7 +174,7 @@ int kvbm_block_mass_events(const kvbm_problem* p, void* mass_out, void* workspac
  * `stream`; synchronises `stream`.  The exp/sum warps of both passes are
  * bound by this rate, so benchmarks report it as the roofline denominator.
  * No counterpart in the reference. */
-int kvbm_measure_ex2_rate(void* stream, double* ex2_per_second);
+KVBM_API int kvbm_measure_ex2_rate(void* stream, double* ex2_per_second);
 
 /* kvbm_block_mass for callers that cannot allocate device memory.  It has
  * no counterpart in the reference.
@@ -196,16 +204,16 @@ int kvbm_measure_ex2_rate(void* stream, double* ex2_per_second);
  * to be cleared between calls.  Calls that can overlap on the GPU (different
  * streams without ordering between them) race on the array and give wrong
  * results; order them on one stream or with events. */
-int kvbm_block_mass_static(const kvbm_problem* p, void* mass_out, void* stream);
+KVBM_API int kvbm_block_mass_static(const kvbm_problem* p, void* mass_out, void* stream);
 
 /* Size in bytes of the fixed scratch array used by kvbm_block_mass_static.
  * No counterpart in the reference. */
-size_t kvbm_static_scratch_bytes(void);
+KVBM_API size_t kvbm_static_scratch_bytes(void);
 
 /* Reads and clears the device-side error word of the current device (set
  * when a bounded wait inside a tcgen05 kernel gave up).  Synchronises
  * `stream`.  Returns KVBM_OK, KVBM_ERR_TIMEOUT or KVBM_ERR_CUDA. */
-int kvbm_check_device_errors(void* stream);
+KVBM_API int kvbm_check_device_errors(void* stream);
 
 #ifdef __cplusplus
 }

@@ -23,7 +23,7 @@ INCLUDE = REPO_ROOT / "include"
 LIB = PKG_ROOT / "kvblockmass_b200" / "libkvbm.so"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2", "-shared",
+NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2,-fvisibility=hidden", "-shared",
               "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]
 
 

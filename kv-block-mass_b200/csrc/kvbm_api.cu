@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 #include <stdio.h>
 
+#include <atomic>
+
 #include "kvbm_internal.cuh"
 
 namespace kvbm {
@@ -13,18 +15,23 @@ size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 constexpr int kMaxDevices = 64;
 // Lazily filled per-device attribute cache: 0 unknown, 1 sm_100, 2 other.
-int g_dev_kind[kMaxDevices] = {0};
+// Threads that race on a first lookup compute and store the same value.
+std::atomic<int> g_dev_kind[kMaxDevices] = {};
 
 int device_kind(int dev) {
   if (dev < 0 || dev >= kMaxDevices) return 2;
-  if (g_dev_kind[dev] == 0) {
+  int kind = g_dev_kind[dev].load(std::memory_order_acquire);
+  if (kind == 0) {
     int major = 0, minor = 0;
     if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
+      cudaGetLastError();
       return 2;
-    g_dev_kind[dev] = (major == 10 && minor == 0) ? 1 : 2;
+    }
+    kind = (major == 10 && minor == 0) ? 1 : 2;
+    g_dev_kind[dev].store(kind, std::memory_order_release);
   }
-  return g_dev_kind[dev];
+  return kind;
 }
 
 }  // namespace

@@ -13,6 +13,8 @@
 // process exits.
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "kvbm_internal.cuh"
 
 namespace kvbm {
@@ -27,7 +29,7 @@ static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBy
 constexpr int kMaxDevices = 64;
 // Device address of g_static_scratch, looked up once per device.  In host
 // code the array's name is only a host-side stand-in, not a device address.
-void* g_scratch_addr[kMaxDevices] = {nullptr};
+std::atomic<void*> g_scratch_addr[kMaxDevices] = {};
 
 }  // namespace
 }  // namespace kvbm
@@ -47,15 +49,15 @@ extern "C" int kvbm_block_mass_static(const kvbm_problem* p, void* mass_out, voi
   if (dev < 0 || dev >= kMaxDevices) return KVBM_ERR_DEVICE;
   const size_t need = layout_for(p, select_path(p, dev)).total;
   if (need > kStaticScratchBytes) return KVBM_ERR_SCRATCH;
-  if (g_scratch_addr[dev] == nullptr) {
+  void* ptr = g_scratch_addr[dev].load(std::memory_order_acquire);
+  if (ptr == nullptr) {
     // First call on this device: resolve the array's device address with
-    // this device current.
-    void* ptr = nullptr;
+    // this device current (threads racing here store the same address).
     if (cudaGetSymbolAddress(&ptr, g_static_scratch) != cudaSuccess || ptr == nullptr) {
       cudaGetLastError();
       return KVBM_ERR_CUDA;
     }
-    g_scratch_addr[dev] = ptr;
+    g_scratch_addr[dev].store(ptr, std::memory_order_release);
   }
-  return kvbm_block_mass(p, mass_out, g_scratch_addr[dev], kStaticScratchBytes, stream);
+  return kvbm_block_mass(p, mass_out, ptr, kStaticScratchBytes, stream);
 }

@@ -26,6 +26,8 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <mutex>
+
 #include "kvbm_internal.cuh"
 #include "kvbm_sm100.cuh"
 
@@ -544,7 +546,8 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
 
 EncodeTiledFn encode_fn() {
   static EncodeTiledFn fn = nullptr;
-  if (fn == nullptr) {
+  static std::once_flag once;
+  std::call_once(once, [] {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
@@ -552,7 +555,7 @@ EncodeTiledFn encode_fn() {
       fn = reinterpret_cast<EncodeTiledFn>(p);
     else
       cudaGetLastError();
-  }
+  });
   return fn;
 }
 
