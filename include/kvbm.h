@@ -132,6 +132,8 @@ KVBM_API size_t kvbm_workspace_bytes(const kvbm_problem* p);
 /* Which kernel family will run `p` on the current device:
  * 0 = SIMT (fp32 FFMA / fp64 DFMA, any mask, D <= 256),
  * 1 = tcgen05 tensor cores with TMA and TMEM (bf16/fp16, D in {64, 128}),
+ * 2 = tcgen05 3xTF32 for fp32 inputs (D in {32, 64}): tf32 hi/lo split,
+ *     three MMAs per step, fp32-grade scores,
  * negative = a kvbm_status error code, negated. */
 KVBM_API int kvbm_kernel_path(const kvbm_problem* p);
 

@@ -56,41 +56,48 @@ int validate(const kvbm_problem* p) {
   return KVBM_OK;
 }
 
-// Path 1 (tcgen05) needs a 16-bit dtype, D in {64, 128}, a unit-stride head
-// dim, 16-byte aligned base pointers and row/head/batch strides (TMA rules),
-// and no pair mask; everything else runs the SIMT kernels.
+// Path 1 (tcgen05, bf16/fp16) needs D in {64, 128}, a unit-stride head dim,
+// 16-byte aligned base pointers and row/head/batch strides (TMA rules).
+// Path 2 (tcgen05 3xTF32 for fp32 inputs) needs D in {32, 64}; it reads q/k
+// with a split kernel, so any strides work.  Both need a positive scale and
+// no pair mask; everything else runs the SIMT kernels.
 int select_path(const kvbm_problem* p, int device) {
   if (device >= 0 && device_kind(device) != 1) return 0;
-  if (p->dtype != KVBM_BF16 && p->dtype != KVBM_F16) return 0;
-  if (p->D != 64 && p->D != 128) return 0;
   if (p->pair_mask != nullptr) return 0;
   if (!(p->scale > 0.0)) return 0;  // the exp/sum warps assume a positive scale
+  if (!tc_path_enabled()) return 0;
+  if (p->dtype == KVBM_F32) return (p->D == 32 || p->D == 64) ? 2 : 0;
+  if (p->dtype != KVBM_BF16 && p->dtype != KVBM_F16) return 0;
+  if (p->D != 64 && p->D != 128) return 0;
   const int64_t* qs = p->q_stride;
   const int64_t* ks = p->k_stride;
   if (qs[3] != 1 || ks[3] != 1) return 0;
   for (int i = 0; i < 3; ++i)
     if ((qs[i] * 2) % 16 != 0 || (ks[i] * 2) % 16 != 0) return 0;
   if (((uintptr_t)p->q % 16) != 0 || ((uintptr_t)p->k % 16) != 0) return 0;
-  return tc_path_enabled() ? 1 : 0;
+  return 1;
 }
 
 WsLayout layout_for(const kvbm_problem* p, int path) {
   WsLayout L;
   L.path = path;
   L.acc_bytes = (p->dtype == KVBM_F64) ? 8 : 4;
-  L.qchunk = path == 1 ? kTcQChunk : kSimtQChunk;
-  L.key_tile = path == 1 ? kTcTile : kSimtBN;
+  const bool tc = path >= 1;
+  L.qchunk = tc ? kTcQChunk : kSimtQChunk;
+  L.key_tile = tc ? kTcTile : kSimtBN;
   L.nchunk = (p->N + L.qchunk - 1) / L.qchunk;
   const size_t U = (size_t)(p->unit_end - p->unit_begin);
   const size_t G = (size_t)(p->Hq / p->Hkv);
   // The tensor-core path pads each head's lse2 row to whole 128-row tiles
   // (padding rows hold +inf) so that pass 2 can bulk-copy full tiles.
-  const size_t n_lse = path == 1 ? (size_t)(p->N + kTcTile - 1) / kTcTile * kTcTile : (size_t)p->N;
+  const size_t n_lse = tc ? (size_t)(p->N + kTcTile - 1) / kTcTile * kTcTile : (size_t)p->N;
   L.lse_off = 0;
   L.lse_bytes = U * G * n_lse * L.acc_bytes;
   L.part_off = align_up(L.lse_off + L.lse_bytes, 256);
   L.part_bytes = U * (size_t)L.nchunk * (size_t)p->N * L.acc_bytes;
-  L.total = align_up(L.part_off + L.part_bytes, 256);
+  L.split_off = align_up(L.part_off + L.part_bytes, 256);
+  L.split_bytes = path == 2 ? (size_t)2 * 4 * p->N * p->D * ((size_t)p->B * p->Hq + (size_t)p->B * p->Hkv) : 0;
+  L.total = align_up(L.split_off + L.split_bytes, 256);
   return L;
 }
 
@@ -110,7 +117,7 @@ int run_passes(const kvbm_problem* p, const WsLayout& L, int path, void* mass_ou
   int st = KVBM_OK;
   if (lse != nullptr) st = launch_lse_import(p, L, lse, lse_stride, ws, s);
   if (st != KVBM_OK) return st;
-  st = (path == 1) ? launch_tc(p, L, mass_out, ws, s, o) : launch_simt(p, L, mass_out, ws, s, o);
+  st = (path >= 1) ? launch_tc(p, L, mass_out, ws, s, o) : launch_simt(p, L, mass_out, ws, s, o);
   if (st != KVBM_OK) return st;
   if (!mark(2)) return KVBM_ERR_CUDA;
   st = launch_reduce(p, L, mass_out, ws, s);
@@ -165,8 +172,12 @@ size_t kvbm_workspace_bytes(const kvbm_problem* p) {
   // Size for the larger of the two layouts when the device is unknown, so a
   // workspace sized on the host is valid for whichever path runs.
   if (dev < 0) {
-    const WsLayout a = layout_for(p, 0), b = layout_for(p, 1);
-    return a.total > b.total ? a.total : b.total;
+    size_t m = 0;
+    for (int path_i = 0; path_i <= 2; ++path_i) {
+      const size_t t = layout_for(p, path_i).total;
+      m = t > m ? t : m;
+    }
+    return m;
   }
   return layout_for(p, path).total;
 }
@@ -184,7 +195,14 @@ int kvbm_kernel_path(const kvbm_problem* p) {
 
 int kvbm_launches_per_call(const kvbm_problem* p) {
   if (validate(p) != KVBM_OK) return 0;
-  return 3;  // pass 1 (lse2) or the lse import, pass 2 (per-key partials), bucket reduce
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    dev = -1;
+  }
+  // pass 1 (lse2) or the lse import, pass 2 (per-key partials), bucket reduce,
+  // and for 3xTF32 the split of q/k into tf32 pairs
+  return 3 + (select_path(p, dev) == 2 ? 1 : 0);
 }
 
 int kvbm_block_mass(const kvbm_problem* p, void* mass_out, void* workspace,

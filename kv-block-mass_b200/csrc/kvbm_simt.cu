@@ -395,12 +395,12 @@ __global__ void lse_import_kernel(const float* lse, long long s0, long long s1, 
 int launch_lse_import(const kvbm_problem* p, const WsLayout& L, const float* lse, const int64_t* st, void* ws,
                       cudaStream_t s) {
   const int U = p->unit_end - p->unit_begin, G = p->Hq / p->Hkv;
-  const int Nrow = L.path == 1 ? (p->N + kTcTile - 1) / kTcTile * kTcTile : p->N;
+  const int Nrow = L.path >= 1 ? (p->N + kTcTile - 1) / kTcTile * kTcTile : p->N;
   const long long rows = (long long)U * G * Nrow;
   const int threads = 256;
   const long long blocks = (rows + threads - 1) / threads;
   char* base = static_cast<char*>(ws) + L.lse_off;
-  if (L.path == 1) {
+  if (L.path >= 1) {
     lse_import_kernel<float, true><<<(unsigned)blocks, threads, 0, s>>>(
         lse, st[0], st[1], st[2], reinterpret_cast<float*>(base), p->N, Nrow, G, p->Hkv, p->unit_begin, rows,
         p->query_mask, p->query_mask_bstride);

@@ -130,6 +130,17 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64
       : "memory");
 }
 
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::tf32 (fp32 storage read as tf32, fp32 accumulate).
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive (once) on `bar` when all tcgen05.mma previously issued by this thread complete.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -169,14 +180,21 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
          | ((uint64_t)2 << 61);                 // swizzle mode: 128-byte
 }
 
-// Instruction descriptor, kind::f16: fp32 accumulate, A/B both bf16 (or both
-// fp16), both K-major, shape M x N.
-__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16) {
+// Instruction descriptor, kind::f16 / kind::tf32: fp32 accumulate, A and B of
+// the same input format (0 = fp16, 1 = bf16, 2 = tf32), both K-major, shape M x N.
+__host__ __device__ constexpr uint32_t idesc_mma(int M, int N, uint32_t fmt) {
   return (1u << 4)                               // D format: f32
-         | ((bf16 ? 1u : 0u) << 7)               // A format
-         | ((bf16 ? 1u : 0u) << 10)              // B format
+         | (fmt << 7)                            // A format
+         | (fmt << 10)                           // B format
          | ((uint32_t)(N >> 3) << 17)            // N / 8
          | ((uint32_t)(M >> 4) << 24);           // M / 16
+}
+
+// Round fp32 to the nearest tf32 (10 explicit mantissa bits, low 13 bits zero).
+__device__ __forceinline__ float to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
 }
 
 __device__ __forceinline__ float ex2(float x) {

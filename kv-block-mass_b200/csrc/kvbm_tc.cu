@@ -72,12 +72,24 @@ __host__ __device__ inline int keys_in_chunk(const TcArgs& a, int y) {
   return lim < ntiles ? lim : ntiles;
 }
 
-template <int D>
+// Operand type of the MMAs.  TF32X3 carries an fp32 operand as a tf32 pair
+// hi + lo (hi = tf32(x), lo = x - hi, both stored as fp32) and multiplies
+// A.B ~= A_hi.B_lo + A_lo.B_hi + A_hi.B_hi, about 2^-22 relative error (the
+// A_lo.B_lo term is below that), i.e. fp32-grade scores from tf32 MMAs.
+enum class Op { F16, BF16, TF32X3 };
+
+template <int D, Op kOp>
 struct Cfg {
-  static constexpr int kBlocks = D / 64;          // 128-byte K-blocks per row
-  static constexpr int kBlockBytes = TILE * 128;  // 16 KB
-  static constexpr int kTileBytes = TILE * D * 2;
-  static constexpr int kSteps = D / 16;           // K=16 MMAs per tile
+  static constexpr int kElem = kOp == Op::TF32X3 ? 4 : 2;    // bytes per element in smem
+  static constexpr int kBlockElems = 128 / kElem;            // elements per 128-byte row block
+  static constexpr int kBlocks = D * kElem / 128;            // 128-byte K-blocks per row
+  static constexpr int kBlockBytes = TILE * 128;             // 16 KB
+  static constexpr int kTileBytes = TILE * D * kElem;        // one component tile
+  static constexpr int kParts = kOp == Op::TF32X3 ? 2 : 1;   // tiles per operand (hi, lo)
+  static constexpr int kOperandBytes = kTileBytes * kParts;  // one ring slot
+  static constexpr int kSteps = kBlocks * 4;                 // 32-byte (K=16 f16 / K=8 tf32) MMA steps
+  static constexpr uint32_t kFmt = kOp == Op::F16 ? 0u : kOp == Op::BF16 ? 1u : 2u;
+  static_assert(kBlocks >= 1 && D * kElem % 128 == 0, "row must be whole 128-byte blocks");
 };
 
 __device__ __forceinline__ uint8_t* align1k(uint8_t* p) {
@@ -90,14 +102,37 @@ __device__ __forceinline__ void exp_bar_sync() {
 }
 
 // Issue the MMAs of one 128 x 128 tile: D[tmem] = A[128 x D] * B[128 x D]^T.
-template <int D>
+template <int D, Op kOp>
 __device__ __forceinline__ void issue_tile_mma(uint32_t d_tmem, uint32_t a_smem, uint32_t b_smem,
                                                uint32_t idesc) {
+  using C = Cfg<D, kOp>;
 #pragma unroll
-  for (int kk = 0; kk < Cfg<D>::kSteps; ++kk) {
-    const uint32_t koff = (kk >> 2) * Cfg<D>::kBlockBytes + (kk & 3) * 32;
-    mma_f16(d_tmem, sw128_desc(a_smem + koff), sw128_desc(b_smem + koff), idesc, kk > 0 ? 1u : 0u);
+  for (int kk = 0; kk < C::kSteps; ++kk) {
+    const uint32_t koff = (kk >> 2) * C::kBlockBytes + (kk & 3) * 32;
+    if constexpr (kOp == Op::TF32X3) {
+      // the small cross terms first, then hi.hi
+      mma_tf32(d_tmem, sw128_desc(a_smem + C::kTileBytes + koff), sw128_desc(b_smem + koff), idesc,
+               kk > 0 ? 1u : 0u);
+      mma_tf32(d_tmem, sw128_desc(a_smem + koff), sw128_desc(b_smem + C::kTileBytes + koff), idesc, 1u);
+      mma_tf32(d_tmem, sw128_desc(a_smem + koff), sw128_desc(b_smem + koff), idesc, 1u);
+    } else {
+      mma_f16(d_tmem, sw128_desc(a_smem + koff), sw128_desc(b_smem + koff), idesc, kk > 0 ? 1u : 0u);
+    }
   }
+}
+
+// TMA-load one operand (all its component tiles) of rows [row, row + 128) of
+// head h of batch b into `dst`, completing on `bar`.
+template <int D, Op kOp>
+__device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* m0, const CUtensorMap* m1,
+                                             uint64_t* bar, int row, int h, int b) {
+  using C = Cfg<D, kOp>;
+#pragma unroll
+  for (int part = 0; part < C::kParts; ++part)
+#pragma unroll
+    for (int kb = 0; kb < C::kBlocks; ++kb)
+      tma_load_4d(dst + part * C::kTileBytes + kb * C::kBlockBytes, part == 0 ? m0 : m1, bar,
+                  kb * C::kBlockElems, row, h, b);
 }
 
 __device__ __forceinline__ void load_half(uint32_t taddr, float (&v)[HALF]) {
@@ -199,12 +234,13 @@ __device__ __forceinline__ void merge_ml(float& m, float& l, float mo, float lo)
 // ============================================================ pass 1: lse2
 // grid (U_sel * G, ceil(N / 128)); blockIdx.y counts query tiles from the
 // last (longest under causal_skip) to the first.
-template <int D, bool kBF16, bool kKeyMask>
+template <int D, Op kOp, bool kKeyMask>
 __global__ void __launch_bounds__(kThreads, 2)
-    tc_lse_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk, TcArgs a) {
+    tc_lse_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tq2,
+                  const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tk2, TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1k(smem_raw);
-  constexpr int TB = Cfg<D>::kTileBytes;
+  constexpr int TB = Cfg<D, kOp>::kOperandBytes;
   uint8_t* q_tile = smem;
   uint8_t* k_ring = smem + TB;
   float2* merge = reinterpret_cast<float2*>(smem + TB * (1 + kStages));  // [128] (m, l) of the upper halves
@@ -253,18 +289,13 @@ __global__ void __launch_bounds__(kThreads, 2)
       prefetch_tmap(&tq);
       prefetch_tmap(&tk);
       mbar_arrive_expect_tx(q_full, TB);
-#pragma unroll
-      for (int kb = 0; kb < Cfg<D>::kBlocks; ++kb)
-        tma_load_4d(q_tile + kb * Cfg<D>::kBlockBytes, &tq, q_full, kb * 64, r0, h, b);
+      load_operand<D, kOp>(q_tile, &tq, &tq2, q_full, r0, h, b);
       int issued = 0;
       for (int j = 0; j < nkt; ++j) {
         const int s = j % kStages, n = j / kStages;
         if (n > 0 && !mbar_wait(&k_empty[s], (n - 1) & 1, abort_flag)) break;
-        uint8_t* dst = k_ring + s * TB;
         mbar_arrive_expect_tx(&k_full[s], TB);
-#pragma unroll
-        for (int kb = 0; kb < Cfg<D>::kBlocks; ++kb)
-          tma_load_4d(dst + kb * Cfg<D>::kBlockBytes, &tk, &k_full[s], kb * 64, j * TILE, g, b);
+        load_operand<D, kOp>(k_ring + s * TB, &tk, &tk2, &k_full[s], j * TILE, g, b);
         issued = j + 1;
       }
       // Do not leave while our copies are in flight.
@@ -274,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(TILE, TILE, kBF16);
+      const uint32_t idesc = idesc_mma(TILE, TILE, Cfg<D, kOp>::kFmt);
       const uint32_t qs = smem_u32(q_tile), ks = smem_u32(k_ring);
       int issued = 0;
       if (mbar_wait(q_full, 0, abort_flag)) {
@@ -283,7 +314,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           if (!mbar_wait(&k_full[s], (j / kStages) & 1, abort_flag)) break;
           if (j >= 2 && !mbar_wait(&s_empty[buf], ((j >> 1) - 1) & 1, abort_flag)) break;
           tc_fence_after();
-          issue_tile_mma<D>(tmem + buf * TILE, qs, ks + s * TB, idesc);
+          issue_tile_mma<D, kOp>(tmem + buf * TILE, qs, ks + s * TB, idesc);
           mma_commit(&k_empty[s]);
           mma_commit(&s_full[buf]);
           issued = j + 1;
@@ -369,12 +400,13 @@ __global__ void __launch_bounds__(kThreads, 2)
 // the last (most key tiles under causal_skip) to the first, and all key tiles
 // of a chunk are adjacent, so the CTAs resident at one time share that
 // chunk's query tiles in L2.
-template <int D, bool kBF16, bool kKeyMask>
+template <int D, Op kOp, bool kKeyMask>
 __global__ void __launch_bounds__(kThreads, 2)
-    tc_mass_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk, TcArgs a) {
+    tc_mass_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tq2,
+                   const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tk2, TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1k(smem_raw);
-  constexpr int TB = Cfg<D>::kTileBytes;
+  constexpr int TB = Cfg<D, kOp>::kOperandBytes;
   constexpr int LB = TILE * 4;  // lse2 bytes of one query tile
   uint8_t* k_tile = smem;
   uint8_t* q_ring = smem + TB;
@@ -442,9 +474,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       prefetch_tmap(&tq);
       prefetch_tmap(&tk);
       mbar_arrive_expect_tx(k_full, TB);
-#pragma unroll
-      for (int kb = 0; kb < Cfg<D>::kBlocks; ++kb)
-        tma_load_4d(k_tile + kb * Cfg<D>::kBlockBytes, &tk, k_full, kb * 64, c0, g, b);
+      load_operand<D, kOp>(k_tile, &tk, &tk2, k_full, c0, g, b);
       int issued = 0;
       for (int j = 0; j < J; ++j) {
         const int s = j % kStages, n = j / kStages;
@@ -455,9 +485,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int r = rs + (j - hh * nqt) * TILE;
         const int h = g * a.G + hh;
         mbar_arrive_expect_tx(&q_full[s], TB);
-#pragma unroll
-        for (int kb = 0; kb < Cfg<D>::kBlocks; ++kb)
-          tma_load_4d(q_ring + s * TB + kb * Cfg<D>::kBlockBytes, &tq, &q_full[s], kb * 64, r, h, b);
+        load_operand<D, kOp>(q_ring + s * TB, &tq, &tq2, &q_full[s], r, h, b);
         mbar_arrive_expect_tx(&l_full[t], LB);
         bulk_load(l_ring + t * TILE, a.lse + (long long)(uu * a.G + hh) * a.Npad + r, LB, &l_full[t]);
         issued = j + 1;
@@ -471,7 +499,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(TILE, TILE, kBF16);
+      const uint32_t idesc = idesc_mma(TILE, TILE, Cfg<D, kOp>::kFmt);
       const uint32_t ks = smem_u32(k_tile), qs = smem_u32(q_ring);
       int issued = 0;
       if (mbar_wait(k_full, 0, abort_flag)) {
@@ -480,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           if (!mbar_wait(&q_full[s], (j / kStages) & 1, abort_flag)) break;
           if (j >= 2 && !mbar_wait(&s_empty[buf], ((j >> 1) - 1) & 1, abort_flag)) break;
           tc_fence_after();
-          issue_tile_mma<D>(tmem + buf * TILE, ks, qs + s * TB, idesc);
+          issue_tile_mma<D, kOp>(tmem + buf * TILE, ks, qs + s * TB, idesc);
           mma_commit(&q_empty[s]);
           mma_commit(&s_full[buf]);
           issued = j + 1;
@@ -559,46 +587,91 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 4-D map over a [B, H, N, D] operand with unit-stride D: box 64 x 128 x 1 x 1,
-// 128-byte swizzle, zero fill outside [N) so ragged tiles read zeros.
-bool make_map(CUtensorMap* map, const void* base, bool bf16, int B, int H, int N, int D,
-              const int64_t* st) {
+// 4-D map over a [B, H, N, D] operand with unit-stride D: box (128 bytes of
+// D) x 128 rows x 1 x 1, 128-byte swizzle, zero fill outside [N) so ragged
+// tiles read zeros.
+bool make_map(CUtensorMap* map, const void* base, CUtensorMapDataType type, int esize, int B, int H, int N,
+              int D, const int64_t* st) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return false;
   const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)N, (cuuint64_t)H, (cuuint64_t)B};
   // Size-1 dims get a harmless nonzero stride (TMA wants multiples of 16 bytes).
-  const uint64_t row = (uint64_t)st[2] * 2;
-  uint64_t hs = (uint64_t)st[1] * 2, bs = (uint64_t)st[0] * 2;
+  const uint64_t row = (uint64_t)st[2] * esize;
+  uint64_t hs = (uint64_t)st[1] * esize, bs = (uint64_t)st[0] * esize;
   if (H == 1) hs = row * (uint64_t)N;
   if (B == 1) bs = hs * (uint64_t)H;
   const cuuint64_t strides[3] = {row, hs, bs};
-  const cuuint32_t box[4] = {64, (cuuint32_t)TILE, 1, 1};
+  const cuuint32_t box[4] = {(cuuint32_t)(128 / esize), (cuuint32_t)TILE, 1, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
-  const CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
-                        const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUresult r = fn(map, type, 4, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+// fp32 operand -> contiguous [B, H, N, D] tf32 pair: hi = tf32(x), lo = x - hi
+// (exact in fp32).  One launch splits q (first q_elems elements) and k.
+__global__ void split_tf32_kernel(const float* q, long long q0, long long q1, long long q2, long long q3,
+                                  int Hq, const float* k, long long k0, long long k1, long long k2,
+                                  long long k3, int Hkv, int N, int D, long long q_elems, long long k_elems,
+                                  float* q_hi, float* q_lo, float* k_hi, float* k_lo) {
+  const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (idx >= q_elems + k_elems) return;
+  const bool is_q = idx < q_elems;
+  const long long e = is_q ? idx : idx - q_elems;
+  const int d = (int)(e % D);
+  const long long r = e / D;
+  const int n = (int)(r % N);
+  const long long bh = r / N;
+  const int H = is_q ? Hq : Hkv;
+  const int h = (int)(bh % H), b = (int)(bh / H);
+  const float x = is_q ? q[b * q0 + h * q1 + n * q2 + d * q3] : k[b * k0 + h * k1 + n * k2 + d * k3];
+  const float hi = to_tf32(x);
+  (is_q ? q_hi : k_hi)[e] = hi;
+  (is_q ? q_lo : k_lo)[e] = x - hi;
 }
 
 constexpr size_t kBarBytes = 8 * (1 + 2 * kStages + 4) + 16;  // mbarriers + TMEM slot + abort flag
 
-template <int D>
+template <int D, Op kOp>
 constexpr size_t smem_lse() {
-  return 1024 + (size_t)Cfg<D>::kTileBytes * (1 + kStages) + TILE * 8 + kBarBytes;
+  return 1024 + (size_t)Cfg<D, kOp>::kOperandBytes * (1 + kStages) + TILE * 8 + kBarBytes;
 }
-template <int D>
+template <int D, Op kOp>
 constexpr size_t smem_mass() {
-  return 1024 + (size_t)Cfg<D>::kTileBytes * (1 + kStages) + TILE * 4 * kLStages + TILE * 8 + kBarBytes +
+  return 1024 + (size_t)Cfg<D, kOp>::kOperandBytes * (1 + kStages) + TILE * 4 * kLStages + TILE * 8 + kBarBytes +
          16 * kLStages;
 }
 
-template <int D, bool kBF16, bool kKeyMask>
+template <int D, Op kOp, bool kKeyMask>
 int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s, const LaunchOpts& o) {
-  CUtensorMap tq, tk;
-  if (!make_map(&tq, p->q, kBF16, p->B, p->Hq, p->N, D, p->q_stride) ||
-      !make_map(&tk, p->k, kBF16, p->B, p->Hkv, p->N, D, p->k_stride))
-    return KVBM_ERR_CUDA;
+  CUtensorMap tq, tq2, tk, tk2;
+  if constexpr (kOp == Op::TF32X3) {
+    // split q/k into tf32 hi/lo pairs in the workspace, then map those
+    float* base = reinterpret_cast<float*>(static_cast<char*>(ws) + L.split_off);
+    const long long qe = (long long)p->B * p->Hq * p->N * D, ke = (long long)p->B * p->Hkv * p->N * D;
+    float *q_hi = base, *q_lo = base + qe, *k_hi = base + 2 * qe, *k_lo = base + 2 * qe + ke;
+    const long long total = qe + ke;
+    split_tf32_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(
+        static_cast<const float*>(p->q), p->q_stride[0], p->q_stride[1], p->q_stride[2], p->q_stride[3], p->Hq,
+        static_cast<const float*>(p->k), p->k_stride[0], p->k_stride[1], p->k_stride[2], p->k_stride[3], p->Hkv,
+        p->N, D, qe, ke, q_hi, q_lo, k_hi, k_lo);
+    if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
+    const int64_t qs[4] = {(int64_t)p->Hq * p->N * D, (int64_t)p->N * D, D, 1};
+    const int64_t ks[4] = {(int64_t)p->Hkv * p->N * D, (int64_t)p->N * D, D, 1};
+    const CUtensorMapDataType t = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    if (!make_map(&tq, q_hi, t, 4, p->B, p->Hq, p->N, D, qs) || !make_map(&tq2, q_lo, t, 4, p->B, p->Hq, p->N, D, qs) ||
+        !make_map(&tk, k_hi, t, 4, p->B, p->Hkv, p->N, D, ks) || !make_map(&tk2, k_lo, t, 4, p->B, p->Hkv, p->N, D, ks))
+      return KVBM_ERR_CUDA;
+  } else {
+    const CUtensorMapDataType t =
+        kOp == Op::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    if (!make_map(&tq, p->q, t, 2, p->B, p->Hq, p->N, D, p->q_stride) ||
+        !make_map(&tk, p->k, t, 2, p->B, p->Hkv, p->N, D, p->k_stride))
+      return KVBM_ERR_CUDA;
+    tq2 = tq;
+    tk2 = tk;
+  }
   TcArgs a;
   a.N = p->N;
   a.Npad = (p->N + TILE - 1) / TILE * TILE;
@@ -621,31 +694,28 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
   const int U = p->unit_end - p->unit_begin;
   const int ntiles = a.Npad / TILE;
 
-  const size_t sm1 = smem_lse<D>() > (size_t)kMinSmem ? smem_lse<D>() : (size_t)kMinSmem;
-  const size_t sm2 = smem_mass<D>() > (size_t)kMinSmem ? smem_mass<D>() : (size_t)kMinSmem;
-  auto k1 = tc_lse_kernel<D, kBF16, kKeyMask>;
-  auto k2 = tc_mass_kernel<D, kBF16, kKeyMask>;
+  const size_t sm1 = smem_lse<D, kOp>() > (size_t)kMinSmem ? smem_lse<D, kOp>() : (size_t)kMinSmem;
+  const size_t sm2 = smem_mass<D, kOp>() > (size_t)kMinSmem ? smem_mass<D, kOp>() : (size_t)kMinSmem;
+  auto k1 = tc_lse_kernel<D, kOp, kKeyMask>;
+  auto k2 = tc_mass_kernel<D, kOp, kKeyMask>;
   if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1) != cudaSuccess ||
       cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2) != cudaSuccess)
     return KVBM_ERR_CUDA;
   if (o.run_pass1) {
-    k1<<<dim3(U * a.G, ntiles), kThreads, sm1, s>>>(tq, tk, a);
+    k1<<<dim3(U * a.G, ntiles), kThreads, sm1, s>>>(tq, tq2, tk, tk2, a);
     if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
   }
   if (o.mid_event != nullptr && cudaEventRecord(static_cast<cudaEvent_t>(o.mid_event), s) != cudaSuccess)
     return KVBM_ERR_CUDA;
-  k2<<<dim3(U * a.per_unit), kThreads, sm2, s>>>(tq, tk, a);
+  k2<<<dim3(U * a.per_unit), kThreads, sm2, s>>>(tq, tq2, tk, tk2, a);
   if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
   return KVBM_OK;
 }
 
-template <int D>
-int launch_d(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s, const LaunchOpts& ev) {
-  const bool bf16 = p->dtype == KVBM_BF16;
-  const bool km = p->key_mask != nullptr;
-  if (bf16)
-    return km ? launch_variant<D, true, true>(p, L, ws, s, ev) : launch_variant<D, true, false>(p, L, ws, s, ev);
-  return km ? launch_variant<D, false, true>(p, L, ws, s, ev) : launch_variant<D, false, false>(p, L, ws, s, ev);
+template <int D, Op kOp>
+int launch_km(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s, const LaunchOpts& o) {
+  return p->key_mask != nullptr ? launch_variant<D, kOp, true>(p, L, ws, s, o)
+                                : launch_variant<D, kOp, false>(p, L, ws, s, o);
 }
 
 }  // namespace
@@ -655,8 +725,14 @@ bool tc_path_enabled() { return encode_fn() != nullptr; }
 int launch_tc(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws, cudaStream_t s,
               const LaunchOpts& o) {
   (void)mass_out;
-  if (p->D == 64) return launch_d<64>(p, L, ws, s, o);
-  if (p->D == 128) return launch_d<128>(p, L, ws, s, o);
+  if (L.path == 2) {  // fp32 inputs on tf32 tensor cores (3 MMAs per step)
+    if (p->D == 32) return launch_km<32, Op::TF32X3>(p, L, ws, s, o);
+    if (p->D == 64) return launch_km<64, Op::TF32X3>(p, L, ws, s, o);
+    return KVBM_ERR_HEAD_DIM;
+  }
+  const bool bf16 = p->dtype == KVBM_BF16;
+  if (p->D == 64) return bf16 ? launch_km<64, Op::BF16>(p, L, ws, s, o) : launch_km<64, Op::F16>(p, L, ws, s, o);
+  if (p->D == 128) return bf16 ? launch_km<128, Op::BF16>(p, L, ws, s, o) : launch_km<128, Op::F16>(p, L, ws, s, o);
   return KVBM_ERR_HEAD_DIM;
 }
 
