@@ -134,6 +134,8 @@ KVBM_API size_t kvbm_workspace_bytes(const kvbm_problem* p);
  * 1 = tcgen05 tensor cores with TMA and TMEM (bf16/fp16, D in {64, 128}),
  * 2 = tcgen05 3xTF32 for fp32 inputs (D in {32, 64}): tf32 hi/lo split,
  *     three MMAs per step, fp32-grade scores,
+ * (paths 1 and 2 take pair masks as packed bits: 2 * Npad^2 / 8 bytes of
+ * workspace per mask batch entry, Npad = N rounded up to 128),
  * negative = a kvbm_status error code, negated. */
 KVBM_API int kvbm_kernel_path(const kvbm_problem* p);
 

@@ -59,11 +59,11 @@ int validate(const kvbm_problem* p) {
 // Path 1 (tcgen05, bf16/fp16) needs D in {64, 128}, a unit-stride head dim,
 // 16-byte aligned base pointers and row/head/batch strides (TMA rules).
 // Path 2 (tcgen05 3xTF32 for fp32 inputs) needs D in {32, 64}; it reads q/k
-// with a split kernel, so any strides work.  Both need a positive scale and
-// no pair mask; everything else runs the SIMT kernels.
+// with a split kernel, so any strides work.  Both need a positive scale;
+// pair masks are packed to bits for them.  Everything else runs the SIMT
+// kernels.
 int select_path(const kvbm_problem* p, int device) {
   if (device >= 0 && device_kind(device) != 1) return 0;
-  if (p->pair_mask != nullptr) return 0;
   if (!(p->scale > 0.0)) return 0;  // the exp/sum warps assume a positive scale
   if (!tc_path_enabled()) return 0;
   if (p->dtype == KVBM_F32) return (p->D == 32 || p->D == 64) ? 2 : 0;
@@ -97,7 +97,15 @@ WsLayout layout_for(const kvbm_problem* p, int path) {
   L.part_bytes = U * (size_t)L.nchunk * (size_t)p->N * L.acc_bytes;
   L.split_off = align_up(L.part_off + L.part_bytes, 256);
   L.split_bytes = path == 2 ? (size_t)2 * 4 * p->N * p->D * ((size_t)p->B * p->Hq + (size_t)p->B * p->Hkv) : 0;
-  L.total = align_up(L.split_off + L.split_bytes, 256);
+  L.bits_off = align_up(L.split_off + L.split_bytes, 256);
+  if (tc && p->pair_mask != nullptr) {
+    const bool per_b = p->pair_mask_bstride != 0 || (p->key_mask && p->key_mask_bstride != 0) ||
+                       (p->query_mask && p->query_mask_bstride != 0);
+    L.bits_batches = per_b ? p->B : 1;
+    const size_t npad = n_lse;  // whole 128-row tiles
+    L.bits_bytes = (size_t)2 * L.bits_batches * npad * (npad / 32) * 4;  // row bits + column bits
+  }
+  L.total = align_up(L.bits_off + L.bits_bytes, 256);
   return L;
 }
 
@@ -201,8 +209,9 @@ int kvbm_launches_per_call(const kvbm_problem* p) {
     dev = -1;
   }
   // pass 1 (lse2) or the lse import, pass 2 (per-key partials), bucket reduce,
-  // and for 3xTF32 the split of q/k into tf32 pairs
-  return 3 + (select_path(p, dev) == 2 ? 1 : 0);
+  // for 3xTF32 the split of q/k into tf32 pairs, for a pair mask its packing
+  const int path = select_path(p, dev);
+  return 3 + (path == 2 ? 1 : 0) + (path >= 1 && p->pair_mask != nullptr ? 1 : 0);
 }
 
 int kvbm_block_mass(const kvbm_problem* p, void* mass_out, void* workspace,

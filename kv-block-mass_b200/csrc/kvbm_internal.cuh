@@ -30,6 +30,8 @@ struct WsLayout {
   size_t lse_off = 0, lse_bytes = 0;     // [U_sel * G * N] lse2 (Acc)
   size_t part_off = 0, part_bytes = 0;   // [U_sel * nchunk * N] per-key partials (Acc)
   size_t split_off = 0, split_bytes = 0; // path 2: tf32 hi/lo copies of q and k (fp32)
+  size_t bits_off = 0, bits_bytes = 0;   // tensor-core paths with a pair mask: packed bits
+  int bits_batches = 0;                  // batch entries of the packed bits (1 or B)
   size_t total = 0;
   int path = 0;        // 0 SIMT, 1 tcgen05 (bf16/fp16), 2 tcgen05 3xTF32 (fp32)
   int qchunk = 0;      // query rows per mass-pass CTA

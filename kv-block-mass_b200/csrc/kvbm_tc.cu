@@ -59,6 +59,10 @@ struct TcArgs {
   long long qmb;
   float* lse;              // [U_sel * G, Npad], stored negated (-lse2)
   float* part;             // [U_sel, nchunk, N]
+  const uint32_t* prow;    // pair mask bits, [Bm, Npad, W]: row = query, bit = key (or null)
+  const uint32_t* pcol;    // the same bits transposed: row = key, bit = query
+  long long pb;            // batch stride of prow/pcol in words (0: shared by all batch entries)
+  int W;                   // words per bit row (Npad / 32)
   int qchunk, nchunk;
   int per_unit;            // pass-2 CTAs per unit (sum of keys_in_chunk over chunks)
 };
@@ -71,6 +75,11 @@ __host__ __device__ inline int keys_in_chunk(const TcArgs& a, int y) {
   const int lim = (y + 1) * (a.qchunk / TILE);
   return lim < ntiles ? lim : ntiles;
 }
+
+// Mask handled inside the tensor-core kernels (causality is always index math).
+constexpr int kMaskNone = 0;   // no mask
+constexpr int kMaskKeys = 1;   // [B|1, N] key mask
+constexpr int kMaskPairs = 2;  // [B|1, N, N] pair mask, packed to bits (key/query masks folded in)
 
 // Operand type of the MMAs.  TF32X3 carries an fp32 operand as a tf32 pair
 // hi + lo (hi = tf32(x), lo = x - hi, both stored as fp32) and multiplies
@@ -179,10 +188,11 @@ __device__ __forceinline__ float row_sum_exp2(const float (&v)[HALF], float C, f
 }
 
 // acc += 2^(v[c]*C + nL[c]) over the half row, per-column nL = -lse2 (query
-// columns); with kDiag, columns c < keep_from are masked to 0.
-template <bool kDiag>
+// columns); with kDiag, columns c < keep_from are masked to 0; with kBits,
+// columns whose bit in `bits` (bit c of word c / 32) is clear are masked to 0.
+template <bool kDiag, bool kBits = false>
 __device__ __forceinline__ float2 col_sum_exp2(const float (&v)[HALF], float C, const float* nL, int keep_from,
-                                               float2 acc) {
+                                               float2 acc, uint2 bits = make_uint2(0xffffffffu, 0xffffffffu)) {
   const float2 C2 = make_float2(C, C);
   float2 a1 = make_float2(0.f, 0.f);
 #pragma unroll
@@ -195,6 +205,13 @@ __device__ __forceinline__ float2 col_sum_exp2(const float (&v)[HALF], float C, 
       v0.y = (c + 1 >= keep_from) ? v0.y : -INFINITY;
       v1.x = (c + 2 >= keep_from) ? v1.x : -INFINITY;
       v1.y = (c + 3 >= keep_from) ? v1.y : -INFINITY;
+    }
+    if (kBits) {
+      const uint32_t w = c < 32 ? bits.x : bits.y;
+      v0.x = ((w >> ((c + 0) & 31)) & 1u) ? v0.x : -INFINITY;
+      v0.y = ((w >> ((c + 1) & 31)) & 1u) ? v0.y : -INFINITY;
+      v1.x = ((w >> ((c + 2) & 31)) & 1u) ? v1.x : -INFINITY;
+      v1.y = ((w >> ((c + 3) & 31)) & 1u) ? v1.y : -INFINITY;
     }
     const float2 x0 = ffma2(v0, C2, make_float2(l4.x, l4.y));
     const float2 x1 = ffma2(v1, C2, make_float2(l4.z, l4.w));
@@ -234,7 +251,7 @@ __device__ __forceinline__ void merge_ml(float& m, float& l, float mo, float lo)
 // ============================================================ pass 1: lse2
 // grid (U_sel * G, ceil(N / 128)); blockIdx.y counts query tiles from the
 // last (longest under causal_skip) to the first.
-template <int D, Op kOp, bool kKeyMask>
+template <int D, Op kOp, int kMask>
 __global__ void __launch_bounds__(kThreads, 2)
     tc_lse_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tq2,
                   const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tk2, TcArgs a) {
@@ -329,10 +346,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int rl = sub * 32 + lane;
     const int row = r0 + rl;
     const uint32_t trow = tmem + ((uint32_t)(sub * 32) << 16) + hf * HALF;
-    const uint8_t* kmask = kKeyMask ? a.kmask + b * a.kmb : nullptr;
+    const uint8_t* kmask = kMask == kMaskKeys ? a.kmask + b * a.kmb : nullptr;
+    const uint32_t* prow = kMask == kMaskPairs ? a.prow + b * a.pb + (long long)row * a.W : nullptr;
     float m = -INFINITY, l = 0.f;
     for (int j = 0; j < nkt; ++j) {
       const int buf = j & 1;
+      uint2 pw = make_uint2(0xffffffffu, 0xffffffffu);
+      if (kMask == kMaskPairs)  // issued before the wait so the load overlaps it
+        pw = *reinterpret_cast<const uint2*>(prow + ((j * TILE + hf * HALF) >> 5));
       const bool ok = mbar_wait(&s_full[buf], (j >> 1) & 1, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
@@ -342,15 +363,15 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_arrive(&s_empty[buf]);
 
       const int c0 = j * TILE + hf * HALF;  // first key of this thread's half
-      uint32_t kw[2] = {0xffffffffu, 0xffffffffu};
-      if (kKeyMask) {
+      uint32_t kw[2] = {pw.x, pw.y};
+      if (kMask == kMaskKeys) {
 #pragma unroll
         for (int qd = 0; qd < 2; ++qd) {
           const int col = c0 + qd * 32 + lane;
           kw[qd] = __ballot_sync(0xffffffffu, col < a.N && kmask[col] != 0);
         }
       }
-      const bool need_mask = kKeyMask || (c0 + HALF > a.N) || (a.causal && c0 + HALF - 1 > r0);
+      const bool need_mask = kMask != kMaskNone || (c0 + HALF > a.N) || (a.causal && c0 + HALF - 1 > r0);
       if (need_mask) {
         const int lim_causal = a.causal ? row - c0 : HALF - 1;  // keep col_local <= row - c0
         const int lim = min(lim_causal, a.N - 1 - c0);          // and col < N
@@ -400,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 // the last (most key tiles under causal_skip) to the first, and all key tiles
 // of a chunk are adjacent, so the CTAs resident at one time share that
 // chunk's query tiles in L2.
-template <int D, Op kOp, bool kKeyMask>
+template <int D, Op kOp, int kMask>
 __global__ void __launch_bounds__(kThreads, 2)
     tc_mass_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tq2,
                    const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tk2, TcArgs a) {
@@ -524,9 +545,16 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int key = c0 + rl;
     const uint32_t trow = tmem + ((uint32_t)(sub * 32) << 16) + hf * HALF;
     const float C = a.C;
+    const uint32_t* pcol = kMask == kMaskPairs ? a.pcol + b * a.pb + (long long)key * a.W : nullptr;
     float2 acc = make_float2(0.f, 0.f);
     for (int j = 0; j < J; ++j) {
       const int buf = j & 1, t = j % kLStages;
+      uint2 pw = make_uint2(0xffffffffu, 0xffffffffu);
+      if (kMask == kMaskPairs) {  // issued before the waits so the load overlaps them
+        const int hq = j / nqt;
+        const int rq = rs + (j - hq * nqt) * TILE;
+        pw = *reinterpret_cast<const uint2*>(pcol + ((rq + hf * HALF) >> 5));
+      }
       bool ok = mbar_wait(&s_full[buf], (j >> 1) & 1, abort_flag);
       ok = ok && mbar_wait(&l_full[t], (j / kLStages) & 1, abort_flag);  // lse2 bytes landed
       if (!__all_sync(0xffffffffu, ok)) break;
@@ -539,11 +567,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int hh = j / nqt;
       const int r = rs + (j - hh * nqt) * TILE;
       const float* nL = l_ring + t * TILE + hf * HALF;  // -lse2 of this half's 64 query rows
+      constexpr bool kB = kMask == kMaskPairs;
       if (!a.causal || r > c0) {
-        acc = col_sum_exp2<false>(v, C, nL, 0, acc);  // every pair kept
+        acc = col_sum_exp2<false, kB>(v, C, nL, 0, acc, pw);  // every pair kept by causality
       } else if (r == c0) {
         // diagonal: query r + hf*64 + c keeps key c0 + rl iff hf*64 + c >= rl
-        acc = col_sum_exp2<true>(v, C, nL, rl - hf * HALF, acc);
+        acc = col_sum_exp2<true, kB>(v, C, nL, rl - hf * HALF, acc, pw);
       }
       // r < c0 (only without causal_skip): every pair is above the diagonal, adds 0.
       mbar_arrive(&l_empty[t]);
@@ -554,7 +583,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (hf == 0 && key < a.N) {
       const float2 o = merge[rl];
       float total = (acc.x + acc.y) + (o.x + o.y);
-      if (kKeyMask && a.kmask[b * a.kmb + key] == 0) total = 0.f;
+      if (kMask == kMaskKeys && a.kmask[b * a.kmb + key] == 0) total = 0.f;
       a.part[((long long)uu * a.nchunk + y) * a.N + key] = total;
     }
   }
@@ -631,6 +660,39 @@ __global__ void split_tf32_kernel(const float* q, long long q0, long long q1, lo
   (is_q ? q_lo : k_lo)[e] = x - hi;
 }
 
+// Pair mask (bytes, nonzero = keep) ANDed with the key and query masks ->
+// bit rows for pass 1 (row = query i, bit c of word c/32 = key c) and the
+// transposed bits for pass 2 (row = key c, bit i = query i), over [Npad]^2
+// with zero padding.  One warp packs one 32 x 32 block: 32 ballots give the
+// row words; the column words are their bit transpose, built in registers.
+__global__ void pack_pair_mask_kernel(const uint8_t* pm, long long pbs, long long prs, const uint8_t* km,
+                                      long long kbs, const uint8_t* qm, long long qbs, int N, int Npad,
+                                      long long nblk, uint32_t* prow, uint32_t* pcol) {
+  const long long wid = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= nblk) return;  // whole warps exit together
+  const int nb = Npad / 32;
+  const long long per_b = (long long)nb * nb;
+  const int bm = (int)(wid / per_b);
+  const long long rem = wid - bm * per_b;
+  const int ib = (int)(rem / nb), cb = (int)(rem % nb);
+  const int i0 = ib * 32, c = cb * 32 + lane;
+  const bool col_ok = c < N && (km == nullptr || km[bm * kbs + c] != 0);
+  uint32_t myrow = 0, mycol = 0;
+#pragma unroll 4
+  for (int r = 0; r < 32; ++r) {
+    const int i = i0 + r;
+    bool v = col_ok && i < N && pm[bm * pbs + (long long)i * prs + c] != 0;
+    if (qm != nullptr && i < N) v = v && qm[bm * qbs + i] != 0;
+    const uint32_t R = __ballot_sync(0xffffffffu, v);
+    if (lane == r) myrow = R;
+    mycol |= ((R >> lane) & 1u) << r;
+  }
+  const long long Wl = nb;
+  prow[((long long)bm * Npad + i0 + lane) * Wl + cb] = myrow;
+  pcol[((long long)bm * Npad + cb * 32 + lane) * Wl + ib] = mycol;
+}
+
 constexpr size_t kBarBytes = 8 * (1 + 2 * kStages + 4) + 16;  // mbarriers + TMEM slot + abort flag
 
 template <int D, Op kOp>
@@ -643,7 +705,7 @@ constexpr size_t smem_mass() {
          16 * kLStages;
 }
 
-template <int D, Op kOp, bool kKeyMask>
+template <int D, Op kOp, int kMask>
 int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s, const LaunchOpts& o) {
   CUtensorMap tq, tq2, tk, tk2;
   if constexpr (kOp == Op::TF32X3) {
@@ -691,13 +753,30 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
   a.nchunk = L.nchunk;
   a.per_unit = 0;
   for (int y = 0; y < a.nchunk; ++y) a.per_unit += keys_in_chunk(a, y);
+  a.prow = a.pcol = nullptr;
+  a.pb = 0;
+  a.W = a.Npad / 32;
+  if (kMask == kMaskPairs) {
+    uint32_t* bits = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + L.bits_off);
+    const long long words = (long long)L.bits_batches * a.Npad * a.W;
+    a.prow = bits;
+    a.pcol = bits + words;
+    a.pb = L.bits_batches > 1 ? (long long)a.Npad * a.W : 0;
+    const long long nblk = (long long)L.bits_batches * (a.Npad / 32) * (a.Npad / 32);
+    const bool per_b = L.bits_batches > 1;
+    pack_pair_mask_kernel<<<(unsigned)((nblk * 32 + 255) / 256), 256, 0, s>>>(
+        p->pair_mask, per_b ? p->pair_mask_bstride : 0, p->pair_mask_rstride, p->key_mask,
+        per_b ? p->key_mask_bstride : 0, p->query_mask, per_b ? p->query_mask_bstride : 0, p->N, a.Npad, nblk,
+        bits, bits + words);
+    if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
+  }
   const int U = p->unit_end - p->unit_begin;
   const int ntiles = a.Npad / TILE;
 
   const size_t sm1 = smem_lse<D, kOp>() > (size_t)kMinSmem ? smem_lse<D, kOp>() : (size_t)kMinSmem;
   const size_t sm2 = smem_mass<D, kOp>() > (size_t)kMinSmem ? smem_mass<D, kOp>() : (size_t)kMinSmem;
-  auto k1 = tc_lse_kernel<D, kOp, kKeyMask>;
-  auto k2 = tc_mass_kernel<D, kOp, kKeyMask>;
+  auto k1 = tc_lse_kernel<D, kOp, kMask>;
+  auto k2 = tc_mass_kernel<D, kOp, kMask>;
   if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1) != cudaSuccess ||
       cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2) != cudaSuccess)
     return KVBM_ERR_CUDA;
@@ -714,8 +793,9 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
 
 template <int D, Op kOp>
 int launch_km(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s, const LaunchOpts& o) {
-  return p->key_mask != nullptr ? launch_variant<D, kOp, true>(p, L, ws, s, o)
-                                : launch_variant<D, kOp, false>(p, L, ws, s, o);
+  if (p->pair_mask != nullptr) return launch_variant<D, kOp, kMaskPairs>(p, L, ws, s, o);
+  return p->key_mask != nullptr ? launch_variant<D, kOp, kMaskKeys>(p, L, ws, s, o)
+                                : launch_variant<D, kOp, kMaskNone>(p, L, ws, s, o);
 }
 
 }  // namespace
