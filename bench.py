@@ -16,6 +16,11 @@ Reported beside the device-timed value:
   e2e           the same metric through the public API (block_mass_b200 on
                 pinned host tensors, device="cuda"), H2D of q/k and D2H of the
                 mass inside the timed region;
+  lse_input     the device-resident step with the row LSE supplied (pass 2
+                and the reduce only);
+  paged         the device-resident step with k read from a paged cache
+                (16-key pages in shuffled order + block table): page gather,
+                both passes, reduce;
   roofline      the dominant kernel's algorithmic tensor FLOP/s against the
                 measured bf16 peak, and its exp rate against the MUFU ex2
                 rate measured live on this GPU (the binding unit);
@@ -401,6 +406,51 @@ def b200_arm(args, w):
                      "api": "kvbm_block_mass_lse (row LSE supplied, as an attention forward returns it)"}
         del lse_buf
 
+    # Paged key cache (16-key pages, shuffled page ids): page gather + both passes.
+    paged = None
+    if not args.no_e2e:
+        P = 16
+        B_, Hkv_, N_, D_ = k.shape
+        npg = -(-N_ // P)
+        gen = torch.Generator().manual_seed(7)
+        table = torch.randperm(B_ * npg, generator=gen).reshape(B_, npg).to(torch.int32).to(dev)
+        kp = torch.zeros(B_, Hkv_, npg * P, D_, dtype=k.dtype, device=dev)
+        kp[:, :, :N_] = k
+        cache = torch.empty(B_ * npg, P, Hkv_, D_, dtype=k.dtype, device=dev)
+        cache[table.flatten().long()] = kp.reshape(B_, Hkv_, npg, P, D_).permute(0, 2, 3, 1, 4).reshape(
+            B_ * npg, P, Hkv_, D_)
+        del kp
+        pp = ops.make_paged_problem(q, cache, table, attn_mask=kmd, query_mask=qmd, causal=w.causal,
+                                    block_size=w.block_size)
+        ws_p = torch.empty(ops.paged_workspace_bytes(pp), dtype=torch.uint8, device=dev)
+        out_p = torch.empty_like(out)
+
+        def paged_step():
+            code = lib.kvbm_block_mass_paged(ctypes.byref(pp.prep.prob), ctypes.byref(pp.kv), None, None,
+                                             out_p.data_ptr(), ws_p.data_ptr(), ws_p.numel(), stream.cuda_stream)
+            if code != 0:
+                raise RuntimeError(f"kvbm_block_mass_paged failed: {_lib.status_string(code)}")
+
+        for _ in range(2):
+            paged_step()
+        torch.cuda.synchronize()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(K):
+            paged_step()
+        g1.record(stream)
+        torch.cuda.synchronize()
+        if lib.kvbm_check_device_errors(stream.cuda_stream) != 0:
+            raise RuntimeError("device error in the paged run")
+        ms_p = g0.elapsed_time(g1) / K
+        dense_out = ops.run_prepared(prep, workspace=ws)
+        torch.cuda.synchronize()
+        paged = {"value": pairs_rank / (ms_p * 1e-3), "unit": UNIT, "ms_per_step": ms_p, "per_gpu": True,
+                 "page_size": P, "pages": B_ * npg, "bits_equal_dense": bool(torch.equal(out_p, dense_out)),
+                 "gathered_bytes_per_step": int(2 * k.numel() * k.element_size()),
+                 "api": "kvbm_block_mass_paged (k from a [pages, 16, H_kv, D] cache + block table)"}
+        del cache, ws_p, table, dense_out
+
     # End to end through the public API: pinned host q/k in, mass back on the host.
     e2e = None
     if not args.no_e2e:
@@ -476,6 +526,8 @@ def b200_arm(args, w):
         line["e2e"] = e2e
     if lse_input:
         line["lse_input"] = lse_input
+    if paged:
+        line["paged"] = paged
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = {k: v for k, v in cpu_sample(w, args.cpu_seconds).items()
                                 if k not in ("seconds", "pairs")}

@@ -69,7 +69,8 @@ enum kvbm_status {
   KVBM_ERR_CUDA = 9,        /* a CUDA runtime call or launch failed           */
   KVBM_ERR_DEVICE = 10,     /* current device is not an sm_100 GPU            */
   KVBM_ERR_TIMEOUT = 11,    /* a device-side wait ran out its iteration limit */
-  KVBM_ERR_SCRATCH = 12     /* problem needs more scratch than the fixed area  */
+  KVBM_ERR_SCRATCH = 12,    /* problem needs more scratch than the fixed area  */
+  KVBM_ERR_PAGE = 13        /* a block-table entry was outside [0, num_pages) */
 };
 
 /* Attention-mass problem.  Strides are in ELEMENTS for the dims [B, H, N, D]
@@ -214,9 +215,54 @@ KVBM_API int kvbm_block_mass_static(const kvbm_problem* p, void* mass_out, void*
  * No counterpart in the reference. */
 KVBM_API size_t kvbm_static_scratch_bytes(void);
 
-/* Reads and clears the device-side error word of the current device (set
- * when a bounded wait inside a tcgen05 kernel gave up).  Synchronises
- * `stream`.  Returns KVBM_OK, KVBM_ERR_TIMEOUT or KVBM_ERR_CUDA. */
+/* Paged key cache (extension; the reference takes dense k only).
+ *
+ *   k_cache      [num_pages, page_size, H_kv, D] of the problem's dtype, on
+ *                the device; cache_stride = element strides of those dims
+ *   block_table  [B, max_pages] int32 page ids on the device: logical key n
+ *                of sequence b is slot n % page_size of page
+ *                block_table[b * block_table_stride + n / page_size]
+ *
+ * This is the layout of the paged KV-cache managers that consume block mass
+ * (the companion paged-kv block manager, README.md:7-10 and
+ * src/kvblockmass/reclaim.py:14-16 of kv-block-mass).  Every sequence has
+ * the problem's N keys; max_pages * page_size must be >= N.  Table entries
+ * past ceil(N / page_size) are not read.  block_size == page_size gives one
+ * mass bucket per page. */
+typedef struct kvbm_paged_kv {
+  const void* k_cache;
+  int64_t cache_stride[4];
+  int32_t num_pages;
+  int32_t page_size;
+  const int32_t* block_table;
+  int64_t block_table_stride;
+  int32_t max_pages;
+} kvbm_paged_kv;
+
+/* Host-only checks of a paged problem (p->k and p->k_stride are ignored). */
+KVBM_API int kvbm_validate_paged(const kvbm_problem* p, const kvbm_paged_kv* kv);
+
+/* Workspace bytes kvbm_block_mass_paged needs (0 on invalid input): the
+ * kvbm_workspace_bytes of the dense problem plus a dense copy of the key
+ * rows of the units [unit_begin, unit_end) touch. */
+KVBM_API size_t kvbm_paged_workspace_bytes(const kvbm_problem* p, const kvbm_paged_kv* kv);
+
+/* kvbm_block_mass (lse == NULL) or kvbm_block_mass_lse (lse != NULL) with k
+ * read from a paged cache.  A first kernel copies the key rows of the
+ * requested units, page by page, into a dense array in the workspace; the
+ * dense kernels then run on it, so the result has the same bits as the dense
+ * call on the same key values.  A block-table entry outside [0, num_pages)
+ * is not read: its rows count as zero vectors and kvbm_check_device_errors
+ * reports KVBM_ERR_PAGE.  Workspace: kvbm_paged_workspace_bytes(p, kv). */
+KVBM_API int kvbm_block_mass_paged(const kvbm_problem* p, const kvbm_paged_kv* kv, const float* lse,
+                          const int64_t* lse_stride, void* mass_out, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+/* Reads and clears the device-side error words of the current device (set
+ * when a bounded wait inside a tcgen05 kernel gave up, or when a page gather
+ * met a block-table entry out of range).  Synchronises `stream`.  Returns
+ * KVBM_OK, KVBM_ERR_TIMEOUT (takes precedence), KVBM_ERR_PAGE or
+ * KVBM_ERR_CUDA. */
 KVBM_API int kvbm_check_device_errors(void* stream);
 
 #ifdef __cplusplus

@@ -109,6 +109,18 @@ WsLayout layout_for(const kvbm_problem* p, int path) {
   return L;
 }
 
+// Largest workspace over the kernel paths `p`'s dtype can take: SIMT, plus
+// tcgen05 for bf16/fp16 (path 1) or 3xTF32 for fp32 (path 2).
+size_t max_layout_bytes(const kvbm_problem* p) {
+  size_t m = layout_for(p, 0).total;
+  const int tc = p->dtype == KVBM_F32 ? 2 : (p->dtype == KVBM_F64 ? 0 : 1);
+  if (tc != 0) {
+    const size_t t = layout_for(p, tc).total;
+    m = t > m ? t : m;
+  }
+  return m;
+}
+
 // Launch sequence shared by the entry points: (pass 1 | lse import), pass 2,
 // bucket reduce, with optional events around them.
 int run_passes(const kvbm_problem* p, const WsLayout& L, int path, void* mass_out, void* ws, cudaStream_t s,
@@ -131,6 +143,65 @@ int run_passes(const kvbm_problem* p, const WsLayout& L, int path, void* mass_ou
   st = launch_reduce(p, L, mass_out, ws, s);
   if (st != KVBM_OK) return st;
   return mark(3) ? KVBM_OK : KVBM_ERR_CUDA;
+}
+
+// A paged call: the dense sub-problem over the smallest box of batches x
+// kv-heads that holds the requested units, and where its gathered keys go.
+struct PagedPlan {
+  kvbm_problem sub;        // batch/head origin shifted to (b0, g0); k set at launch
+  int b0 = 0, g0 = 0;
+  size_t gather_off = 0;   // gathered [B', H_kv', N, D] keys, after the dense workspace
+  size_t gather_bytes = 0;
+};
+
+int plan_paged(const kvbm_problem* p, const kvbm_paged_kv* kv, PagedPlan* out) {
+  if (p == nullptr || kv == nullptr) return KVBM_ERR_NULL;
+  if (kv->k_cache == nullptr || kv->block_table == nullptr) return KVBM_ERR_NULL;
+  if (kv->num_pages < 1 || kv->page_size < 1 || kv->max_pages < 1 || kv->block_table_stride < 0)
+    return KVBM_ERR_SHAPE;
+  for (int i = 0; i < 4; ++i)
+    if (kv->cache_stride[i] < 0) return KVBM_ERR_SHAPE;
+  kvbm_problem sub = *p;
+  sub.k = kv->k_cache;  // stands in for validate(); replaced by the gathered rows
+  for (int i = 0; i < 4; ++i) sub.k_stride[i] = 0;
+  int st = validate(&sub);
+  if (st != KVBM_OK) return st;
+  if ((int64_t)kv->max_pages * kv->page_size < p->N) return KVBM_ERR_SHAPE;
+  // unit u = b*H_kv + g: a range inside one batch keeps only its heads,
+  // otherwise whole batches
+  const int G = p->Hq / p->Hkv;
+  const int b0 = p->unit_begin / p->Hkv, b1 = (p->unit_end - 1) / p->Hkv;
+  int g0 = 0, ng = p->Hkv;
+  if (b0 == b1) {
+    g0 = p->unit_begin % p->Hkv;
+    ng = (p->unit_end - 1) % p->Hkv - g0 + 1;
+  }
+  const int esize = p->dtype == KVBM_F64 ? 8 : (p->dtype == KVBM_F32 ? 4 : 2);
+  sub.B = b1 - b0 + 1;
+  sub.Hkv = ng;
+  sub.Hq = ng * G;
+  sub.q = static_cast<const char*>(p->q) + (b0 * p->q_stride[0] + (int64_t)g0 * G * p->q_stride[1]) * esize;
+  sub.k_stride[0] = (int64_t)ng * p->N * p->D;
+  sub.k_stride[1] = (int64_t)p->N * p->D;
+  sub.k_stride[2] = p->D;
+  sub.k_stride[3] = 1;
+  if (sub.key_mask != nullptr) sub.key_mask += b0 * p->key_mask_bstride;
+  if (sub.query_mask != nullptr) sub.query_mask += b0 * p->query_mask_bstride;
+  if (sub.pair_mask != nullptr) sub.pair_mask += b0 * p->pair_mask_bstride;
+  sub.unit_begin = p->unit_begin - b0 * p->Hkv - g0;
+  sub.unit_end = p->unit_end - b0 * p->Hkv - g0;
+  st = validate(&sub);
+  if (st != KVBM_OK) return st;
+  // The dense workspace must fit whichever kernel path runs: size it for the
+  // largest layout (the gathered base address decides nothing but TMA
+  // alignment, which the 256-byte offset satisfies).
+  const size_t dense = max_layout_bytes(&sub);
+  out->sub = sub;
+  out->b0 = b0;
+  out->g0 = g0;
+  out->gather_off = align_up(dense, 256);
+  out->gather_bytes = align_up((size_t)sub.B * ng * p->N * p->D * esize, 256);
+  return KVBM_OK;
 }
 
 }  // namespace kvbm
@@ -158,6 +229,8 @@ const char* kvbm_status_string(int status) {
     case KVBM_ERR_SCRATCH:
       return "problem needs more scratch than the fixed area of kvbm_block_mass_static "
              "(see kvbm_static_scratch_bytes); split it into unit ranges";
+    case KVBM_ERR_PAGE:
+      return "a block-table entry was outside [0, num_pages); its keys were read as zeros";
     default: return "unknown status";
   }
 }
@@ -177,16 +250,9 @@ size_t kvbm_workspace_bytes(const kvbm_problem* p) {
     dev = -1;
   }
   const int path = select_path(p, dev);
-  // Size for the larger of the two layouts when the device is unknown, so a
-  // workspace sized on the host is valid for whichever path runs.
-  if (dev < 0) {
-    size_t m = 0;
-    for (int path_i = 0; path_i <= 2; ++path_i) {
-      const size_t t = layout_for(p, path_i).total;
-      m = t > m ? t : m;
-    }
-    return m;
-  }
+  // Size for the largest layout the dtype can select when the device is
+  // unknown, so a workspace sized on the host is valid for whichever path runs.
+  if (dev < 0) return max_layout_bytes(p);
   return layout_for(p, path).total;
 }
 
@@ -259,11 +325,59 @@ int kvbm_block_mass_lse(const kvbm_problem* p, const float* lse, const int64_t* 
                     lse_stride);
 }
 
-int kvbm_check_device_errors(void* stream) {
-  int err = 0;
-  const int st = read_and_clear_device_error(static_cast<cudaStream_t>(stream), &err);
+int kvbm_validate_paged(const kvbm_problem* p, const kvbm_paged_kv* kv) {
+  PagedPlan plan;
+  return plan_paged(p, kv, &plan);
+}
+
+size_t kvbm_paged_workspace_bytes(const kvbm_problem* p, const kvbm_paged_kv* kv) {
+  PagedPlan plan;
+  if (plan_paged(p, kv, &plan) != KVBM_OK) return 0;
+  return plan.gather_off + plan.gather_bytes;
+}
+
+int kvbm_block_mass_paged(const kvbm_problem* p, const kvbm_paged_kv* kv, const float* lse,
+                          const int64_t* lse_stride, void* mass_out, void* workspace, size_t workspace_bytes,
+                          void* stream) {
+  PagedPlan plan;
+  int st = plan_paged(p, kv, &plan);
   if (st != KVBM_OK) return st;
-  return err ? KVBM_ERR_TIMEOUT : KVBM_OK;
+  if (mass_out == nullptr) return KVBM_ERR_NULL;
+  if (lse != nullptr) {
+    if (lse_stride == nullptr) return KVBM_ERR_NULL;
+    for (int i = 0; i < 3; ++i)
+      if (lse_stride[i] < 0) return KVBM_ERR_SHAPE;
+  }
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return KVBM_ERR_CUDA;
+  }
+  if (device_kind(dev) != 1) return KVBM_ERR_DEVICE;
+  if (workspace == nullptr || workspace_bytes < plan.gather_off + plan.gather_bytes ||
+      ((uintptr_t)workspace % 256) != 0)
+    return KVBM_ERR_WORKSPACE;
+  // the dense sub-problem reads k from the gathered rows
+  kvbm_problem sub = plan.sub;
+  sub.k = static_cast<char*>(workspace) + plan.gather_off;
+  const int path = select_path(&sub, dev);
+  const WsLayout L = layout_for(&sub, path);
+  if (L.total > plan.gather_off) return KVBM_ERR_WORKSPACE;  // cannot happen: plan sized the larger layout
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = launch_page_gather(kv, p->dtype, plan.b0, plan.g0, sub.B, sub.Hkv, p->N, p->D, const_cast<void*>(sub.k), s);
+  if (st != KVBM_OK) return st;
+  const float* sub_lse = nullptr;
+  if (lse != nullptr) sub_lse = lse + plan.b0 * lse_stride[0] + (int64_t)plan.g0 * (p->Hq / p->Hkv) * lse_stride[1];
+  return run_passes(&sub, L, path, mass_out, workspace, s, nullptr, sub_lse, lse_stride);
+}
+
+int kvbm_check_device_errors(void* stream) {
+  int err = 0, perr = 0;
+  int st = read_and_clear_device_error(static_cast<cudaStream_t>(stream), &err);
+  if (st != KVBM_OK) return st;
+  st = read_and_clear_page_error(static_cast<cudaStream_t>(stream), &perr);
+  if (st != KVBM_OK) return st;
+  return err ? KVBM_ERR_TIMEOUT : (perr ? KVBM_ERR_PAGE : KVBM_OK);
 }
 
 }  // extern "C"

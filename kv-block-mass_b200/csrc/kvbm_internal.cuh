@@ -64,4 +64,12 @@ int launch_reduce(const kvbm_problem* p, const WsLayout& L, void* mass_out, cons
 // Device error word: set when a bounded wait in a tcgen05 kernel gives up.
 int read_and_clear_device_error(cudaStream_t s, int* err);
 
+// Paged-KV input (kvbm_paged.cu): copies the key rows of batches
+// [b0, b0 + nb) x kv-heads [g0, g0 + ng) out of the paged cache into a dense
+// contiguous [nb, ng, N, D] array `out`.
+int launch_page_gather(const kvbm_paged_kv* kv, int dtype, int b0, int g0, int nb, int ng, int N, int D,
+                       void* out, cudaStream_t s);
+// Page error word: set when a block-table entry was outside [0, num_pages).
+int read_and_clear_page_error(cudaStream_t s, int* err);
+
 }  // namespace kvbm

@@ -12,10 +12,15 @@ __version__ = "0.1.0"
 from .ops import (  # noqa: F401
     block_mass,
     block_mass_b200,
+    block_mass_paged,
     block_mass_triton,
+    check_device_errors,
     kernel_path,
     launches_per_call,
+    make_paged_problem,
     make_problem,
+    paged_workspace_bytes,
+    run_paged,
     workspace_bytes,
 )
 from .workloads import WORKLOADS, Workload, make_inputs, pairs  # noqa: F401
@@ -24,6 +29,11 @@ __all__ = [
     "block_mass_b200",
     "block_mass_triton",
     "block_mass",
+    "block_mass_paged",
+    "make_paged_problem",
+    "paged_workspace_bytes",
+    "run_paged",
+    "check_device_errors",
     "kernel_path",
     "make_problem",
     "workspace_bytes",

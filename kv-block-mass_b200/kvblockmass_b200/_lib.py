@@ -27,6 +27,7 @@ KVBM_ERR_CUDA = 9
 KVBM_ERR_DEVICE = 10
 KVBM_ERR_TIMEOUT = 11
 KVBM_ERR_SCRATCH = 12
+KVBM_ERR_PAGE = 13
 
 # Symbols include/kvbm.h declares; tests check the library exports each one.
 EXPORTED = [
@@ -44,6 +45,9 @@ EXPORTED = [
     "kvbm_check_device_errors",
     "kvbm_block_mass_static",
     "kvbm_static_scratch_bytes",
+    "kvbm_validate_paged",
+    "kvbm_paged_workspace_bytes",
+    "kvbm_block_mass_paged",
 ]
 
 
@@ -74,6 +78,20 @@ class Problem(ctypes.Structure):
         ("causal_skip", ctypes.c_int32),
         ("unit_begin", ctypes.c_int32),
         ("unit_end", ctypes.c_int32),
+    ]
+
+
+class PagedKV(ctypes.Structure):
+    """Mirror of ``struct kvbm_paged_kv``."""
+
+    _fields_ = [
+        ("k_cache", ctypes.c_void_p),
+        ("cache_stride", ctypes.c_int64 * 4),
+        ("num_pages", ctypes.c_int32),
+        ("page_size", ctypes.c_int32),
+        ("block_table", ctypes.c_void_p),
+        ("block_table_stride", ctypes.c_int64),
+        ("max_pages", ctypes.c_int32),
     ]
 
 
@@ -121,6 +139,15 @@ def load() -> ctypes.CDLL:
     lib.kvbm_block_mass_static.argtypes = [P, ctypes.c_void_p, ctypes.c_void_p]
     lib.kvbm_static_scratch_bytes.restype = ctypes.c_size_t
     lib.kvbm_static_scratch_bytes.argtypes = []
+    # Paged key cache (gathered into the workspace, then the dense kernels).
+    K = ctypes.POINTER(PagedKV)
+    lib.kvbm_validate_paged.restype = ctypes.c_int
+    lib.kvbm_validate_paged.argtypes = [P, K]
+    lib.kvbm_paged_workspace_bytes.restype = ctypes.c_size_t
+    lib.kvbm_paged_workspace_bytes.argtypes = [P, K]
+    lib.kvbm_block_mass_paged.restype = ctypes.c_int
+    lib.kvbm_block_mass_paged.argtypes = [P, K, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64), ctypes.c_void_p,
+                                          ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
     lib.kvbm_check_device_errors.restype = ctypes.c_int
     lib.kvbm_check_device_errors.argtypes = [ctypes.c_void_p]
     if lib.kvbm_abi_version() != 1:

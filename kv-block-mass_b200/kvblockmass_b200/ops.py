@@ -24,7 +24,8 @@ import torch
 from . import _lib
 
 __all__ = ["block_mass_b200", "block_mass_triton", "block_mass", "kernel_path", "make_problem",
-           "workspace_bytes", "launches_per_call"]
+           "workspace_bytes", "launches_per_call", "block_mass_paged", "make_paged_problem",
+           "paged_workspace_bytes", "run_paged", "check_device_errors"]
 
 _DTYPES = {
     torch.float32: _lib.KVBM_F32,
@@ -314,3 +315,131 @@ def block_mass(q, k, **kwargs):
         return block_mass_b200(q, k, **kwargs)
     raise ValueError("kvblockmass_b200.block_mass handles CUDA tensors; CPU tensors belong to "
                      "the reference's block_mass_reference")
+
+
+class _PagedPrepared:
+    """A dense ``kvbm_problem`` (its k ignored) plus the ``kvbm_paged_kv`` of the cache."""
+
+    def __init__(self, prep: _Prepared, kv, keep):
+        self.prep = prep
+        self.kv = kv
+        self.keep = keep
+
+
+def make_paged_problem(q, k_cache, block_table, attn_mask=None, causal=False, block_size=64, scale=None,
+                       causal_skip=True, query_mask=None, units=None) -> _PagedPrepared:
+    """Validate a paged call and build its C structs.
+
+    ``k_cache`` is ``[num_pages, page_size, H_kv, D]`` (any strides, the dtype
+    of ``q``); ``block_table`` is ``[B, max_pages]`` of page ids (converted to
+    int32): key ``n`` of sequence ``b`` is ``k_cache[block_table[b, n // P], n % P]``.
+    Every sequence has ``N = q.shape[2]`` keys.
+    """
+    if not all(isinstance(t, torch.Tensor) for t in (q, k_cache, block_table)):
+        raise TypeError("q, k_cache and block_table must be torch tensors")
+    if q.dim() != 4 or k_cache.dim() != 4:
+        raise ValueError(f"q must be [B, H_q, N, D] and k_cache [num_pages, page_size, H_kv, D], "
+                         f"got {tuple(q.shape)} and {tuple(k_cache.shape)}")
+    B, Hq, N, D = q.shape
+    num_pages, page_size, Hkv, Dk = k_cache.shape
+    if Dk != D:
+        raise ValueError(f"k_cache head dim {Dk} != q head dim {D}")
+    if block_table.dim() != 2 or block_table.shape[0] != B:
+        raise ValueError(f"block_table must be [B={B}, max_pages], got {tuple(block_table.shape)}")
+    if block_table.dtype.is_floating_point or block_table.dtype == torch.bool:
+        raise ValueError(f"block_table must hold integer page ids, got {block_table.dtype}")
+    if k_cache.dtype != q.dtype:
+        raise ValueError(f"k_cache dtype {k_cache.dtype} != q dtype {q.dtype}")
+    if not (q.device == k_cache.device == block_table.device):
+        raise ValueError("q, k_cache and block_table must be on one device")
+    if num_pages == 0 or page_size == 0:
+        raise ValueError("k_cache has no pages")
+    if block_table.shape[1] * page_size < N:
+        raise ValueError(f"block_table covers {block_table.shape[1] * page_size} keys < N={N}")
+    table = block_table.to(torch.int32)
+    if table.stride(1) != 1:
+        table = table.contiguous()
+    # stand-in dense k: make_problem checks shapes and masks; the C call ignores it
+    k_shape = torch.empty((), dtype=q.dtype, device=q.device).expand(B, Hkv, N, D)
+    prep = make_problem(q, k_shape, attn_mask=attn_mask, causal=causal, block_size=block_size, scale=scale,
+                        causal_skip=causal_skip, query_mask=query_mask, units=units)
+    kv = _lib.PagedKV()
+    kv.k_cache = k_cache.data_ptr()
+    for i in range(4):
+        kv.cache_stride[i] = k_cache.stride(i)
+    kv.num_pages, kv.page_size = num_pages, page_size
+    kv.block_table = table.data_ptr()
+    kv.block_table_stride = table.stride(0)
+    kv.max_pages = table.shape[1]
+    code = _lib.load().kvbm_validate_paged(ctypes.byref(prep.prob), ctypes.byref(kv))
+    if code != _lib.KVBM_OK:
+        _raise(code, prep.prob)
+    return _PagedPrepared(prep, kv, [k_cache, table])
+
+
+def paged_workspace_bytes(pp: _PagedPrepared) -> int:
+    return int(_lib.load().kvbm_paged_workspace_bytes(ctypes.byref(pp.prep.prob), ctypes.byref(pp.kv)))
+
+
+def run_paged(pp: _PagedPrepared, out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+              stream: torch.cuda.Stream | None = None, lse: torch.Tensor | None = None) -> torch.Tensor:
+    """Launch a prepared paged problem (page gather, then the dense kernels) on ``stream``."""
+    prep = pp.prep
+    dev = prep.keep[0].device
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        need = paged_workspace_bytes(pp)
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
+        if out is None:
+            out = torch.empty(prep.nb, dtype=prep.out_dtype, device=dev)
+        elif out.dtype != prep.out_dtype or out.numel() != prep.nb or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous {prep.out_dtype} tensor of {prep.nb} elements")
+        s = stream if stream is not None else torch.cuda.current_stream(dev)
+        lse_ptr, st = None, None
+        if lse is not None:
+            B, Hq, N = prep.prob.B, prep.prob.Hq, prep.prob.N
+            if tuple(lse.shape) != (B, Hq, N):
+                raise ValueError(f"lse must be [B, H_q, N] = {(B, Hq, N)}, got {tuple(lse.shape)}")
+            lse = lse.to(device=dev, dtype=torch.float32)
+            pp.keep.append(lse)
+            lse_ptr, st = lse.data_ptr(), (ctypes.c_int64 * 3)(*lse.stride())
+        code = lib.kvbm_block_mass_paged(ctypes.byref(prep.prob), ctypes.byref(pp.kv), lse_ptr, st,
+                                         out.data_ptr(), workspace.data_ptr(), workspace.numel(), s.cuda_stream)
+    if code != _lib.KVBM_OK:
+        _raise(code, prep.prob)
+    return out
+
+
+def block_mass_paged(q, k_cache, block_table, attn_mask=None, causal=False, block_size=64, scale=None,
+                     causal_skip=True, query_mask=None, *, units=None, out=None, workspace=None, lse=None):
+    """``block_mass_b200`` with keys read from a paged KV cache.
+
+    ``k_cache [num_pages, page_size, H_kv, D]`` and ``block_table [B,
+    max_pages]`` (page ids) on the device of ``q [B, H_q, N, D]``; the other
+    arguments as ``block_mass_b200``.  ``block_size == page_size`` gives one
+    bucket per page.  The result has the same bits as ``block_mass_b200`` on
+    the dense keys the table names.  A page id outside ``[0, num_pages)`` is
+    not read (its keys count as zero vectors); ``check_device_errors()``
+    reports it.
+    """
+    if not (q.is_cuda and k_cache.is_cuda):
+        raise ValueError("block_mass_paged needs CUDA tensors (there is no CPU path)")
+    pp = make_paged_problem(q, k_cache, block_table, attn_mask=attn_mask, causal=causal, block_size=block_size,
+                            scale=scale, causal_skip=causal_skip, query_mask=query_mask, units=units)
+    return run_paged(pp, out=out, workspace=workspace, lse=lse)
+
+
+def check_device_errors(device=None) -> None:
+    """Raise ``RuntimeError`` if a kernel on ``device`` recorded an error since the last check.
+
+    Two conditions are recorded on the device instead of faulting: a bounded
+    wait in a tensor-core kernel that ran out (``KVBM_ERR_TIMEOUT``) and a
+    block-table entry outside the cache (``KVBM_ERR_PAGE``).  Synchronises the
+    current stream; both words are cleared.
+    """
+    dev = torch.device("cuda") if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        code = _lib.load().kvbm_check_device_errors(torch.cuda.current_stream(dev).cuda_stream)
+    if code != _lib.KVBM_OK:
+        raise RuntimeError(f"kvbm error {code}: {_lib.status_string(code)}")

@@ -29,6 +29,11 @@ sum over ``b`` of the reference run on batch ``b`` alone with that batch's
 mask, and a row with ``query_mask`` False behaves like a pair-mask row that
 keeps nothing.
 
+A paged key cache (``[num_pages, page_size, H_kv, D]`` plus a block table
+``[B, max_pages]`` of page ids, the layout of the paged KV managers that
+consume block mass) is another extension; it is defined by the dense keys it
+names (``dense_keys_from_pages``), on which the reference algorithm runs.
+
 The restatement is pinned against outputs of the reference itself, stored
 under ``tests/golden/`` by ``tests/golden/gen_golden.py``.
 """
@@ -40,7 +45,7 @@ from concurrent.futures import ThreadPoolExecutor
 
 import numpy as np
 
-__all__ = ["block_mass_stream", "normalize_masks", "num_blocks"]
+__all__ = ["block_mass_stream", "normalize_masks", "num_blocks", "dense_keys_from_pages"]
 
 
 def num_blocks(n: int, block_size: int) -> int:
@@ -278,3 +283,19 @@ if __name__ == "__main__":  # pragma: no cover - manual smoke
     a = block_mass_stream(q, k, causal=True, block_size=32)
     d = dense_block_mass(q, k, causal=True, block_size=32)
     print(a, d, float(np.abs(a - d).max()), math.isclose(a.sum(), 400.0))
+
+
+def dense_keys_from_pages(k_cache, block_table, n: int):
+    """Dense ``k [B, H_kv, N, D]`` named by a paged cache.
+
+    Key ``c`` of sequence ``b`` is slot ``c % P`` of page
+    ``block_table[b, c // P]`` of ``k_cache [num_pages, P, H_kv, D]``.  The
+    reference takes dense keys only; this defines the paged input by them.
+    """
+    k_cache = np.asarray(k_cache)
+    table = np.asarray(block_table).astype(np.int64)
+    p = k_cache.shape[1]
+    c = np.arange(n)
+    pages = table[:, c // p]                     # [B, N]
+    rows = k_cache[pages, (c % p)[None, :]]      # [B, N, H_kv, D]
+    return np.ascontiguousarray(rows.transpose(0, 2, 1, 3))
