@@ -21,6 +21,8 @@ Reported beside the device-timed value:
   paged         the device-resident step with k read from a paged cache
                 (16-key pages in shuffled order + block table): page gather,
                 both passes, reduce;
+  ragged        a packed (varlen) batch of six sequences, 32768 tokens, in one
+                call, beside one dense call per sequence;
   roofline      the dominant kernel's algorithmic tensor FLOP/s against the
                 measured bf16 peak, and its exp rate against the MUFU ex2
                 rate measured live on this GPU (the binding unit);
@@ -451,6 +453,49 @@ def b200_arm(args, w):
                  "api": "kvbm_block_mass_paged (k from a [pages, 16, H_kv, D] cache + block table)"}
         del cache, ws_p, table, dense_out
 
+    # Ragged serving batch (packed varlen layout, the workload's heads, 32768 tokens in
+    # six sequences): one call against one dense call per sequence.
+    ragged = None
+    if not args.no_e2e and path == 1:
+        lens_r = [16384, 8192, 4096, 2048, 1024, 1024]
+        T = sum(lens_r)
+        gen = torch.Generator(device=dev).manual_seed(11)
+        qp = torch.randn(T, q.shape[1], q.shape[3], device=dev, generator=gen).to(q.dtype)
+        kp = torch.randn(T, k.shape[1], k.shape[3], device=dev, generator=gen).to(k.dtype)
+        cu = torch.tensor([0] + list(np.cumsum(lens_r)), dtype=torch.int32, device=dev)
+        vprep = ops.make_varlen_problem(qp, kp, cu, max_seqlen=max(lens_r), causal=w.causal,
+                                        block_size=w.block_size)
+        ws_r = torch.empty(ops.workspace_bytes(vprep), dtype=torch.uint8, device=dev)
+        out_r = torch.empty(vprep.out_shape, dtype=torch.float32, device=dev)
+        singles = []
+        for i, L in enumerate(lens_r):
+            s0 = int(cu[i])
+            singles.append(ops.make_problem(qp[s0:s0 + L].transpose(0, 1).unsqueeze(0),
+                                            kp[s0:s0 + L].transpose(0, 1).unsqueeze(0), causal=w.causal,
+                                            block_size=w.block_size))
+
+        def timed(fn, reps):
+            for _ in range(2):
+                fn()
+            torch.cuda.synchronize()
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record(stream)
+            for _ in range(reps):
+                fn()
+            t1.record(stream)
+            torch.cuda.synchronize()
+            return t0.elapsed_time(t1) / reps
+
+        ms_r = timed(lambda: ops.run_prepared(vprep, out=out_r, workspace=ws_r), K)
+        ms_loop = timed(lambda: [ops.run_prepared(sp, workspace=ws_r) for sp in singles], K)
+        per_head_r = sum(L * (L + 1) // 2 if w.causal else L * L for L in lens_r)
+        pairs_r = q.shape[1] * per_head_r
+        ragged = {"value": pairs_r / (ms_r * 1e-3), "unit": UNIT, "ms_per_step": ms_r, "per_gpu": True,
+                  "seq_lens": lens_r, "tokens": T,
+                  "one_call_per_sequence_ms": ms_loop,
+                  "api": "kvbm_block_mass_ex (packed q/k + cu_seqlens), vs one kvbm_block_mass per sequence"}
+        del qp, kp, ws_r, singles
+
     # End to end through the public API: pinned host q/k in, mass back on the host.
     e2e = None
     if not args.no_e2e:
@@ -528,6 +573,8 @@ def b200_arm(args, w):
         line["lse_input"] = lse_input
     if paged:
         line["paged"] = paged
+    if ragged:
+        line["ragged"] = ragged
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = {k: v for k, v in cpu_sample(w, args.cpu_seconds).items()
                                 if k not in ("seconds", "pairs")}

@@ -258,6 +258,60 @@ KVBM_API int kvbm_block_mass_paged(const kvbm_problem* p, const kvbm_paged_kv* k
                           const int64_t* lse_stride, void* mass_out, void* workspace, size_t workspace_bytes,
                           void* stream);
 
+/* Options of kvbm_block_mass_ex (extensions; the reference has one dense
+ * [B, H, N, D] layout, one length N and a mass summed over the batch).
+ * Zero-initialise and set what is used; every pointer may be NULL.
+ *
+ *   lse, lse_stride   row LSE input as kvbm_block_mass_lse (skips pass 1);
+ *                     with cu_seqlens the LSE is packed like q: row i of
+ *                     sequence b, head h is lse[h*s1 + (cu_seqlens[b] + i)*s2]
+ *                     (s0 unused; [H_q, total_tokens] as FlashAttention's
+ *                     varlen forward returns it)
+ *   paged             k from a paged cache as kvbm_block_mass_paged
+ *   seq_lens          [B] int32 on the device: sequence b has seq_lens[b] <= N
+ *                     keys and queries (padded layout: q/k as in kvbm_problem,
+ *                     positions >= seq_lens[b] are never part of any pair)
+ *   cu_seqlens        [B + 1] int32 on the device: packed (varlen) layout.
+ *                     Sequence b is rows [cu_seqlens[b], cu_seqlens[b+1]) of
+ *                     q [total_tokens, H_q, D] (and of k [total_tokens, H_kv, D]
+ *                     unless `paged`); its length must be <= N (p->N is the
+ *                     longest sequence, longer ones are cut at N).  q_stride /
+ *                     k_stride give {unused, head, row, d} in elements.
+ *                     seq_lens and cu_seqlens are exclusive.
+ *   total_tokens      rows of the packed q/k (required with cu_seqlens)
+ *   per_sequence      0: mass_out is [num_blocks], summed over the batch (the
+ *                     reference's output); 1: mass_out is [B, num_blocks],
+ *                     row b the mass of sequence b alone (rows of sequences
+ *                     outside the unit range are written as zeros)
+ *   events            4 cudaEvent_t as kvbm_block_mass_events (or NULL)
+ *
+ * Every ragged/per-sequence result equals the sum over sequences of the
+ * reference run on each sequence alone (its first seq_lens[b] positions);
+ * buckets j >= ceil(len / block_size) of a sequence get 0 from it. */
+typedef struct kvbm_options {
+  const float* lse;
+  int64_t lse_stride[3];
+  const kvbm_paged_kv* paged;
+  const int32_t* seq_lens;
+  const int32_t* cu_seqlens;
+  int64_t total_tokens;
+  int32_t per_sequence;
+  void* const* events;
+} kvbm_options;
+
+/* Host-only checks of `p` with options `o` (o may be NULL). */
+KVBM_API int kvbm_validate_ex(const kvbm_problem* p, const kvbm_options* o);
+
+/* Workspace bytes kvbm_block_mass_ex needs (0 on invalid input). */
+KVBM_API size_t kvbm_workspace_bytes_ex(const kvbm_problem* p, const kvbm_options* o);
+
+/* Every option combined: dense, paged, padded-ragged or packed-varlen k/q,
+ * optional LSE input, summed or per-sequence output.  `o` may be NULL (then
+ * this is kvbm_block_mass).  Deterministic; the dense entry points above are
+ * this call with the matching options. */
+KVBM_API int kvbm_block_mass_ex(const kvbm_problem* p, const kvbm_options* o, void* mass_out, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
 /* Reads and clears the device-side error words of the current device (set
  * when a bounded wait inside a tcgen05 kernel gave up, or when a page gather
  * met a block-table entry out of range).  Synchronises `stream`.  Returns

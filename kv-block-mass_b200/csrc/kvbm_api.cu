@@ -78,7 +78,7 @@ int select_path(const kvbm_problem* p, int device) {
   return 1;
 }
 
-WsLayout layout_for(const kvbm_problem* p, int path) {
+WsLayout layout_for(const kvbm_problem* p, int path, const Ragged* rg) {
   WsLayout L;
   L.path = path;
   L.acc_bytes = (p->dtype == KVBM_F64) ? 8 : 4;
@@ -96,7 +96,11 @@ WsLayout layout_for(const kvbm_problem* p, int path) {
   L.part_off = align_up(L.lse_off + L.lse_bytes, 256);
   L.part_bytes = U * (size_t)L.nchunk * (size_t)p->N * L.acc_bytes;
   L.split_off = align_up(L.part_off + L.part_bytes, 256);
-  L.split_bytes = path == 2 ? (size_t)2 * 4 * p->N * p->D * ((size_t)p->B * p->Hq + (size_t)p->B * p->Hkv) : 0;
+  // path 2: tf32 hi/lo copies of every q and k row (packed operands: total_tokens rows per head)
+  const bool q_packed = rg != nullptr && rg->cu != nullptr, k_packed = rg != nullptr && rg->k_packed;
+  const size_t q_rows = q_packed ? (size_t)rg->total : (size_t)p->B * p->N;
+  const size_t k_rows = k_packed ? (size_t)rg->total : (size_t)p->B * p->N;
+  L.split_bytes = path == 2 ? (size_t)2 * 4 * p->D * (q_rows * p->Hq + k_rows * p->Hkv) : 0;
   L.bits_off = align_up(L.split_off + L.split_bytes, 256);
   if (tc && p->pair_mask != nullptr) {
     const bool per_b = p->pair_mask_bstride != 0 || (p->key_mask && p->key_mask_bstride != 0) ||
@@ -111,11 +115,11 @@ WsLayout layout_for(const kvbm_problem* p, int path) {
 
 // Largest workspace over the kernel paths `p`'s dtype can take: SIMT, plus
 // tcgen05 for bf16/fp16 (path 1) or 3xTF32 for fp32 (path 2).
-size_t max_layout_bytes(const kvbm_problem* p) {
-  size_t m = layout_for(p, 0).total;
+size_t max_layout_bytes(const kvbm_problem* p, const Ragged* rg = nullptr) {
+  size_t m = layout_for(p, 0, rg).total;
   const int tc = p->dtype == KVBM_F32 ? 2 : (p->dtype == KVBM_F64 ? 0 : 1);
   if (tc != 0) {
-    const size_t t = layout_for(p, tc).total;
+    const size_t t = layout_for(p, tc, rg).total;
     m = t > m ? t : m;
   }
   return m;
@@ -124,84 +128,191 @@ size_t max_layout_bytes(const kvbm_problem* p) {
 // Launch sequence shared by the entry points: (pass 1 | lse import), pass 2,
 // bucket reduce, with optional events around them.
 int run_passes(const kvbm_problem* p, const WsLayout& L, int path, void* mass_out, void* ws, cudaStream_t s,
-               void* const* events, const float* lse, const int64_t* lse_stride) {
+               void* const* events, const float* lse, const int64_t* lse_stride, const Ragged& rg = Ragged(),
+               bool per_sequence = false, bool marked = false) {
   auto mark = [&](int i) {
     if (events != nullptr && events[i] != nullptr)
       return cudaEventRecord(static_cast<cudaEvent_t>(events[i]), s) == cudaSuccess;
     return true;
   };
-  if (!mark(0)) return KVBM_ERR_CUDA;
+  if (!marked && !mark(0)) return KVBM_ERR_CUDA;
   LaunchOpts o;
   o.mid_event = events != nullptr ? events[1] : nullptr;
   o.run_pass1 = lse == nullptr;
+  o.rg = rg;
   int st = KVBM_OK;
-  if (lse != nullptr) st = launch_lse_import(p, L, lse, lse_stride, ws, s);
+  if (lse != nullptr) st = launch_lse_import(p, L, lse, lse_stride, ws, s, rg);
   if (st != KVBM_OK) return st;
   st = (path >= 1) ? launch_tc(p, L, mass_out, ws, s, o) : launch_simt(p, L, mass_out, ws, s, o);
   if (st != KVBM_OK) return st;
   if (!mark(2)) return KVBM_ERR_CUDA;
-  st = launch_reduce(p, L, mass_out, ws, s);
+  st = launch_reduce(p, L, mass_out, ws, s, per_sequence);
   if (st != KVBM_OK) return st;
   return mark(3) ? KVBM_OK : KVBM_ERR_CUDA;
 }
 
-// A paged call: the dense sub-problem over the smallest box of batches x
-// kv-heads that holds the requested units, and where its gathered keys go.
-struct PagedPlan {
-  kvbm_problem sub;        // batch/head origin shifted to (b0, g0); k set at launch
-  int b0 = 0, g0 = 0;
-  size_t gather_off = 0;   // gathered [B', H_kv', N, D] keys, after the dense workspace
-  size_t gather_bytes = 0;
+// One kvbm_block_mass_ex call resolved into what the kernels see.  A paged k
+// becomes a dense sub-problem over the smallest box of batches x kv-heads
+// that holds the requested units (a range inside one batch keeps only its
+// heads, otherwise whole batches), whose keys are gathered after the dense
+// workspace; q, the masks, the LSE, the ragged arrays and a per-sequence
+// output are shifted to that box's origin.
+struct Plan {
+  kvbm_problem sub;                  // the problem the kernels see (paged: k set at launch)
+  Ragged rg;                         // ragged arrays, shifted to the box
+  const int32_t* lens0 = nullptr;    // the caller's ragged arrays (page gather indexes b0 + b)
+  const int32_t* cu0 = nullptr;
+  const float* lse = nullptr;
+  int64_t lse_stride[3] = {0, 0, 0};
+  const kvbm_paged_kv* paged = nullptr;
+  bool per_sequence = false;
+  int B = 0;                         // the caller's batch (rows of a per-sequence output)
+  int b0 = 0, g0 = 0;                // origin of the box
+  int path = -1;                     // kernel path (-1: unknown device)
+  WsLayout L;
+  size_t gather_off = 0, gather_bytes = 0;
+  size_t total = 0;                  // workspace bytes
 };
 
-int plan_paged(const kvbm_problem* p, const kvbm_paged_kv* kv, PagedPlan* out) {
-  if (p == nullptr || kv == nullptr) return KVBM_ERR_NULL;
-  if (kv->k_cache == nullptr || kv->block_table == nullptr) return KVBM_ERR_NULL;
-  if (kv->num_pages < 1 || kv->page_size < 1 || kv->max_pages < 1 || kv->block_table_stride < 0)
-    return KVBM_ERR_SHAPE;
-  for (int i = 0; i < 4; ++i)
-    if (kv->cache_stride[i] < 0) return KVBM_ERR_SHAPE;
-  kvbm_problem sub = *p;
-  sub.k = kv->k_cache;  // stands in for validate(); replaced by the gathered rows
-  for (int i = 0; i < 4; ++i) sub.k_stride[i] = 0;
-  int st = validate(&sub);
-  if (st != KVBM_OK) return st;
-  if ((int64_t)kv->max_pages * kv->page_size < p->N) return KVBM_ERR_SHAPE;
-  // unit u = b*H_kv + g: a range inside one batch keeps only its heads,
-  // otherwise whole batches
-  const int G = p->Hq / p->Hkv;
-  const int b0 = p->unit_begin / p->Hkv, b1 = (p->unit_end - 1) / p->Hkv;
-  int g0 = 0, ng = p->Hkv;
-  if (b0 == b1) {
-    g0 = p->unit_begin % p->Hkv;
-    ng = (p->unit_end - 1) % p->Hkv - g0 + 1;
+int esize_of(int dtype) { return dtype == KVBM_F64 ? 8 : (dtype == KVBM_F32 ? 4 : 2); }
+
+// dev < 0: the device is unknown; the workspace is sized for the largest
+// layout the dtype can select.
+int make_plan(const kvbm_problem* p, const kvbm_options* o, int dev, Plan* out) {
+  if (p == nullptr) return KVBM_ERR_NULL;
+  kvbm_options opt{};
+  if (o != nullptr) opt = *o;
+  if (opt.seq_lens != nullptr && opt.cu_seqlens != nullptr) return KVBM_ERR_SHAPE;
+  if (opt.cu_seqlens != nullptr && (opt.total_tokens < 1 || opt.total_tokens > INT32_MAX)) return KVBM_ERR_SHAPE;
+  Plan pl;
+  pl.sub = *p;
+  kvbm_problem& sub = pl.sub;
+  const bool packed = opt.cu_seqlens != nullptr;
+  if (packed) sub.q_stride[0] = 0;  // rows are addressed through cu_seqlens
+  if (opt.lse != nullptr) {
+    for (int i = 0; i < 3; ++i) {
+      if (opt.lse_stride[i] < 0) return KVBM_ERR_SHAPE;
+      pl.lse_stride[i] = opt.lse_stride[i];
+    }
+    if (packed) pl.lse_stride[0] = 0;
+    pl.lse = opt.lse;
   }
-  const int esize = p->dtype == KVBM_F64 ? 8 : (p->dtype == KVBM_F32 ? 4 : 2);
-  sub.B = b1 - b0 + 1;
-  sub.Hkv = ng;
-  sub.Hq = ng * G;
-  sub.q = static_cast<const char*>(p->q) + (b0 * p->q_stride[0] + (int64_t)g0 * G * p->q_stride[1]) * esize;
-  sub.k_stride[0] = (int64_t)ng * p->N * p->D;
-  sub.k_stride[1] = (int64_t)p->N * p->D;
-  sub.k_stride[2] = p->D;
-  sub.k_stride[3] = 1;
-  if (sub.key_mask != nullptr) sub.key_mask += b0 * p->key_mask_bstride;
-  if (sub.query_mask != nullptr) sub.query_mask += b0 * p->query_mask_bstride;
-  if (sub.pair_mask != nullptr) sub.pair_mask += b0 * p->pair_mask_bstride;
-  sub.unit_begin = p->unit_begin - b0 * p->Hkv - g0;
-  sub.unit_end = p->unit_end - b0 * p->Hkv - g0;
+  int st = KVBM_OK;
+  const kvbm_paged_kv* kv = opt.paged;
+  if (kv != nullptr) {
+    if (kv->k_cache == nullptr || kv->block_table == nullptr) return KVBM_ERR_NULL;
+    if (kv->num_pages < 1 || kv->page_size < 1 || kv->max_pages < 1 || kv->block_table_stride < 0)
+      return KVBM_ERR_SHAPE;
+    for (int i = 0; i < 4; ++i)
+      if (kv->cache_stride[i] < 0) return KVBM_ERR_SHAPE;
+    sub.k = kv->k_cache;  // stands in for validate(); replaced by the gathered rows
+    for (int i = 0; i < 4; ++i) sub.k_stride[i] = 0;
+    st = validate(&sub);
+    if (st != KVBM_OK) return st;
+    if ((int64_t)kv->max_pages * kv->page_size < p->N) return KVBM_ERR_SHAPE;
+    const int G = p->Hq / p->Hkv;
+    const int b0 = p->unit_begin / p->Hkv, b1 = (p->unit_end - 1) / p->Hkv;
+    int g0 = 0, ng = p->Hkv;
+    if (b0 == b1) {
+      g0 = p->unit_begin % p->Hkv;
+      ng = (p->unit_end - 1) % p->Hkv - g0 + 1;
+    }
+    const int es = esize_of(p->dtype);
+    sub.B = b1 - b0 + 1;
+    sub.Hkv = ng;
+    sub.Hq = ng * G;
+    sub.q = static_cast<const char*>(p->q) + (b0 * sub.q_stride[0] + (int64_t)g0 * G * sub.q_stride[1]) * es;
+    sub.k_stride[0] = (int64_t)ng * p->N * p->D;
+    sub.k_stride[1] = (int64_t)p->N * p->D;
+    sub.k_stride[2] = p->D;
+    sub.k_stride[3] = 1;
+    if (sub.key_mask != nullptr) sub.key_mask += b0 * p->key_mask_bstride;
+    if (sub.query_mask != nullptr) sub.query_mask += b0 * p->query_mask_bstride;
+    if (sub.pair_mask != nullptr) sub.pair_mask += b0 * p->pair_mask_bstride;
+    sub.unit_begin = p->unit_begin - b0 * p->Hkv - g0;
+    sub.unit_end = p->unit_end - b0 * p->Hkv - g0;
+    if (pl.lse != nullptr) pl.lse += b0 * pl.lse_stride[0] + (int64_t)g0 * G * pl.lse_stride[1];
+    pl.b0 = b0;
+    pl.g0 = g0;
+    pl.paged = kv;
+    pl.gather_bytes = align_up((size_t)sub.B * ng * p->N * p->D * es, 256);
+    // the gathered rows start on a 256-byte boundary: path selection sees an aligned k
+    sub.k = reinterpret_cast<const void*>(uintptr_t(256));
+  } else if (packed) {
+    sub.k_stride[0] = 0;
+  }
   st = validate(&sub);
   if (st != KVBM_OK) return st;
-  // The dense workspace must fit whichever kernel path runs: size it for the
-  // largest layout (the gathered base address decides nothing but TMA
-  // alignment, which the 256-byte offset satisfies).
-  const size_t dense = max_layout_bytes(&sub);
-  out->sub = sub;
-  out->b0 = b0;
-  out->g0 = g0;
-  out->gather_off = align_up(dense, 256);
-  out->gather_bytes = align_up((size_t)sub.B * ng * p->N * p->D * esize, 256);
+  pl.lens0 = opt.seq_lens;
+  pl.cu0 = opt.cu_seqlens;
+  pl.rg.lens = opt.seq_lens ? opt.seq_lens + pl.b0 : nullptr;
+  pl.rg.cu = packed ? opt.cu_seqlens + pl.b0 : nullptr;
+  pl.rg.total = packed ? opt.total_tokens : 0;
+  pl.rg.k_packed = packed && kv == nullptr;
+  pl.per_sequence = opt.per_sequence != 0;
+  pl.B = p->B;
+  size_t dense = 0;
+  if (dev >= 0) {
+    pl.path = select_path(&sub, dev);
+    pl.L = layout_for(&sub, pl.path, &pl.rg);
+    dense = pl.L.total;
+  } else {
+    dense = max_layout_bytes(&sub, &pl.rg);
+  }
+  pl.gather_off = align_up(dense, 256);
+  pl.total = pl.gather_off + pl.gather_bytes;
+  *out = pl;
   return KVBM_OK;
+}
+
+int current_device(int* dev) {
+  if (cudaGetDevice(dev) != cudaSuccess) {
+    cudaGetLastError();
+    *dev = -1;
+    return KVBM_ERR_CUDA;
+  }
+  return KVBM_OK;
+}
+
+int run_plan(Plan& pl, void* mass_out, void* workspace, size_t workspace_bytes, cudaStream_t s,
+             void* const* events) {
+  if (mass_out == nullptr) return KVBM_ERR_NULL;
+  if (workspace == nullptr || workspace_bytes < pl.total || ((uintptr_t)workspace % 256) != 0)
+    return KVBM_ERR_WORKSPACE;
+  kvbm_problem& sub = pl.sub;
+  if (events != nullptr && events[0] != nullptr &&
+      cudaEventRecord(static_cast<cudaEvent_t>(events[0]), s) != cudaSuccess)
+    return KVBM_ERR_CUDA;
+  if (pl.paged != nullptr) {
+    void* gathered = static_cast<char*>(workspace) + pl.gather_off;
+    sub.k = gathered;
+    const int st = launch_page_gather(pl.paged, sub.dtype, pl.b0, pl.g0, sub.B, sub.Hkv, sub.N, sub.D, pl.lens0,
+                                      pl.cu0, gathered, s);
+    if (st != KVBM_OK) return st;
+  }
+  void* out = mass_out;
+  if (pl.per_sequence && (sub.B != pl.B)) {
+    // rows of sequences outside the box are zeros; the box writes its own rows
+    const size_t row = (size_t)kvbm_num_blocks(sub.N, sub.block_size) * (sub.dtype == KVBM_F64 ? 8 : 4);
+    char* base = static_cast<char*>(mass_out);
+    if (pl.b0 > 0 && cudaMemsetAsync(base, 0, row * pl.b0, s) != cudaSuccess) return KVBM_ERR_CUDA;
+    const int tail = pl.B - pl.b0 - sub.B;
+    if (tail > 0 && cudaMemsetAsync(base + row * (pl.b0 + sub.B), 0, row * tail, s) != cudaSuccess)
+      return KVBM_ERR_CUDA;
+    out = base + row * pl.b0;
+  }
+  return run_passes(&sub, pl.L, pl.path, out, workspace, s, events, pl.lse, pl.lse_stride, pl.rg,
+                    pl.per_sequence, true);
+}
+
+int plan_on_device(const kvbm_problem* p, const kvbm_options* o, Plan* pl) {
+  int dev = -1;
+  if (current_device(&dev) != KVBM_OK) return KVBM_ERR_CUDA;
+  if (device_kind(dev) != 1) {
+    const int st = make_plan(p, o, -1, pl);  // argument errors first
+    return st != KVBM_OK ? st : KVBM_ERR_DEVICE;
+  }
+  return make_plan(p, o, dev, pl);
 }
 
 }  // namespace kvbm
@@ -287,88 +398,70 @@ int kvbm_block_mass(const kvbm_problem* p, void* mass_out, void* workspace,
 
 int kvbm_block_mass_events(const kvbm_problem* p, void* mass_out, void* workspace,
                            size_t workspace_bytes, void* stream, void* const* events) {
-  int st = validate(p);
+  Plan pl;
+  const int st = plan_on_device(p, nullptr, &pl);
   if (st != KVBM_OK) return st;
-  if (mass_out == nullptr) return KVBM_ERR_NULL;
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess) {
-    cudaGetLastError();
-    return KVBM_ERR_CUDA;
-  }
-  if (device_kind(dev) != 1) return KVBM_ERR_DEVICE;
-  const int path = select_path(p, dev);
-  const WsLayout L = layout_for(p, path);
-  if (workspace == nullptr || workspace_bytes < L.total || ((uintptr_t)workspace % 256) != 0)
-    return KVBM_ERR_WORKSPACE;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return run_passes(p, L, path, mass_out, workspace, s, events, nullptr, nullptr);
+  return run_plan(pl, mass_out, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), events);
 }
 
 int kvbm_block_mass_lse(const kvbm_problem* p, const float* lse, const int64_t* lse_stride, void* mass_out,
                         void* workspace, size_t workspace_bytes, void* stream) {
-  int st = validate(p);
-  if (st != KVBM_OK) return st;
-  if (mass_out == nullptr || lse == nullptr || lse_stride == nullptr) return KVBM_ERR_NULL;
-  for (int i = 0; i < 3; ++i)
-    if (lse_stride[i] < 0) return KVBM_ERR_SHAPE;
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess) {
-    cudaGetLastError();
-    return KVBM_ERR_CUDA;
-  }
-  if (device_kind(dev) != 1) return KVBM_ERR_DEVICE;
-  const int path = select_path(p, dev);
-  const WsLayout L = layout_for(p, path);
-  if (workspace == nullptr || workspace_bytes < L.total || ((uintptr_t)workspace % 256) != 0)
-    return KVBM_ERR_WORKSPACE;
-  return run_passes(p, L, path, mass_out, workspace, static_cast<cudaStream_t>(stream), nullptr, lse,
-                    lse_stride);
+  if (lse == nullptr || lse_stride == nullptr) return KVBM_ERR_NULL;
+  kvbm_options o{};
+  o.lse = lse;
+  for (int i = 0; i < 3; ++i) o.lse_stride[i] = lse_stride[i];
+  return kvbm_block_mass_ex(p, &o, mass_out, workspace, workspace_bytes, stream);
 }
 
 int kvbm_validate_paged(const kvbm_problem* p, const kvbm_paged_kv* kv) {
-  PagedPlan plan;
-  return plan_paged(p, kv, &plan);
+  if (kv == nullptr) return KVBM_ERR_NULL;
+  kvbm_options o{};
+  o.paged = kv;
+  return kvbm_validate_ex(p, &o);
 }
 
 size_t kvbm_paged_workspace_bytes(const kvbm_problem* p, const kvbm_paged_kv* kv) {
-  PagedPlan plan;
-  if (plan_paged(p, kv, &plan) != KVBM_OK) return 0;
-  return plan.gather_off + plan.gather_bytes;
+  if (kv == nullptr) return 0;
+  kvbm_options o{};
+  o.paged = kv;
+  return kvbm_workspace_bytes_ex(p, &o);
 }
 
 int kvbm_block_mass_paged(const kvbm_problem* p, const kvbm_paged_kv* kv, const float* lse,
                           const int64_t* lse_stride, void* mass_out, void* workspace, size_t workspace_bytes,
                           void* stream) {
-  PagedPlan plan;
-  int st = plan_paged(p, kv, &plan);
-  if (st != KVBM_OK) return st;
-  if (mass_out == nullptr) return KVBM_ERR_NULL;
+  if (kv == nullptr) return KVBM_ERR_NULL;
+  kvbm_options o{};
+  o.paged = kv;
   if (lse != nullptr) {
     if (lse_stride == nullptr) return KVBM_ERR_NULL;
-    for (int i = 0; i < 3; ++i)
-      if (lse_stride[i] < 0) return KVBM_ERR_SHAPE;
+    o.lse = lse;
+    for (int i = 0; i < 3; ++i) o.lse_stride[i] = lse_stride[i];
   }
+  return kvbm_block_mass_ex(p, &o, mass_out, workspace, workspace_bytes, stream);
+}
+
+int kvbm_validate_ex(const kvbm_problem* p, const kvbm_options* o) {
+  Plan pl;
+  return make_plan(p, o, -1, &pl);
+}
+
+size_t kvbm_workspace_bytes_ex(const kvbm_problem* p, const kvbm_options* o) {
   int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess) {
-    cudaGetLastError();
-    return KVBM_ERR_CUDA;
-  }
-  if (device_kind(dev) != 1) return KVBM_ERR_DEVICE;
-  if (workspace == nullptr || workspace_bytes < plan.gather_off + plan.gather_bytes ||
-      ((uintptr_t)workspace % 256) != 0)
-    return KVBM_ERR_WORKSPACE;
-  // the dense sub-problem reads k from the gathered rows
-  kvbm_problem sub = plan.sub;
-  sub.k = static_cast<char*>(workspace) + plan.gather_off;
-  const int path = select_path(&sub, dev);
-  const WsLayout L = layout_for(&sub, path);
-  if (L.total > plan.gather_off) return KVBM_ERR_WORKSPACE;  // cannot happen: plan sized the larger layout
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  st = launch_page_gather(kv, p->dtype, plan.b0, plan.g0, sub.B, sub.Hkv, p->N, p->D, const_cast<void*>(sub.k), s);
+  current_device(&dev);
+  if (dev >= 0 && device_kind(dev) != 1) dev = -1;
+  Plan pl;
+  if (make_plan(p, o, dev, &pl) != KVBM_OK) return 0;
+  return pl.total;
+}
+
+int kvbm_block_mass_ex(const kvbm_problem* p, const kvbm_options* o, void* mass_out, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  Plan pl;
+  const int st = plan_on_device(p, o, &pl);
   if (st != KVBM_OK) return st;
-  const float* sub_lse = nullptr;
-  if (lse != nullptr) sub_lse = lse + plan.b0 * lse_stride[0] + (int64_t)plan.g0 * (p->Hq / p->Hkv) * lse_stride[1];
-  return run_passes(&sub, L, path, mass_out, workspace, s, nullptr, sub_lse, lse_stride);
+  return run_plan(pl, mass_out, workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
+                  o != nullptr ? o->events : nullptr);
 }
 
 int kvbm_check_device_errors(void* stream) {

@@ -40,16 +40,55 @@ struct WsLayout {
   int acc_bytes = 4;   // 4 (float) or 8 (double)
 };
 
+// Ragged batches (kvbm_options.seq_lens / cu_seqlens) as the kernels see them.
+// With neither, every sequence has the problem's N positions.
+struct Ragged {
+  const int32_t* lens = nullptr;  // [B] lengths (padded layout), or null
+  const int32_t* cu = nullptr;    // [B + 1] row offsets (packed layout of q), or null
+  long long total = 0;            // rows of the packed q (and k when k_packed)
+  bool k_packed = false;          // k packed like q (false: k is [B, H_kv, N, D])
+};
+
+// Where sequence b lives: its length n (<= N) and, per operand, the first row
+// and the batch coordinate of its rows (packed: row cu[b], batch 0; padded:
+// row 0, batch b).
+struct SeqView {
+  int n;
+  int q_row, q_b;
+  int k_row, k_b;
+};
+
+__host__ __device__ inline SeqView seq_view(const int32_t* lens, const int32_t* cu, bool k_packed, int b, int N) {
+  SeqView v{N, 0, b, 0, b};
+  if (cu != nullptr) {
+    const int s0 = cu[b];
+    const int len = cu[b + 1] - s0;
+    v.n = len < 0 ? 0 : (len < N ? len : N);
+    v.q_row = s0;
+    v.q_b = 0;
+    if (k_packed) {
+      v.k_row = s0;
+      v.k_b = 0;
+    }
+  } else if (lens != nullptr) {
+    const int len = lens[b];
+    v.n = len < 0 ? 0 : (len < N ? len : N);
+  }
+  return v;
+}
+
 // Host helpers (kvbm_api.cu).
 bool tc_path_enabled();  // kvbm_tc.cu
 int validate(const kvbm_problem* p);
 int select_path(const kvbm_problem* p, int device);
-WsLayout layout_for(const kvbm_problem* p, int path);
+// `rg` sizes the tf32 split copies of a packed q/k (path 2) by their rows.
+WsLayout layout_for(const kvbm_problem* p, int path, const Ragged* rg = nullptr);
 
 // Launchers (return a kvbm_status).
 struct LaunchOpts {
   void* mid_event = nullptr;  // cudaEvent_t recorded between pass 1 and pass 2 (or null)
   bool run_pass1 = true;      // false: lse2 is already in the workspace (kvbm_block_mass_lse)
+  Ragged rg;                  // ragged batch lengths / packed layout
 };
 int launch_simt(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws, cudaStream_t s,
                 const LaunchOpts& o);
@@ -57,9 +96,10 @@ int launch_tc(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws
               const LaunchOpts& o);
 // Writes a caller's natural-log row LSE into the workspace's lse2 layout of `L.path`.
 int launch_lse_import(const kvbm_problem* p, const WsLayout& L, const float* lse, const int64_t* lse_stride,
-                      void* ws, cudaStream_t s);
+                      void* ws, cudaStream_t s, const Ragged& rg);
+// per_sequence: mass_out is [B, num_blocks] (row b: the units of batch b in the range).
 int launch_reduce(const kvbm_problem* p, const WsLayout& L, void* mass_out, const void* ws,
-                  cudaStream_t s);
+                  cudaStream_t s, bool per_sequence);
 
 // Device error word: set when a bounded wait in a tcgen05 kernel gives up.
 int read_and_clear_device_error(cudaStream_t s, int* err);
@@ -67,8 +107,10 @@ int read_and_clear_device_error(cudaStream_t s, int* err);
 // Paged-KV input (kvbm_paged.cu): copies the key rows of batches
 // [b0, b0 + nb) x kv-heads [g0, g0 + ng) out of the paged cache into a dense
 // contiguous [nb, ng, N, D] array `out`.
+// Rows n >= the sequence's length (lens / cu, batch index b0 + b) are written
+// as zeros without reading the block table.
 int launch_page_gather(const kvbm_paged_kv* kv, int dtype, int b0, int g0, int nb, int ng, int N, int D,
-                       void* out, cudaStream_t s);
+                       const int32_t* lens, const int32_t* cu, void* out, cudaStream_t s);
 // Page error word: set when a block-table entry was outside [0, num_pages).
 int read_and_clear_page_error(cudaStream_t s, int* err);
 

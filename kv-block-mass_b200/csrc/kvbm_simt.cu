@@ -39,6 +39,9 @@ struct Args {
   Acc* lse;   // [U_sel*G, N]
   Acc* part;  // [U_sel, nchunk, N]
   int qchunk, nchunk;
+  const int32_t* lens;  // ragged lengths [B] or null
+  const int32_t* cu;    // packed row offsets [B+1] or null
+  int kpacked;          // k packed like q
 };
 
 template <typename In, typename Acc>
@@ -76,10 +79,11 @@ __device__ __forceinline__ float neg_inf<float>() { return -INFINITY; }
 template <>
 __device__ __forceinline__ double neg_inf<double>() { return -(double)INFINITY; }
 
-// keep(b, row, col): causal & key mask & query mask & pair mask (reference.py:83-87).
+// keep(b, row, col): causal & key mask & query mask & pair mask (reference.py:83-87),
+// for positions of a sequence of n <= N positions.
 template <typename Acc>
-__device__ __forceinline__ bool keep_at(const Args<Acc>& a, int b, int row, int col) {
-  if (row >= a.N || col >= a.N) return false;
+__device__ __forceinline__ bool keep_at(const Args<Acc>& a, int b, int n, int row, int col) {
+  if (row >= n || col >= n) return false;
   if (a.causal && col > row) return false;
   if (a.kmask && !a.kmask[b * a.kmb + col]) return false;
   if (a.qmask && !a.qmask[b * a.qmb + row]) return false;
@@ -146,17 +150,20 @@ __global__ void __launch_bounds__(NT) simt_lse_kernel(Args<Acc> a) {
   const int hidx = blockIdx.y;                         // (u - ub) * G + hh
   const int u = a.ub + hidx / a.G, hh = hidx % a.G;
   const int b = u / a.Hkv, g = u % a.Hkv, h = g * a.G + hh;
+  const SeqView sv = seq_view(a.lens, a.cu, a.kpacked != 0, b, a.N);
+  const int n = sv.n;
+  if (r0 >= n) return;  // past the sequence: pass 2 never reads these rows
 
-  stage_tile<In, Acc>(Qs, a.q, b * a.qs0 + h * a.qs1, a.qs2, a.qs3, r0, a.N, a.D);
+  stage_tile<In, Acc>(Qs, a.q, sv.q_b * a.qs0 + h * a.qs1 + sv.q_row * a.qs2, a.qs2, a.qs3, r0, n, a.D);
 
-  const int n_end = (a.causal && a.skip) ? min(a.N, r0 + BM) : a.N;
+  const int n_end = (a.causal && a.skip) ? min(n, r0 + BM) : n;
   Acc m[4], l[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) { m[i] = neg_inf<Acc>(); l[i] = Acc(0); }
 
   for (int n0 = 0; n0 < n_end; n0 += BN) {
     __syncthreads();
-    stage_tile<In, Acc>(Ks, a.k, b * a.ks0 + g * a.ks1, a.ks2, a.ks3, n0, a.N, a.D);
+    stage_tile<In, Acc>(Ks, a.k, sv.k_b * a.ks0 + g * a.ks1 + sv.k_row * a.ks2, a.ks2, a.ks3, n0, n, a.D);
     __syncthreads();
     Acc acc[4][4];
     tile_scores(Qs, Ks, a.D, tx, ty, acc);
@@ -168,7 +175,7 @@ __global__ void __launch_bounds__(NT) simt_lse_kernel(Args<Acc> a) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int col = n0 + tx * 4 + j;
-        t[j] = keep_at(a, b, row, col) ? acc[i][j] * a.C : neg_inf<Acc>();
+        t[j] = keep_at(a, b, n, row, col) ? acc[i][j] * a.C : neg_inf<Acc>();
         tmax = t[j] > tmax ? t[j] : tmax;
       }
       // Rescale only when the running max grows: a tile that is fully masked
@@ -200,7 +207,7 @@ __global__ void __launch_bounds__(NT) simt_lse_kernel(Args<Acc> a) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int row = r0 + ty * 4 + i;
-      if (row < a.N) {
+      if (row < n) {
         // Rows that keep no key get +inf: 2^(t - inf) = 0, so they contribute 0.
         a.lse[(long long)hidx * a.N + row] =
             (m[i] == neg_inf<Acc>()) ? -neg_inf<Acc>() : m[i] + acc_log2(l[i]);
@@ -223,8 +230,15 @@ __global__ void __launch_bounds__(NT) simt_mass_kernel(Args<Acc> a) {
   const int uu = blockIdx.z;
   const int u = a.ub + uu;
   const int b = u / a.Hkv, g = u % a.Hkv;
+  const SeqView sv = seq_view(a.lens, a.cu, a.kpacked != 0, b, a.N);
+  const int n = sv.n;
   const int qa = y * a.qchunk;
-  const int qb = min(a.N, qa + a.qchunk);
+  if (c0 >= n || qa >= n) {
+    // nothing of this sequence here: the reduce reads exact zeros
+    if (tid < BN && c0 + tid < a.N) a.part[((long long)uu * a.nchunk + y) * a.N + c0 + tid] = Acc(0);
+    return;
+  }
+  const int qb = min(n, qa + a.qchunk);
   // Causal: rows < c0 keep no key of this tile.  With causal_skip the CTA
   // starts at the first row tile that reaches c0 (tile boundaries stay those
   // of the unskipped loop, so the same non-zero terms add in the same order).
@@ -233,14 +247,14 @@ __global__ void __launch_bounds__(NT) simt_mass_kernel(Args<Acc> a) {
     if (qb - 1 < c0) return;  // whole chunk above the diagonal: nothing to add
     if (c0 > qa) rs = qa + ((c0 - qa) / BM) * BM;
   }
-  stage_tile<In, Acc>(Ks, a.k, b * a.ks0 + g * a.ks1, a.ks2, a.ks3, c0, a.N, a.D);
+  stage_tile<In, Acc>(Ks, a.k, sv.k_b * a.ks0 + g * a.ks1 + sv.k_row * a.ks2, a.ks2, a.ks3, c0, n, a.D);
   Acc cs[4] = {Acc(0), Acc(0), Acc(0), Acc(0)};
   for (int hh = 0; hh < a.G; ++hh) {
     const int h = g * a.G + hh;
     const Acc* lse_h = a.lse + (long long)(uu * a.G + hh) * a.N;
     for (int r0 = rs; r0 < qb; r0 += BM) {
       __syncthreads();
-      stage_tile<In, Acc>(Qs, a.q, b * a.qs0 + h * a.qs1, a.qs2, a.qs3, r0, qb, a.D);
+      stage_tile<In, Acc>(Qs, a.q, sv.q_b * a.qs0 + h * a.qs1 + sv.q_row * a.qs2, a.qs2, a.qs3, r0, qb, a.D);
       if (tid < BM) Ls[tid] = (r0 + tid < qb) ? lse_h[r0 + tid] : Acc(0);
       __syncthreads();
       Acc acc[4][4];
@@ -253,7 +267,7 @@ __global__ void __launch_bounds__(NT) simt_mass_kernel(Args<Acc> a) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int col = c0 + tx * 4 + j;
-          if (keep_at(a, b, row, col)) cs[j] += fast_exp2(acc[i][j] * a.C - L);
+          if (keep_at(a, b, n, row, col)) cs[j] += fast_exp2(acc[i][j] * a.C - L);
         }
       }
     }
@@ -267,7 +281,7 @@ __global__ void __launch_bounds__(NT) simt_mass_kernel(Args<Acc> a) {
 #pragma unroll
     for (int r = 0; r < 16; ++r) s += red[r * 64 + tid];
     const int col = c0 + tid;
-    if (col < a.N) a.part[((long long)uu * a.nchunk + y) * a.N + col] = s;
+    if (col < a.N) a.part[((long long)uu * a.nchunk + y) * a.N + col] = col < n ? s : Acc(0);
   }
 }
 
@@ -289,6 +303,9 @@ int launch_typed(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_
   a.part = reinterpret_cast<Acc*>(static_cast<char*>(ws) + L.part_off);
   a.qchunk = L.qchunk;
   a.nchunk = L.nchunk;
+  a.lens = o.rg.lens;
+  a.cu = o.rg.cu;
+  a.kpacked = o.rg.k_packed ? 1 : 0;
 
   const int U = p->unit_end - p->unit_begin;
   const size_t smem1 = size_t(2) * p->D * 64 * sizeof(Acc);
@@ -349,6 +366,42 @@ __global__ void __launch_bounds__(256) reduce_kernel(const Acc* part, Out* mass,
   }
 }
 
+// Per-sequence variant: mass[b][j] sums the units of batch b inside
+// [ub, ub + U) (none: 0), same order and skips as reduce_kernel.
+template <typename Acc, typename Out>
+__global__ void __launch_bounds__(256) reduce_seq_kernel(const Acc* part, Out* mass, int N, int bs, int nb,
+                                                         int ub, int U, int Hkv, int nchunk, int qchunk,
+                                                         int key_tile, int causal) {
+  __shared__ double warp_sums[8];
+  const int j = blockIdx.x, b = blockIdx.y;
+  const int cb = j * bs;
+  const int ce = min(N, cb + bs);
+  const int nk = ce - cb;
+  const int u0 = max(ub, b * Hkv), u1 = min(ub + U, (b + 1) * Hkv);
+  const long long total = u1 > u0 ? (long long)(u1 - u0) * nchunk * nk : 0;
+  double s = 0.0;
+  for (long long idx = threadIdx.x; idx < total; idx += blockDim.x) {
+    const int c = cb + (int)(idx % nk);
+    const long long rest = idx / nk;
+    const int y = (int)(rest % nchunk);
+    const long long uu = (u0 - ub) + rest / nchunk;
+    if (causal) {
+      const int c0 = (c / key_tile) * key_tile;
+      if ((long long)(y + 1) * qchunk - 1 < c0) continue;
+    }
+    s += (double)part[(uu * nchunk + y) * N + c];
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if ((threadIdx.x & 31) == 0) warp_sums[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += warp_sums[w];
+    mass[(long long)b * nb + j] = static_cast<Out>(t);
+  }
+}
+
 }  // namespace
 
 int launch_simt(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws,
@@ -372,17 +425,19 @@ int launch_simt(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* 
 template <typename Acc, bool kNegated>
 __global__ void lse_import_kernel(const float* lse, long long s0, long long s1, long long s2, Acc* out, int N,
                                   int Nrow, int G, int Hkv, int ub, long long rows_total, const uint8_t* qmask,
-                                  long long qmb) {
+                                  long long qmb, const int32_t* lens, const int32_t* cu) {
   const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   if (idx >= rows_total) return;
   const int i = (int)(idx % Nrow);
   const long long hidx = idx / Nrow;  // (u - ub) * G + hh
   const int u = ub + (int)(hidx / G), hh = (int)(hidx % G);
   const int b = u / Hkv, h = (u % Hkv) * G + hh;
-  bool dead = i >= N;
+  // a packed batch indexes its LSE like q: row cu[b] + i of [H_q, total_tokens]
+  const SeqView sv = seq_view(lens, cu, false, b, N);
+  bool dead = i >= sv.n;
   double v = 0.0;
   if (!dead) {
-    v = (double)lse[b * s0 + h * s1 + (long long)i * s2];
+    v = (double)lse[sv.q_b * s0 + h * s1 + ((long long)sv.q_row + i) * s2];
     dead = !isfinite(v) || (qmask != nullptr && qmask[b * qmb + i] == 0);
   }
   const double l2 = v * kLog2e;
@@ -393,7 +448,7 @@ __global__ void lse_import_kernel(const float* lse, long long s0, long long s1, 
 }
 
 int launch_lse_import(const kvbm_problem* p, const WsLayout& L, const float* lse, const int64_t* st, void* ws,
-                      cudaStream_t s) {
+                      cudaStream_t s, const Ragged& rg) {
   const int U = p->unit_end - p->unit_begin, G = p->Hq / p->Hkv;
   const int Nrow = L.path >= 1 ? (p->N + kTcTile - 1) / kTcTile * kTcTile : p->N;
   const long long rows = (long long)U * G * Nrow;
@@ -403,24 +458,36 @@ int launch_lse_import(const kvbm_problem* p, const WsLayout& L, const float* lse
   if (L.path >= 1) {
     lse_import_kernel<float, true><<<(unsigned)blocks, threads, 0, s>>>(
         lse, st[0], st[1], st[2], reinterpret_cast<float*>(base), p->N, Nrow, G, p->Hkv, p->unit_begin, rows,
-        p->query_mask, p->query_mask_bstride);
+        p->query_mask, p->query_mask_bstride, rg.lens, rg.cu);
   } else if (p->dtype == KVBM_F64) {
     lse_import_kernel<double, false><<<(unsigned)blocks, threads, 0, s>>>(
         lse, st[0], st[1], st[2], reinterpret_cast<double*>(base), p->N, Nrow, G, p->Hkv, p->unit_begin, rows,
-        p->query_mask, p->query_mask_bstride);
+        p->query_mask, p->query_mask_bstride, rg.lens, rg.cu);
   } else {
     lse_import_kernel<float, false><<<(unsigned)blocks, threads, 0, s>>>(
         lse, st[0], st[1], st[2], reinterpret_cast<float*>(base), p->N, Nrow, G, p->Hkv, p->unit_begin, rows,
-        p->query_mask, p->query_mask_bstride);
+        p->query_mask, p->query_mask_bstride, rg.lens, rg.cu);
   }
   return cudaGetLastError() == cudaSuccess ? KVBM_OK : KVBM_ERR_CUDA;
 }
 
 int launch_reduce(const kvbm_problem* p, const WsLayout& L, void* mass_out, const void* ws,
-                  cudaStream_t s) {
+                  cudaStream_t s, bool per_sequence) {
   const int nb = (int)kvbm_num_blocks(p->N, p->block_size);
   const int U = p->unit_end - p->unit_begin;
   const char* base = static_cast<const char*>(ws) + L.part_off;
+  if (per_sequence) {
+    const dim3 grid(nb, p->B);
+    if (p->dtype == KVBM_F64)
+      reduce_seq_kernel<double, double><<<grid, 256, 0, s>>>(
+          reinterpret_cast<const double*>(base), static_cast<double*>(mass_out), p->N, p->block_size, nb,
+          p->unit_begin, U, p->Hkv, L.nchunk, L.qchunk, L.key_tile, p->causal != 0);
+    else
+      reduce_seq_kernel<float, float><<<grid, 256, 0, s>>>(
+          reinterpret_cast<const float*>(base), static_cast<float*>(mass_out), p->N, p->block_size, nb,
+          p->unit_begin, U, p->Hkv, L.nchunk, L.qchunk, L.key_tile, p->causal != 0);
+    return cudaGetLastError() == cudaSuccess ? KVBM_OK : KVBM_ERR_CUDA;
+  }
   if (p->dtype == KVBM_F64) {
     reduce_kernel<double, double><<<nb, 256, 0, s>>>(reinterpret_cast<const double*>(base),
                                                      static_cast<double*>(mass_out), p->N,

@@ -65,6 +65,9 @@ struct TcArgs {
   int W;                   // words per bit row (Npad / 32)
   int qchunk, nchunk;
   int per_unit;            // pass-2 CTAs per unit (sum of keys_in_chunk over chunks)
+  const int32_t* lens;     // ragged lengths [B] or null
+  const int32_t* cu;       // packed row offsets [B+1] or null
+  int kpacked;             // k packed like q
 };
 
 // Key tiles of query chunk y that hold a kept pair: with causal_skip only
@@ -251,7 +254,7 @@ __device__ __forceinline__ void merge_ml(float& m, float& l, float mo, float lo)
 // ============================================================ pass 1: lse2
 // grid (U_sel * G, ceil(N / 128)); blockIdx.y counts query tiles from the
 // last (longest under causal_skip) to the first.
-template <int D, Op kOp, int kMask>
+template <int D, Op kOp, int kMask, bool kRagged>
 __global__ void __launch_bounds__(kThreads, 2)
     tc_lse_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tq2,
                   const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tk2, TcArgs a) {
@@ -274,8 +277,13 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int hidx = blockIdx.x;
   const int u = a.ub + hidx / a.G, hh = hidx % a.G;
   const int b = u / a.Hkv, g = u % a.Hkv, h = g * a.G + hh;
-  const int ntiles = (a.N + TILE - 1) / TILE;
-  const int qt = ntiles - 1 - (int)blockIdx.y;
+  // kRagged: per-sequence lengths / packed rows (kvbm_options); otherwise
+  // every sequence has a.N positions at rows [0, a.N) of batch entry b
+  const SeqView sv = kRagged ? seq_view(a.lens, a.cu, a.kpacked != 0, b, a.N) : SeqView{a.N, 0, b, 0, b};
+  const int N = sv.n;  // positions of this sequence
+  const int qt = (a.N + TILE - 1) / TILE - 1 - (int)blockIdx.y;
+  const int ntiles = (N + TILE - 1) / TILE;
+  if (qt >= ntiles) return;  // past the sequence: pass 2 never reads these rows
   const int r0 = qt * TILE;
   const int nkt = (a.causal && a.skip) ? min(ntiles, qt + 1) : ntiles;
 
@@ -306,13 +314,13 @@ __global__ void __launch_bounds__(kThreads, 2)
       prefetch_tmap(&tq);
       prefetch_tmap(&tk);
       mbar_arrive_expect_tx(q_full, TB);
-      load_operand<D, kOp>(q_tile, &tq, &tq2, q_full, r0, h, b);
+      load_operand<D, kOp>(q_tile, &tq, &tq2, q_full, sv.q_row + r0, h, sv.q_b);
       int issued = 0;
       for (int j = 0; j < nkt; ++j) {
         const int s = j % kStages, n = j / kStages;
         if (n > 0 && !mbar_wait(&k_empty[s], (n - 1) & 1, abort_flag)) break;
         mbar_arrive_expect_tx(&k_full[s], TB);
-        load_operand<D, kOp>(k_ring + s * TB, &tk, &tk2, &k_full[s], j * TILE, g, b);
+        load_operand<D, kOp>(k_ring + s * TB, &tk, &tk2, &k_full[s], sv.k_row + j * TILE, g, sv.k_b);
         issued = j + 1;
       }
       // Do not leave while our copies are in flight.
@@ -368,13 +376,13 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int qd = 0; qd < 2; ++qd) {
           const int col = c0 + qd * 32 + lane;
-          kw[qd] = __ballot_sync(0xffffffffu, col < a.N && kmask[col] != 0);
+          kw[qd] = __ballot_sync(0xffffffffu, col < N && kmask[col] != 0);
         }
       }
-      const bool need_mask = kMask != kMaskNone || (c0 + HALF > a.N) || (a.causal && c0 + HALF - 1 > r0);
+      const bool need_mask = kMask != kMaskNone || (c0 + HALF > N) || (a.causal && c0 + HALF - 1 > r0);
       if (need_mask) {
         const int lim_causal = a.causal ? row - c0 : HALF - 1;  // keep col_local <= row - c0
-        const int lim = min(lim_causal, a.N - 1 - c0);          // and col < N
+        const int lim = min(lim_causal, N - 1 - c0);            // and col < N
 #pragma unroll
         for (int c = 0; c < HALF; ++c) {
           const bool keep = (c <= lim) && ((kw[c >> 5] >> (c & 31)) & 1u);
@@ -399,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (hf == 0) {
       const float2 o = merge[rl];
       merge_ml(m, l, o.x, o.y);
-      bool dead = (m == -INFINITY) || row >= a.N;
+      bool dead = (m == -INFINITY) || row >= N;
       if (!dead && a.qmask != nullptr) dead = a.qmask[b * a.qmb + row] == 0;
       // Stored negated (pass 2 adds it): rows that keep no key, and padding
       // rows, get -inf, so 2^(t - lse2) = 0 for them.
@@ -421,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 // the last (most key tiles under causal_skip) to the first, and all key tiles
 // of a chunk are adjacent, so the CTAs resident at one time share that
 // chunk's query tiles in L2.
-template <int D, Op kOp, int kMask>
+template <int D, Op kOp, int kMask, bool kRagged>
 __global__ void __launch_bounds__(kThreads, 2)
     tc_mass_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tq2,
                    const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tk2, TcArgs a) {
@@ -453,9 +461,17 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   const int u = a.ub + uu;
   const int b = u / a.Hkv, g = u % a.Hkv;
+  const SeqView sv = kRagged ? seq_view(a.lens, a.cu, a.kpacked != 0, b, a.N) : SeqView{a.N, 0, b, 0, b};
+  const int N = sv.n;  // positions of this sequence
   const int c0 = kt * TILE;
   const int qa = y * a.qchunk;
-  const int qb = min(a.N, qa + a.qchunk);
+  if (kRagged && (c0 >= N || qa >= N)) {
+    // nothing of this sequence here: the reduce reads exact zeros
+    for (int i = threadIdx.x; i < TILE; i += blockDim.x)
+      if (c0 + i < a.N) a.part[((long long)uu * a.nchunk + y) * a.N + c0 + i] = 0.f;
+    return;
+  }
+  const int qb = min(N, qa + a.qchunk);
   int rs = qa;
   if (a.causal && a.skip) {
     if (qb - 1 < c0) return;  // chunk entirely above the diagonal: nothing kept
@@ -495,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       prefetch_tmap(&tq);
       prefetch_tmap(&tk);
       mbar_arrive_expect_tx(k_full, TB);
-      load_operand<D, kOp>(k_tile, &tk, &tk2, k_full, c0, g, b);
+      load_operand<D, kOp>(k_tile, &tk, &tk2, k_full, sv.k_row + c0, g, sv.k_b);
       int issued = 0;
       for (int j = 0; j < J; ++j) {
         const int s = j % kStages, n = j / kStages;
@@ -506,7 +522,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int r = rs + (j - hh * nqt) * TILE;
         const int h = g * a.G + hh;
         mbar_arrive_expect_tx(&q_full[s], TB);
-        load_operand<D, kOp>(q_ring + s * TB, &tq, &tq2, &q_full[s], r, h, b);
+        load_operand<D, kOp>(q_ring + s * TB, &tq, &tq2, &q_full[s], sv.q_row + r, h, sv.q_b);
         mbar_arrive_expect_tx(&l_full[t], LB);
         bulk_load(l_ring + t * TILE, a.lse + (long long)(uu * a.G + hh) * a.Npad + r, LB, &l_full[t]);
         issued = j + 1;
@@ -546,6 +562,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t trow = tmem + ((uint32_t)(sub * 32) << 16) + hf * HALF;
     const float C = a.C;
     const uint32_t* pcol = kMask == kMaskPairs ? a.pcol + b * a.pb + (long long)key * a.W : nullptr;
+    // kRagged: the sequence length is re-read from shared memory per tile
+    // rather than held in a register across the loop (register budget).
+    __shared__ int s_len;
+    if (kRagged && threadIdx.x == 64) s_len = N;
+    if (kRagged) exp_bar_sync();
+    const volatile int* len_v = &s_len;
     float2 acc = make_float2(0.f, 0.f);
     for (int j = 0; j < J; ++j) {
       const int buf = j & 1, t = j % kLStages;
@@ -568,13 +590,25 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int r = rs + (j - hh * nqt) * TILE;
       const float* nL = l_ring + t * TILE + hf * HALF;  // -lse2 of this half's 64 query rows
       constexpr bool kB = kMask == kMaskPairs;
-      if (!a.causal || r > c0) {
-        acc = col_sum_exp2<false, kB>(v, C, nL, 0, acc, pw);  // every pair kept by causality
-      } else if (r == c0) {
-        // diagonal: query r + hf*64 + c keeps key c0 + rl iff hf*64 + c >= rl
-        acc = col_sum_exp2<true, kB>(v, C, nL, rl - hf * HALF, acc, pw);
-      }
+      // On the diagonal, query r + hf*64 + c keeps key c0 + rl iff hf*64 + c >= rl.
       // r < c0 (only without causal_skip): every pair is above the diagonal, adds 0.
+      // kRagged: query columns at or past the sequence's end contribute 0
+      // whatever their scores (their rows may hold another sequence's, or
+      // undefined, values).  Otherwise those rows are the TMA's zero fill
+      // past N, whose lse2 is -inf.
+      if (!a.causal || r >= c0) {
+        if (kRagged) {
+          const int keep_to = *len_v - r - hf * HALF;
+          if (keep_to < HALF) {
+#pragma unroll
+            for (int c = 0; c < HALF; ++c) v[c] = c < keep_to ? v[c] : -INFINITY;
+          }
+        }
+        if (a.causal && r == c0)
+          acc = col_sum_exp2<true, kB>(v, C, nL, rl - hf * HALF, acc, pw);
+        else
+          acc = col_sum_exp2<false, kB>(v, C, nL, 0, acc, pw);  // every pair kept
+      }
       mbar_arrive(&l_empty[t]);
     }
     // Merge the two query halves of each key (fixed order: lower half first).
@@ -583,7 +617,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (hf == 0 && key < a.N) {
       const float2 o = merge[rl];
       float total = (acc.x + acc.y) + (o.x + o.y);
-      if (kMask == kMaskKeys && a.kmask[b * a.kmb + key] == 0) total = 0.f;
+      if (kRagged && key >= *len_v) total = 0.f;  // past the sequence's end
+      else if (kMask == kMaskKeys && a.kmask[b * a.kmb + key] == 0) total = 0.f;
       a.part[((long long)uu * a.nchunk + y) * a.N + key] = total;
     }
   }
@@ -639,17 +674,20 @@ bool make_map(CUtensorMap* map, const void* base, CUtensorMapDataType type, int 
 }
 
 // fp32 operand -> contiguous [B, H, N, D] tf32 pair: hi = tf32(x), lo = x - hi
-// (exact in fp32).  One launch splits q (first q_elems elements) and k.
+// (exact in fp32).  One launch splits q (first q_elems elements; rows Nq per
+// head) and k (rows Nk per head); a packed operand is one batch entry of
+// total_tokens rows.
 __global__ void split_tf32_kernel(const float* q, long long q0, long long q1, long long q2, long long q3,
                                   int Hq, const float* k, long long k0, long long k1, long long k2,
-                                  long long k3, int Hkv, int N, int D, long long q_elems, long long k_elems,
-                                  float* q_hi, float* q_lo, float* k_hi, float* k_lo) {
+                                  long long k3, int Hkv, int Nq, int Nk, int D, long long q_elems,
+                                  long long k_elems, float* q_hi, float* q_lo, float* k_hi, float* k_lo) {
   const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   if (idx >= q_elems + k_elems) return;
   const bool is_q = idx < q_elems;
   const long long e = is_q ? idx : idx - q_elems;
   const int d = (int)(e % D);
   const long long r = e / D;
+  const int N = is_q ? Nq : Nk;
   const int n = (int)(r % N);
   const long long bh = r / N;
   const int H = is_q ? Hq : Hkv;
@@ -705,31 +743,36 @@ constexpr size_t smem_mass() {
          16 * kLStages;
 }
 
-template <int D, Op kOp, int kMask>
+template <int D, Op kOp, int kMask, bool kRagged>
 int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s, const LaunchOpts& o) {
   CUtensorMap tq, tq2, tk, tk2;
+  // A packed operand is one batch entry of total_tokens rows; sequence b
+  // starts at row cu[b] (TMA coordinates from seq_view).
+  const Ragged& rg = o.rg;
+  const int Bq = rg.cu ? 1 : p->B, Nq = rg.cu ? (int)rg.total : p->N;
+  const int Bk = rg.k_packed ? 1 : p->B, Nk = rg.k_packed ? (int)rg.total : p->N;
   if constexpr (kOp == Op::TF32X3) {
     // split q/k into tf32 hi/lo pairs in the workspace, then map those
     float* base = reinterpret_cast<float*>(static_cast<char*>(ws) + L.split_off);
-    const long long qe = (long long)p->B * p->Hq * p->N * D, ke = (long long)p->B * p->Hkv * p->N * D;
+    const long long qe = (long long)Bq * p->Hq * Nq * D, ke = (long long)Bk * p->Hkv * Nk * D;
     float *q_hi = base, *q_lo = base + qe, *k_hi = base + 2 * qe, *k_lo = base + 2 * qe + ke;
     const long long total = qe + ke;
     split_tf32_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(
         static_cast<const float*>(p->q), p->q_stride[0], p->q_stride[1], p->q_stride[2], p->q_stride[3], p->Hq,
         static_cast<const float*>(p->k), p->k_stride[0], p->k_stride[1], p->k_stride[2], p->k_stride[3], p->Hkv,
-        p->N, D, qe, ke, q_hi, q_lo, k_hi, k_lo);
+        Nq, Nk, D, qe, ke, q_hi, q_lo, k_hi, k_lo);
     if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
-    const int64_t qs[4] = {(int64_t)p->Hq * p->N * D, (int64_t)p->N * D, D, 1};
-    const int64_t ks[4] = {(int64_t)p->Hkv * p->N * D, (int64_t)p->N * D, D, 1};
+    const int64_t qs[4] = {(int64_t)p->Hq * Nq * D, (int64_t)Nq * D, D, 1};
+    const int64_t ks[4] = {(int64_t)p->Hkv * Nk * D, (int64_t)Nk * D, D, 1};
     const CUtensorMapDataType t = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-    if (!make_map(&tq, q_hi, t, 4, p->B, p->Hq, p->N, D, qs) || !make_map(&tq2, q_lo, t, 4, p->B, p->Hq, p->N, D, qs) ||
-        !make_map(&tk, k_hi, t, 4, p->B, p->Hkv, p->N, D, ks) || !make_map(&tk2, k_lo, t, 4, p->B, p->Hkv, p->N, D, ks))
+    if (!make_map(&tq, q_hi, t, 4, Bq, p->Hq, Nq, D, qs) || !make_map(&tq2, q_lo, t, 4, Bq, p->Hq, Nq, D, qs) ||
+        !make_map(&tk, k_hi, t, 4, Bk, p->Hkv, Nk, D, ks) || !make_map(&tk2, k_lo, t, 4, Bk, p->Hkv, Nk, D, ks))
       return KVBM_ERR_CUDA;
   } else {
     const CUtensorMapDataType t =
         kOp == Op::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    if (!make_map(&tq, p->q, t, 2, p->B, p->Hq, p->N, D, p->q_stride) ||
-        !make_map(&tk, p->k, t, 2, p->B, p->Hkv, p->N, D, p->k_stride))
+    if (!make_map(&tq, p->q, t, 2, Bq, p->Hq, Nq, D, p->q_stride) ||
+        !make_map(&tk, p->k, t, 2, Bk, p->Hkv, Nk, D, p->k_stride))
       return KVBM_ERR_CUDA;
     tq2 = tq;
     tk2 = tk;
@@ -756,6 +799,9 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
   a.prow = a.pcol = nullptr;
   a.pb = 0;
   a.W = a.Npad / 32;
+  a.lens = rg.lens;
+  a.cu = rg.cu;
+  a.kpacked = rg.k_packed ? 1 : 0;
   if (kMask == kMaskPairs) {
     uint32_t* bits = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + L.bits_off);
     const long long words = (long long)L.bits_batches * a.Npad * a.W;
@@ -775,8 +821,8 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
 
   const size_t sm1 = smem_lse<D, kOp>() > (size_t)kMinSmem ? smem_lse<D, kOp>() : (size_t)kMinSmem;
   const size_t sm2 = smem_mass<D, kOp>() > (size_t)kMinSmem ? smem_mass<D, kOp>() : (size_t)kMinSmem;
-  auto k1 = tc_lse_kernel<D, kOp, kMask>;
-  auto k2 = tc_mass_kernel<D, kOp, kMask>;
+  auto k1 = tc_lse_kernel<D, kOp, kMask, kRagged>;
+  auto k2 = tc_mass_kernel<D, kOp, kMask, kRagged>;
   if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1) != cudaSuccess ||
       cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2) != cudaSuccess)
     return KVBM_ERR_CUDA;
@@ -793,9 +839,14 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
 
 template <int D, Op kOp>
 int launch_km(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s, const LaunchOpts& o) {
-  if (p->pair_mask != nullptr) return launch_variant<D, kOp, kMaskPairs>(p, L, ws, s, o);
-  return p->key_mask != nullptr ? launch_variant<D, kOp, kMaskKeys>(p, L, ws, s, o)
-                                : launch_variant<D, kOp, kMaskNone>(p, L, ws, s, o);
+  if (o.rg.lens != nullptr || o.rg.cu != nullptr) {
+    if (p->pair_mask != nullptr) return launch_variant<D, kOp, kMaskPairs, true>(p, L, ws, s, o);
+    return p->key_mask != nullptr ? launch_variant<D, kOp, kMaskKeys, true>(p, L, ws, s, o)
+                                  : launch_variant<D, kOp, kMaskNone, true>(p, L, ws, s, o);
+  }
+  if (p->pair_mask != nullptr) return launch_variant<D, kOp, kMaskPairs, false>(p, L, ws, s, o);
+  return p->key_mask != nullptr ? launch_variant<D, kOp, kMaskKeys, false>(p, L, ws, s, o)
+                                : launch_variant<D, kOp, kMaskNone, false>(p, L, ws, s, o);
 }
 
 }  // namespace

@@ -14,13 +14,16 @@ from .ops import (  # noqa: F401
     block_mass_b200,
     block_mass_paged,
     block_mass_triton,
+    block_mass_varlen,
     check_device_errors,
     kernel_path,
     launches_per_call,
     make_paged_problem,
     make_problem,
+    make_varlen_problem,
     paged_workspace_bytes,
     run_paged,
+    run_prepared,
     workspace_bytes,
 )
 from .workloads import WORKLOADS, Workload, make_inputs, pairs  # noqa: F401
@@ -30,6 +33,9 @@ __all__ = [
     "block_mass_triton",
     "block_mass",
     "block_mass_paged",
+    "block_mass_varlen",
+    "make_varlen_problem",
+    "run_prepared",
     "make_paged_problem",
     "paged_workspace_bytes",
     "run_paged",

@@ -48,6 +48,9 @@ EXPORTED = [
     "kvbm_validate_paged",
     "kvbm_paged_workspace_bytes",
     "kvbm_block_mass_paged",
+    "kvbm_validate_ex",
+    "kvbm_workspace_bytes_ex",
+    "kvbm_block_mass_ex",
 ]
 
 
@@ -92,6 +95,21 @@ class PagedKV(ctypes.Structure):
         ("block_table", ctypes.c_void_p),
         ("block_table_stride", ctypes.c_int64),
         ("max_pages", ctypes.c_int32),
+    ]
+
+
+class Options(ctypes.Structure):
+    """Mirror of ``struct kvbm_options``."""
+
+    _fields_ = [
+        ("lse", ctypes.c_void_p),
+        ("lse_stride", ctypes.c_int64 * 3),
+        ("paged", ctypes.POINTER(PagedKV)),
+        ("seq_lens", ctypes.c_void_p),
+        ("cu_seqlens", ctypes.c_void_p),
+        ("total_tokens", ctypes.c_int64),
+        ("per_sequence", ctypes.c_int32),
+        ("events", ctypes.POINTER(ctypes.c_void_p)),
     ]
 
 
@@ -148,6 +166,14 @@ def load() -> ctypes.CDLL:
     lib.kvbm_block_mass_paged.restype = ctypes.c_int
     lib.kvbm_block_mass_paged.argtypes = [P, K, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64), ctypes.c_void_p,
                                           ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    # Every option combined (paged / ragged / packed / LSE input / per-sequence output).
+    O = ctypes.POINTER(Options)
+    lib.kvbm_validate_ex.restype = ctypes.c_int
+    lib.kvbm_validate_ex.argtypes = [P, O]
+    lib.kvbm_workspace_bytes_ex.restype = ctypes.c_size_t
+    lib.kvbm_workspace_bytes_ex.argtypes = [P, O]
+    lib.kvbm_block_mass_ex.restype = ctypes.c_int
+    lib.kvbm_block_mass_ex.argtypes = [P, O, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
     lib.kvbm_check_device_errors.restype = ctypes.c_int
     lib.kvbm_check_device_errors.argtypes = [ctypes.c_void_p]
     if lib.kvbm_abi_version() != 1:

@@ -25,7 +25,8 @@ from . import _lib
 
 __all__ = ["block_mass_b200", "block_mass_triton", "block_mass", "kernel_path", "make_problem",
            "workspace_bytes", "launches_per_call", "block_mass_paged", "make_paged_problem",
-           "paged_workspace_bytes", "run_paged", "check_device_errors"]
+           "paged_workspace_bytes", "run_paged", "check_device_errors", "block_mass_varlen",
+           "make_varlen_problem", "run_prepared"]
 
 _DTYPES = {
     torch.float32: _lib.KVBM_F32,
@@ -57,57 +58,56 @@ def _as_mask(m: torch.Tensor, device) -> torch.Tensor:
 
 
 class _Prepared:
-    """A filled ``kvbm_problem`` plus the tensors it points into (kept alive)."""
+    """A filled ``kvbm_problem`` (+ ``kvbm_options``) and the tensors they point into."""
 
     def __init__(self, prob, keep, out_dtype, nb):
         self.prob = prob
         self.keep = keep
         self.out_dtype = out_dtype
         self.nb = nb
+        self.opts = None          # _lib.Options when any extension is used
+        self.per_sequence = False
+        self.packed = False       # q rows addressed through cu_seqlens
+        self.total = 0            # rows of a packed q
+
+    @property
+    def out_shape(self):
+        return (self.prob.B, self.nb) if self.per_sequence else (self.nb,)
+
+    def options(self) -> "_lib.Options":
+        if self.opts is None:
+            self.opts = _lib.Options()
+        return self.opts
 
 
-def make_problem(q, k, attn_mask=None, causal=False, block_size=64, scale=None,
-                 causal_skip=True, query_mask=None, units=None) -> _Prepared:
-    """Validate arguments and build the C ``kvbm_problem`` for ``q``/``k``.
+def _int32_on(t: torch.Tensor, dev, name: str) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor) or t.dim() != 1:
+        raise ValueError(f"{name} must be a 1-D integer tensor")
+    if t.dtype.is_floating_point or t.dtype == torch.bool:
+        raise ValueError(f"{name} must hold integers, got {t.dtype}")
+    return t.to(device=dev, dtype=torch.int32).contiguous()
 
-    Mask shapes (True = keep; combined with ``causal`` by AND):
-    ``attn_mask``: ``[N]`` key mask, ``[N, N]`` pair mask (the reference's two
-    forms), ``[B|1, 1, N]`` per-batch key mask, ``[B|1, N, N]`` per-batch pair
-    mask; ``query_mask``: ``[N]`` or ``[B, N]`` rows to keep (a dropped row
-    contributes exactly 0, as a pair-mask row that keeps nothing would).
-    """
-    if not (isinstance(q, torch.Tensor) and isinstance(k, torch.Tensor)):
-        raise TypeError("q and k must be torch tensors")
-    if q.dim() != 4 or k.dim() != 4:
-        raise ValueError(f"q and k must be 4-D [B, H, N, D], got {tuple(q.shape)} and {tuple(k.shape)}")
-    B, Hq, N, D = q.shape
-    if k.shape[0] != B or k.shape[2] != N or k.shape[3] != D:
-        raise ValueError(f"k shape {tuple(k.shape)} does not match q shape {tuple(q.shape)}")
-    Hkv = k.shape[1]
+
+def _fill_problem(q_ptr, q_strides, k_ptr, k_strides, dtype, B, Hq, Hkv, N, D, dev, keep, attn_mask, causal,
+                  block_size, scale, causal_skip, query_mask, units) -> _Prepared:
+    """Shared tail of the make_*_problem functions: masks, scalars, validation."""
     if Hkv == 0 or Hq % Hkv != 0:
         raise ValueError(f"GQA requires H_q % H_kv == 0, got H_q={Hq}, H_kv={Hkv}")
-    if q.device != k.device:
-        raise ValueError(f"q and k are on different devices ({q.device}, {k.device})")
-    if q.dtype != k.dtype:
-        common = torch.promote_types(q.dtype, k.dtype)
-        q, k = q.to(common), k.to(common)
-    if q.dtype not in _DTYPES:
-        raise ValueError(f"unsupported dtype {q.dtype}; expected float32, bfloat16, float16 or float64")
+    if dtype not in _DTYPES:
+        raise ValueError(f"unsupported dtype {dtype}; expected float32, bfloat16, float16 or float64")
     if N == 0:
         raise ValueError("N must be >= 1")
     if block_size is None or int(block_size) < 1:
         raise ValueError("block_size must be >= 1")
     if scale is None:
         scale = 1.0 / D ** 0.5
-    dev = q.device
-    keep = [q, k]
     prob = _lib.Problem()
-    prob.q = q.data_ptr()
-    prob.k = k.data_ptr()
+    prob.q = q_ptr
+    prob.k = k_ptr
     for i in range(4):
-        prob.q_stride[i] = q.stride(i)
-        prob.k_stride[i] = k.stride(i)
-    prob.dtype = _DTYPES[q.dtype]
+        prob.q_stride[i] = q_strides[i]
+        prob.k_stride[i] = k_strides[i]
+    prob.dtype = _DTYPES[dtype]
     prob.B, prob.Hq, prob.Hkv, prob.N, prob.D = B, Hq, Hkv, N, D
 
     if attn_mask is not None:
@@ -158,21 +158,137 @@ def make_problem(q, k, attn_mask=None, causal=False, block_size=64, scale=None,
     if code != _lib.KVBM_OK:
         _raise(code, prob)
     nb = (N + int(block_size) - 1) // int(block_size)
-    out_dtype = torch.float64 if q.dtype == torch.float64 else torch.float32
+    out_dtype = torch.float64 if dtype == torch.float64 else torch.float32
     return _Prepared(prob, keep, out_dtype, nb)
 
 
+def _set_ragged(prep: _Prepared, dev, seq_lens=None, cu_seqlens=None, total=0, per_sequence=False):
+    if seq_lens is not None and cu_seqlens is not None:
+        raise ValueError("seq_lens and cu_seqlens are exclusive")
+    B = prep.prob.B
+    if seq_lens is not None:
+        lens = _int32_on(seq_lens, dev, "seq_lens")
+        if lens.shape[0] != B:
+            raise ValueError(f"seq_lens must have B={B} entries, got {lens.shape[0]}")
+        prep.keep.append(lens)
+        prep.options().seq_lens = lens.data_ptr()
+    if cu_seqlens is not None:
+        cu = _int32_on(cu_seqlens, dev, "cu_seqlens")
+        if cu.shape[0] != B + 1:
+            raise ValueError(f"cu_seqlens must have B + 1 = {B + 1} entries, got {cu.shape[0]}")
+        prep.keep.append(cu)
+        o = prep.options()
+        o.cu_seqlens = cu.data_ptr()
+        o.total_tokens = int(total)
+        prep.packed = True
+        prep.total = int(total)
+    if per_sequence:
+        prep.per_sequence = True
+        prep.options().per_sequence = 1
+
+
+def _validate_ex(prep: _Prepared):
+    if prep.opts is None:
+        return
+    code = _lib.load().kvbm_validate_ex(ctypes.byref(prep.prob), ctypes.byref(prep.opts))
+    if code != _lib.KVBM_OK:
+        _raise(code, prep.prob)
+
+
+def make_problem(q, k, attn_mask=None, causal=False, block_size=64, scale=None,
+                 causal_skip=True, query_mask=None, units=None, seq_lens=None,
+                 per_sequence=False) -> _Prepared:
+    """Validate arguments and build the C ``kvbm_problem`` for ``q``/``k``.
+
+    Mask shapes (True = keep; combined with ``causal`` by AND):
+    ``attn_mask``: ``[N]`` key mask, ``[N, N]`` pair mask (the reference's two
+    forms), ``[B|1, 1, N]`` per-batch key mask, ``[B|1, N, N]`` per-batch pair
+    mask; ``query_mask``: ``[N]`` or ``[B, N]`` rows to keep (a dropped row
+    contributes exactly 0, as a pair-mask row that keeps nothing would).
+    ``seq_lens`` ``[B]``: sequence ``b`` is its first ``seq_lens[b] <= N``
+    positions (ragged batch in the padded layout); ``per_sequence``: the
+    output is ``[B, num_blocks]``, one row per sequence.
+    """
+    if not (isinstance(q, torch.Tensor) and isinstance(k, torch.Tensor)):
+        raise TypeError("q and k must be torch tensors")
+    if q.dim() != 4 or k.dim() != 4:
+        raise ValueError(f"q and k must be 4-D [B, H, N, D], got {tuple(q.shape)} and {tuple(k.shape)}")
+    B, Hq, N, D = q.shape
+    if k.shape[0] != B or k.shape[2] != N or k.shape[3] != D:
+        raise ValueError(f"k shape {tuple(k.shape)} does not match q shape {tuple(q.shape)}")
+    Hkv = k.shape[1]
+    if Hkv == 0 or Hq % Hkv != 0:
+        raise ValueError(f"GQA requires H_q % H_kv == 0, got H_q={Hq}, H_kv={Hkv}")
+    if q.device != k.device:
+        raise ValueError(f"q and k are on different devices ({q.device}, {k.device})")
+    if q.dtype != k.dtype:
+        common = torch.promote_types(q.dtype, k.dtype)
+        q, k = q.to(common), k.to(common)
+    prep = _fill_problem(q.data_ptr(), q.stride(), k.data_ptr(), k.stride(), q.dtype, B, Hq, Hkv, N, D,
+                         q.device, [q, k], attn_mask, causal, block_size, scale, causal_skip, query_mask, units)
+    _set_ragged(prep, q.device, seq_lens=seq_lens, per_sequence=per_sequence)
+    _validate_ex(prep)
+    return prep
+
+
+def make_varlen_problem(q, k, cu_seqlens, max_seqlen=None, attn_mask=None, causal=False, block_size=64,
+                        scale=None, causal_skip=True, query_mask=None, units=None,
+                        per_sequence=False) -> _Prepared:
+    """Packed (varlen) batch: ``q [T, H_q, D]``, ``k [T, H_kv, D]``, sequence ``b``
+    is rows ``[cu_seqlens[b], cu_seqlens[b + 1])``.  ``max_seqlen`` (host int,
+    read from ``cu_seqlens`` when omitted) is the bucket extent ``N``; masks
+    index positions inside a sequence, as for ``[B, N]`` tensors."""
+    if not all(isinstance(t, torch.Tensor) for t in (q, k, cu_seqlens)):
+        raise TypeError("q, k and cu_seqlens must be torch tensors")
+    if q.dim() != 3 or k.dim() != 3:
+        raise ValueError(f"packed q and k must be 3-D [T, H, D], got {tuple(q.shape)} and {tuple(k.shape)}")
+    T, Hq, D = q.shape
+    if k.shape[0] != T or k.shape[2] != D:
+        raise ValueError(f"k shape {tuple(k.shape)} does not match q shape {tuple(q.shape)}")
+    if q.device != k.device:
+        raise ValueError(f"q and k are on different devices ({q.device}, {k.device})")
+    if q.dtype != k.dtype:
+        raise ValueError(f"q dtype {q.dtype} != k dtype {k.dtype}")
+    if cu_seqlens.dim() != 1 or cu_seqlens.shape[0] < 2:
+        raise ValueError("cu_seqlens must be [B + 1] with B >= 1")
+    if max_seqlen is None:
+        cu_h = cu_seqlens.detach().to("cpu", torch.int64)
+        max_seqlen = int((cu_h[1:] - cu_h[:-1]).max())
+    B, Hkv = cu_seqlens.shape[0] - 1, k.shape[1]
+    qs = (0, q.stride(1), q.stride(0), q.stride(2))
+    ks = (0, k.stride(1), k.stride(0), k.stride(2))
+    prep = _fill_problem(q.data_ptr(), qs, k.data_ptr(), ks, q.dtype, B, Hq, Hkv, int(max_seqlen), D, q.device,
+                         [q, k], attn_mask, causal, block_size, scale, causal_skip, query_mask, units)
+    _set_ragged(prep, q.device, cu_seqlens=cu_seqlens, total=T, per_sequence=per_sequence)
+    _validate_ex(prep)
+    return prep
+
+
 def workspace_bytes(prep: _Prepared) -> int:
-    return int(_lib.load().kvbm_workspace_bytes(ctypes.byref(prep.prob)))
+    lib = _lib.load()
+    if prep.opts is not None:
+        return int(lib.kvbm_workspace_bytes_ex(ctypes.byref(prep.prob), ctypes.byref(prep.opts)))
+    return int(lib.kvbm_workspace_bytes(ctypes.byref(prep.prob)))
 
 
 def kernel_path(prep: _Prepared) -> int:
-    """0 = SIMT kernels, 1 = tcgen05 tensor-core kernels (on the current device)."""
+    """0 = SIMT kernels, 1 = tcgen05 tensor-core kernels, 2 = tcgen05 3xTF32 (current device)."""
     return int(_lib.load().kvbm_kernel_path(ctypes.byref(prep.prob)))
 
 
 def launches_per_call(prep: _Prepared) -> int:
     return int(_lib.load().kvbm_launches_per_call(ctypes.byref(prep.prob)))
+
+
+def _lse_strides(prep: _Prepared, lse: torch.Tensor):
+    B, Hq, N = prep.prob.B, prep.prob.Hq, prep.prob.N
+    if prep.packed:
+        if tuple(lse.shape) != (Hq, prep.total):
+            raise ValueError(f"packed lse must be [H_q, T] = {(Hq, prep.total)}, got {tuple(lse.shape)}")
+        return (0, lse.stride(0), lse.stride(1))
+    if tuple(lse.shape) != (B, Hq, N):
+        raise ValueError(f"lse must be [B, H_q, N] = {(B, Hq, N)}, got {tuple(lse.shape)}")
+    return tuple(lse.stride())
 
 
 def run_prepared(prep: _Prepared, out: torch.Tensor | None = None,
@@ -181,32 +297,38 @@ def run_prepared(prep: _Prepared, out: torch.Tensor | None = None,
                  lse: torch.Tensor | None = None) -> torch.Tensor:
     """Launch the kernels of a prepared problem on ``stream`` (default: current).
 
-    With ``lse`` ([B, H_q, N] natural-log row log-sum-exp) pass 1 is skipped.
+    With ``lse`` (``[B, H_q, N]`` natural-log row log-sum-exp; ``[H_q, T]`` for
+    a packed batch) pass 1 is skipped.
     """
     q = prep.keep[0]
     dev = q.device
     lib = _lib.load()
     with torch.cuda.device(dev):
-        ws_need = int(lib.kvbm_workspace_bytes(ctypes.byref(prep.prob)))
+        opts = prep.opts
+        if lse is not None:
+            lse = lse.to(device=dev, dtype=torch.float32)
+            st = _lse_strides(prep, lse)
+            prep.keep.append(lse)
+            opts = prep.options()
+            opts.lse = lse.data_ptr()
+            for i in range(3):
+                opts.lse_stride[i] = st[i]
+        ws_need = workspace_bytes(prep)
         if workspace is None or workspace.numel() < ws_need:
             workspace = torch.empty(max(ws_need, 256), dtype=torch.uint8, device=dev)
         if out is None:
-            out = torch.empty(prep.nb, dtype=prep.out_dtype, device=dev)
-        elif out.dtype != prep.out_dtype or out.numel() != prep.nb or not out.is_contiguous():
-            raise ValueError(f"out must be a contiguous {prep.out_dtype} tensor of {prep.nb} elements")
+            out = torch.empty(prep.out_shape, dtype=prep.out_dtype, device=dev)
+        elif out.dtype != prep.out_dtype or tuple(out.shape) != prep.out_shape or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous {prep.out_dtype} tensor of shape {prep.out_shape}")
         s = stream if stream is not None else torch.cuda.current_stream(dev)
-        if lse is None:
+        if opts is None:
             code = lib.kvbm_block_mass(ctypes.byref(prep.prob), out.data_ptr(), workspace.data_ptr(),
                                        workspace.numel(), s.cuda_stream)
         else:
-            B, Hq, N = prep.prob.B, prep.prob.Hq, prep.prob.N
-            if tuple(lse.shape) != (B, Hq, N):
-                raise ValueError(f"lse must be [B, H_q, N] = {(B, Hq, N)}, got {tuple(lse.shape)}")
-            lse = lse.to(device=dev, dtype=torch.float32)
-            prep.keep.append(lse)
-            st = (ctypes.c_int64 * 3)(*lse.stride())
-            code = lib.kvbm_block_mass_lse(ctypes.byref(prep.prob), lse.data_ptr(), st, out.data_ptr(),
-                                           workspace.data_ptr(), workspace.numel(), s.cuda_stream)
+            code = lib.kvbm_block_mass_ex(ctypes.byref(prep.prob), ctypes.byref(opts), out.data_ptr(),
+                                          workspace.data_ptr(), workspace.numel(), s.cuda_stream)
+        if lse is not None:
+            opts.lse = None
     if code != _lib.KVBM_OK:
         _raise(code, prep.prob)
     return out
@@ -214,7 +336,8 @@ def run_prepared(prep: _Prepared, out: torch.Tensor | None = None,
 
 def block_mass_b200(q, k, attn_mask=None, causal=False, block_size=64, scale=None,
                     causal_skip=True, query_mask=None, *, BLOCK_M=None, BLOCK_N=None,
-                    query_chunk=None, device=None, units=None, out=None, workspace=None, lse=None):
+                    query_chunk=None, device=None, units=None, out=None, workspace=None, lse=None,
+                    seq_lens=None, per_sequence=False):
     """Block-pooled column sums of the softmax attention matrix on a B200.
 
     Returns ``mass [ceil(N / block_size)]`` (float32; float64 for float64
@@ -223,7 +346,9 @@ def block_mass_b200(q, k, attn_mask=None, causal=False, block_size=64, scale=Non
     the multi-GPU shards); ``out``/``workspace`` let callers reuse buffers.
     ``lse`` ([B, H_q, N], natural log of sum_c exp(scale * q.k_c) over the kept
     keys, e.g. the softmax LSE an attention forward returns) skips the row
-    statistics pass: about half the work.
+    statistics pass: about half the work.  ``seq_lens [B]`` makes the batch
+    ragged (sequence ``b`` is its first ``seq_lens[b]`` positions; the padding
+    is never read into a pair); ``per_sequence`` returns ``[B, num_blocks]``.
     """
     del BLOCK_M, BLOCK_N, query_chunk  # tiling is fixed by the kernels
     if device is not None:
@@ -231,7 +356,8 @@ def block_mass_b200(q, k, attn_mask=None, causal=False, block_size=64, scale=Non
         if dev.type != "cuda":
             raise ValueError(f"block_mass_b200 computes on CUDA devices only, got device={device}")
         if (not q.is_cuda and not k.is_cuda and q.is_pinned() and k.is_pinned() and units is None
-                and lse is None and out is None and q.dim() == 4 and k.dim() == 4):
+                and lse is None and out is None and q.dim() == 4 and k.dim() == 4 and seq_lens is None
+                and not per_sequence):
             return _from_pinned_host(q, k, dev, attn_mask=attn_mask, causal=causal, block_size=block_size,
                                      scale=scale, causal_skip=causal_skip, query_mask=query_mask,
                                      workspace=workspace)
@@ -240,7 +366,8 @@ def block_mass_b200(q, k, attn_mask=None, causal=False, block_size=64, scale=Non
         raise ValueError("block_mass_b200 needs CUDA tensors (there is no CPU path); "
                          "pass device='cuda' or use the reference's block_mass_reference")
     prep = make_problem(q, k, attn_mask=attn_mask, causal=causal, block_size=block_size,
-                        scale=scale, causal_skip=causal_skip, query_mask=query_mask, units=units)
+                        scale=scale, causal_skip=causal_skip, query_mask=query_mask, units=units,
+                        seq_lens=seq_lens, per_sequence=per_sequence)
     return run_prepared(prep, out=out, workspace=workspace, lse=lse)
 
 
@@ -318,7 +445,7 @@ def block_mass(q, k, **kwargs):
 
 
 class _PagedPrepared:
-    """A dense ``kvbm_problem`` (its k ignored) plus the ``kvbm_paged_kv`` of the cache."""
+    """A prepared problem whose k comes from a paged cache (``prep.opts.paged``)."""
 
     def __init__(self, prep: _Prepared, kv, keep):
         self.prep = prep
@@ -327,21 +454,25 @@ class _PagedPrepared:
 
 
 def make_paged_problem(q, k_cache, block_table, attn_mask=None, causal=False, block_size=64, scale=None,
-                       causal_skip=True, query_mask=None, units=None) -> _PagedPrepared:
+                       causal_skip=True, query_mask=None, units=None, seq_lens=None, cu_seqlens=None,
+                       max_seqlen=None, per_sequence=False) -> _PagedPrepared:
     """Validate a paged call and build its C structs.
 
     ``k_cache`` is ``[num_pages, page_size, H_kv, D]`` (any strides, the dtype
     of ``q``); ``block_table`` is ``[B, max_pages]`` of page ids (converted to
     int32): key ``n`` of sequence ``b`` is ``k_cache[block_table[b, n // P], n % P]``.
-    Every sequence has ``N = q.shape[2]`` keys.
+    ``q`` is ``[B, H_q, N, D]`` (every sequence N long, or ``seq_lens[b]``
+    long), or packed ``[T, H_q, D]`` with ``cu_seqlens`` (as ``block_mass_varlen``).
     """
     if not all(isinstance(t, torch.Tensor) for t in (q, k_cache, block_table)):
         raise TypeError("q, k_cache and block_table must be torch tensors")
-    if q.dim() != 4 or k_cache.dim() != 4:
-        raise ValueError(f"q must be [B, H_q, N, D] and k_cache [num_pages, page_size, H_kv, D], "
-                         f"got {tuple(q.shape)} and {tuple(k_cache.shape)}")
-    B, Hq, N, D = q.shape
+    packed = cu_seqlens is not None
+    if (q.dim() != (3 if packed else 4)) or k_cache.dim() != 4:
+        raise ValueError(f"q must be [B, H_q, N, D] ([T, H_q, D] with cu_seqlens) and k_cache "
+                         f"[num_pages, page_size, H_kv, D], got {tuple(q.shape)} and {tuple(k_cache.shape)}")
     num_pages, page_size, Hkv, Dk = k_cache.shape
+    D = q.shape[-1]
+    B = (cu_seqlens.shape[0] - 1) if packed else q.shape[0]
     if Dk != D:
         raise ValueError(f"k_cache head dim {Dk} != q head dim {D}")
     if block_table.dim() != 2 or block_table.shape[0] != B:
@@ -354,15 +485,24 @@ def make_paged_problem(q, k_cache, block_table, attn_mask=None, causal=False, bl
         raise ValueError("q, k_cache and block_table must be on one device")
     if num_pages == 0 or page_size == 0:
         raise ValueError("k_cache has no pages")
+    if packed:
+        if max_seqlen is None:
+            cu_h = cu_seqlens.detach().to("cpu", torch.int64)
+            max_seqlen = int((cu_h[1:] - cu_h[:-1]).max())
+        N = int(max_seqlen)
+        qs = (0, q.stride(1), q.stride(0), q.stride(2))
+    else:
+        N = q.shape[2]
+        qs = q.stride()
     if block_table.shape[1] * page_size < N:
         raise ValueError(f"block_table covers {block_table.shape[1] * page_size} keys < N={N}")
     table = block_table.to(torch.int32)
     if table.stride(1) != 1:
         table = table.contiguous()
-    # stand-in dense k: make_problem checks shapes and masks; the C call ignores it
-    k_shape = torch.empty((), dtype=q.dtype, device=q.device).expand(B, Hkv, N, D)
-    prep = make_problem(q, k_shape, attn_mask=attn_mask, causal=causal, block_size=block_size, scale=scale,
-                        causal_skip=causal_skip, query_mask=query_mask, units=units)
+    Hq = q.shape[1]
+    # k in the problem is ignored (the options carry the cache); any non-null pointer
+    prep = _fill_problem(q.data_ptr(), qs, k_cache.data_ptr(), (0, 0, 0, 0), q.dtype, B, Hq, Hkv, N, D, q.device,
+                         [q], attn_mask, causal, block_size, scale, causal_skip, query_mask, units)
     kv = _lib.PagedKV()
     kv.k_cache = k_cache.data_ptr()
     for i in range(4):
@@ -371,63 +511,67 @@ def make_paged_problem(q, k_cache, block_table, attn_mask=None, causal=False, bl
     kv.block_table = table.data_ptr()
     kv.block_table_stride = table.stride(0)
     kv.max_pages = table.shape[1]
-    code = _lib.load().kvbm_validate_paged(ctypes.byref(prep.prob), ctypes.byref(kv))
-    if code != _lib.KVBM_OK:
-        _raise(code, prep.prob)
+    prep.keep += [k_cache, table, kv]
+    prep.options().paged = ctypes.pointer(kv)
+    _set_ragged(prep, q.device, seq_lens=seq_lens, cu_seqlens=cu_seqlens, total=q.shape[0] if packed else 0,
+                per_sequence=per_sequence)
+    _validate_ex(prep)
     return _PagedPrepared(prep, kv, [k_cache, table])
 
 
 def paged_workspace_bytes(pp: _PagedPrepared) -> int:
-    return int(_lib.load().kvbm_paged_workspace_bytes(ctypes.byref(pp.prep.prob), ctypes.byref(pp.kv)))
+    return workspace_bytes(pp.prep)
 
 
 def run_paged(pp: _PagedPrepared, out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
               stream: torch.cuda.Stream | None = None, lse: torch.Tensor | None = None) -> torch.Tensor:
     """Launch a prepared paged problem (page gather, then the dense kernels) on ``stream``."""
-    prep = pp.prep
-    dev = prep.keep[0].device
-    lib = _lib.load()
-    with torch.cuda.device(dev):
-        need = paged_workspace_bytes(pp)
-        if workspace is None or workspace.numel() < need:
-            workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
-        if out is None:
-            out = torch.empty(prep.nb, dtype=prep.out_dtype, device=dev)
-        elif out.dtype != prep.out_dtype or out.numel() != prep.nb or not out.is_contiguous():
-            raise ValueError(f"out must be a contiguous {prep.out_dtype} tensor of {prep.nb} elements")
-        s = stream if stream is not None else torch.cuda.current_stream(dev)
-        lse_ptr, st = None, None
-        if lse is not None:
-            B, Hq, N = prep.prob.B, prep.prob.Hq, prep.prob.N
-            if tuple(lse.shape) != (B, Hq, N):
-                raise ValueError(f"lse must be [B, H_q, N] = {(B, Hq, N)}, got {tuple(lse.shape)}")
-            lse = lse.to(device=dev, dtype=torch.float32)
-            pp.keep.append(lse)
-            lse_ptr, st = lse.data_ptr(), (ctypes.c_int64 * 3)(*lse.stride())
-        code = lib.kvbm_block_mass_paged(ctypes.byref(prep.prob), ctypes.byref(pp.kv), lse_ptr, st,
-                                         out.data_ptr(), workspace.data_ptr(), workspace.numel(), s.cuda_stream)
-    if code != _lib.KVBM_OK:
-        _raise(code, prep.prob)
-    return out
+    return run_prepared(pp.prep, out=out, workspace=workspace, stream=stream, lse=lse)
 
 
 def block_mass_paged(q, k_cache, block_table, attn_mask=None, causal=False, block_size=64, scale=None,
-                     causal_skip=True, query_mask=None, *, units=None, out=None, workspace=None, lse=None):
+                     causal_skip=True, query_mask=None, *, seq_lens=None, cu_seqlens=None, max_seqlen=None,
+                     per_sequence=False, units=None, out=None, workspace=None, lse=None):
     """``block_mass_b200`` with keys read from a paged KV cache.
 
     ``k_cache [num_pages, page_size, H_kv, D]`` and ``block_table [B,
-    max_pages]`` (page ids) on the device of ``q [B, H_q, N, D]``; the other
-    arguments as ``block_mass_b200``.  ``block_size == page_size`` gives one
-    bucket per page.  The result has the same bits as ``block_mass_b200`` on
-    the dense keys the table names.  A page id outside ``[0, num_pages)`` is
-    not read (its keys count as zero vectors); ``check_device_errors()``
-    reports it.
+    max_pages]`` (page ids) on the device of ``q``: ``[B, H_q, N, D]``
+    (optionally ``seq_lens [B]``), or packed ``[T, H_q, D]`` with
+    ``cu_seqlens [B + 1]``.  Other arguments as ``block_mass_b200``;
+    ``block_size == page_size`` gives one bucket per page.  The result has the
+    same bits as the dense call on the keys the table names.  A page id
+    outside ``[0, num_pages)`` is not read (its keys count as zero vectors);
+    ``check_device_errors()`` reports it.  Table entries past a sequence's
+    length are never read.
     """
     if not (q.is_cuda and k_cache.is_cuda):
         raise ValueError("block_mass_paged needs CUDA tensors (there is no CPU path)")
     pp = make_paged_problem(q, k_cache, block_table, attn_mask=attn_mask, causal=causal, block_size=block_size,
-                            scale=scale, causal_skip=causal_skip, query_mask=query_mask, units=units)
+                            scale=scale, causal_skip=causal_skip, query_mask=query_mask, units=units,
+                            seq_lens=seq_lens, cu_seqlens=cu_seqlens, max_seqlen=max_seqlen,
+                            per_sequence=per_sequence)
     return run_paged(pp, out=out, workspace=workspace, lse=lse)
+
+
+def block_mass_varlen(q, k, cu_seqlens, max_seqlen=None, attn_mask=None, causal=False, block_size=64,
+                      scale=None, causal_skip=True, query_mask=None, *, per_sequence=False, units=None, out=None,
+                      workspace=None, lse=None):
+    """Block mass of a packed (varlen) batch, as FlashAttention's varlen layout.
+
+    ``q [T, H_q, D]``, ``k [T, H_kv, D]``; sequence ``b`` is rows
+    ``[cu_seqlens[b], cu_seqlens[b + 1])`` (``cu_seqlens [B + 1]`` int32 on the
+    device).  ``max_seqlen`` (host int; read from ``cu_seqlens`` when omitted,
+    which synchronises) sets ``N``: the output is ``[ceil(N / block_size)]``
+    summed over sequences, or ``[B, ceil(N / block_size)]`` with
+    ``per_sequence``.  Each sequence contributes exactly what the reference
+    computes for it alone.  ``lse`` is ``[H_q, T]``.
+    """
+    if not (q.is_cuda and k.is_cuda):
+        raise ValueError("block_mass_varlen needs CUDA tensors (there is no CPU path)")
+    prep = make_varlen_problem(q, k, cu_seqlens, max_seqlen=max_seqlen, attn_mask=attn_mask, causal=causal,
+                               block_size=block_size, scale=scale, causal_skip=causal_skip,
+                               query_mask=query_mask, units=units, per_sequence=per_sequence)
+    return run_prepared(prep, out=out, workspace=workspace, lse=lse)
 
 
 def check_device_errors(device=None) -> None:

@@ -29,6 +29,10 @@ sum over ``b`` of the reference run on batch ``b`` alone with that batch's
 mask, and a row with ``query_mask`` False behaves like a pair-mask row that
 keeps nothing.
 
+Ragged batches (sequence ``b`` has its own length ``L_b <= N``) are defined
+the same way, by linearity over the batch: sequence ``b`` contributes the
+reference run on its first ``L_b`` positions alone (``block_mass_ragged``).
+
 A paged key cache (``[num_pages, page_size, H_kv, D]`` plus a block table
 ``[B, max_pages]`` of page ids, the layout of the paged KV managers that
 consume block mass) is another extension; it is defined by the dense keys it
@@ -45,7 +49,7 @@ from concurrent.futures import ThreadPoolExecutor
 
 import numpy as np
 
-__all__ = ["block_mass_stream", "normalize_masks", "num_blocks", "dense_keys_from_pages"]
+__all__ = ["block_mass_stream", "normalize_masks", "num_blocks", "dense_keys_from_pages", "block_mass_ragged"]
 
 
 def num_blocks(n: int, block_size: int) -> int:
@@ -299,3 +303,52 @@ def dense_keys_from_pages(k_cache, block_table, n: int):
     pages = table[:, c // p]                     # [B, N]
     rows = k_cache[pages, (c % p)[None, :]]      # [B, N, H_kv, D]
     return np.ascontiguousarray(rows.transpose(0, 2, 1, 3))
+
+
+def _batch_slice(m, b, length, pair_ok=True):
+    """Batch ``b``'s part of a mask of the supported shapes, cut to ``length`` positions."""
+    if m is None:
+        return None
+    m = np.asarray(m)
+    if m.ndim == 1:
+        return m[:length]
+    if m.ndim == 2:
+        if m.shape[0] == m.shape[1] and pair_ok and m.shape[0] != 1:
+            return m[:length, :length]          # [N, N] pair mask shared by the batch
+        return m[b if m.shape[0] > 1 else 0, :length]   # [B, N] row mask
+    mb = m[b if m.shape[0] > 1 else 0]
+    if mb.shape[0] == 1:
+        return mb[None, :, :length]             # [1, 1, N] key mask of batch b
+    return mb[:length, :length]                 # [N, N] pair mask of batch b
+
+
+def block_mass_ragged(q, k, lens, attn_mask=None, causal=False, block_size=64, scale=None, query_mask=None,
+                      per_sequence=False):
+    """Block mass of a ragged batch: ``q [B,H_q,N,D]``, ``k [B,H_kv,N,D]``,
+    sequence ``b`` being its first ``lens[b] <= N`` positions.
+
+    Each sequence is the reference's computation on ``q[b:b+1, :, :L]``,
+    ``k[b:b+1, :, :L]`` with its slice of the masks (``reference.py:35-126``);
+    its ``ceil(L / block_size)`` buckets land in the first buckets of the
+    ``ceil(N / block_size)``-long output.  Returns the sum over sequences, or
+    ``[B, num_blocks]`` with ``per_sequence``.  Positions past ``L`` are never
+    read, so they may hold anything.
+    """
+    q = np.asarray(q)
+    k = np.asarray(k)
+    B, _, N, D = q.shape
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    nb = num_blocks(N, block_size)
+    acc = np.float64 if q.dtype == np.float64 else np.float32
+    out = np.zeros((B, nb), dtype=acc)
+    for b in range(B):
+        L = int(min(max(int(lens[b]), 0), N))
+        if L == 0:
+            continue
+        m = block_mass_stream(q[b:b + 1, :, :L], k[b:b + 1, :, :L],
+                              attn_mask=_batch_slice(attn_mask, b, L),
+                              query_mask=_batch_slice(query_mask, b, L, pair_ok=False),
+                              causal=causal, block_size=block_size, scale=scale)
+        out[b, :m.shape[0]] = m
+    return out if per_sequence else out.sum(axis=0, dtype=np.float64).astype(acc)
