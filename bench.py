@@ -23,6 +23,8 @@ Reported beside the device-timed value:
                 both passes, reduce;
   ragged        a packed (varlen) batch of six sequences, 32768 tokens, in one
                 call, beside one dense call per sequence;
+  design        the device-side eviction design of the step's mass (the
+                reference's consumers, evict.py, on the GPU);
   roofline      the dominant kernel's algorithmic tensor FLOP/s against the
                 measured bf16 peak, and its exp rate against the MUFU ex2
                 rate measured live on this GPU (the binding unit);
@@ -496,6 +498,47 @@ def b200_arm(args, w):
                   "api": "kvbm_block_mass_ex (packed q/k + cu_seqlens), vs one kvbm_block_mass per sequence"}
         del qp, kp, ws_r, singles
 
+    # Device-side consumer: the eviction design of the step's mass (kvbm_design), as
+    # plan_reclaim sets it up (tail budget N/8, top slice half of it, 4 sinks, 32 recent).
+    design = None
+    design_mass_host = None
+    if not args.no_e2e:
+        from kvblockmass_b200 import design as dsg
+        Nd, bsd = q.shape[2], w.block_size
+        mass_d = ops.run_prepared(prep, workspace=ws)
+        a_d, m2 = dsg._args(mass_d, Nd, bsd, Nd // 8, 4, 32, Nd // 16, 1e-6, False)
+        a_d.seed = 1
+        outs = {n: torch.empty(Nd, dtype=dt, device=dev) for n, dt in
+                (("pi", torch.float64), ("keep", torch.bool), ("cert", torch.bool))}
+        counts = torch.empty(1, 5, dtype=torch.int64, device=dev)
+        o_d = _lib.DesignOut()
+        o_d.pi = ctypes.cast(outs["pi"].data_ptr(), ctypes.POINTER(ctypes.c_double))
+        o_d.keep = ctypes.cast(outs["keep"].data_ptr(), ctypes.POINTER(ctypes.c_uint8))
+        o_d.certainty = ctypes.cast(outs["cert"].data_ptr(), ctypes.POINTER(ctypes.c_uint8))
+        o_d.counts = ctypes.cast(counts.data_ptr(), ctypes.POINTER(ctypes.c_int64))
+        ws_d = torch.empty(max(256, lib.kvbm_design_workspace_bytes(ctypes.byref(a_d))), dtype=torch.uint8,
+                           device=dev)
+
+        def design_step():
+            if lib.kvbm_design(ctypes.byref(a_d), ctypes.byref(o_d), ws_d.data_ptr(), ws_d.numel(),
+                               stream.cuda_stream) != 0:
+                raise RuntimeError("kvbm_design failed")
+
+        for _ in range(3):
+            design_step()
+        torch.cuda.synchronize()
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        d0.record(stream)
+        for _ in range(50):
+            design_step()
+        d1.record(stream)
+        torch.cuda.synchronize()
+        design_mass_host = mass_d.cpu().numpy()
+        design = {"ms_per_design": d0.elapsed_time(d1) / 50, "tokens": Nd, "block_size": bsd,
+                  "tail_budget": Nd // 8, "top_slice": Nd // 16, "kept_tokens": int(counts[0, 0]),
+                  "launches": 3, "api": "kvbm_design (expand_block_scores + design_from_scores + block retention)"}
+        del mass_d, m2, outs, ws_d
+
     # End to end through the public API: pinned host q/k in, mass back on the host.
     e2e = None
     if not args.no_e2e:
@@ -575,9 +618,22 @@ def b200_arm(args, w):
         line["paged"] = paged
     if ragged:
         line["ragged"] = ragged
+    if design:
+        line["design"] = design
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = {k: v for k, v in cpu_sample(w, args.cpu_seconds).items()
                                 if k not in ("seconds", "pairs")}
+        if design is not None and design_mass_host is not None:
+            # the same design on the host: the oracle's restatement of evict.py (float64 numpy)
+            from oracle import evict_np as ev
+            Nd = design["tokens"]
+            t0 = time.perf_counter()
+            reps = 20
+            for _ in range(reps):
+                sc = ev.expand_block_scores(design_mass_host, Nd, design["block_size"])
+                ev.design_from_scores(sc, design["tail_budget"], n_sinks=4, recency=32,
+                                      top_slice=design["top_slice"], uniforms=np.zeros(Nd))
+            line["cpu_baseline"]["design_ms"] = (time.perf_counter() - t0) * 1e3 / reps
     print(json.dumps(line), flush=True)
 
 

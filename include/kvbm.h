@@ -312,6 +312,71 @@ KVBM_API size_t kvbm_workspace_bytes_ex(const kvbm_problem* p, const kvbm_option
 KVBM_API int kvbm_block_mass_ex(const kvbm_problem* p, const kvbm_options* o, void* mass_out, void* workspace,
                        size_t workspace_bytes, void* stream);
 
+/* Device-side consumers of the mass vector: the eviction design of
+ * kv-block-mass (src/kvblockmass/evict.py), for `rows` sequences at once.
+ *
+ *   expand_block_scores  evict.py:64-83    scores[i] = mass[i / block_size] (float64)
+ *   design_from_scores   evict.py:95-171   certainty = first n_sinks tokens, last
+ *                                          recency tokens, the top_slice highest
+ *                                          scores (ties: lower index first, the
+ *                                          rule _top_slice's docstring states,
+ *                                          evict.py:86-87); tail pi =
+ *                                          clip(tail_budget * w / sum_tail w, eps, 1),
+ *                                          w = scores (1 with uniform_tail, and a
+ *                                          uniform design when the tail's scores
+ *                                          sum to 0), eps for every tail token when
+ *                                          tail_budget = 0; keep = certainty | u < pi
+ *   hajek_log_offsets    evict.py:174-187  log_offsets = -log(pi)
+ *   block retention      reclaim.py:46-55  blocks with at least one kept token
+ *
+ * Tail draws u: uniforms[row * uniforms_row_stride + t] for the t-th tail token
+ * (ascending index) when `uniforms` is not NULL: the reference's
+ * torch.rand(n_tail, dtype=float64, generator) gives bit parity; otherwise
+ * Philox4x32-10 keyed by `seed`, counter = (token, row).
+ * Row r's block mass is mass[r * mass_row_stride + b], b < num_blocks
+ * (float32 or float64); blocks past ceil(seq_len / block_size) are ignored. */
+typedef struct kvbm_design_args {
+  const void* mass;
+  int32_t mass_dtype;            /* KVBM_F32 or KVBM_F64 */
+  int32_t rows;
+  int64_t mass_row_stride;
+  int32_t num_blocks;
+  int32_t seq_len;
+  int32_t block_size;
+  int32_t n_sinks;
+  int32_t recency;
+  int32_t top_slice;
+  int64_t tail_budget;
+  double eps;                    /* > 0 */
+  int32_t uniform_tail;
+  const double* uniforms;        /* or NULL */
+  int64_t uniforms_row_stride;
+  uint64_t seed;
+} kvbm_design_args;
+
+/* Outputs, [rows, seq_len] each, on the device; any may be NULL except
+ * counts.  counts [rows, 5] int64: kept tokens, certainty tokens, tail tokens,
+ * blocks kept (0 when keep is NULL), flags (1: a block mass is negative or
+ * NaN, where the reference raises ValueError). */
+typedef struct kvbm_design_out {
+  double* pi;
+  uint8_t* keep;
+  uint8_t* certainty;
+  double* scores;
+  double* log_offsets;
+  int64_t* counts;
+} kvbm_design_out;
+
+/* Workspace bytes of kvbm_design (0 on invalid arguments). */
+KVBM_API size_t kvbm_design_workspace_bytes(const kvbm_design_args* d);
+
+/* The design on the device, asynchronous on `stream` (three kernels: a
+ * per-row select/scan CTA, a token kernel, a block-retention kernel).
+ * No counterpart in the reference's GPU path: there the design runs in torch
+ * on the host after mass.cpu(). */
+KVBM_API int kvbm_design(const kvbm_design_args* d, const kvbm_design_out* out, void* workspace,
+                size_t workspace_bytes, void* stream);
+
 /* Reads and clears the device-side error words of the current device (set
  * when a bounded wait inside a tcgen05 kernel gave up, or when a page gather
  * met a block-table entry out of range).  Synchronises `stream`.  Returns

@@ -26,6 +26,7 @@ from .ops import (  # noqa: F401
     run_prepared,
     workspace_bytes,
 )
+from .design import DeviceDesign, design_from_mass  # noqa: F401
 from .workloads import WORKLOADS, Workload, make_inputs, pairs  # noqa: F401
 
 __all__ = [
@@ -40,6 +41,8 @@ __all__ = [
     "paged_workspace_bytes",
     "run_paged",
     "check_device_errors",
+    "design_from_mass",
+    "DeviceDesign",
     "kernel_path",
     "make_problem",
     "workspace_bytes",

@@ -51,6 +51,8 @@ EXPORTED = [
     "kvbm_validate_ex",
     "kvbm_workspace_bytes_ex",
     "kvbm_block_mass_ex",
+    "kvbm_design_workspace_bytes",
+    "kvbm_design",
 ]
 
 
@@ -110,6 +112,42 @@ class Options(ctypes.Structure):
         ("total_tokens", ctypes.c_int64),
         ("per_sequence", ctypes.c_int32),
         ("events", ctypes.POINTER(ctypes.c_void_p)),
+    ]
+
+
+class DesignArgs(ctypes.Structure):
+    """Mirror of ``struct kvbm_design_args``."""
+
+    _fields_ = [
+        ("mass", ctypes.c_void_p),
+        ("mass_dtype", ctypes.c_int32),
+        ("rows", ctypes.c_int32),
+        ("mass_row_stride", ctypes.c_int64),
+        ("num_blocks", ctypes.c_int32),
+        ("seq_len", ctypes.c_int32),
+        ("block_size", ctypes.c_int32),
+        ("n_sinks", ctypes.c_int32),
+        ("recency", ctypes.c_int32),
+        ("top_slice", ctypes.c_int32),
+        ("tail_budget", ctypes.c_int64),
+        ("eps", ctypes.c_double),
+        ("uniform_tail", ctypes.c_int32),
+        ("uniforms", ctypes.POINTER(ctypes.c_double)),
+        ("uniforms_row_stride", ctypes.c_int64),
+        ("seed", ctypes.c_uint64),
+    ]
+
+
+class DesignOut(ctypes.Structure):
+    """Mirror of ``struct kvbm_design_out``."""
+
+    _fields_ = [
+        ("pi", ctypes.POINTER(ctypes.c_double)),
+        ("keep", ctypes.POINTER(ctypes.c_uint8)),
+        ("certainty", ctypes.POINTER(ctypes.c_uint8)),
+        ("scores", ctypes.POINTER(ctypes.c_double)),
+        ("log_offsets", ctypes.POINTER(ctypes.c_double)),
+        ("counts", ctypes.POINTER(ctypes.c_int64)),
     ]
 
 
@@ -174,6 +212,12 @@ def load() -> ctypes.CDLL:
     lib.kvbm_workspace_bytes_ex.argtypes = [P, O]
     lib.kvbm_block_mass_ex.restype = ctypes.c_int
     lib.kvbm_block_mass_ex.argtypes = [P, O, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    # Device-side consumers (eviction design).
+    lib.kvbm_design_workspace_bytes.restype = ctypes.c_size_t
+    lib.kvbm_design_workspace_bytes.argtypes = [ctypes.POINTER(DesignArgs)]
+    lib.kvbm_design.restype = ctypes.c_int
+    lib.kvbm_design.argtypes = [ctypes.POINTER(DesignArgs), ctypes.POINTER(DesignOut), ctypes.c_void_p,
+                                ctypes.c_size_t, ctypes.c_void_p]
     lib.kvbm_check_device_errors.restype = ctypes.c_int
     lib.kvbm_check_device_errors.argtypes = [ctypes.c_void_p]
     if lib.kvbm_abi_version() != 1:
