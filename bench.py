@@ -577,6 +577,7 @@ def b200_arm(args, w):
         return
 
     peaks = measured_peaks()
+    fma_frac = float(lib.kvbm_exp2_fma_fraction()) if path >= 1 else 0.0
     t1, t2, t3 = statistics.mean(p1), statistics.mean(p2), statistics.mean(p3)
     dom_name, dom_ms = ("pass2_mass", t2) if t2 >= t1 else ("pass1_lse", t1)
     flops = pairs_rank * 2 * w.D                      # algorithmic tensor FLOPs per launch
@@ -603,7 +604,11 @@ def b200_arm(args, w):
             "peak_source": f"{peaks['source']} bf16_tflops (burst) of MEASURED_PEAKS.json",
             "binding_unit": binding,
             "mufu": {"achieved_ex2_per_s": exp_rate, "peak_ex2_per_s": ex2.value,
-                     "frac": exp_rate / ex2.value, "peak_source": "measured live (kvbm_measure_ex2_rate)"},
+                     "frac": exp_rate / ex2.value, "peak_source": "measured live (kvbm_measure_ex2_rate)",
+                     "note": "achieved counts every exp2 of the algorithm (one per pair); fma_pipe_fraction "
+                             "of them run on the FMA pipe, so the MUFU unit itself is at mufu_unit_frac",
+                     "fma_pipe_fraction": fma_frac,
+                     "mufu_unit_frac": exp_rate * (1.0 - fma_frac) / ex2.value},
             "frac_of_binding": (bound_time / (dom_ms * 1e-3)),
             "algorithmic_per_launch": {"pairs": pairs_rank, "tensor_flops": flops, "ex2": pairs_rank},
         },

@@ -181,6 +181,11 @@ KVBM_API int kvbm_block_mass_events(const kvbm_problem* p, void* mass_out, void*
  * No counterpart in the reference. */
 KVBM_API int kvbm_measure_ex2_rate(void* stream, double* ex2_per_second);
 
+/* Share of the tensor-core kernels' exp2 evaluations done on the FMA pipe
+ * (a minimax polynomial) instead of MUFU ex2.approx: the MUFU unit sees
+ * (1 - this) of the exponentials.  No counterpart in the reference. */
+KVBM_API double kvbm_exp2_fma_fraction(void);
+
 /* kvbm_block_mass for callers that cannot allocate device memory.  It has
  * no counterpart in the reference.
  *

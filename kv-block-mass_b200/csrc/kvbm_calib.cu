@@ -67,3 +67,5 @@ extern "C" int kvbm_measure_ex2_rate(void* stream, double* ex2_per_second) {
     *ex2_per_second = (double)blocks * threads * iters * kChains / (ms * 1e-3);
   return st;
 }
+
+extern "C" double kvbm_exp2_fma_fraction(void) { return kvbm::exp2_fma_fraction(); }

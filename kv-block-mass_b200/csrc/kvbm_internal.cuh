@@ -79,6 +79,7 @@ __host__ __device__ inline SeqView seq_view(const int32_t* lens, const int32_t* 
 
 // Host helpers (kvbm_api.cu).
 bool tc_path_enabled();  // kvbm_tc.cu
+double exp2_fma_fraction();  // kvbm_tc.cu: share of exp2 evaluated on the FMA pipe
 int validate(const kvbm_problem* p);
 int select_path(const kvbm_problem* p, int device);
 // `rg` sizes the tf32 split copies of a packed q/k (path 2) by their rows.

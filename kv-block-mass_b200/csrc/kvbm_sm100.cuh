@@ -232,23 +232,34 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 
 // 2^x for two arguments on the FMA pipe (no MUFU): x = j + f with
 // j = rint(x) (the 1.5 * 2^23 shift rounds to nearest), f in [-1/2, 1/2];
-// p(f) ~= 2^f is the degree-4 minimax polynomial for relative error on that
-// interval (max 2.7e-6, kv-block-mass_b200/csrc/gen_exp2_poly.py), and 2^j is
+// p(f) ~= 2^f is the degree-kDeg minimax polynomial for relative error on
+// that interval (degree 4: max 2.7e-6; degree 3: 7.5e-5;
+// kv-block-mass_b200/csrc/gen_exp2_poly.py), and 2^j is
 // added into the exponent field.  x is clamped at -126.75 so that every
 // result below 2^-126 is a positive denormal (never a wrapped exponent); a
 // flush-to-zero accumulate adds those as exact zeros, like ex2.approx.ftz.
+template <int kDeg = 4>
 __device__ __forceinline__ float2 exp2_fma2(float2 x) {
+  static_assert(kDeg == 3 || kDeg == 4, "minimax degree 3 or 4");
   constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
   x.x = fmaxf(x.x, -126.75f);
   x.y = fmaxf(x.y, -126.75f);
   const float2 t = fadd2(x, make_float2(kShift, kShift));
   const float2 j = fadd2(t, make_float2(-kShift, -kShift));
   const float2 f = ffma2(j, make_float2(-1.f, -1.f), x);
-  float2 p = ffma2(f, make_float2(0.009570102207362652f, 0.009570102207362652f),
-                   make_float2(0.05591785907745361f, 0.05591785907745361f));
-  p = ffma2(p, f, make_float2(0.240247443318367f, 0.240247443318367f));
-  p = ffma2(p, f, make_float2(0.6931217908859253f, 0.6931217908859253f));
-  p = ffma2(p, f, make_float2(0.9999992847442627f, 0.9999992847442627f));
+  float2 p;
+  if constexpr (kDeg == 4) {  // max relative error 2.7e-6
+    p = ffma2(f, make_float2(0.009570102207362652f, 0.009570102207362652f),
+              make_float2(0.05591785907745361f, 0.05591785907745361f));
+    p = ffma2(p, f, make_float2(0.240247443318367f, 0.240247443318367f));
+    p = ffma2(p, f, make_float2(0.6931217908859253f, 0.6931217908859253f));
+    p = ffma2(p, f, make_float2(0.9999992847442627f, 0.9999992847442627f));
+  } else {  // max relative error 7.5e-5
+    p = ffma2(f, make_float2(0.0551716685295105f, 0.0551716685295105f),
+              make_float2(0.2426111251115799f, 0.2426111251115799f));
+    p = ffma2(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
+    p = ffma2(p, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
+  }
   // bits(t) = bits(1.5 * 2^23) + j and 0x4B400000 << 23 == 0 (mod 2^32), so
   // (bits(t) << 23) is j << 23: the exponent increment of 2^j.
   const uint32_t rx = __float_as_uint(p.x) + (__float_as_uint(t.x) << 23);

@@ -158,8 +158,19 @@ __device__ __forceinline__ void load_half(uint32_t taddr, float (&v)[HALF]) {
 // ex2 per score element is the binding unit of both passes, and the FMA pipe
 // has room to absorb part of it.  The groups are spread evenly so that the
 // scheduler can interleave both kinds.
+// 4 of 16 groups, degree-4 polynomial: on the Llama-3-8B N=32768 step a
+// sweep of 2-6 groups x degree 3/4 gave 10.05 ms for this choice against
+// 10.1-10.2 ms for 2 groups.  Degree 3 (max relative error 7.5e-5) was about
+// 1% faster still, but its bias does not cancel between the two passes: the
+// sum rule of the Llama-3-70B N=131072 shape came out 1.15e-5 off, over the
+// 1e-5 that the sum rule must hold to.
 #ifndef KVBM_EMU_GROUPS
-#define KVBM_EMU_GROUPS 2
+#define KVBM_EMU_GROUPS 4
+#endif
+// Degree of the FMA-pipe polynomial for bf16/fp16 inputs (4: max relative
+// error 2.7e-6; fp32 inputs on the 3xTF32 path always use degree 4).
+#ifndef KVBM_EXP2_DEGREE
+#define KVBM_EXP2_DEGREE 4
 #endif
 constexpr int kGroups = HALF / 4;
 constexpr int kEmuGroups = KVBM_EMU_GROUPS;
@@ -169,7 +180,13 @@ __host__ __device__ constexpr bool emu_group(int g) {
   return ((g + 1) * kEmuGroups) / kGroups != (g * kEmuGroups) / kGroups;  // Bresenham spread
 }
 
+template <Op kOp>
+constexpr int exp2_degree() {
+  return kOp == Op::TF32X3 ? 4 : KVBM_EXP2_DEGREE;
+}
+
 // Sum over the half row of 2^(v*C + nm), nm = -(running max); masked entries hold -inf.
+template <int kDeg>
 __device__ __forceinline__ float row_sum_exp2(const float (&v)[HALF], float C, float nm) {
   const float2 C2 = make_float2(C, C), N2 = make_float2(nm, nm);
   float2 a0 = make_float2(0.f, 0.f), a1 = a0;
@@ -179,8 +196,8 @@ __device__ __forceinline__ float row_sum_exp2(const float (&v)[HALF], float C, f
     const float2 x0 = ffma2(make_float2(v[c], v[c + 1]), C2, N2);
     const float2 x1 = ffma2(make_float2(v[c + 2], v[c + 3]), C2, N2);
     if (emu_group(g)) {
-      a0 = fadd2_ftz(a0, exp2_fma2(x0));
-      a1 = fadd2_ftz(a1, exp2_fma2(x1));
+      a0 = fadd2_ftz(a0, exp2_fma2<kDeg>(x0));
+      a1 = fadd2_ftz(a1, exp2_fma2<kDeg>(x1));
     } else {
       a0 = fadd2_ftz(a0, make_float2(ex2(x0.x), ex2(x0.y)));
       a1 = fadd2_ftz(a1, make_float2(ex2(x1.x), ex2(x1.y)));
@@ -193,7 +210,7 @@ __device__ __forceinline__ float row_sum_exp2(const float (&v)[HALF], float C, f
 // acc += 2^(v[c]*C + nL[c]) over the half row, per-column nL = -lse2 (query
 // columns); with kDiag, columns c < keep_from are masked to 0; with kBits,
 // columns whose bit in `bits` (bit c of word c / 32) is clear are masked to 0.
-template <bool kDiag, bool kBits = false>
+template <int kDeg, bool kDiag, bool kBits = false>
 __device__ __forceinline__ float2 col_sum_exp2(const float (&v)[HALF], float C, const float* nL, int keep_from,
                                                float2 acc, uint2 bits = make_uint2(0xffffffffu, 0xffffffffu)) {
   const float2 C2 = make_float2(C, C);
@@ -219,8 +236,8 @@ __device__ __forceinline__ float2 col_sum_exp2(const float (&v)[HALF], float C, 
     const float2 x0 = ffma2(v0, C2, make_float2(l4.x, l4.y));
     const float2 x1 = ffma2(v1, C2, make_float2(l4.z, l4.w));
     if (emu_group(g)) {
-      acc = fadd2_ftz(acc, exp2_fma2(x0));
-      a1 = fadd2_ftz(a1, exp2_fma2(x1));
+      acc = fadd2_ftz(acc, exp2_fma2<kDeg>(x0));
+      a1 = fadd2_ftz(a1, exp2_fma2<kDeg>(x1));
     } else {
       acc = fadd2_ftz(acc, make_float2(ex2(x0.x), ex2(x0.y)));
       a1 = fadd2_ftz(a1, make_float2(ex2(x1.x), ex2(x1.y)));
@@ -398,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           l = l * ex2(m - mt);
           m = mt;
         }
-        l += row_sum_exp2(v, a.C, -m);
+        l += row_sum_exp2<exp2_degree<kOp>()>(v, a.C, -m);
       }
     }
     // Merge the two column halves of each row (fixed order: lower half first).
@@ -604,10 +621,11 @@ __global__ void __launch_bounds__(kThreads, 2)
             for (int c = 0; c < HALF; ++c) v[c] = c < keep_to ? v[c] : -INFINITY;
           }
         }
+        constexpr int kDeg = exp2_degree<kOp>();
         if (a.causal && r == c0)
-          acc = col_sum_exp2<true, kB>(v, C, nL, rl - hf * HALF, acc, pw);
+          acc = col_sum_exp2<kDeg, true, kB>(v, C, nL, rl - hf * HALF, acc, pw);
         else
-          acc = col_sum_exp2<false, kB>(v, C, nL, 0, acc, pw);  // every pair kept
+          acc = col_sum_exp2<kDeg, false, kB>(v, C, nL, 0, acc, pw);  // every pair kept
       }
       mbar_arrive(&l_empty[t]);
     }
@@ -852,6 +870,8 @@ int launch_km(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s
 }  // namespace
 
 bool tc_path_enabled() { return encode_fn() != nullptr; }
+
+double exp2_fma_fraction() { return (double)kEmuGroups / kGroups; }
 
 int launch_tc(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws, cudaStream_t s,
               const LaunchOpts& o) {

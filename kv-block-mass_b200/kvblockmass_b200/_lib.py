@@ -42,6 +42,7 @@ EXPORTED = [
     "kvbm_block_mass_events",
     "kvbm_block_mass_lse",
     "kvbm_measure_ex2_rate",
+    "kvbm_exp2_fma_fraction",
     "kvbm_check_device_errors",
     "kvbm_block_mass_static",
     "kvbm_static_scratch_bytes",
@@ -190,6 +191,8 @@ def load() -> ctypes.CDLL:
                                         ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
     lib.kvbm_measure_ex2_rate.restype = ctypes.c_int
     lib.kvbm_measure_ex2_rate.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_double)]
+    lib.kvbm_exp2_fma_fraction.restype = ctypes.c_double
+    lib.kvbm_exp2_fma_fraction.argtypes = []
     # No-allocation variant: scratch from a fixed device array inside the library.
     lib.kvbm_block_mass_static.restype = ctypes.c_int
     lib.kvbm_block_mass_static.argtypes = [P, ctypes.c_void_p, ctypes.c_void_p]
