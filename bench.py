@@ -31,7 +31,8 @@ Reported beside the device-timed value:
   cpu_baseline  the CPU oracle (a numpy restatement of the reference's
                 streaming algorithm) on a bounded sample, all host cores.
 `--impl reference` times only that CPU restatement (rank 0), as the
-reference arm.
+reference arm.  `--impl reference-triton` times the reference's own Triton
+kernel (installed in baseline/_ref) on the same GPU: a secondary comparison.
 """
 
 from __future__ import annotations
@@ -65,7 +66,9 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--impl", choices=["b200", "reference", "reference-triton"], default="b200",
+                    help="reference: the CPU path (reference arm); reference-triton: the reference's own "
+                         "Triton kernel on this GPU (secondary comparison)")
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
     ap.add_argument("--seq-len", type=int, default=None,
                     help="override N of the workload (small cases for profiler captures)")
@@ -240,6 +243,57 @@ def reference_arm(args, w):
         "note": ("the reference is pure Python (torch CPU + Triton); its CPU path is timed through "
                  "the committed numpy restatement of src/kvblockmass/reference.py:35-126"),
     }
+    print(json.dumps(line), flush=True)
+
+
+def reference_triton_arm(args, w):
+    """--impl reference-triton: the reference's own GPU kernel on this GPU, rank 0 only.
+
+    A secondary, GPU-to-GPU comparison (the reference arm proper is the CPU
+    path above): kv-block-mass's unmodified ``block_mass_triton``
+    (src/kvblockmass/triton_kernel.py:148-196) from the package installed in
+    ``baseline/_ref`` (pip install --target), called through its public API on
+    the workload's inputs in HBM, each call with its own allocations as the
+    API makes them.  Prints an ``unavailable`` line if the package or Triton
+    is missing.
+    """
+    ref_dir = ROOT / "baseline" / "_ref"
+    try:
+        sys.path.insert(0, str(ref_dir))
+        from kvblockmass.triton_kernel import block_mass_triton  # noqa: E402
+    except Exception as e:  # the package is not installed on this box
+        print(json.dumps({"impl": "reference-triton", "unavailable": f"{type(e).__name__}: {e}"}), flush=True)
+        return
+    from kvblockmass_b200.workloads import make_inputs, pairs
+    import kvblockmass_b200 as kb
+
+    dev = torch.device("cuda", 0)
+    q, k, km, qm = make_inputs(w)
+    q, k = q.to(dev), k.to(dev)
+    mask = None if km is None else km.to(dev)
+    note = None
+    if qm is not None:
+        note = "the reference takes no query mask: its run keeps the dead rows this workload drops"
+    kw = dict(attn_mask=mask, causal=w.causal, block_size=w.block_size)
+    for _ in range(max(args.warmup, 1)):
+        ref = block_mass_triton(q, k, **kw)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        ref = block_mass_triton(q, k, **kw)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    ours = kb.block_mass_b200(q, k, **kw)
+    torch.cuda.synchronize()
+    rel = float(((ours.double() - ref.double()).abs() / ref.double().abs().clamp_min(1e-30)).max())
+    line = {"metric": METRIC, "value": pairs(w) / (ms * 1e-3), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "impl": "reference-triton",
+            "dtype": str(q.dtype).replace("torch.", ""), "data": "synthetic", "config": workload_config(w, 1),
+            "max_rel_vs_b200": rel, "api": "kvblockmass.triton_kernel.block_mass_triton (baseline/_ref)"}
+    if note:
+        line["note"] = note
     print(json.dumps(line), flush=True)
 
 
@@ -654,6 +708,11 @@ def main():
         if int(os.environ.get("RANK", "0")) != 0:
             return 0
         reference_arm(args, w)
+        return 0
+    if args.impl == "reference-triton":
+        if int(os.environ.get("RANK", "0")) != 0:
+            return 0
+        reference_triton_arm(args, w)
         return 0
     b200_arm(args, w)
     return 0
