@@ -282,6 +282,8 @@ KVBM_API int kvbm_block_mass_paged(const kvbm_problem* p, const kvbm_paged_kv* k
  *                     unless `paged`); its length must be <= N (p->N is the
  *                     longest sequence, longer ones are cut at N).  q_stride /
  *                     k_stride give {unused, head, row, d} in elements.
+ *                     Offsets outside [0, total_tokens] are clamped into it
+ *                     on the device: no row past the packed tensors is read.
  *                     seq_lens and cu_seqlens are exclusive.
  *   total_tokens      rows of the packed q/k (required with cu_seqlens)
  *   per_sequence      0: mass_out is [num_blocks], summed over the batch (the

@@ -287,7 +287,7 @@ int run_plan(Plan& pl, void* mass_out, void* workspace, size_t workspace_bytes, 
     void* gathered = static_cast<char*>(workspace) + pl.gather_off;
     sub.k = gathered;
     const int st = launch_page_gather(pl.paged, sub.dtype, pl.b0, pl.g0, sub.B, sub.Hkv, sub.N, sub.D, pl.lens0,
-                                      pl.cu0, gathered, s);
+                                      pl.cu0, pl.rg.total, gathered, s);
     if (st != KVBM_OK) return st;
   }
   void* out = mass_out;

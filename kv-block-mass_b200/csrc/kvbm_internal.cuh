@@ -51,19 +51,24 @@ struct Ragged {
 
 // Where sequence b lives: its length n (<= N) and, per operand, the first row
 // and the batch coordinate of its rows (packed: row cu[b], batch 0; padded:
-// row 0, batch b).
+// row 0, batch b).  A packed sequence's rows are clamped into
+// [0, total): offsets that a caller got wrong never reach memory past the
+// packed tensors.
 struct SeqView {
   int n;
   int q_row, q_b;
   int k_row, k_b;
 };
 
-__host__ __device__ inline SeqView seq_view(const int32_t* lens, const int32_t* cu, bool k_packed, int b, int N) {
+__host__ __device__ inline SeqView seq_view(const int32_t* lens, const int32_t* cu, bool k_packed, int b, int N,
+                                            long long total) {
   SeqView v{N, 0, b, 0, b};
   if (cu != nullptr) {
-    const int s0 = cu[b];
-    const int len = cu[b + 1] - s0;
-    v.n = len < 0 ? 0 : (len < N ? len : N);
+    long long s0 = cu[b], s1 = cu[b + 1];
+    s0 = s0 < 0 ? 0 : (s0 > total ? total : s0);
+    s1 = s1 < s0 ? s0 : (s1 > total ? total : s1);
+    const long long len = s1 - s0;
+    v.n = (int)(len < N ? len : N);
     v.q_row = s0;
     v.q_b = 0;
     if (k_packed) {
@@ -111,7 +116,7 @@ int read_and_clear_device_error(cudaStream_t s, int* err);
 // Rows n >= the sequence's length (lens / cu, batch index b0 + b) are written
 // as zeros without reading the block table.
 int launch_page_gather(const kvbm_paged_kv* kv, int dtype, int b0, int g0, int nb, int ng, int N, int D,
-                       const int32_t* lens, const int32_t* cu, void* out, cudaStream_t s);
+                       const int32_t* lens, const int32_t* cu, long long total, void* out, cudaStream_t s);
 // Page error word: set when a block-table entry was outside [0, num_pages).
 int read_and_clear_page_error(cudaStream_t s, int* err);
 

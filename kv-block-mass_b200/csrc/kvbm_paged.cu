@@ -36,7 +36,8 @@ template <typename V>
 __global__ void __launch_bounds__(kGatherThreads) gather_pages_kernel(
     const V* __restrict__ cache, long long cs0, long long cs1, long long cs2, long long cs3, int num_pages,
     int page_size, const int32_t* __restrict__ table, long long ts, int b0, int g0, int ng, int N, int dv,
-    long long rows, const int32_t* __restrict__ lens, const int32_t* __restrict__ cu, V* __restrict__ out) {
+    long long rows, const int32_t* __restrict__ lens, const int32_t* __restrict__ cu, long long total,
+    V* __restrict__ out) {
   const int rpb = kGatherThreads / dv;  // rows per block step
   const int t = threadIdx.x;
   if (t >= rpb * dv) return;
@@ -54,7 +55,7 @@ __global__ void __launch_bounds__(kGatherThreads) gather_pages_kernel(
         const long long bg = r / N;
         const int g = (int)(bg % ng), b = (int)(bg / ng);
         // keys past the sequence's length stay zero: their table entries are not read
-        if (n >= seq_view(lens, cu, false, b0 + b, N).n) continue;
+        if (n >= seq_view(lens, cu, false, b0 + b, N, total).n) continue;
         const int page = table[(long long)(b0 + b) * ts + n / page_size];
         if (page >= 0 && page < num_pages) {
           v[j] = cache[(long long)page * cs0 + (long long)(n % page_size) * cs1 + (long long)(g0 + g) * cs2 +
@@ -74,7 +75,7 @@ __global__ void __launch_bounds__(kGatherThreads) gather_pages_kernel(
 
 template <typename V>
 int launch_gather(const kvbm_paged_kv* kv, int esize, int b0, int g0, int nb, int ng, int N, int D,
-                  const int32_t* lens, const int32_t* cu, void* out, cudaStream_t s) {
+                  const int32_t* lens, const int32_t* cu, long long total, void* out, cudaStream_t s) {
   const int per = (int)sizeof(V) / esize;  // elements per V
   const int dv = D / per;
   const long long rows = (long long)nb * ng * N;
@@ -85,23 +86,23 @@ int launch_gather(const kvbm_paged_kv* kv, int esize, int b0, int g0, int nb, in
   gather_pages_kernel<V><<<(unsigned)blocks, kGatherThreads, 0, s>>>(
       static_cast<const V*>(kv->k_cache), cs[0] / per, cs[1] / per, cs[2] / per, per == 1 ? cs[3] : 1,
       kv->num_pages, kv->page_size, kv->block_table, kv->block_table_stride, b0, g0, ng, N, dv, rows, lens, cu,
-      static_cast<V*>(out));
+      total, static_cast<V*>(out));
   return cudaGetLastError() == cudaSuccess ? KVBM_OK : KVBM_ERR_CUDA;
 }
 
 }  // namespace
 
 int launch_page_gather(const kvbm_paged_kv* kv, int dtype, int b0, int g0, int nb, int ng, int N, int D,
-                       const int32_t* lens, const int32_t* cu, void* out, cudaStream_t s) {
+                       const int32_t* lens, const int32_t* cu, long long total, void* out, cudaStream_t s) {
   const int esize = dtype == KVBM_F64 ? 8 : (dtype == KVBM_F32 ? 4 : 2);
   const int64_t* cs = kv->cache_stride;
   // 16-byte vectors when every row of D elements starts on a 16-byte boundary
   bool vec = cs[3] == 1 && (D * esize) % 16 == 0 && ((uintptr_t)kv->k_cache % 16) == 0;
   for (int i = 0; i < 3; ++i) vec = vec && (cs[i] * esize) % 16 == 0;
-  if (vec) return launch_gather<uint4>(kv, esize, b0, g0, nb, ng, N, D, lens, cu, out, s);
-  if (esize == 8) return launch_gather<unsigned long long>(kv, esize, b0, g0, nb, ng, N, D, lens, cu, out, s);
-  if (esize == 4) return launch_gather<unsigned int>(kv, esize, b0, g0, nb, ng, N, D, lens, cu, out, s);
-  return launch_gather<unsigned short>(kv, esize, b0, g0, nb, ng, N, D, lens, cu, out, s);
+  if (vec) return launch_gather<uint4>(kv, esize, b0, g0, nb, ng, N, D, lens, cu, total, out, s);
+  if (esize == 8) return launch_gather<unsigned long long>(kv, esize, b0, g0, nb, ng, N, D, lens, cu, total, out, s);
+  if (esize == 4) return launch_gather<unsigned int>(kv, esize, b0, g0, nb, ng, N, D, lens, cu, total, out, s);
+  return launch_gather<unsigned short>(kv, esize, b0, g0, nb, ng, N, D, lens, cu, total, out, s);
 }
 
 int read_and_clear_page_error(cudaStream_t s, int* err) {

@@ -42,6 +42,7 @@ struct Args {
   const int32_t* lens;  // ragged lengths [B] or null
   const int32_t* cu;    // packed row offsets [B+1] or null
   int kpacked;          // k packed like q
+  long long total;      // rows of the packed q (and k)
 };
 
 template <typename In, typename Acc>
@@ -150,7 +151,7 @@ __global__ void __launch_bounds__(NT) simt_lse_kernel(Args<Acc> a) {
   const int hidx = blockIdx.y;                         // (u - ub) * G + hh
   const int u = a.ub + hidx / a.G, hh = hidx % a.G;
   const int b = u / a.Hkv, g = u % a.Hkv, h = g * a.G + hh;
-  const SeqView sv = seq_view(a.lens, a.cu, a.kpacked != 0, b, a.N);
+  const SeqView sv = seq_view(a.lens, a.cu, a.kpacked != 0, b, a.N, a.total);
   const int n = sv.n;
   if (r0 >= n) return;  // past the sequence: pass 2 never reads these rows
 
@@ -230,7 +231,7 @@ __global__ void __launch_bounds__(NT) simt_mass_kernel(Args<Acc> a) {
   const int uu = blockIdx.z;
   const int u = a.ub + uu;
   const int b = u / a.Hkv, g = u % a.Hkv;
-  const SeqView sv = seq_view(a.lens, a.cu, a.kpacked != 0, b, a.N);
+  const SeqView sv = seq_view(a.lens, a.cu, a.kpacked != 0, b, a.N, a.total);
   const int n = sv.n;
   const int qa = y * a.qchunk;
   if (c0 >= n || qa >= n) {
@@ -306,6 +307,7 @@ int launch_typed(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_
   a.lens = o.rg.lens;
   a.cu = o.rg.cu;
   a.kpacked = o.rg.k_packed ? 1 : 0;
+  a.total = o.rg.total;
 
   const int U = p->unit_end - p->unit_begin;
   const size_t smem1 = size_t(2) * p->D * 64 * sizeof(Acc);
@@ -425,7 +427,7 @@ int launch_simt(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* 
 template <typename Acc, bool kNegated>
 __global__ void lse_import_kernel(const float* lse, long long s0, long long s1, long long s2, Acc* out, int N,
                                   int Nrow, int G, int Hkv, int ub, long long rows_total, const uint8_t* qmask,
-                                  long long qmb, const int32_t* lens, const int32_t* cu) {
+                                  long long qmb, const int32_t* lens, const int32_t* cu, long long total) {
   const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   if (idx >= rows_total) return;
   const int i = (int)(idx % Nrow);
@@ -433,7 +435,7 @@ __global__ void lse_import_kernel(const float* lse, long long s0, long long s1, 
   const int u = ub + (int)(hidx / G), hh = (int)(hidx % G);
   const int b = u / Hkv, h = (u % Hkv) * G + hh;
   // a packed batch indexes its LSE like q: row cu[b] + i of [H_q, total_tokens]
-  const SeqView sv = seq_view(lens, cu, false, b, N);
+  const SeqView sv = seq_view(lens, cu, false, b, N, total);
   bool dead = i >= sv.n;
   double v = 0.0;
   if (!dead) {
@@ -458,15 +460,15 @@ int launch_lse_import(const kvbm_problem* p, const WsLayout& L, const float* lse
   if (L.path >= 1) {
     lse_import_kernel<float, true><<<(unsigned)blocks, threads, 0, s>>>(
         lse, st[0], st[1], st[2], reinterpret_cast<float*>(base), p->N, Nrow, G, p->Hkv, p->unit_begin, rows,
-        p->query_mask, p->query_mask_bstride, rg.lens, rg.cu);
+        p->query_mask, p->query_mask_bstride, rg.lens, rg.cu, rg.total);
   } else if (p->dtype == KVBM_F64) {
     lse_import_kernel<double, false><<<(unsigned)blocks, threads, 0, s>>>(
         lse, st[0], st[1], st[2], reinterpret_cast<double*>(base), p->N, Nrow, G, p->Hkv, p->unit_begin, rows,
-        p->query_mask, p->query_mask_bstride, rg.lens, rg.cu);
+        p->query_mask, p->query_mask_bstride, rg.lens, rg.cu, rg.total);
   } else {
     lse_import_kernel<float, false><<<(unsigned)blocks, threads, 0, s>>>(
         lse, st[0], st[1], st[2], reinterpret_cast<float*>(base), p->N, Nrow, G, p->Hkv, p->unit_begin, rows,
-        p->query_mask, p->query_mask_bstride, rg.lens, rg.cu);
+        p->query_mask, p->query_mask_bstride, rg.lens, rg.cu, rg.total);
   }
   return cudaGetLastError() == cudaSuccess ? KVBM_OK : KVBM_ERR_CUDA;
 }

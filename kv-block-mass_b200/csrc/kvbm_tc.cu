@@ -68,6 +68,7 @@ struct TcArgs {
   const int32_t* lens;     // ragged lengths [B] or null
   const int32_t* cu;       // packed row offsets [B+1] or null
   int kpacked;             // k packed like q
+  long long total;         // rows of the packed q (and k)
 };
 
 // Key tiles of query chunk y that hold a kept pair: with causal_skip only
@@ -296,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int b = u / a.Hkv, g = u % a.Hkv, h = g * a.G + hh;
   // kRagged: per-sequence lengths / packed rows (kvbm_options); otherwise
   // every sequence has a.N positions at rows [0, a.N) of batch entry b
-  const SeqView sv = kRagged ? seq_view(a.lens, a.cu, a.kpacked != 0, b, a.N) : SeqView{a.N, 0, b, 0, b};
+  const SeqView sv = kRagged ? seq_view(a.lens, a.cu, a.kpacked != 0, b, a.N, a.total) : SeqView{a.N, 0, b, 0, b};
   const int N = sv.n;  // positions of this sequence
   const int qt = (a.N + TILE - 1) / TILE - 1 - (int)blockIdx.y;
   const int ntiles = (N + TILE - 1) / TILE;
@@ -478,7 +479,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   const int u = a.ub + uu;
   const int b = u / a.Hkv, g = u % a.Hkv;
-  const SeqView sv = kRagged ? seq_view(a.lens, a.cu, a.kpacked != 0, b, a.N) : SeqView{a.N, 0, b, 0, b};
+  const SeqView sv = kRagged ? seq_view(a.lens, a.cu, a.kpacked != 0, b, a.N, a.total) : SeqView{a.N, 0, b, 0, b};
   const int N = sv.n;  // positions of this sequence
   const int c0 = kt * TILE;
   const int qa = y * a.qchunk;
@@ -820,6 +821,7 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
   a.lens = rg.lens;
   a.cu = rg.cu;
   a.kpacked = rg.k_packed ? 1 : 0;
+  a.total = rg.total;
   if (kMask == kMaskPairs) {
     uint32_t* bits = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + L.bits_off);
     const long long words = (long long)L.bits_batches * a.Npad * a.W;

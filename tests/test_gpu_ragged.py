@@ -180,3 +180,18 @@ def test_ragged_serving_batch_full_size(cuda_device):
         assert abs(float(per[b].double().sum()) - 32 * L) <= 1e-5 * 32 * L
     padded = kb.block_mass_b200(q, k, causal=True, block_size=64, seq_lens=lens, per_sequence=True)
     assert torch.equal(per, padded)
+
+
+@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.float64, 64), (torch.bfloat16, 80)])
+def test_cu_seqlens_past_total_are_clamped(cuda_device, dtype, D):
+    """A cu_seqlens entry past total_tokens reads nothing past the packed tensors:
+    the sequence is cut at total_tokens (same result as the clamped offsets)."""
+    lens_l = [300, 200]
+    q, k, qp, kp, cu, lens, _, _ = ragged_inputs(2, 8, 2, 300, D, dtype, lens_l, 69, cuda_device)
+    bad = torch.tensor([0, 300, 700], dtype=torch.int32, device=cuda_device)   # total is 500
+    want = kb.block_mass_varlen(qp, kp, cu, max_seqlen=300, causal=True, block_size=64)
+    got = kb.block_mass_varlen(qp, kp, bad, max_seqlen=300, causal=True, block_size=64)
+    assert torch.equal(got, want)
+    lse = torch.zeros(8, qp.shape[0], device=cuda_device)
+    kb.block_mass_varlen(qp, kp, bad, max_seqlen=300, causal=True, block_size=64, lse=lse)
+    torch.cuda.synchronize()
