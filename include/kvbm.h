@@ -384,6 +384,16 @@ KVBM_API size_t kvbm_design_workspace_bytes(const kvbm_design_args* d);
 KVBM_API int kvbm_design(const kvbm_design_args* d, const kvbm_design_out* out, void* workspace,
                 size_t workspace_bytes, void* stream);
 
+/* Self-test of the failure path of the tcgen05 kernels' pipeline waits: one
+ * thread waits on an mbarrier that nothing arrives at, through the same
+ * bounded wait the kernels use, with a limit of limit_ns (1 us .. 2 s).  The
+ * wait gives up, sets the device error word (kvbm_check_device_errors then
+ * returns KVBM_ERR_TIMEOUT) and the kernel returns; *waited = 1 if the wait
+ * was satisfied (it never is), 0 if it gave up.  Synchronises `stream`.
+ * Nothing faults or hangs, and the context stays usable.  No counterpart in
+ * the reference. */
+KVBM_API int kvbm_selftest_wait_timeout(void* stream, uint64_t limit_ns, int* waited);
+
 /* Reads and clears the device-side error words of the current device (set
  * when a bounded wait inside a tcgen05 kernel gave up, or when a page gather
  * met a block-table entry out of range).  Synchronises `stream`.  Returns

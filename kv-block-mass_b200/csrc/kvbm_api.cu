@@ -1,6 +1,7 @@
 // C ABI entry points (include/kvbm.h): validation, kernel-path choice,
 // workspace layout and the two-pass + reduce launch sequence.
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 #include <stdio.h>
 
 #include <atomic>
@@ -141,12 +142,22 @@ int run_passes(const kvbm_problem* p, const WsLayout& L, int path, void* mass_ou
   o.run_pass1 = lse == nullptr;
   o.rg = rg;
   int st = KVBM_OK;
-  if (lse != nullptr) st = launch_lse_import(p, L, lse, lse_stride, ws, s, rg);
+  if (lse != nullptr) {
+    nvtxRangePushA("kvbm lse import");
+    st = launch_lse_import(p, L, lse, lse_stride, ws, s, rg);
+    nvtxRangePop();
+  }
   if (st != KVBM_OK) return st;
+  // NVTX ranges mark the host-side enqueue of each pass (a profiler pairs
+  // them with the kernels they launch)
+  nvtxRangePushA(lse != nullptr ? "kvbm pass 2 (mass)" : "kvbm pass 1 (lse) + pass 2 (mass)");
   st = (path >= 1) ? launch_tc(p, L, mass_out, ws, s, o) : launch_simt(p, L, mass_out, ws, s, o);
+  nvtxRangePop();
   if (st != KVBM_OK) return st;
   if (!mark(2)) return KVBM_ERR_CUDA;
+  nvtxRangePushA("kvbm bucket reduce");
   st = launch_reduce(p, L, mass_out, ws, s, per_sequence);
+  nvtxRangePop();
   if (st != KVBM_OK) return st;
   return mark(3) ? KVBM_OK : KVBM_ERR_CUDA;
 }
@@ -286,8 +297,10 @@ int run_plan(Plan& pl, void* mass_out, void* workspace, size_t workspace_bytes, 
   if (pl.paged != nullptr) {
     void* gathered = static_cast<char*>(workspace) + pl.gather_off;
     sub.k = gathered;
+    nvtxRangePushA("kvbm page gather");
     const int st = launch_page_gather(pl.paged, sub.dtype, pl.b0, pl.g0, sub.B, sub.Hkv, sub.N, sub.D, pl.lens0,
                                       pl.cu0, pl.rg.total, gathered, s);
+    nvtxRangePop();
     if (st != KVBM_OK) return st;
   }
   void* out = mass_out;
@@ -462,6 +475,18 @@ int kvbm_block_mass_ex(const kvbm_problem* p, const kvbm_options* o, void* mass_
   if (st != KVBM_OK) return st;
   return run_plan(pl, mass_out, workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
                   o != nullptr ? o->events : nullptr);
+}
+
+int kvbm_selftest_wait_timeout(void* stream, uint64_t limit_ns, int* waited) {
+  if (waited == nullptr) return KVBM_ERR_NULL;
+  if (limit_ns < 1000 || limit_ns > 2000000000ull) return KVBM_ERR_SHAPE;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return KVBM_ERR_CUDA;
+  }
+  if (device_kind(dev) != 1) return KVBM_ERR_DEVICE;
+  return selftest_wait_timeout(static_cast<cudaStream_t>(stream), limit_ns, waited);
 }
 
 int kvbm_check_device_errors(void* stream) {

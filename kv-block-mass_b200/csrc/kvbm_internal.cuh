@@ -109,6 +109,8 @@ int launch_reduce(const kvbm_problem* p, const WsLayout& L, void* mass_out, cons
 
 // Device error word: set when a bounded wait in a tcgen05 kernel gives up.
 int read_and_clear_device_error(cudaStream_t s, int* err);
+// kvbm_tc.cu: a bounded wait that nothing satisfies (kvbm_selftest_wait_timeout).
+int selftest_wait_timeout(cudaStream_t s, unsigned long long limit_ns, int* waited);
 
 // Paged-KV input (kvbm_paged.cu): copies the key rows of batches
 // [b0, b0 + nb) x kv-heads [g0, g0 + ng) out of the paged cache into a dense

@@ -873,6 +873,36 @@ int launch_km(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s
 
 bool tc_path_enabled() { return encode_fn() != nullptr; }
 
+namespace {
+__device__ int g_selftest_result = -1;
+
+// One thread waits on an mbarrier that nothing arrives at, through the same
+// bounded wait as the pipeline kernels: it gives up after limit_ns, sets the
+// device error word and the kernel returns (no async copy targets the
+// barrier, so leaving it pending is harmless).
+__global__ void selftest_wait_kernel(unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) g_selftest_result = mbar_wait(&bar, 0, &abort_flag, limit_ns) ? 1 : 0;
+}
+}  // namespace
+
+int selftest_wait_timeout(cudaStream_t s, unsigned long long limit_ns, int* waited) {
+  selftest_wait_kernel<<<1, 32, 0, s>>>(limit_ns);
+  if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
+  if (cudaMemcpyFromSymbolAsync(waited, g_selftest_result, sizeof(int), 0, cudaMemcpyDeviceToHost, s) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return KVBM_ERR_CUDA;
+  return KVBM_OK;
+}
+
 double exp2_fma_fraction() { return (double)kEmuGroups / kGroups; }
 
 int launch_tc(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws, cudaStream_t s,

@@ -44,6 +44,7 @@ EXPORTED = [
     "kvbm_measure_ex2_rate",
     "kvbm_exp2_fma_fraction",
     "kvbm_check_device_errors",
+    "kvbm_selftest_wait_timeout",
     "kvbm_block_mass_static",
     "kvbm_static_scratch_bytes",
     "kvbm_validate_paged",
@@ -221,6 +222,8 @@ def load() -> ctypes.CDLL:
     lib.kvbm_design.restype = ctypes.c_int
     lib.kvbm_design.argtypes = [ctypes.POINTER(DesignArgs), ctypes.POINTER(DesignOut), ctypes.c_void_p,
                                 ctypes.c_size_t, ctypes.c_void_p]
+    lib.kvbm_selftest_wait_timeout.restype = ctypes.c_int
+    lib.kvbm_selftest_wait_timeout.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.POINTER(ctypes.c_int)]
     lib.kvbm_check_device_errors.restype = ctypes.c_int
     lib.kvbm_check_device_errors.argtypes = [ctypes.c_void_p]
     if lib.kvbm_abi_version() != 1:

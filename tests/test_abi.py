@@ -139,3 +139,14 @@ def test_signatures_are_drop_in():
     for name in ref_reference + ref_triton:
         assert name in params, name
     assert list(inspect.signature(block_mass_triton).parameters) == ref_triton
+
+
+def test_selftest_argument_checks():
+    lib = _lib.load()
+    w = ctypes.c_int(0)
+    assert lib.kvbm_selftest_wait_timeout(None, 10, ctypes.byref(w)) == _lib.KVBM_ERR_SHAPE   # < 1 us
+    assert lib.kvbm_selftest_wait_timeout(None, 3_000_000_000, ctypes.byref(w)) == _lib.KVBM_ERR_SHAPE
+    assert lib.kvbm_selftest_wait_timeout(None, 1_000_000, None) == _lib.KVBM_ERR_NULL
+    if not torch.cuda.is_available():
+        code = lib.kvbm_selftest_wait_timeout(None, 1_000_000, ctypes.byref(w))
+        assert code in (_lib.KVBM_ERR_CUDA, _lib.KVBM_ERR_DEVICE)
