@@ -68,6 +68,7 @@ CASES = [
     ("top_covers_all", 4, 200, 64, 20, 0, 0, 500, 1e-6, False, "distinct", 12),
     ("tied_blocks", 16, 1000, 64, 100, 4, 32, 100, 1e-6, False, "tied", 13),
     ("causal_like", 32, 2048, 64, 256, 4, 32, 128, 1e-6, False, "causal", 14),
+    ("eps_floor_binds", 16, 1024, 64, 64, 4, 32, 64, 1e-4, False, "tiny", 15),
 ]
 
 
@@ -81,6 +82,8 @@ def mass_for(recipe: str, nb: int, seed: int) -> np.ndarray:
         return np.zeros(nb)
     if recipe == "tied":
         return rng.integers(1, 4, nb).astype(np.float64)
+    if recipe == "tiny":  # half the blocks ~1e-9 of the others: their pi falls under eps
+        return np.where(rng.random(nb) < 0.5, 1e-9, 1.0) * (1.0 + rng.random(nb))
     if recipe == "causal":  # fp32-valued, decaying like a causal mass vector
         return (np.arange(nb, 0, -1) * (1.0 + 0.1 * rng.random(nb))).astype(np.float32).astype(np.float64)
     raise ValueError(recipe)

@@ -291,3 +291,34 @@ def test_pinned_host_inputs_pipelined(cuda_device, shape):
     assert max_rel(a.cpu().numpy(), b.cpu().numpy()) < 1e-6
     c = kb.block_mass_b200(q, k, attn_mask=km, query_mask=qm, causal=True, block_size=64, device=cuda_device)
     assert torch.equal(a, c)
+
+
+def test_causal_skip_is_engaged(cuda_device):
+    """causal_skip must skip work, not only give the same bits (the reference's
+    engagement test, tests/test_reference.py:148-158 and :189-215, records the
+    key extents its chunks visit).  Skipping the tiles above the diagonal
+    halves a causal step: the time with the skip must be well under the time
+    without it, on the same inputs."""
+    g = torch.Generator().manual_seed(90)
+    q = torch.randn(1, 16, 8192, 128, generator=g).to(torch.bfloat16).to(cuda_device)
+    k = torch.randn(1, 4, 8192, 128, generator=g).to(torch.bfloat16).to(cuda_device)
+
+    def timed(skip):
+        prep = kb.make_problem(q, k, causal=True, block_size=64, causal_skip=skip)
+        ws = torch.empty(kb.workspace_bytes(prep), dtype=torch.uint8, device=cuda_device)
+        out = torch.empty(prep.nb, device=cuda_device)
+        for _ in range(3):
+            kb.run_prepared(prep, out=out, workspace=ws)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(10):
+            kb.run_prepared(prep, out=out, workspace=ws)
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b), out.clone()
+
+    t_off, m_off = timed(False)
+    t_on, m_on = timed(True)
+    assert torch.equal(m_on, m_off)
+    assert t_on < 0.75 * t_off, (t_on, t_off)

@@ -109,3 +109,57 @@ def test_top_slice_ties_go_to_lower_index():
     s = np.array([1.0, 3.0, 3.0, 2.0, 3.0, 3.0])
     assert np.array_equal(ev.top_slice_mask(s, 3), [0, 1, 1, 0, 1, 0])
     assert np.array_equal(ev.top_slice_mask(s, 10), np.ones(6, dtype=bool))
+
+
+# ---------------------------------------------------------------- mutation gate
+# Each mutant plants one mistake in a copy of the oracle's design; the golden
+# comparison above must catch every one, and the unmutated control must pass.
+
+def _mutant_design(kind):
+    def design(scores, tail_budget, *, n_sinks=4, recency=32, top_slice=0, eps=1e-6, uniforms=None,
+               uniform_tail=False):
+        if kind == "recency_off_by_one" and recency:
+            recency -= 1
+        if kind == "sinks_dropped":
+            n_sinks = 0
+        if kind == "top_slice_dropped":
+            top_slice = 0
+        keep, pi, cert = ev.design_from_scores(scores, tail_budget, n_sinks=n_sinks, recency=recency,
+                                               top_slice=top_slice, eps=eps, uniforms=uniforms,
+                                               uniform_tail=uniform_tail)
+        tail = ~cert
+        if kind == "no_eps_floor" and tail.any() and tail_budget > 0:
+            s = np.asarray(scores, dtype=np.float64)
+            w = np.ones(tail.sum()) if uniform_tail else s[tail]
+            if not w.sum() > 0:
+                w = np.ones(tail.sum())
+            pi[tail] = np.minimum(tail_budget * w / w.sum(), 1.0)
+        if kind == "keep_threshold_loose" and tail.any():
+            u = np.asarray(uniforms)[: int(tail.sum())]
+            keep = cert.copy()
+            keep[tail] = u <= 1.5 * pi[tail]
+        return keep, pi, cert
+    return design
+
+
+def _caught(design):
+    for c in load_cases():
+        mass, u, ref_pi, ref_keep, ref_cert = case_arrays(c)
+        sc = ev.expand_block_scores(mass, c["seq_len"], c["block_size"])
+        keep, pi, cert = design(sc, c["tail_budget"], n_sinks=c["n_sinks"], recency=c["recency"],
+                                top_slice=c["top_slice"], eps=c["eps"], uniforms=u, uniform_tail=c["uniform_tail"])
+        try:
+            compare_design(c, keep, pi, cert, mass, ref_pi, ref_keep, ref_cert)
+        except AssertionError:
+            return True
+    return False
+
+
+@pytest.mark.parametrize("kind", ["recency_off_by_one", "sinks_dropped", "top_slice_dropped", "no_eps_floor",
+                                  "keep_threshold_loose"])
+def test_mutants_are_caught(kind):
+    assert _caught(_mutant_design(kind)), f"mutant {kind} passed every golden design"
+
+
+def test_mutation_gate_control_passes():
+    assert not _caught(_mutant_design("none"))
