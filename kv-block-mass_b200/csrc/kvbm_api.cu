@@ -84,7 +84,12 @@ WsLayout layout_for(const kvbm_problem* p, int path, const Ragged* rg) {
   L.path = path;
   L.acc_bytes = (p->dtype == KVBM_F64) ? 8 : 4;
   const bool tc = path >= 1;
+  // The per-key partials hold one row per query chunk: with at most
+  // kMaxQueryChunks chunks they stay O(N) per unit, so long sequences widen
+  // the chunks (multiples of 128 rows) instead of multiplying the rows.
   L.qchunk = tc ? kTcQChunk : kSimtQChunk;
+  const int min_chunk = (p->N + kMaxQueryChunks - 1) / kMaxQueryChunks;
+  if (L.qchunk < min_chunk) L.qchunk = (min_chunk + kTcTile - 1) / kTcTile * kTcTile;
   L.key_tile = tc ? kTcTile : kSimtBN;
   L.nchunk = (p->N + L.qchunk - 1) / L.qchunk;
   const size_t U = (size_t)(p->unit_end - p->unit_begin);

@@ -24,6 +24,10 @@ constexpr int kTcTile = 128;       // rows of an MMA tile (M) and key/query tile
 #define KVBM_TC_QCHUNK 2048
 #endif
 constexpr int kTcQChunk = KVBM_TC_QCHUNK;  // query rows per mass-pass CTA
+// Upper bound on query chunks (partial rows per unit) on both paths; above
+// N = 64 * chunk the chunks grow (Llama-3-70B N=131072 keeps 2048-row chunks
+// on the tensor-core path).
+constexpr int kMaxQueryChunks = 64;
 
 // Where each array lives inside the caller's workspace.
 struct WsLayout {

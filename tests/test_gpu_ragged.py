@@ -195,3 +195,23 @@ def test_cu_seqlens_past_total_are_clamped(cuda_device, dtype, D):
     lse = torch.zeros(8, qp.shape[0], device=cuda_device)
     kb.block_mass_varlen(qp, kp, bad, max_seqlen=300, causal=True, block_size=64, lse=lse)
     torch.cuda.synchronize()
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("dtype,D,N,short", [(torch.bfloat16, 128, 262144, 100000), (torch.float64, 32, 40000, 20000)])
+def test_wide_query_chunks_past_64_chunks(cuda_device, dtype, D, N, short):
+    """Past 64 query chunks per unit the chunks widen, keeping the partials O(N)
+    (tensor-core path above N=131072, SIMT above N=32768).  A short sequence in
+    the same call, which gets the wide chunks, has the mass of that sequence
+    computed alone with the normal chunks (up to the fp64 reduce's grouping)."""
+    g = torch.Generator().manual_seed(91)
+    q = torch.randn(2, 4, N, D, generator=g).to(dtype).to(cuda_device)
+    k = torch.randn(2, 1, N, D, generator=g).to(dtype).to(cuda_device)
+    lens = torch.tensor([N, short], dtype=torch.int32, device=cuda_device)
+    per = kb.block_mass_b200(q, k, causal=True, block_size=256, seq_lens=lens, per_sequence=True)
+    for b, L in enumerate((N, short)):
+        assert abs(float(per[b].double().sum()) - 4 * L) <= 1e-5 * 4 * L
+    alone = kb.block_mass_b200(q[1:, :, :short], k[1:, :, :short], causal=True, block_size=256)
+    tol = 1e-12 if dtype == torch.float64 else 1e-6
+    assert max_rel(per[1, :alone.numel()].double().cpu().numpy(), alone.double().cpu().numpy()) < tol
+    assert torch.all(per[1, alone.numel():] == 0)
