@@ -5,6 +5,15 @@
 A drop-in for the GPU path of kv-block-mass (``block_mass`` /
 ``block_mass_triton``), computed by hand-written CUDA kernels behind the C ABI
 of ``include/kvbm.h`` (``libkvbm.so``, loaded with ctypes).
+
+Beyond the reference's entry points:
+
+* ``block_mass_b200(..., lse=, seq_lens=, per_sequence=)``: row LSE input,
+  ragged batches, one mass row per sequence;
+* ``block_mass_varlen``: packed (varlen) batches with ``cu_seqlens``;
+* ``block_mass_paged``: keys from a paged KV cache and block table;
+* ``design_from_mass``: the reference's eviction design (evict.py) on the GPU;
+* ``kvblockmass_b200.distributed``: (batch, kv-head) shards over ranks.
 """
 
 __version__ = "0.1.0"
