@@ -115,7 +115,20 @@ WsLayout layout_for(const kvbm_problem* p, int path, const Ragged* rg) {
     const size_t npad = n_lse;  // whole 128-row tiles
     L.bits_bytes = (size_t)2 * L.bits_batches * npad * (npad / 32) * 4;  // row bits + column bits
   }
-  L.total = align_up(L.bits_off + L.bits_bytes, 256);
+  L.plan_off = align_up(L.bits_off + L.bits_bytes, 256);
+  if (tc && rg != nullptr && (rg->lens != nullptr || rg->cu != nullptr)) {
+    // work lists of the ragged tensor-core passes, sized for every sequence at full length
+    const long long ntmax = (p->N + kTcTile - 1) / kTcTile;
+    long long per_unit = 0;
+    for (int y = 0; y < L.nchunk; ++y) {
+      const long long lim = (long long)(y + 1) * (L.qchunk / kTcTile);
+      per_unit += (p->causal && p->causal_skip) ? (lim < ntmax ? lim : ntmax) : ntmax;
+    }
+    L.work1_cap = (long long)U * G * ntmax;
+    L.work2_cap = (long long)U * per_unit;
+    L.plan_bytes = ragged_plan_layout((long long)U, ntmax, L.work1_cap, L.work2_cap).total;
+  }
+  L.total = align_up(L.plan_off + L.plan_bytes, 256);
   return L;
 }
 

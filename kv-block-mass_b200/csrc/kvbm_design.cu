@@ -80,35 +80,6 @@ __device__ __forceinline__ unsigned long long score_key(double s) {
   return s > 0.0 ? (unsigned long long)__double_as_longlong(s) : 0ull;
 }
 
-// Exclusive prefix sum over the CTA (one value per thread, thread order);
-// returns the CTA total in *total.  Fixed order: deterministic.
-template <typename T>
-__device__ T cta_exclusive_scan(T v, T* warp_buf, T* total) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  T x = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const T y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
-  }
-  if (lane == 31) warp_buf[w] = x;
-  __syncthreads();
-  if (w == 0) {
-    T s = lane < kWarps ? warp_buf[lane] : T(0);
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const T y = __shfl_up_sync(0xffffffffu, s, o);
-      if (lane >= o) s += y;
-    }
-    if (lane < kWarps) warp_buf[lane] = s;  // inclusive warp prefix
-  }
-  __syncthreads();
-  const T before = (w > 0 ? warp_buf[w - 1] : T(0)) + x - v;
-  *total = warp_buf[kWarps - 1];
-  __syncthreads();
-  return before;
-}
-
 __global__ void __launch_bounds__(kSelThreads) design_select_kernel(DesignArgs a) {
   __shared__ unsigned int hist[256];
   __shared__ long long sh_ll[kWarps];
@@ -195,8 +166,8 @@ __global__ void __launch_bounds__(kSelThreads) design_select_kernel(DesignArgs a
     const double s = valid ? mass_at(a, row, b) : 0.0;
     const unsigned long long key = score_key(s);
     long long eq_tot;
-    const long long eq_before =
-        eq_carry + cta_exclusive_scan<long long>((valid && a.top > 0 && key == T) ? len : 0, sh_ll, &eq_tot);
+    const long long eq_before = eq_carry + block_exclusive_scan<long long, kSelThreads>(
+                                               (valid && a.top > 0 && key == T) ? len : 0, sh_ll, &eq_tot);
     eq_carry += eq_tot;
     long long top_b = 0;
     if (valid && a.top > 0) {
@@ -208,7 +179,7 @@ __global__ void __launch_bounds__(kSelThreads) design_select_kernel(DesignArgs a
     const long long suf = valid ? max(0ll, start + len - max(R, start)) : 0;
     const long long uni = min((long long)len, pref + suf);
     long long cert_tot;
-    const long long cb = cert_carry + cta_exclusive_scan<long long>(uni, sh_ll, &cert_tot);
+    const long long cb = cert_carry + block_exclusive_scan<long long, kSelThreads>(uni, sh_ll, &cert_tot);
     cert_carry += cert_tot;
     if (valid) {
       a.prefix[(long long)row * nb + b] = (int)pref;

@@ -36,6 +36,10 @@ struct WsLayout {
   size_t split_off = 0, split_bytes = 0; // path 2: tf32 hi/lo copies of q and k (fp32)
   size_t bits_off = 0, bits_bytes = 0;   // tensor-core paths with a pair mask: packed bits
   int bits_batches = 0;                  // batch entries of the packed bits (1 or B)
+  // tensor-core paths with ragged lengths: the CTA work lists and their plan
+  size_t plan_off = 0, plan_bytes = 0;
+  long long work1_cap = 0;               // pass-1 items: U * G * ceil(N / 128)
+  long long work2_cap = 0;               // pass-2 items: U * (pass-2 CTAs of a full-length unit)
   size_t total = 0;
   int path = 0;        // 0 SIMT, 1 tcgen05 (bf16/fp16), 2 tcgen05 3xTF32 (fp32)
   int qchunk = 0;      // query rows per mass-pass CTA
@@ -84,6 +88,69 @@ __host__ __device__ inline SeqView seq_view(const int32_t* lens, const int32_t* 
     v.n = len < 0 ? 0 : (len < N ? len : N);
   }
   return v;
+}
+
+// Exclusive prefix sum over a CTA of kThreads threads (one value per thread,
+// in thread order); *total receives the CTA's sum.  Every thread must call it;
+// warp_buf holds kThreads / 32 values in shared memory.  Fixed order:
+// deterministic.
+template <typename T, int kThreads>
+__device__ T block_exclusive_scan(T v, T* warp_buf, T* total) {
+  constexpr int kWarps = kThreads / 32;
+  static_assert(kWarps >= 1 && kWarps <= 32, "one warp scans the warp sums");
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  T x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const T y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_buf[w] = x;
+  __syncthreads();
+  if (w == 0) {
+    T s = lane < kWarps ? warp_buf[lane] : T(0);
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const T y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    if (lane < kWarps) warp_buf[lane] = s;  // inclusive warp prefix
+  }
+  __syncthreads();
+  const T before = (w > 0 ? warp_buf[w - 1] : T(0)) + x - v;
+  *total = warp_buf[kWarps - 1];
+  __syncthreads();
+  return before;
+}
+
+// Byte offsets, inside the workspace's plan region, of the arrays that the
+// ragged plan kernel (kvbm_tc.cu) builds and the tensor-core passes read.
+struct RaggedPlanLayout {
+  size_t work1 = 0, work2 = 0;  // u64 items: pass 1 (unit, head, query tile), pass 2 (unit, chunk, key tile)
+  size_t counts = 0;            // long long[2]: items in work1, work2
+  size_t nt = 0, rank = 0;      // int[U]: query tiles of each unit, its place in the longest-first order
+  size_t hist = 0, start = 0, fill = 0;  // int[ntmax + 1]: units per tile count, suffix sums, cursors
+  size_t lvl_off = 0;           // long long[ntmax]: first pass-1 item of each query tile level
+  size_t unit_off = 0;          // long long[U + 1]: first pass-2 item of each unit
+  size_t total = 0;
+};
+
+inline RaggedPlanLayout ragged_plan_layout(long long U, long long ntmax, long long cap1, long long cap2) {
+  auto up = [](size_t x) { return (x + 255) / 256 * 256; };
+  RaggedPlanLayout r;
+  size_t o = 0;
+  r.work1 = o; o = up(o + 8 * (size_t)cap1);
+  r.work2 = o; o = up(o + 8 * (size_t)cap2);
+  r.counts = o; o = up(o + 2 * sizeof(long long));
+  r.nt = o; o = up(o + 4 * (size_t)U);
+  r.rank = o; o = up(o + 4 * (size_t)U);
+  r.hist = o; o = up(o + 4 * (size_t)(ntmax + 1));
+  r.start = o; o = up(o + 4 * (size_t)(ntmax + 1));
+  r.fill = o; o = up(o + 4 * (size_t)(ntmax + 1));
+  r.lvl_off = o; o = up(o + 8 * (size_t)ntmax);
+  r.unit_off = o; o = up(o + 8 * (size_t)(U + 1));
+  r.total = o;
+  return r;
 }
 
 // Host helpers (kvbm_api.cu).
