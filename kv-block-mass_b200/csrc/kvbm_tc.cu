@@ -1100,6 +1100,10 @@ int launch_tc(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws
   const bool bf16 = p->dtype == KVBM_BF16;
   if (p->D == 64) return bf16 ? launch_km<64, Op::BF16>(p, L, ws, s, o) : launch_km<64, Op::F16>(p, L, ws, s, o);
   if (p->D == 128) return bf16 ? launch_km<128, Op::BF16>(p, L, ws, s, o) : launch_km<128, Op::F16>(p, L, ws, s, o);
+  // D = 192 / 256: one CTA per SM (operand tiles of 48 / 64 KB); the tensor
+  // pipe, not the exp unit, bounds these
+  if (p->D == 192) return bf16 ? launch_km<192, Op::BF16>(p, L, ws, s, o) : launch_km<192, Op::F16>(p, L, ws, s, o);
+  if (p->D == 256) return bf16 ? launch_km<256, Op::BF16>(p, L, ws, s, o) : launch_km<256, Op::F16>(p, L, ws, s, o);
   return KVBM_ERR_HEAD_DIM;
 }
 

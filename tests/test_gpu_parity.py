@@ -164,7 +164,7 @@ def test_ragged_lengths(cuda_device, N, dtype):
         assert max_rel(got.cpu().numpy(), want) < TOL[dtype], (N, causal)
 
 
-@pytest.mark.parametrize("D", [8, 16, 32, 64, 96, 128, 256])
+@pytest.mark.parametrize("D", [8, 16, 32, 64, 96, 128, 192, 256])
 def test_head_dims(cuda_device, D):
     g = torch.Generator().manual_seed(D)
     q = torch.randn(1, 2, 300, D, generator=g)
@@ -322,3 +322,35 @@ def test_causal_skip_is_engaged(cuda_device):
     t_on, m_on = timed(True)
     assert torch.equal(m_on, m_off)
     assert t_on < 0.75 * t_off, (t_on, t_off)
+
+
+@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 192), (torch.bfloat16, 256), (torch.float16, 256)])
+def test_wide_heads_on_tensor_cores(cuda_device, dtype, D):
+    """D = 192 / 256 run the tcgen05 kernels (one CTA per SM): parity with every
+    mask kind and the LSE input, causal_skip on/off with the same bits."""
+    g = torch.Generator().manual_seed(D + 7)
+    B, Hq, Hkv, N = 2, 8, 2, 700
+    q = torch.randn(B, Hq, N, D, generator=g).to(dtype)
+    k = torch.randn(B, Hkv, N, D, generator=g).to(dtype)
+    qd, kd = q.to(cuda_device), k.to(cuda_device)
+    assert kb.kernel_path(kb.make_problem(qd, kd, causal=True)) == 1
+    km = torch.rand(N, generator=g) > 0.2
+    pm = torch.rand(N, N, generator=g) > 0.3
+    for causal in (True, False):
+        for mask in (None, km, pm):
+            dm = None if mask is None else mask.to(cuda_device)
+            got = run(qd, kd, attn_mask=dm, causal=causal, block_size=64)
+            want = oracle_for(q, k, attn_mask=mask, causal=causal, block_size=64)
+            assert max_rel(got.cpu().numpy(), want) < 1e-3, (causal, None if mask is None else mask.dim())
+    a = run(qd, kd, causal=True, block_size=64)
+    assert torch.equal(a, run(qd, kd, causal=True, block_size=64, causal_skip=False))
+    # the LSE input gives the mass of the two-pass call
+    s_ = (q.float() @ k.float().repeat_interleave(Hq // Hkv, dim=1).transpose(-1, -2)) / D ** 0.5
+    lse = s_.masked_fill(~torch.ones(N, N, dtype=torch.bool).tril(), float("-inf")).logsumexp(-1)
+    b = kb.block_mass_b200(qd, kd, causal=True, block_size=64, lse=lse.to(cuda_device))
+    assert max_rel(b.cpu().numpy(), a.cpu().numpy()) < 2e-3
+    # ragged lengths
+    lens = torch.tensor([N, 333], dtype=torch.int32, device=cuda_device)
+    r = kb.block_mass_b200(qd, kd, causal=True, block_size=64, seq_lens=lens, per_sequence=True)
+    alone = run(qd[1:, :, :333], kd[1:, :, :333], causal=True, block_size=64)
+    assert max_rel(r[1, :alone.numel()].double().cpu().numpy(), alone.double().cpu().numpy()) < 1e-6
