@@ -132,10 +132,11 @@ KVBM_API size_t kvbm_workspace_bytes(const kvbm_problem* p);
 
 /* Which kernel family will run `p` on the current device:
  * 0 = SIMT (fp32 FFMA / fp64 DFMA, any mask, D <= 256),
- * 1 = tcgen05 tensor cores with TMA and TMEM (bf16/fp16, D in {64, 128, 192,
- *     256}; 192 and 256 run one CTA per SM and are bound by the tensor pipe),
- * 2 = tcgen05 3xTF32 for fp32 inputs (D in {32, 64}): tf32 hi/lo split,
- *     three MMAs per step, fp32-grade scores,
+ * 1 = tcgen05 tensor cores with TMA and TMEM (bf16/fp16, D <= 256 with
+ *     D % 8 == 0, padded to 64/128/192/256 by the TMA's zero fill; 192 and
+ *     256 run one CTA per SM and are bound by the tensor pipe),
+ * 2 = tcgen05 3xTF32 for fp32 inputs (D <= 64 with D % 4 == 0): tf32 hi/lo
+ *     split, three MMAs per step, fp32-grade scores,
  * (paths 1 and 2 take pair masks as packed bits: 2 * Npad^2 / 8 bytes of
  * workspace per mask batch entry, Npad = N rounded up to 128),
  * negative = a kvbm_status error code, negated. */

@@ -909,6 +909,10 @@ constexpr size_t smem_mass() {
 template <int D, Op kOp, int kMask, bool kRagged>
 int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_t s, const LaunchOpts& o) {
   CUtensorMap tq, tq2, tk, tk2;
+  // The kernels work on D-element rows (whole 128-byte blocks); a head dim
+  // Dr < D is mapped with its real extent, and the TMA's zero fill past it
+  // makes the extra columns add exact zeros to every dot product.
+  const int Dr = p->D;
   // A packed operand is one batch entry of total_tokens rows; sequence b
   // starts at row cu[b] (TMA coordinates from seq_view).
   const Ragged& rg = o.rg;
@@ -917,25 +921,25 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
   if constexpr (kOp == Op::TF32X3) {
     // split q/k into tf32 hi/lo pairs in the workspace, then map those
     float* base = reinterpret_cast<float*>(static_cast<char*>(ws) + L.split_off);
-    const long long qe = (long long)Bq * p->Hq * Nq * D, ke = (long long)Bk * p->Hkv * Nk * D;
+    const long long qe = (long long)Bq * p->Hq * Nq * Dr, ke = (long long)Bk * p->Hkv * Nk * Dr;
     float *q_hi = base, *q_lo = base + qe, *k_hi = base + 2 * qe, *k_lo = base + 2 * qe + ke;
     const long long total = qe + ke;
     split_tf32_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(
         static_cast<const float*>(p->q), p->q_stride[0], p->q_stride[1], p->q_stride[2], p->q_stride[3], p->Hq,
         static_cast<const float*>(p->k), p->k_stride[0], p->k_stride[1], p->k_stride[2], p->k_stride[3], p->Hkv,
-        Nq, Nk, D, qe, ke, q_hi, q_lo, k_hi, k_lo);
+        Nq, Nk, Dr, qe, ke, q_hi, q_lo, k_hi, k_lo);
     if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
-    const int64_t qs[4] = {(int64_t)p->Hq * Nq * D, (int64_t)Nq * D, D, 1};
-    const int64_t ks[4] = {(int64_t)p->Hkv * Nk * D, (int64_t)Nk * D, D, 1};
+    const int64_t qs[4] = {(int64_t)p->Hq * Nq * Dr, (int64_t)Nq * Dr, Dr, 1};
+    const int64_t ks[4] = {(int64_t)p->Hkv * Nk * Dr, (int64_t)Nk * Dr, Dr, 1};
     const CUtensorMapDataType t = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-    if (!make_map(&tq, q_hi, t, 4, Bq, p->Hq, Nq, D, qs) || !make_map(&tq2, q_lo, t, 4, Bq, p->Hq, Nq, D, qs) ||
-        !make_map(&tk, k_hi, t, 4, Bk, p->Hkv, Nk, D, ks) || !make_map(&tk2, k_lo, t, 4, Bk, p->Hkv, Nk, D, ks))
+    if (!make_map(&tq, q_hi, t, 4, Bq, p->Hq, Nq, Dr, qs) || !make_map(&tq2, q_lo, t, 4, Bq, p->Hq, Nq, Dr, qs) ||
+        !make_map(&tk, k_hi, t, 4, Bk, p->Hkv, Nk, Dr, ks) || !make_map(&tk2, k_lo, t, 4, Bk, p->Hkv, Nk, Dr, ks))
       return KVBM_ERR_CUDA;
   } else {
     const CUtensorMapDataType t =
         kOp == Op::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    if (!make_map(&tq, p->q, t, 2, Bq, p->Hq, Nq, D, p->q_stride) ||
-        !make_map(&tk, p->k, t, 2, Bk, p->Hkv, Nk, D, p->k_stride))
+    if (!make_map(&tq, p->q, t, 2, Bq, p->Hq, Nq, Dr, p->q_stride) ||
+        !make_map(&tk, p->k, t, 2, Bk, p->Hkv, Nk, Dr, p->k_stride))
       return KVBM_ERR_CUDA;
     tq2 = tq;
     tk2 = tk;
@@ -1093,17 +1097,18 @@ int launch_tc(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws
               const LaunchOpts& o) {
   (void)mass_out;
   if (L.path == 2) {  // fp32 inputs on tf32 tensor cores (3 MMAs per step)
-    if (p->D == 32) return launch_km<32, Op::TF32X3>(p, L, ws, s, o);
-    if (p->D == 64) return launch_km<64, Op::TF32X3>(p, L, ws, s, o);
+    if (p->D <= 32) return launch_km<32, Op::TF32X3>(p, L, ws, s, o);
+    if (p->D <= 64) return launch_km<64, Op::TF32X3>(p, L, ws, s, o);
     return KVBM_ERR_HEAD_DIM;
   }
+  // Head dims run on the next whole number of 128-byte blocks (64 bf16/fp16
+  // elements); 192 and 256 take one CTA per SM (operand tiles of 48 / 64 KB)
+  // and are bound by the tensor pipe, not the exp unit.
   const bool bf16 = p->dtype == KVBM_BF16;
-  if (p->D == 64) return bf16 ? launch_km<64, Op::BF16>(p, L, ws, s, o) : launch_km<64, Op::F16>(p, L, ws, s, o);
-  if (p->D == 128) return bf16 ? launch_km<128, Op::BF16>(p, L, ws, s, o) : launch_km<128, Op::F16>(p, L, ws, s, o);
-  // D = 192 / 256: one CTA per SM (operand tiles of 48 / 64 KB); the tensor
-  // pipe, not the exp unit, bounds these
-  if (p->D == 192) return bf16 ? launch_km<192, Op::BF16>(p, L, ws, s, o) : launch_km<192, Op::F16>(p, L, ws, s, o);
-  if (p->D == 256) return bf16 ? launch_km<256, Op::BF16>(p, L, ws, s, o) : launch_km<256, Op::F16>(p, L, ws, s, o);
+  if (p->D <= 64) return bf16 ? launch_km<64, Op::BF16>(p, L, ws, s, o) : launch_km<64, Op::F16>(p, L, ws, s, o);
+  if (p->D <= 128) return bf16 ? launch_km<128, Op::BF16>(p, L, ws, s, o) : launch_km<128, Op::F16>(p, L, ws, s, o);
+  if (p->D <= 192) return bf16 ? launch_km<192, Op::BF16>(p, L, ws, s, o) : launch_km<192, Op::F16>(p, L, ws, s, o);
+  if (p->D <= 256) return bf16 ? launch_km<256, Op::BF16>(p, L, ws, s, o) : launch_km<256, Op::F16>(p, L, ws, s, o);
   return KVBM_ERR_HEAD_DIM;
 }
 

@@ -354,3 +354,38 @@ def test_wide_heads_on_tensor_cores(cuda_device, dtype, D):
     r = kb.block_mass_b200(qd, kd, causal=True, block_size=64, seq_lens=lens, per_sequence=True)
     alone = run(qd[1:, :, :333], kd[1:, :, :333], causal=True, block_size=64)
     assert max_rel(r[1, :alone.numel()].double().cpu().numpy(), alone.double().cpu().numpy()) < 1e-6
+
+
+@pytest.mark.parametrize("dtype,D,path", [
+    (torch.bfloat16, 8, 1), (torch.bfloat16, 40, 1), (torch.float16, 80, 1), (torch.bfloat16, 96, 1),
+    (torch.bfloat16, 112, 1), (torch.float16, 160, 1), (torch.bfloat16, 224, 1),
+    (torch.float32, 4, 2), (torch.float32, 12, 2), (torch.float32, 48, 2), (torch.float32, 60, 2),
+])
+def test_padded_head_dims_on_tensor_cores(cuda_device, dtype, D, path):
+    """Head dims between the kernels' 64/128/192/256 (and 32/64 for fp32) run the
+    next larger tensor-core configuration: the tensor map has the real extent,
+    and its zero fill makes the padding columns add exact zeros."""
+    g = torch.Generator().manual_seed(D + 100)
+    q = torch.randn(2, 8, 500, D, generator=g).to(dtype)
+    k = torch.randn(2, 2, 500, D, generator=g).to(dtype)
+    qd, kd = q.to(cuda_device), k.to(cuda_device)
+    assert kb.kernel_path(kb.make_problem(qd, kd, causal=True)) == path
+    for causal in (True, False):
+        got = run(qd, kd, causal=causal, block_size=64)
+        want = oracle_for(q, k, causal=causal, block_size=64)
+        assert max_rel(got.cpu().numpy(), want) < TOL[dtype], causal
+
+
+def test_head_dim_view_reads_no_padding(cuda_device):
+    """A [..., :96] view of a wider tensor: the columns past 96 are never read
+    (they hold NaN here), and the bits equal those of a contiguous copy."""
+    g = torch.Generator().manual_seed(5)
+    qw = torch.randn(1, 8, 600, 128, generator=g).to(torch.bfloat16)
+    kw = torch.randn(1, 2, 600, 128, generator=g).to(torch.bfloat16)
+    qw[..., 96:] = float("nan")
+    kw[..., 96:] = float("nan")
+    qv, kv = qw.to(cuda_device)[..., :96], kw.to(cuda_device)[..., :96]
+    assert kb.kernel_path(kb.make_problem(qv, kv, causal=True)) == 1
+    a = run(qv, kv, causal=True, block_size=64)
+    b = run(qv.contiguous(), kv.contiguous(), causal=True, block_size=64)
+    assert torch.isfinite(a).all() and torch.equal(a, b)

@@ -54,7 +54,7 @@ LENS = [1000, 333, 128, 1, 0, 777]
 
 @pytest.mark.parametrize("dtype,D,path", [
     (torch.bfloat16, 128, 1), (torch.float16, 64, 1), (torch.float32, 64, 2),
-    (torch.float64, 64, 0), (torch.bfloat16, 80, 0),
+    (torch.float64, 64, 0), (torch.bfloat16, 80, 1), (torch.bfloat16, 84, 0),
 ])
 @pytest.mark.parametrize("causal", [True, False])
 def test_ragged_padded_and_packed_vs_oracle(cuda_device, dtype, D, path, causal):
@@ -182,7 +182,7 @@ def test_ragged_serving_batch_full_size(cuda_device):
     assert torch.equal(per, padded)
 
 
-@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.float64, 64), (torch.bfloat16, 80)])
+@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.float64, 64), (torch.bfloat16, 84)])
 def test_cu_seqlens_past_total_are_clamped(cuda_device, dtype, D):
     """A cu_seqlens entry past total_tokens reads nothing past the packed tensors:
     the sequence is cut at total_tokens (same result as the clamped offsets)."""
