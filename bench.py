@@ -655,7 +655,8 @@ def b200_arm(args, w):
         "roofline": {
             "bound": "tensor", "achieved": achieved_tflops, "peak": tensor_peak, "unit": "TFLOP/s",
             "frac": achieved_tflops / tensor_peak, "traffic": traffic, "kernel": dom_name,
-            "peak_source": f"{peaks['source']} bf16_tflops (burst) of MEASURED_PEAKS.json",
+            "peak_source": ("measured bf16_tflops (burst) of MEASURED_PEAKS.json" if peaks["source"] == "measured"
+                            else "fallback 1590 TFLOP/s bf16 burst (MEASURED_PEAKS.json absent)"),
             "binding_unit": binding,
             "mufu": {"achieved_ex2_per_s": exp_rate, "peak_ex2_per_s": ex2.value,
                      "frac": exp_rate / ex2.value, "peak_source": "measured live (kvbm_measure_ex2_rate)",

@@ -26,6 +26,7 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "kvbm_internal.cuh"
@@ -47,6 +48,11 @@ constexpr int kStages = KVBM_STAGES;  // K (pass 1) / Q (pass 2) ring depth
 constexpr int kLStages = 4;         // lse2 ring depth (pass 2)
 constexpr int kTmemCols = 256;      // two 128-column fp32 accumulators
 constexpr int kMinSmem = 100 * 1024;  // caps residency at 2 CTAs/SM (TMEM: 2 x 256 columns)
+// k bytes that the units of one pass-1 CTA group may hold together (L2 is 126 MB).
+#ifndef KVBM_P1_GROUP_MIB
+#define KVBM_P1_GROUP_MIB 32
+#endif
+constexpr long long kPass1GroupBytes = (long long)KVBM_P1_GROUP_MIB << 20;
 constexpr int kExpBarrier = 1;      // named barrier of the 256 exp threads
 
 struct TcArgs {
@@ -65,6 +71,7 @@ struct TcArgs {
   int W;                   // words per bit row (Npad / 32)
   int qchunk, nchunk;
   int per_unit;            // pass-2 CTAs per unit (sum of keys_in_chunk over chunks)
+  int usel, ugroup;        // pass 1 (uniform grid): units selected, units per CTA group
   const int32_t* lens;     // ragged lengths [B] or null
   const int32_t* cu;       // packed row offsets [B+1] or null
   int kpacked;             // k packed like q
@@ -283,8 +290,11 @@ __device__ __forceinline__ void merge_ml(float& m, float& l, float mo, float lo)
 }
 
 // ============================================================ pass 1: lse2
-// grid (U_sel * G, ceil(N / 128)); blockIdx.y counts query tiles from the
-// last (longest under causal_skip) to the first.
+// 1-D grid of U_sel * G * ceil(N / 128) CTAs.  The units are cut into groups
+// of a.ugroup (the last may be smaller) whose k fits in L2 together; the grid
+// runs the groups one after another, and inside a group the query tiles from
+// the last (longest under causal_skip) to the first, every (unit, head) of the
+// group per tile.
 template <int D, Op kOp, int kMask, bool kRagged>
 __global__ void __launch_bounds__(kThreads, 2)
     tc_lse_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tq2,
@@ -315,8 +325,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     hidx = item_hi(it) * a.G + item_mid(it);
     qt = item_lo(it);
   } else {
-    hidx = blockIdx.x;
-    qt = (a.N + TILE - 1) / TILE - 1 - (int)blockIdx.y;
+    const int nt_all = a.Npad / TILE;
+    const long long per_group = (long long)a.ugroup * a.G * nt_all;
+    const int grp = (int)(blockIdx.x / per_group);
+    const int r = (int)(blockIdx.x - grp * per_group);
+    const int width = min(a.ugroup, a.usel - grp * a.ugroup) * a.G;  // (unit, head) pairs of this group
+    hidx = grp * a.ugroup * a.G + r % width;
+    qt = nt_all - 1 - r / width;
   }
   const int u = a.ub + hidx / a.G, hh = hidx % a.G;
   const int b = u / a.Hkv, g = u % a.Hkv, h = g * a.G + hh;
@@ -988,7 +1003,17 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
   }
   const int U = p->unit_end - p->unit_begin;
   const int ntiles = a.Npad / TILE;
-  dim3 grid1(U * a.G, ntiles), grid2(U * a.per_unit);
+  // Pass-1 CTAs of a unit all stream its whole k (under causal_skip, from the
+  // first tile up); running the units in groups whose k fits in L2 reads each
+  // k from DRAM about once.  On the Llama-3-8B N=32768 shape (8 MiB of k per
+  // unit) one group of all 8 units read 597 MB per launch against 335 MB of
+  // q + k.
+  const long long k_unit_bytes = (long long)Nk * Dr * (kOp == Op::TF32X3 ? 8 : 2);
+  a.usel = U;
+  a.ugroup = (int)std::max(1LL, std::min<long long>(U, kPass1GroupBytes / std::max(1LL, k_unit_bytes)));
+  const long long n1 = (long long)U * a.G * ntiles;
+  if (n1 > 0x7fffffffLL) return KVBM_ERR_SHAPE;
+  dim3 grid1((unsigned)n1), grid2(U * a.per_unit);
   if constexpr (kRagged) {
     // plan the work lists on the device, and zero the partials no CTA will write
     if (L.work1_cap > 0x7fffffffLL || L.work2_cap > 0x7fffffffLL) return KVBM_ERR_SHAPE;
