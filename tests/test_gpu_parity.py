@@ -199,6 +199,24 @@ def test_units_shard_and_sum(cuda_device):
     assert max_rel(u2.cpu().numpy(), (parts[1].double() + parts[2].double()).cpu().numpy()) < 1e-6
 
 
+def test_pass1_unit_groups_cover_every_tile(cuda_device):
+    """Pass 1 runs its CTAs in groups of units whose k fits in 32 MiB: at
+    N=65536, D=128 bf16 (16 MiB of k per unit) 3 units form the uneven groups
+    {0, 1} and {2}.  Every (unit, head, query tile) must still get its row LSE:
+    the whole call equals the sum of one-unit calls, and the sum rule holds."""
+    g = torch.Generator().manual_seed(23)
+    N = 65536
+    q = torch.randn(1, 6, N, 128, generator=g).to(torch.bfloat16).to(cuda_device)
+    k = torch.randn(1, 3, N, 128, generator=g).to(torch.bfloat16).to(cuda_device)
+    full = run(q, k, causal=True, block_size=64)
+    parts = [run(q, k, causal=True, block_size=64, units=(u, u + 1)) for u in range(3)]
+    assert max_rel(sum(p.double() for p in parts).cpu().numpy(), full.double().cpu().numpy()) < 1e-6
+    expect = 6 * N
+    assert abs(float(full.double().sum()) - expect) <= 1e-5 * expect
+    nc = run(q, k, causal=False, block_size=64)
+    assert abs(float(nc.double().sum()) - expect) <= 1e-5 * expect
+
+
 def test_drop_in_entry_points(cuda_device):
     g = torch.Generator().manual_seed(31)
     q = torch.randn(2, 4, 256, 32, generator=g, dtype=torch.float64).float()
