@@ -85,6 +85,10 @@ enum kvbm_status {
  *   pair_mask  [B|1, N, N]  pair mask: pair_mask[b*bstride + i*rstride + c]
  *                           (an [N, N] attn_mask of the reference is bstride 0)
  *
+ * Sizes: B, H_q, H_kv, D >= 1 with B*H_q <= 65535, and 1 <= N <= 2^28
+ * (268,435,456 positions, a bound that keeps every tile and work-list index
+ * in range); larger values return KVBM_ERR_SHAPE.
+ *
  * `units`: the problem splits into B*H_kv independent (batch, kv-head) units,
  * u = b*H_kv + g, each owning q-heads [g*G, (g+1)*G).  One call computes the
  * mass of units [unit_begin, unit_end); the full problem is [0, B*H_kv).

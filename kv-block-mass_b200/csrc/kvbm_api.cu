@@ -48,7 +48,8 @@ int validate(const kvbm_problem* p) {
   const long long units = (long long)p->B * p->Hkv;
   if (p->unit_begin < 0 || p->unit_end > units || p->unit_begin >= p->unit_end)
     return KVBM_ERR_UNITS;
-  if ((long long)p->B * p->Hq > 65535) return KVBM_ERR_SHAPE;  // grid.y of pass 1
+  if ((long long)p->B * p->Hq > 65535) return KVBM_ERR_SHAPE;  // grid.y of the SIMT pass 1
+  if (p->N > kMaxN) return KVBM_ERR_SHAPE;  // tile indexes fit the 21-bit work-item fields
   if (p->q == nullptr || p->k == nullptr) return KVBM_ERR_NULL;
   for (int i = 0; i < 4; ++i)
     if (p->q_stride[i] < 0 || p->k_stride[i] < 0) return KVBM_ERR_SHAPE;

@@ -28,6 +28,9 @@ constexpr int kTcQChunk = KVBM_TC_QCHUNK;  // query rows per mass-pass CTA
 // N = 64 * chunk the chunks grow (Llama-3-70B N=131072 keeps 2048-row chunks
 // on the tensor-core path).
 constexpr int kMaxQueryChunks = 64;
+// Largest sequence length accepted (2^28 positions): 128-row tiles then stay
+// below 2^21, the width of a work-item field, and padded lengths fit int.
+constexpr int kMaxN = 1 << 28;
 
 // Where each array lives inside the caller's workspace.
 struct WsLayout {

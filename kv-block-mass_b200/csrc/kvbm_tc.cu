@@ -1011,9 +1011,9 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
   const long long k_unit_bytes = (long long)Nk * Dr * (kOp == Op::TF32X3 ? 8 : 2);
   a.usel = U;
   a.ugroup = (int)std::max(1LL, std::min<long long>(U, kPass1GroupBytes / std::max(1LL, k_unit_bytes)));
-  const long long n1 = (long long)U * a.G * ntiles;
-  if (n1 > 0x7fffffffLL) return KVBM_ERR_SHAPE;
-  dim3 grid1((unsigned)n1), grid2(U * a.per_unit);
+  const long long n1 = (long long)U * a.G * ntiles, n2 = (long long)U * a.per_unit;
+  if (n1 > 0x7fffffffLL || n2 > 0x7fffffffLL) return KVBM_ERR_SHAPE;
+  dim3 grid1((unsigned)n1), grid2((unsigned)n2);
   if constexpr (kRagged) {
     // plan the work lists on the device, and zero the partials no CTA will write
     if (L.work1_cap > 0x7fffffffLL || L.work2_cap > 0x7fffffffLL) return KVBM_ERR_SHAPE;

@@ -5,6 +5,7 @@ import re
 import subprocess
 from pathlib import Path
 
+import numpy as np
 import pytest
 import torch
 
@@ -71,6 +72,10 @@ def _problem(**kw):
     ({"block_size": 0}, _lib.KVBM_ERR_BLOCK_SIZE),
     ({"units": (0, 3)}, _lib.KVBM_ERR_UNITS),
     ({"units": (1, 1)}, _lib.KVBM_ERR_UNITS),
+    ({"shape": (1, 8, 2, 1 << 28, 64)}, _lib.KVBM_OK),
+    ({"shape": (1, 8, 2, (1 << 28) + 1, 64)}, _lib.KVBM_ERR_SHAPE),
+    ({"shape": (1, 8, 2, 2**31 - 1, 64)}, _lib.KVBM_ERR_SHAPE),
+    ({"shape": (4096, 16, 2, 128, 64)}, _lib.KVBM_ERR_SHAPE),
 ])
 def test_validate_codes(kw, code):
     lib = _lib.load()
@@ -150,3 +155,77 @@ def test_selftest_argument_checks():
     if not torch.cuda.is_available():
         code = lib.kvbm_selftest_wait_timeout(None, 1_000_000, ctypes.byref(w))
         assert code in (_lib.KVBM_ERR_CUDA, _lib.KVBM_ERR_DEVICE)
+
+
+def test_validate_survives_random_problems():
+    """kvbm_validate / kvbm_workspace_bytes / kvbm_num_blocks on 3000 random
+    problems (negative, zero, huge and mismatched sizes and strides): every call
+    returns a known status, and an accepted problem has a workspace size."""
+    lib = _lib.load()
+    rng = np.random.default_rng(5)
+    known = {_lib.KVBM_OK, _lib.KVBM_ERR_GQA, _lib.KVBM_ERR_SHAPE, _lib.KVBM_ERR_DTYPE,
+             _lib.KVBM_ERR_HEAD_DIM, _lib.KVBM_ERR_BLOCK_SIZE, _lib.KVBM_ERR_UNITS, _lib.KVBM_ERR_NULL}
+    picks = [-(2**31), -5, -1, 0, 1, 2, 3, 7, 8, 64, 100, 128, 257, 4096, 65536, 1 << 28, 2**31 - 1]
+    for _ in range(3000):
+        B, Hq, Hkv, N, D, bs = (int(rng.choice(picks)) for _ in range(6))
+        p = _problem(shape=(B, Hq, Hkv, N, D), dtype=int(rng.integers(-1, 5)), block_size=bs,
+                     units=(int(rng.choice(picks)), int(rng.choice(picks))))
+        if rng.random() < 0.2:
+            p.q_stride[int(rng.integers(0, 4))] = -int(rng.integers(1, 1 << 40))
+        if rng.random() < 0.1:
+            p.scale = float("nan")
+        st = lib.kvbm_validate(ctypes.byref(p))
+        assert st in known
+        ws = lib.kvbm_workspace_bytes(ctypes.byref(p))
+        if st == _lib.KVBM_OK:
+            assert ws > 0
+        else:
+            assert ws == 0
+        lib.kvbm_num_blocks(N, bs)
+
+
+def test_validate_ex_survives_random_options():
+    """kvbm_validate_ex / kvbm_workspace_bytes_ex with random extension options
+    (LSE strides, paged caches, padded or packed lengths).  The option pointers
+    are device addresses the host must never read, so they are fake here: a
+    host-side read would crash this test."""
+    lib = _lib.load()
+    rng = np.random.default_rng(6)
+    known = {_lib.KVBM_OK, _lib.KVBM_ERR_GQA, _lib.KVBM_ERR_SHAPE, _lib.KVBM_ERR_DTYPE,
+             _lib.KVBM_ERR_HEAD_DIM, _lib.KVBM_ERR_BLOCK_SIZE, _lib.KVBM_ERR_UNITS, _lib.KVBM_ERR_NULL}
+    fake = 0x10000
+    picks = [-(2**31), -3, -1, 0, 1, 2, 16, 64, 129, 4096, 1 << 28, 2**31 - 1]
+    for _ in range(2000):
+        N = int(rng.choice([1, 64, 1000, 4096, 1 << 20]))
+        p = _problem(shape=(int(rng.choice([1, 2, 3])), 8, 2, N, 64), dtype=int(rng.integers(0, 4)))
+        o = _lib.Options()
+        if rng.random() < 0.4:
+            o.lse = fake
+            for i in range(3):
+                o.lse_stride[i] = int(rng.choice(picks))
+        kv = None
+        if rng.random() < 0.4:
+            kv = _lib.PagedKV()
+            kv.k_cache = fake if rng.random() < 0.9 else None
+            for i in range(4):
+                kv.cache_stride[i] = int(rng.choice(picks))
+            kv.num_pages = int(rng.choice(picks))
+            kv.page_size = int(rng.choice(picks))
+            kv.block_table = fake if rng.random() < 0.9 else None
+            kv.block_table_stride = int(rng.choice(picks))
+            kv.max_pages = int(rng.choice(picks))
+            o.paged = ctypes.pointer(kv)
+        r = rng.random()
+        if r < 0.3:
+            o.seq_lens = fake
+        elif r < 0.6:
+            o.cu_seqlens = fake
+            o.total_tokens = int(rng.choice(picks + [2**40]))
+        elif r < 0.7:
+            o.seq_lens = fake
+            o.cu_seqlens = fake
+        o.per_sequence = int(rng.integers(0, 2))
+        st = lib.kvbm_validate_ex(ctypes.byref(p), ctypes.byref(o))
+        assert st in known
+        ws = lib.kvbm_workspace_bytes_ex(ctypes.byref(p), ctypes.byref(o))
+        assert (ws > 0) == (st == _lib.KVBM_OK)
