@@ -347,7 +347,8 @@ KVBM_API int kvbm_block_mass_ex(const kvbm_problem* p, const kvbm_options* o, vo
  * torch.rand(n_tail, dtype=float64, generator) gives bit parity; otherwise
  * Philox4x32-10 keyed by `seed`, counter = (token, row).
  * Row r's block mass is mass[r * mass_row_stride + b], b < num_blocks
- * (float32 or float64); blocks past ceil(seq_len / block_size) are ignored. */
+ * (float32 or float64); blocks past ceil(seq_len / block_size) are ignored.
+ * 1 <= rows <= 65535 and 1 <= seq_len <= 2^28, else KVBM_ERR_SHAPE. */
 typedef struct kvbm_design_args {
   const void* mass;
   int32_t mass_dtype;            /* KVBM_F32 or KVBM_F64 */

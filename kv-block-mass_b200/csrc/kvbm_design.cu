@@ -321,11 +321,12 @@ int check_design(const kvbm_design_args* d) {
     return KVBM_ERR_SHAPE;
   if (d->uniforms != nullptr && d->uniforms_row_stride < d->seq_len && d->rows > 1) return KVBM_ERR_SHAPE;
   if (d->rows > 65535) return KVBM_ERR_SHAPE;
+  if (d->seq_len > kMaxN) return KVBM_ERR_SHAPE;  // the mass passes' bound on N
   return KVBM_OK;
 }
 
 size_t design_scratch_bytes(const kvbm_design_args* d) {
-  const size_t nb = (size_t)(d->seq_len + d->block_size - 1) / d->block_size;
+  const size_t nb = (size_t)(((long long)d->seq_len + d->block_size - 1) / d->block_size);
   return align256(sizeof(RowPlan) * d->rows) + align256(sizeof(int) * nb * d->rows) +
          align256(sizeof(long long) * nb * d->rows);
 }
@@ -356,7 +357,7 @@ extern "C" int kvbm_design(const kvbm_design_args* d, const kvbm_design_out* out
   a.B = d->rows;
   a.N = d->seq_len;
   a.bs = d->block_size;
-  a.nb = (d->seq_len + d->block_size - 1) / d->block_size;
+  a.nb = (int)(((long long)d->seq_len + d->block_size - 1) / d->block_size);
   a.m = d->tail_budget;
   a.n_sinks = d->n_sinks;
   a.recency = d->recency;

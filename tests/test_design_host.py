@@ -28,6 +28,11 @@ def test_design_workspace_and_checks():
     assert lib.kvbm_design_workspace_bytes(ctypes.byref(_d(num_blocks=15))) == 0   # 15 * 64 < 1000
     assert lib.kvbm_design_workspace_bytes(ctypes.byref(_d(rows=2, mass_row_stride=8))) == 0
     assert lib.kvbm_design_workspace_bytes(None) == 0
+    # sizes near the int32 limit are rejected, not overflowed
+    big = 2**31 - 1
+    assert lib.kvbm_design_workspace_bytes(ctypes.byref(_d(seq_len=big, block_size=2, num_blocks=big))) == 0
+    assert lib.kvbm_design_workspace_bytes(ctypes.byref(_d(seq_len=(1 << 28) + 1, num_blocks=(1 << 22) + 1))) == 0
+    assert lib.kvbm_design_workspace_bytes(ctypes.byref(_d(seq_len=1 << 28, num_blocks=1 << 22))) > 0
     out = _lib.DesignOut()
     code = lib.kvbm_design(ctypes.byref(_d()), ctypes.byref(out), None, 0, None)
     assert code == _lib.KVBM_ERR_NULL          # counts is required
