@@ -335,6 +335,57 @@ int launch_typed(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_
 // accumulated in fp64 in a fixed order (deterministic).  With causal, a chunk
 // whose last row lies before the key tile start holds no kept pair and is not
 // read (its CTA either returned early or wrote exact zeros).
+//
+// Thread t adds the flattened (unit, chunk, key) entries t, t + 256, ... of
+// its bucket in that order; the warp and block sums then follow a fixed tree.
+// The (unit, chunk, key) of the next entry is stepped forward with carries
+// instead of being divided out of the flat index each time (two 64-bit
+// divisions per entry made the reduce latency-bound).  key_tile is a power of
+// two (64 or 128).
+template <typename Acc>
+__device__ __forceinline__ double bucket_partial_sum(const Acc* part, int N, int cb, int nk, long long u0,
+                                                     long long nu, int nchunk, int qchunk, int key_tile,
+                                                     int causal) {
+  constexpr int T = 256;
+  const long long total = nu * nchunk * nk;
+  double s = 0.0;
+  if (threadIdx.x >= total) return s;
+  const int dc = T % nk, dr = T / nk;
+  const int dy = dr % nchunk, du = dr / nchunk;
+  int co = (int)threadIdx.x % nk;
+  const int r0 = (int)threadIdx.x / nk;
+  int y = r0 % nchunk;
+  long long uu = u0 + r0 / nchunk;
+  for (long long idx = threadIdx.x; idx < total; idx += T) {
+    const int c = cb + co;
+    const bool keep = !causal || (long long)(y + 1) * qchunk - 1 >= (long long)(c & ~(key_tile - 1));
+    if (keep) s += (double)part[(uu * nchunk + y) * N + c];
+    co += dc;
+    y += dy;
+    uu += du;
+    if (co >= nk) {
+      co -= nk;
+      ++y;
+    }
+    if (y >= nchunk) {
+      y -= nchunk;
+      ++uu;
+    }
+  }
+  return s;
+}
+
+__device__ __forceinline__ double block_sum_256(double s, double* warp_sums) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if ((threadIdx.x & 31) == 0) warp_sums[threadIdx.x >> 5] = s;
+  __syncthreads();
+  double t = 0.0;
+  if (threadIdx.x == 0)
+    for (int w = 0; w < 8; ++w) t += warp_sums[w];
+  return t;
+}
+
 template <typename Acc, typename Out>
 __global__ void __launch_bounds__(256) reduce_kernel(const Acc* part, Out* mass, int N, int bs,
                                                      int U, int nchunk, int qchunk, int key_tile,
@@ -342,30 +393,10 @@ __global__ void __launch_bounds__(256) reduce_kernel(const Acc* part, Out* mass,
   __shared__ double warp_sums[8];
   const int j = blockIdx.x;
   const int cb = j * bs;
-  const int ce = min(N, cb + bs);
-  const int nk = ce - cb;
-  const long long total = (long long)U * nchunk * nk;
-  double s = 0.0;
-  for (long long idx = threadIdx.x; idx < total; idx += blockDim.x) {
-    const int c = cb + (int)(idx % nk);
-    const long long rest = idx / nk;
-    const int y = (int)(rest % nchunk);
-    const long long uu = rest / nchunk;
-    if (causal) {
-      const int c0 = (c / key_tile) * key_tile;
-      if ((long long)(y + 1) * qchunk - 1 < c0) continue;
-    }
-    s += (double)part[(uu * nchunk + y) * N + c];
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-  if ((threadIdx.x & 31) == 0) warp_sums[threadIdx.x >> 5] = s;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    double t = 0.0;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += warp_sums[w];
-    mass[j] = static_cast<Out>(t);
-  }
+  const int nk = min(N, cb + bs) - cb;
+  const double s = bucket_partial_sum(part, N, cb, nk, 0, U, nchunk, qchunk, key_tile, causal);
+  const double t = block_sum_256(s, warp_sums);
+  if (threadIdx.x == 0) mass[j] = static_cast<Out>(t);
 }
 
 // Per-sequence variant: mass[b][j] sums the units of batch b inside
@@ -377,31 +408,12 @@ __global__ void __launch_bounds__(256) reduce_seq_kernel(const Acc* part, Out* m
   __shared__ double warp_sums[8];
   const int j = blockIdx.x, b = blockIdx.y;
   const int cb = j * bs;
-  const int ce = min(N, cb + bs);
-  const int nk = ce - cb;
+  const int nk = min(N, cb + bs) - cb;
   const int u0 = max(ub, b * Hkv), u1 = min(ub + U, (b + 1) * Hkv);
-  const long long total = u1 > u0 ? (long long)(u1 - u0) * nchunk * nk : 0;
-  double s = 0.0;
-  for (long long idx = threadIdx.x; idx < total; idx += blockDim.x) {
-    const int c = cb + (int)(idx % nk);
-    const long long rest = idx / nk;
-    const int y = (int)(rest % nchunk);
-    const long long uu = (u0 - ub) + rest / nchunk;
-    if (causal) {
-      const int c0 = (c / key_tile) * key_tile;
-      if ((long long)(y + 1) * qchunk - 1 < c0) continue;
-    }
-    s += (double)part[(uu * nchunk + y) * N + c];
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-  if ((threadIdx.x & 31) == 0) warp_sums[threadIdx.x >> 5] = s;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    double t = 0.0;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += warp_sums[w];
-    mass[(long long)b * nb + j] = static_cast<Out>(t);
-  }
+  const double s = u1 > u0 ? bucket_partial_sum(part, N, cb, nk, u0 - ub, u1 - u0, nchunk, qchunk, key_tile, causal)
+                           : 0.0;
+  const double t = block_sum_256(s, warp_sums);
+  if (threadIdx.x == 0) mass[(long long)b * nb + j] = static_cast<Out>(t);
 }
 
 }  // namespace
@@ -475,6 +487,7 @@ int launch_lse_import(const kvbm_problem* p, const WsLayout& L, const float* lse
 
 int launch_reduce(const kvbm_problem* p, const WsLayout& L, void* mass_out, const void* ws,
                   cudaStream_t s, bool per_sequence) {
+  if (L.key_tile <= 0 || (L.key_tile & (L.key_tile - 1)) != 0) return KVBM_ERR_SHAPE;  // power of two
   const int nb = (int)kvbm_num_blocks(p->N, p->block_size);
   const int U = p->unit_end - p->unit_begin;
   const char* base = static_cast<const char*>(ws) + L.part_off;
