@@ -340,8 +340,9 @@ int launch_typed(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_
 // its bucket in that order; the warp and block sums then follow a fixed tree.
 // The (unit, chunk, key) of the next entry is stepped forward with carries
 // instead of being divided out of the flat index each time (two 64-bit
-// divisions per entry made the reduce latency-bound).  key_tile is a power of
-// two (64 or 128).
+// divisions per entry), and loads are issued in batches (one load in flight
+// per thread left the reduce bound by memory latency).  key_tile is a power
+// of two (64 or 128).
 template <typename Acc>
 __device__ __forceinline__ double bucket_partial_sum(const Acc* part, int N, int cb, int nk, long long u0,
                                                      long long nu, int nchunk, int qchunk, int key_tile,
@@ -356,21 +357,34 @@ __device__ __forceinline__ double bucket_partial_sum(const Acc* part, int N, int
   const int r0 = (int)threadIdx.x / nk;
   int y = r0 % nchunk;
   long long uu = u0 + r0 / nchunk;
-  for (long long idx = threadIdx.x; idx < total; idx += T) {
-    const int c = cb + co;
-    const bool keep = !causal || (long long)(y + 1) * qchunk - 1 >= (long long)(c & ~(key_tile - 1));
-    if (keep) s += (double)part[(uu * nchunk + y) * N + c];
-    co += dc;
-    y += dy;
-    uu += du;
-    if (co >= nk) {
-      co -= nk;
-      ++y;
+  // kBatch entries are loaded before any of them is added, so each thread has
+  // kBatch loads in flight; the adds then run in entry order (same bits).
+  constexpr int kBatch = 8;
+  for (long long idx = threadIdx.x; idx < total; idx += (long long)T * kBatch) {
+    Acc v[kBatch];
+    unsigned kept = 0u;
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      const int c = cb + co;
+      const bool keep = idx + (long long)i * T < total &&
+                        (!causal || (long long)(y + 1) * qchunk - 1 >= (long long)(c & ~(key_tile - 1)));
+      v[i] = keep ? part[(uu * nchunk + y) * N + c] : Acc(0);
+      kept |= keep ? (1u << i) : 0u;
+      co += dc;
+      y += dy;
+      uu += du;
+      if (co >= nk) {
+        co -= nk;
+        ++y;
+      }
+      if (y >= nchunk) {
+        y -= nchunk;
+        ++uu;
+      }
     }
-    if (y >= nchunk) {
-      y -= nchunk;
-      ++uu;
-    }
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i)
+      if (kept & (1u << i)) s += (double)v[i];
   }
   return s;
 }
