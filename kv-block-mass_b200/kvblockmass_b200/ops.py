@@ -372,6 +372,7 @@ def block_mass_b200(q, k, attn_mask=None, causal=False, block_size=64, scale=Non
 
 
 _COPY_STREAMS: dict = {}
+_SIDE_STREAMS: dict = {}
 
 
 def _copy_stream(dev: torch.device) -> torch.cuda.Stream:
@@ -380,18 +381,30 @@ def _copy_stream(dev: torch.device) -> torch.cuda.Stream:
     return _COPY_STREAMS[dev]
 
 
+def _side_stream(dev: torch.device) -> torch.cuda.Stream:
+    if dev not in _SIDE_STREAMS:
+        _SIDE_STREAMS[dev] = torch.cuda.Stream(device=dev)
+    return _SIDE_STREAMS[dev]
+
+
 def _from_pinned_host(q, k, dev, attn_mask, causal, block_size, scale, causal_skip, query_mask, workspace,
                       target_units: int = 1):
     """Pinned host q/k: overlap the host-to-device copy with the kernels.
 
-    The (batch, kv-head) units are cut into contiguous segments; a side
-    stream copies segment i + 1 while segment i runs on the caller's stream,
-    and the per-segment mass vectors are added in segment order (deterministic;
-    the grouping of the final sum differs from one call over all units, so the
-    bits can differ from it in the last place).  Only the first segment's copy
-    is exposed, so segments are one unit each: on the Llama-3-8B N=32768 shape
-    that measured 10.4-11.1 ms end to end against 11.4-11.5 ms for two-unit
-    and 12.3-13.0 ms for four-unit segments.
+    The (batch, kv-head) units are cut into contiguous segments; a copy stream
+    copies segment i + 1 while segment i runs, and the per-segment mass
+    vectors are added in segment order (deterministic; the grouping of the
+    final sum differs from one call over all units, so the bits can differ
+    from it in the last place).  Only the first segment's copy is exposed, so
+    segments are one unit each: on the Llama-3-8B N=32768 shape that measured
+    10.4-11.1 ms end to end against 11.4-11.5 ms for two-unit and 12.3-13.0 ms
+    for four-unit segments.
+
+    Consecutive segments alternate between the caller's stream and a second
+    compute stream, each with its own workspace, so that one segment's first
+    pass fills the SMs its predecessor's last CTAs leave idle.  A caller's
+    explicit ``workspace`` is shared by every segment, so it keeps them all on
+    the caller's stream.
     """
     from .distributed import unit_segments
 
@@ -408,21 +421,32 @@ def _from_pinned_host(q, k, dev, attn_mask, causal, block_size, scale, causal_sk
         copy.wait_stream(compute)  # qd/kd may reuse memory the compute stream still reads
         am = None if attn_mask is None else attn_mask.to(dev, non_blocking=True)
         qm = None if query_mask is None else query_mask.to(dev, non_blocking=True)
+        streams = [compute] if workspace is not None else [compute, _side_stream(dev)]
+        for st in streams[1:]:
+            st.wait_stream(compute)  # the masks above, and anything the caller queued
         U = B * Hkv
         step = max(1, min(target_units, U))
         bounds = [(u, min(U, u + step)) for u in range(0, U, step)]
         parts = []
-        for ub, ue in bounds:
+        for i, (ub, ue) in enumerate(bounds):
             with torch.cuda.stream(copy):
                 for b, g0, g1 in unit_segments(ub, ue, Hkv):
                     qd[b, g0 * G:g1 * G].copy_(q[b, g0 * G:g1 * G], non_blocking=True)
                     kd[b, g0:g1].copy_(k[b, g0:g1], non_blocking=True)
                 ev = torch.cuda.Event()
                 ev.record(copy)
-            compute.wait_event(ev)
-            prep = make_problem(qd, kd, attn_mask=am, causal=causal, block_size=block_size, scale=scale,
-                                causal_skip=causal_skip, query_mask=qm, units=(ub, ue))
-            parts.append(run_prepared(prep, workspace=workspace))
+            st = streams[i % len(streams)]
+            st.wait_event(ev)
+            with torch.cuda.stream(st):
+                prep = make_problem(qd, kd, attn_mask=am, causal=causal, block_size=block_size, scale=scale,
+                                    causal_skip=causal_skip, query_mask=qm, units=(ub, ue))
+                parts.append(run_prepared(prep, workspace=workspace))
+        for st in streams[1:]:
+            compute.wait_stream(st)
+            for t in (qd, kd) + tuple(x for x in (am, qm) if x is not None):
+                t.record_stream(st)
+        for m in parts:
+            m.record_stream(compute)
         # qd/kd were written on the copy stream: tell the allocator before they are freed
         qd.record_stream(copy)
         kd.record_stream(copy)
