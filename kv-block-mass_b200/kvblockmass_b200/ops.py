@@ -402,9 +402,12 @@ def _from_pinned_host(q, k, dev, attn_mask, causal, block_size, scale, causal_sk
 
     Consecutive segments alternate between the caller's stream and a second
     compute stream, each with its own workspace, so that one segment's first
-    pass fills the SMs its predecessor's last CTAs leave idle.  A caller's
-    explicit ``workspace`` is shared by every segment, so it keeps them all on
-    the caller's stream.
+    pass fills the SMs its predecessor's last CTAs leave idle.  The first unit
+    is then cut further, into its first q-head and its other q-heads (mass is
+    a sum over heads), which shortens the copy before the first kernel from a
+    whole unit's q to one head's.  A caller's explicit ``workspace`` is shared
+    by every segment, so it keeps them all on the caller's stream, in whole
+    units.
     """
     from .distributed import unit_segments
 
@@ -426,20 +429,43 @@ def _from_pinned_host(q, k, dev, attn_mask, causal, block_size, scale, causal_sk
             st.wait_stream(compute)  # the masks above, and anything the caller queued
         U = B * Hkv
         step = max(1, min(target_units, U))
-        bounds = [(u, min(U, u + step)) for u in range(0, U, step)]
+        # Segments: ("heads", h0, h1) is q-heads [h0, h1) of unit 0 (batch 0,
+        # kv-head 0) as a problem of its own; ("units", ub, ue) is a unit range.
+        # With two streams the first unit is cut into its first q-head and the
+        # rest, so that only one head's q (and the unit's k) is copied before
+        # the first kernel starts.
+        segs = []
+        if len(streams) > 1 and G > 1:
+            segs += [("heads", 0, 1), ("heads", 1, G)]
+            u_from = 1
+        else:
+            u_from = 0
+        segs += [("units", u, min(U, u + step)) for u in range(u_from, U, step)]
+        am0 = am[0:1] if am is not None and am.dim() == 3 else am
+        qm0 = qm[0:1] if qm is not None and qm.dim() == 2 else qm
         parts = []
-        for i, (ub, ue) in enumerate(bounds):
+        for i, (kind, lo, hi) in enumerate(segs):
             with torch.cuda.stream(copy):
-                for b, g0, g1 in unit_segments(ub, ue, Hkv):
-                    qd[b, g0 * G:g1 * G].copy_(q[b, g0 * G:g1 * G], non_blocking=True)
-                    kd[b, g0:g1].copy_(k[b, g0:g1], non_blocking=True)
+                if kind == "heads":
+                    if lo == 0:
+                        kd[0, 0:1].copy_(k[0, 0:1], non_blocking=True)
+                    qd[0, lo:hi].copy_(q[0, lo:hi], non_blocking=True)
+                else:
+                    for b, g0, g1 in unit_segments(lo, hi, Hkv):
+                        qd[b, g0 * G:g1 * G].copy_(q[b, g0 * G:g1 * G], non_blocking=True)
+                        kd[b, g0:g1].copy_(k[b, g0:g1], non_blocking=True)
                 ev = torch.cuda.Event()
                 ev.record(copy)
             st = streams[i % len(streams)]
             st.wait_event(ev)
             with torch.cuda.stream(st):
-                prep = make_problem(qd, kd, attn_mask=am, causal=causal, block_size=block_size, scale=scale,
-                                    causal_skip=causal_skip, query_mask=qm, units=(ub, ue))
+                if kind == "heads":
+                    prep = make_problem(qd[0:1, lo:hi], kd[0:1, 0:1], attn_mask=am0, causal=causal,
+                                        block_size=block_size, scale=scale, causal_skip=causal_skip,
+                                        query_mask=qm0)
+                else:
+                    prep = make_problem(qd, kd, attn_mask=am, causal=causal, block_size=block_size, scale=scale,
+                                        causal_skip=causal_skip, query_mask=qm, units=(lo, hi))
                 parts.append(run_prepared(prep, workspace=workspace))
         for st in streams[1:]:
             compute.wait_stream(st)

@@ -311,6 +311,30 @@ def test_pinned_host_inputs_pipelined(cuda_device, shape):
     assert torch.equal(a, c)
 
 
+@pytest.mark.parametrize("mask_kind", ["batch_pairs", "pairs", "none"])
+def test_pinned_host_first_unit_split_by_heads(cuda_device, mask_kind):
+    """The pinned-host path cuts its first unit into q-head 0 and q-heads
+    1..G-1 (separate problems on two streams); with every mask form that the
+    cut has to slice, the result matches the device-input call."""
+    B, Hq, Hkv, N, D = 2, 8, 2, 1000, 64
+    g = torch.Generator().manual_seed(29)
+    q = torch.randn(B, Hq, N, D, generator=g).to(torch.bfloat16).pin_memory()
+    k = torch.randn(B, Hkv, N, D, generator=g).to(torch.bfloat16).pin_memory()
+    if mask_kind == "batch_pairs":
+        am = torch.rand(B, N, N, generator=g) > 0.2
+    elif mask_kind == "pairs":
+        am = torch.rand(N, N, generator=g) > 0.2
+    else:
+        am = None
+    qm = torch.rand(B, N, generator=g) > 0.1
+    a = kb.block_mass_b200(q, k, attn_mask=am, query_mask=qm, causal=True, block_size=64, device=cuda_device)
+    b = run(q.to(cuda_device), k.to(cuda_device), attn_mask=None if am is None else am.to(cuda_device),
+            query_mask=qm.to(cuda_device), causal=True, block_size=64)
+    assert max_rel(a.cpu().numpy(), b.cpu().numpy()) < 1e-6
+    c = kb.block_mass_b200(q, k, attn_mask=am, query_mask=qm, causal=True, block_size=64, device=cuda_device)
+    assert torch.equal(a, c)
+
+
 def test_causal_skip_is_engaged(cuda_device):
     """causal_skip must skip work, not only give the same bits (the reference's
     engagement test, tests/test_reference.py:148-158 and :189-215, records the
