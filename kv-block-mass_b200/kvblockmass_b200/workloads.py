@@ -17,11 +17,19 @@ The oracle is fed exactly those values upcast to fp32.
 
 from __future__ import annotations
 
+import base64
+import json
+import os
+from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass, field
+from pathlib import Path
 
 import torch
 
-__all__ = ["Workload", "WORKLOADS", "make_inputs", "make_unit_inputs", "pairs"]
+__all__ = ["Workload", "WORKLOADS", "make_inputs", "make_unit_inputs", "unit_states", "compute_unit_states",
+           "pairs"]
+
+_STATES_FILE = Path(__file__).resolve().parent / "workload_states.json"
 
 
 @dataclass(frozen=True)
@@ -118,38 +126,139 @@ def make_inputs(w: Workload, N: int | None = None, device: str | torch.device = 
     return q, k, key_mask, query_mask
 
 
-def make_unit_inputs(w: Workload, unit_begin: int, unit_end: int, device="cpu", N: int | None = None):
-    """Inputs of the (batch, kv-head) units ``[unit_begin, unit_end)`` only.
+def _unit_piece_ok(w: Workload, n: int) -> bool:
+    """Whether per-unit draws can restart the stream at unit boundaries.
 
-    Per-unit protocol for shards of large shapes, so that a rank draws just
-    the q/k it owns (on its own device): unit ``u`` draws its ``G`` q-heads and
-    then its kv-head from a generator seeded ``seed * 1_000_003 + u``.  The
-    per-q-head scales and the sink rows are drawn from a generator seeded
-    ``seed`` and shared by every unit.  Same shapes and distributions as
-    ``make_inputs``; different values.  The units must lie in one batch
-    entry.  Returns ``(q [1, (u1-u0)*G, N, D], k [1, u1-u0, N, D])`` in
-    ``w.dtype``.
+    torch's CPU normal sampler fills a tensor in blocks of 16 values (a tail
+    that is not a whole block is redrawn), so a draw split into pieces equals
+    the draw of the whole only if every piece is a whole number of blocks.
+    """
+    return (w.G * n * w.D) % 16 == 0 and (n * w.D) % 16 == 0
+
+
+def _encode_state(st: torch.Tensor) -> str:
+    return base64.b64encode(st.numpy().tobytes()).decode("ascii")
+
+
+def _decode_state(s: str) -> torch.Tensor:
+    return torch.frombuffer(bytearray(base64.b64decode(s)), dtype=torch.uint8).clone()
+
+
+def compute_unit_states(w: Workload, N: int | None = None) -> dict:
+    """Generator states of ``make_inputs``' stream at every unit boundary.
+
+    ``q`` holds the state before the q-heads of each unit u = b * H_kv + g
+    (heads ``[g*G, (g+1)*G)`` of batch ``b``: contiguous in the draw order),
+    ``k`` the state before each unit's kv-head, and ``extra`` the state after
+    ``k``, where the per-head scales, the key mask and the sink rows are
+    drawn.  Costs one sequential draw of the whole stream.
+    """
+    n = w.N if N is None else N
+    g = torch.Generator().manual_seed(w.seed)
+    qs, ks = [], []
+    for _ in range(w.units):
+        qs.append(g.get_state().clone())
+        torch.randn(1, w.G, n, w.D, generator=g, dtype=torch.float32)
+    for _ in range(w.units):
+        ks.append(g.get_state().clone())
+        torch.randn(1, 1, n, w.D, generator=g, dtype=torch.float32)
+    return {"q": qs, "k": ks, "extra": g.get_state().clone()}
+
+
+def _stored_states(w: Workload, n: int):
+    p = _STATES_FILE
+    if not p.exists():
+        return None
+    rec = json.loads(p.read_text()).get(w.name)
+    if rec is None or rec["N"] != n or rec["seed"] != w.seed or rec["torch"] != torch.__version__.split("+")[0]:
+        return None
+    return {"q": [_decode_state(x) for x in rec["q"]], "k": [_decode_state(x) for x in rec["k"]],
+            "extra": _decode_state(rec["extra"])}
+
+
+def unit_states(w: Workload, N: int | None = None) -> dict:
+    """The stream's states at the unit boundaries: stored ones when this file's
+    companion ``workload_states.json`` has them (the Llama-3-70B N=131072 shape,
+    whose full draw takes a minute of CPU), else computed."""
+    n = w.N if N is None else N
+    st = _stored_states(w, n)
+    return st if st is not None else compute_unit_states(w, n)
+
+
+def write_unit_states(names) -> None:
+    """Record ``unit_states`` of the named workloads (full length) in ``workload_states.json``."""
+    out = json.loads(_STATES_FILE.read_text()) if _STATES_FILE.exists() else {}
+    for name in names:
+        w = WORKLOADS[name]
+        st = compute_unit_states(w)
+        out[name] = {"N": w.N, "seed": w.seed, "torch": torch.__version__.split("+")[0],
+                     "q": [_encode_state(x) for x in st["q"]], "k": [_encode_state(x) for x in st["k"]],
+                     "extra": _encode_state(st["extra"])}
+    _STATES_FILE.write_text(json.dumps(out, indent=0))
+
+
+def _draw(state: torch.Tensor, shape) -> torch.Tensor:
+    g = torch.Generator()
+    g.set_state(state)
+    return torch.randn(*shape, generator=g, dtype=torch.float32)
+
+
+def make_unit_inputs(w: Workload, unit_begin: int, unit_end: int, device="cpu", N: int | None = None,
+                     threads: int | None = None):
+    """q/k of the (batch, kv-head) units ``[unit_begin, unit_end)`` only.
+
+    The values are exactly ``make_inputs(w)``'s slices ``q[b, g0*G:g1*G]`` and
+    ``k[b, g0:g1]``: each unit's q-heads and kv-head are redrawn from the
+    generator state at its place in the stream (``unit_states``), units in
+    parallel threads, so a rank of a multi-GPU run draws only what it owns.
+    The per-head scales and sink rows come from the state after ``k``, as in
+    ``make_inputs``.  The units must lie in one batch entry.  Returns
+    ``(q [1, (u1-u0)*G, N, D], k [1, u1-u0, N, D])`` in ``w.dtype`` on ``device``.
     """
     n = w.N if N is None else N
     G = w.G
+    if not (0 <= unit_begin < unit_end <= w.units):
+        raise ValueError(f"unit range [{unit_begin}, {unit_end}) outside [0, {w.units})")
     if unit_begin // w.Hkv != (unit_end - 1) // w.Hkv:
         raise ValueError("units must belong to one batch entry")
-    dev = torch.device(device)
-    shared = torch.Generator().manual_seed(w.seed)
-    head_scale = (torch.rand(w.Hq, generator=shared) * 1.5 + 0.5) if w.head_scale else None
+    b, g0 = divmod(unit_begin, w.Hkv)
+    g1 = g0 + (unit_end - unit_begin)
+    if not _unit_piece_ok(w, n):  # the stream cannot restart at unit boundaries: draw it all
+        q, k, _, _ = make_inputs(w, N=n)
+        q, k = q[b:b + 1, g0 * G:g1 * G].contiguous(), k[b:b + 1, g0:g1].contiguous()
+        return q.to(device), k.to(device)
+    st = unit_states(w, n)
+    gx = torch.Generator()
+    gx.set_state(st["extra"])
+    head_scale = (torch.rand(w.Hq, generator=gx, dtype=torch.float32) * 1.5 + 0.5) if w.head_scale else None
+    if w.key_mask_frac > 0:
+        torch.rand(n, generator=gx, dtype=torch.float32)  # the key mask: drawn before the sink rows
     sink_rows = None
     if w.sink_frac > 0:
-        sink_rows = torch.randperm(n, generator=shared)[: max(1, int(n * w.sink_frac))].to(dev)
-    qs, ks = [], []
-    for u in range(unit_begin, unit_end):
-        g = torch.Generator(device=dev).manual_seed(w.seed * 1_000_003 + u)
-        q = torch.randn(1, G, n, w.D, generator=g, device=dev, dtype=torch.float32)
-        k = torch.randn(1, 1, n, w.D, generator=g, device=dev, dtype=torch.float32)
+        sink_rows = torch.randperm(n, generator=gx)[: max(1, int(n * w.sink_frac))]
+
+    def one(u):
+        q = _draw(st["q"][u], (1, G, n, w.D))
+        k = _draw(st["k"][u], (1, 1, n, w.D))
         if head_scale is not None:
             h0 = (u % w.Hkv) * G
-            q.mul_(head_scale[h0:h0 + G].to(dev).view(1, G, 1, 1))
+            q.mul_(head_scale[h0:h0 + G].view(1, G, 1, 1))
         if sink_rows is not None:
             k[:, :, sink_rows, :] *= w.sink_gain
-        qs.append(q.to(w.dtype))
-        ks.append(k.to(w.dtype))
-    return torch.cat(qs, dim=1), torch.cat(ks, dim=1)
+        return q.to(w.dtype), k.to(w.dtype)
+
+    units = list(range(unit_begin, unit_end))
+    nthr = max(1, min(len(units), threads or (os.cpu_count() or 1)))
+    with ThreadPoolExecutor(nthr) as ex:
+        parts = list(ex.map(one, units))
+    q = torch.cat([p[0] for p in parts], dim=1)
+    k = torch.cat([p[1] for p in parts], dim=1)
+    return q.to(device), k.to(device)
+
+
+if __name__ == "__main__":
+    import argparse
+
+    ap = argparse.ArgumentParser(description="record the unit-boundary generator states of workloads")
+    ap.add_argument("names", nargs="+", choices=sorted(WORKLOADS))
+    write_unit_states(ap.parse_args().names)
