@@ -28,11 +28,17 @@ Reported beside the device-timed value:
   roofline      the dominant kernel's algorithmic tensor FLOP/s against the
                 measured bf16 peak, and its exp rate against the MUFU ex2
                 rate measured live on this GPU (the binding unit);
-  cpu_baseline  the CPU oracle (a numpy restatement of the reference's
-                streaming algorithm) on a bounded sample, all host cores.
-`--impl reference` times only that CPU restatement (rank 0), as the
-reference arm.  `--impl reference-triton` times the reference's own Triton
-kernel (installed in baseline/_ref) on the same GPU: a secondary comparison.
+  strong_70b    strong scaling of the Llama-3-70B N=131072 shape: its 8
+                (batch, kv-head) units split over the ranks, NCCL reduce
+                inside each step, with the whole problem on one GPU beside it;
+  cpu_baseline  the reference's own CPU path (block_mass_reference from the
+                package installed in baseline/_ref, torch CPU, all host
+                cores) on one whole (batch, kv-head) unit, with the numpy
+                restatement timed on the same unit beside it.
+`--impl reference` times the reference's CPU path alone (rank 0): one q-head
+of that unit per step.  `--impl reference-triton` times the reference's own
+Triton kernel (installed in baseline/_ref) on the same GPU: a secondary
+comparison.
 """
 
 from __future__ import annotations
@@ -72,10 +78,11 @@ def parse():
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
     ap.add_argument("--seq-len", type=int, default=None,
                     help="override N of the workload (small cases for profiler captures)")
-    ap.add_argument("--cpu-seconds", type=float, default=8.0,
-                    help="target CPU time of the bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-strong", action="store_true",
+                    help="skip the strong-scaling record of the Llama-3-70B N=131072 shape")
+    ap.add_argument("--strong-steps", type=int, default=5)
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
                     help="weak: every rank owns a full batch entry of the workload; strong: the "
@@ -102,6 +109,18 @@ def traffic_record(workload: str):
 
 
 # ----------------------------------------------------------------------- clocks
+def rank_gpu_indices(world: int) -> list[int]:
+    """nvidia-smi indices of the GPUs the ranks of this node use (local ranks
+    0..world-1, through CUDA_VISIBLE_DEVICES when it is set): the clock
+    record covers the GPUs under load and no idle one."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [x.strip() for x in vis.split(",") if x.strip()]
+        if all(x.isdigit() for x in ids) and len(ids) >= world:
+            return [int(x) for x in ids[:world]]
+    return list(range(world))
+
+
 class ClockSampler:
     """nvidia-smi clock / throttle sampling in the background (rank 0)."""
 
@@ -172,76 +191,139 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------- CPU sample
-def cpu_sample(w, seconds: float):
-    """Time the CPU oracle on a bounded sample of workload ``w`` (all host cores).
+REF_SITE = ROOT / "baseline" / "_ref"
 
-    The sample is the q-heads of the first (batch, kv-head) unit over a range of
-    query rows [r0, N) at the end of the sequence (the longest causal rows),
-    sized from a one-chunk calibration to take about ``seconds``.
-    """
+
+def stock_reference():
+    """kv-block-mass's unmodified ``block_mass_reference`` (src/kvblockmass/reference.py:35-126)
+    from the package installed in baseline/_ref, or None when it is not installed."""
+    if not (REF_SITE / "kvblockmass").is_dir():
+        return None
+    if str(REF_SITE) not in sys.path:
+        sys.path.insert(0, str(REF_SITE))
+    try:
+        from kvblockmass.reference import block_mass_reference
+    except Exception:
+        return None
+    return block_mass_reference
+
+
+def _unit0_inputs(w, heads: int):
+    """q-heads [0, heads) of unit (batch 0, kv-head 0) with kv-head 0, full length, fp32
+    (the exact values of make_inputs), and batch 0's masks."""
+    from kvblockmass_b200.workloads import make_inputs, make_unit_inputs
+
+    if w.key_mask_frac > 0 or w.dead_tail_rows > 0:
+        q, k, km, qm = make_inputs(w)
+        q, k = q[:1, :heads], k[:1, :1]
+        qm = None if qm is None else qm[0]
+    else:
+        q, k = make_unit_inputs(w, 0, 1)
+        q, km, qm = q[:, :heads], None, None
+    return q.float().contiguous(), k.float().contiguous(), km, qm
+
+
+def _unit_pairs(w, heads: int) -> int:
+    return heads * (w.N * (w.N + 1) // 2 if w.causal else w.N * w.N)
+
+
+def time_stock_reference(fn, w, qf, kf, km, qm):
+    """One call of the stock reference on all host cores (torch CPU); seconds."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    mask = km
+    if qm is not None:  # a query mask becomes the [N, N] keep matrix the reference takes
+        base = km if km is not None else torch.ones(w.N, dtype=torch.bool)
+        mask = base[None, :] & qm[:, None]
+    t0 = time.perf_counter()
+    fn(qf, kf, attn_mask=mask, causal=w.causal, block_size=w.block_size)
+    return time.perf_counter() - t0
+
+
+def time_port(w, qf, kf, km, qm):
+    """One call of the numpy restatement (oracle/block_mass_np.py) on all host cores; seconds."""
     from threadpoolctl import threadpool_limits
 
-    from kvblockmass_b200.workloads import make_inputs
-    from oracle.block_mass_np import block_mass_stream, sample_pairs
+    from oracle.block_mass_np import block_mass_stream
 
-    cores = os.cpu_count() or 1
-    q, k, km, qm = make_inputs(w)
+    with threadpool_limits(limits=1):
+        t0 = time.perf_counter()
+        block_mass_stream(qf.numpy(), kf.numpy(), attn_mask=None if km is None else km.numpy(),
+                          query_mask=None if qm is None else qm.numpy()[None], causal=w.causal,
+                          block_size=w.block_size, threads=os.cpu_count() or 1, split_rows=True)
+        return time.perf_counter() - t0
+
+
+def cpu_baseline_record(w):
+    """The CPU path on one whole (batch 0, kv-head 0) unit of workload ``w``: its
+    G q-heads over every query row (no extrapolation), all host cores.
+
+    ``kind: reference`` times kv-block-mass's own ``block_mass_reference``
+    (baseline/_ref, torch CPU, the reference's streaming path); the numpy
+    restatement is timed on the same unit beside it (``port_value``).  Without
+    the installed reference the port is the baseline (``kind: port``).
+    """
     G = w.Hq // w.Hkv
-    qn = q[:1, :G].float().numpy()
-    kn = k[:1, :1].float().numpy()
-    kmn = None if km is None else km.numpy()
-    qmn = None if qm is None else qm[:1].numpy()
-    chunk = 256
-
-    def run(rows):
-        with threadpool_limits(limits=1):
-            t0 = time.perf_counter()
-            block_mass_stream(qn, kn, attn_mask=kmn, query_mask=qmn, causal=w.causal,
-                              block_size=w.block_size, rows=rows, threads=cores, split_rows=True)
-            return time.perf_counter() - t0
-
-    n = w.N
-    t1 = run((n - chunk, n))
-    pairs1 = sample_pairs(G, 1, n, (n - chunk, n), w.causal)
-    want_pairs = pairs1 * max(1.0, seconds / max(t1, 1e-3))
-    r0 = n - chunk
-    while r0 > 0 and sample_pairs(G, 1, n, (r0, n), w.causal) < want_pairs:
-        r0 -= chunk
-    r0 = max(r0, 0)
-    t = run((r0, n))
-    pairs = sample_pairs(G, 1, n, (r0, n), w.causal)
-    return {
-        "value": pairs / t, "unit": UNIT, "cores": cores, "kind": "port",
-        "sample": (f"oracle/block_mass_np.py (numpy restatement of reference.py:35-126) on "
-                   f"unit (b=0, kv-head 0) = {G} q-heads x query rows [{r0}, {n}) of {w.name}: "
-                   f"{pairs:.3e} pairs in {t:.2f} s"),
-        "seconds": t, "pairs": pairs,
-    }
+    qf, kf, km, qm = _unit0_inputs(w, G)
+    npairs = _unit_pairs(w, G)
+    cores = os.cpu_count() or 1
+    t_port = time_port(w, qf, kf, km, qm)
+    rec = {"unit": UNIT, "cores": cores, "port_value": npairs / t_port, "port_seconds": round(t_port, 3)}
+    fn = stock_reference()
+    what = f"unit (b=0, kv-head 0) = {G} q-heads x all {w.N} query rows of {w.name}: {npairs:.3e} pairs"
+    if fn is not None:
+        t_ref = time_stock_reference(fn, w, qf, kf, km, qm)
+        rec.update(value=npairs / t_ref, kind="reference", seconds=round(t_ref, 3),
+                   sample=(f"kv-block-mass block_mass_reference (baseline/_ref, torch CPU, "
+                           f"{torch.get_num_threads()} threads, causal_skip on, query_chunk 256) on {what} "
+                           f"in {t_ref:.2f} s; the numpy restatement took {t_port:.2f} s on the same unit"),
+                   reference_over_port=round(t_port / t_ref, 3))
+    else:
+        rec.update(value=npairs / t_port, kind="port", seconds=round(t_port, 3),
+                   sample=(f"oracle/block_mass_np.py (numpy restatement of reference.py:35-126) on {what} "
+                           f"in {t_port:.2f} s (the reference package is not installed in baseline/_ref)"))
+    return rec
 
 
 def reference_arm(args, w):
-    """--impl reference: the CPU restatement of the reference's algorithm, rank 0 only."""
+    """--impl reference: the reference's CPU path on this host (rank 0 only).
+
+    Each step runs kv-block-mass's own ``block_mass_reference`` (installed in
+    baseline/_ref; torch CPU on all host cores) on one q-head of unit
+    (batch 0, kv-head 0) over every query row; without the installed package
+    the numpy restatement runs instead.  The value is one host's CPU rate
+    whatever the number of GPUs of the run (``per_host``).
+    """
     steps, warm = args.steps, args.warmup
-    per_step = max(1.0, min(8.0, 150.0 / max(1, steps + warm)))
+    fn = stock_reference()
+    qf, kf, km, qm = _unit0_inputs(w, 1)
+    npairs = _unit_pairs(w, 1)
+    if fn is not None:
+        one = lambda: time_stock_reference(fn, w, qf, kf, km, qm)  # noqa: E731
+        kind = "reference"
+        what = (f"kv-block-mass block_mass_reference (baseline/_ref, torch CPU, all host cores, causal_skip on) "
+                f"on q-head 0 of unit (b=0, kv-head 0) of {w.name}, all {w.N} query rows: {npairs:.3e} pairs "
+                f"per step")
+    else:
+        one = lambda: time_port(w, qf, kf, km, qm)  # noqa: E731
+        kind = "port"
+        what = (f"oracle/block_mass_np.py (numpy restatement of reference.py:35-126; the reference package is "
+                f"not installed) on q-head 0 of unit (b=0, kv-head 0) of {w.name}: {npairs:.3e} pairs per step")
     for _ in range(warm):
-        cpu_sample(w, per_step)
-    rates, secs, last = [], [], None
-    for _ in range(steps):
-        last = cpu_sample(w, per_step)
-        rates.append(last["value"])
-        secs.append(last["seconds"])
-    value = statistics.median(rates)
+        one()
+    secs = [one() for _ in range(steps)]
+    total = sum(secs)
+    value = npairs * steps / total
+    cores = os.cpu_count() or 1
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
-        "warmup": warm, "ms_per_step": statistics.median(secs) * 1e3, "higher_is_better": True,
+        "warmup": warm, "ms_per_step": total / steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "impl": "reference",
+        "impl": "reference", "per_host": True, "host_cores": cores,
         "config": workload_config(w, args.gpus),
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": last["cores"], "kind": "port",
-                         "sample": last["sample"] + " (each step one such sample; value = median rate)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind, "sample": what},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": ("the reference is pure Python (torch CPU + Triton); its CPU path is timed through "
-                 "the committed numpy restatement of src/kvblockmass/reference.py:35-126"),
+        "note": ("one host's CPU cores, whatever n_gpus is: a ratio against an N-GPU line compares N GPUs "
+                 "with one host"),
     }
     print(json.dumps(line), flush=True)
 
@@ -302,8 +384,8 @@ def workload_config(w, world: int, scaling: str = "weak"):
         shard = "each rank owns B_per_rank batch entries (B*H_kv units); NCCL reduce of mass to rank 0"
         gb = w.B * world
     else:
-        shard = (f"the {w.B * w.Hkv} (batch, kv-head) units split contiguously over {world} ranks, "
-                 "inputs drawn per unit on each rank's GPU; NCCL reduce of mass to rank 0")
+        shard = (f"the {w.B * w.Hkv} (batch, kv-head) units split contiguously over {world} ranks, each "
+                 "rank's inputs the exact slices of the workload's draw; NCCL reduce of mass to rank 0")
         gb = w.B
     return {
         "workload": w.name, "B_per_rank": w.B if scaling == "weak" else None, "global_batch": gb,
@@ -313,6 +395,109 @@ def workload_config(w, world: int, scaling: str = "weak"):
         "shard": shard,
         "inputs_exceed_l2": True, "l2_flush": "none (q+k per step exceed the 126 MB L2)",
     }
+
+
+# --------------------------------------------------------- strong scaling, 70B
+def strong_70b_record(args, lib, dev, rank: int, world: int):
+    """Strong scaling of the Llama-3-70B N=131072 shape (B=1, H_q=64, H_kv=8,
+    D=128, block 256, causal, bf16, 1% x8 sink keys) beside the headline.
+
+    Its 8 (batch, kv-head) units are split contiguously over the ranks; each
+    rank draws exactly its units' slices of the workload's inputs
+    (``make_unit_inputs``, the values the reference golden pins) into its own
+    HBM.  A step is every rank's kernels on its units plus the NCCL reduce of
+    the 512-bucket mass to rank 0; steps are timed with CUDA events between
+    barriers, max over ranks.  With more than one rank, rank 0 also times the
+    whole problem alone first (the units gathered over NCCL), which gives the
+    run's own ``efficiency_vs_1gpu``.
+    """
+    import torch.distributed as dist
+
+    from kvblockmass_b200 import ops
+    from kvblockmass_b200.distributed import partition_units
+    from kvblockmass_b200.workloads import WORKLOADS, make_unit_inputs, pairs
+
+    w5 = WORKLOADS["llama3_70b_n128k"]
+    parts = partition_units(w5.units, world)
+    ub, ue = parts[rank]
+    if ue <= ub:
+        return None if rank else {"skipped": f"more ranks ({world}) than units ({w5.units})"}
+    t0 = time.time()
+    q, k = make_unit_inputs(w5, ub, ue)
+    q, k = q.to(dev), k.to(dev)
+    draw_s = time.time() - t0
+    K, warm = max(1, args.strong_steps), 2
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(prep, out, ws, reduce):
+        def step():
+            code = lib.kvbm_block_mass(ctypes.byref(prep.prob), out.data_ptr(), ws.data_ptr(), ws.numel(),
+                                       stream.cuda_stream)
+            if code != 0:
+                raise RuntimeError(f"kvbm_block_mass failed: {code}")
+            if reduce:
+                dist.reduce(out, dst=0, op=dist.ReduceOp.SUM)
+        for _ in range(warm):
+            step()
+        if reduce:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(K):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if reduce:
+            dist.barrier()
+        return e0.elapsed_time(e1) / K
+
+    single_ms = None
+    equal_parts = len({e - b for b, e in parts}) == 1
+    if world > 1 and equal_parts:
+        # the whole problem on rank 0 alone: gather every rank's units there
+        qa = torch.empty((world,) + tuple(q.shape), dtype=q.dtype, device=dev)
+        ka = torch.empty((world,) + tuple(k.shape), dtype=k.dtype, device=dev)
+        dist.all_gather_into_tensor(qa, q.unsqueeze(0).contiguous())
+        dist.all_gather_into_tensor(ka, k.unsqueeze(0).contiguous())
+        if rank == 0:
+            qf = qa.permute(1, 0, 2, 3, 4).reshape(1, w5.Hq, w5.N, w5.D)
+            kf = ka.permute(1, 0, 2, 3, 4).reshape(1, w5.Hkv, w5.N, w5.D)
+            pf = ops.make_problem(qf, kf, causal=True, block_size=w5.block_size)
+            wsf = torch.empty(ops.workspace_bytes(pf), dtype=torch.uint8, device=dev)
+            of = torch.empty(pf.nb, dtype=torch.float32, device=dev)
+            single_ms = timed(pf, of, wsf, False)
+            del qf, kf, pf, wsf, of
+        del qa, ka
+        torch.cuda.empty_cache()
+        dist.barrier()
+    prep = ops.make_problem(q, k, causal=True, block_size=w5.block_size)
+    ws = torch.empty(ops.workspace_bytes(prep), dtype=torch.uint8, device=dev)
+    out = torch.empty(prep.nb, dtype=torch.float32, device=dev)
+    ms = timed(prep, out, ws, world > 1)
+    ms_t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    if lib.kvbm_check_device_errors(stream.cuda_stream) != 0:
+        raise RuntimeError("a device-side wait timed out in the strong-scaling run")
+    total_pairs = pairs(w5)
+    rec = {"workload": w5.name, "n_gpus": world, "units_per_rank": [e - b for b, e in parts], "steps": K,
+           "warmup": warm, "ms_per_step": ms, "value": total_pairs / (ms * 1e-3), "unit": UNIT,
+           "scaling": "strong", "pairs_per_step": total_pairs,
+           "timing": "CUDA events per rank between barriers, max over ranks; NCCL reduce inside each step",
+           "inputs": "exact slices of make_inputs(llama3_70b_n128k) per rank (make_unit_inputs), in HBM",
+           "input_draw_s": round(draw_s, 1)}
+    if world == 1:
+        rec["single_gpu_ms"] = ms
+        rec["efficiency_vs_1gpu"] = 1.0
+    elif single_ms is not None:
+        rec["single_gpu_ms"] = single_ms
+        rec["speedup_vs_1gpu"] = single_ms / ms
+        rec["efficiency_vs_1gpu"] = single_ms / ms / world
+    del q, k, ws, out, prep
+    torch.cuda.empty_cache()
+    return rec if rank == 0 else None
 
 
 # ------------------------------------------------------------------- B200 arm
@@ -341,7 +526,7 @@ def b200_arm(args, w):
         pairs_total_per_step = pairs(w) * world
     else:
         # Rank r owns a contiguous range of the workload's (batch, kv-head) units and
-        # draws only those, on its own GPU (per-unit seeded protocol).
+        # draws only those (exact slices of make_inputs' stream).
         from kvblockmass_b200.distributed import partition_units
         from kvblockmass_b200.workloads import make_unit_inputs
         if w.key_mask_frac > 0 or w.dead_tail_rows > 0:
@@ -349,9 +534,7 @@ def b200_arm(args, w):
         ub, ue = partition_units(w.B * w.Hkv, world)[rank]
         if ue <= ub:
             raise SystemExit(f"rank {rank} has no units: use at most {w.B * w.Hkv} GPUs")
-        qd, kd = make_unit_inputs(w, ub, ue, device=dev)
-        q_cpu, k_cpu = qd.cpu(), kd.cpu()
-        del qd, kd
+        q_cpu, k_cpu = make_unit_inputs(w, ub, ue)
         km = qm = None
         pairs_total_per_step = pairs(w)
     q_pin, k_pin = q_cpu.pin_memory(), k_cpu.pin_memory()
@@ -404,8 +587,7 @@ def b200_arm(args, w):
             e.record(stream)
     torch.cuda.synchronize()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(list(range(torch.cuda.device_count())) if world > 1 else [local]) \
-        if rank == 0 else None
+    sampler = ClockSampler(rank_gpu_indices(world)) if rank == 0 else None
     if sampler:
         sampler.__enter__()
         time.sleep(0.3)
@@ -625,6 +807,10 @@ def b200_arm(args, w):
         sampler.__exit__(None, None, None)
         clocks = sampler.summary(t_wall0, t_wall1)
 
+    strong = None
+    if not args.no_strong:
+        strong = strong_70b_record(args, lib, dev, rank, world)
+
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
@@ -652,6 +838,11 @@ def b200_arm(args, w):
         "config": workload_config(w, world, args.scaling),
         "kernel_path": "tcgen05" if path == 1 else "simt",
         "kernel_ms": {"pass1_lse": t1, "pass2_mass": t2, "reduce": t3},
+        "kernel_mcycles": (None if not clocks or not clocks.get("sm_mhz") else
+                           {"pass1_lse": t1 * clocks["sm_mhz"] / 1e3, "pass2_mass": t2 * clocks["sm_mhz"] / 1e3,
+                            "reduce": t3 * clocks["sm_mhz"] / 1e3,
+                            "note": "kernel ms x median SM MHz of the timed region: cycles at the clock the "
+                                    "power state allowed"}),
         "roofline": {
             "bound": "tensor", "achieved": achieved_tflops, "peak": tensor_peak, "unit": "TFLOP/s",
             "frac": achieved_tflops / tensor_peak, "traffic": traffic, "kernel": dom_name,
@@ -680,9 +871,10 @@ def b200_arm(args, w):
         line["ragged"] = ragged
     if design:
         line["design"] = design
+    if strong:
+        line["strong_70b"] = strong
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = {k: v for k, v in cpu_sample(w, args.cpu_seconds).items()
-                                if k not in ("seconds", "pairs")}
+        line["cpu_baseline"] = cpu_baseline_record(w)
         if design is not None and design_mass_host is not None:
             # the same design on the host: the oracle's restatement of evict.py (float64 numpy)
             from oracle import evict_np as ev

@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define KVBM_ABI_VERSION 1
+#define KVBM_ABI_VERSION 2
 
 /* Only the entry points below are exported from libkvbm.so (it is built with
  * hidden default visibility). */
@@ -208,7 +208,13 @@ KVBM_API double kvbm_exp2_fma_fraction(void);
  * GPU that loads the library holds it until the process exits.  A problem
  * whose workspace (kvbm_workspace_bytes) is larger is rejected with
  * KVBM_ERR_SCRATCH before anything is launched.  Split such a problem into
- * unit ranges (unit_begin/unit_end) that fit.
+ * unit ranges (unit_begin/unit_end) that fit: a range inside one batch entry
+ * needs scratch for its own units only (their lse2 rows and partials, and for
+ * fp32 inputs on kernel path 2 the tf32 copies of their q/k rows), and the
+ * mass vectors of the ranges add up to the whole.  A pair mask needs
+ * Npad^2 / 4 bytes of packed bits per mask batch entry whatever the range
+ * (Npad = N rounded up to 128), so pair-masked problems longer than about
+ * N = 16000 cannot use this entry point.
  *
  * No allocation: the call makes no cudaMalloc, cudaFree or other allocating
  * call.  The first call on each device looks up the array's device address
@@ -297,10 +303,37 @@ KVBM_API int kvbm_block_mass_paged(const kvbm_problem* p, const kvbm_paged_kv* k
  *                     row b the mass of sequence b alone (rows of sequences
  *                     outside the unit range are written as zeros)
  *   events            4 cudaEvent_t as kvbm_block_mass_events (or NULL)
+ *   stages, run_unit_begin/end, run_head_begin/end
+ *                     staged execution (all zero: the whole call).  A caller
+ *                     that receives a problem in pieces, e.g. copying it from
+ *                     host memory one unit at a time, runs the passes piece by
+ *                     piece into ONE workspace sized for the whole problem
+ *                     (kvbm_workspace_bytes_ex of the same p and o), on any
+ *                     streams, and the bucket reduce once at the end; the
+ *                     result then has the bits of one whole call.
+ *                     stages: KVBM_STAGE_* bits (0 = all of them);
+ *                     run_unit_begin/end: passes 1 and 2 cover units
+ *                     [unit_begin + run_unit_begin, unit_begin + run_unit_end)
+ *                     only (end <= begin: every unit of the problem); the
+ *                     reduce always sums every unit;
+ *                     run_head_begin/end: pass 1 covers q-heads [begin, end)
+ *                     of each GQA group, 0 <= begin < end <= H_q/H_kv (end <=
+ *                     begin: all); a head range narrower than the group needs
+ *                     a run range of one unit.  Pass 2 of a unit reads pass 1
+ *                     of all its heads, and (fp32 inputs on path 2) the unit's
+ *                     k rows as converted by the pass-1 piece whose head range
+ *                     starts at 0.  mass_out may be NULL without
+ *                     KVBM_STAGE_REDUCE.  Pieces that write disjoint units or
+ *                     heads may run concurrently.  Not combined with seq_lens,
+ *                     cu_seqlens or paged (KVBM_ERR_SHAPE).
  *
  * Every ragged/per-sequence result equals the sum over sequences of the
  * reference run on each sequence alone (its first seq_lens[b] positions);
  * buckets j >= ceil(len / block_size) of a sequence get 0 from it. */
+#define KVBM_STAGE_MASKS 1   /* pack a pair mask into bits (tensor-core paths)             */
+#define KVBM_STAGE_PASS1 2   /* row lse2, or the LSE import; fp32 path 2: tf32 split first */
+#define KVBM_STAGE_PASS2 4   /* per-key partials                                          */
+#define KVBM_STAGE_REDUCE 8  /* bucket reduce into mass_out                                */
 typedef struct kvbm_options {
   const float* lse;
   int64_t lse_stride[3];
@@ -310,6 +343,11 @@ typedef struct kvbm_options {
   int64_t total_tokens;
   int32_t per_sequence;
   void* const* events;
+  int32_t stages;
+  int32_t run_unit_begin;
+  int32_t run_unit_end;
+  int32_t run_head_begin;
+  int32_t run_head_end;
 } kvbm_options;
 
 /* Host-only checks of `p` with options `o` (o may be NULL). */

@@ -148,46 +148,67 @@ size_t max_layout_bytes(const kvbm_problem* p, const Ragged* rg = nullptr) {
 
 // Launch sequence shared by the entry points: (pass 1 | lse import), pass 2,
 // bucket reduce, with optional events around them.
+// Stages and run ranges of a call (kvbm_options); all stages when not staged.
+struct Staging {
+  int stages = KVBM_STAGE_MASKS | KVBM_STAGE_PASS1 | KVBM_STAGE_PASS2 | KVBM_STAGE_REDUCE;
+  int rb = 0, re = 0, hb = 0, he = 0;
+};
+
 int run_passes(const kvbm_problem* p, const WsLayout& L, int path, void* mass_out, void* ws, cudaStream_t s,
                void* const* events, const float* lse, const int64_t* lse_stride, const Ragged& rg = Ragged(),
-               bool per_sequence = false, bool marked = false) {
+               bool per_sequence = false, bool marked = false, const Staging& sg = Staging()) {
   auto mark = [&](int i) {
     if (events != nullptr && events[i] != nullptr)
       return cudaEventRecord(static_cast<cudaEvent_t>(events[i]), s) == cudaSuccess;
     return true;
   };
   if (!marked && !mark(0)) return KVBM_ERR_CUDA;
+  const bool s1 = (sg.stages & KVBM_STAGE_PASS1) != 0, s2 = (sg.stages & KVBM_STAGE_PASS2) != 0;
+  const bool sm = (sg.stages & KVBM_STAGE_MASKS) != 0, sr = (sg.stages & KVBM_STAGE_REDUCE) != 0;
   LaunchOpts o;
   o.mid_event = events != nullptr ? events[1] : nullptr;
-  o.run_pass1 = lse == nullptr;
+  o.run_pass1 = s1 && lse == nullptr;
+  o.run_pass2 = s2;
+  o.run_split = s1;
+  o.run_masks = sm;
   o.rg = rg;
+  o.rb = sg.rb;
+  o.re = sg.re;
+  o.hb = sg.hb;
+  o.he = sg.he;
   int st = KVBM_OK;
-  if (lse != nullptr) {
+  if (lse != nullptr && s1) {
     nvtxRangePushA("kvbm lse import");
-    st = launch_lse_import(p, L, lse, lse_stride, ws, s, rg);
+    st = launch_lse_import(p, L, lse, lse_stride, ws, s, rg, run_range(p, o));
     nvtxRangePop();
   }
   if (st != KVBM_OK) return st;
-  // NVTX ranges mark the host-side enqueue of each pass (a profiler pairs
-  // them with the kernels they launch)
-  nvtxRangePushA(lse != nullptr ? "kvbm pass 2 (mass)" : "kvbm pass 1 (lse) + pass 2 (mass)");
-  st = (path >= 1) ? launch_tc(p, L, mass_out, ws, s, o) : launch_simt(p, L, mass_out, ws, s, o);
-  nvtxRangePop();
-  if (st != KVBM_OK) return st;
+  if (s1 || s2 || sm) {
+    // NVTX ranges mark the host-side enqueue of each pass (a profiler pairs
+    // them with the kernels they launch)
+    nvtxRangePushA(o.run_pass1 ? "kvbm pass 1 (lse) + pass 2 (mass)" : "kvbm pass 2 (mass)");
+    st = (path >= 1) ? launch_tc(p, L, mass_out, ws, s, o) : launch_simt(p, L, mass_out, ws, s, o);
+    nvtxRangePop();
+    if (st != KVBM_OK) return st;
+  }
   if (!mark(2)) return KVBM_ERR_CUDA;
-  nvtxRangePushA("kvbm bucket reduce");
-  st = launch_reduce(p, L, mass_out, ws, s, per_sequence);
-  nvtxRangePop();
-  if (st != KVBM_OK) return st;
+  if (sr) {
+    nvtxRangePushA("kvbm bucket reduce");
+    st = launch_reduce(p, L, mass_out, ws, s, per_sequence);
+    nvtxRangePop();
+    if (st != KVBM_OK) return st;
+  }
   return mark(3) ? KVBM_OK : KVBM_ERR_CUDA;
 }
 
-// One kvbm_block_mass_ex call resolved into what the kernels see.  A paged k
-// becomes a dense sub-problem over the smallest box of batches x kv-heads
-// that holds the requested units (a range inside one batch keeps only its
-// heads, otherwise whole batches), whose keys are gathered after the dense
-// workspace; q, the masks, the LSE, the ragged arrays and a per-sequence
-// output are shifted to that box's origin.
+// One kvbm_block_mass_ex call resolved into what the kernels see: the
+// sub-problem over the smallest box of batches x kv-heads that holds the
+// requested units (a range inside one batch keeps only its heads, otherwise
+// whole batches).  q, k, the masks, the LSE, the ragged arrays and a
+// per-sequence output are shifted to that box's origin, so the workspace
+// (the tf32 copies of fp32 inputs, per-batch pair-mask bits) covers the box
+// and not the whole tensors.  A paged k is gathered into a dense array of the
+// box after the dense workspace.
 struct Plan {
   kvbm_problem sub;                  // the problem the kernels see (paged: k set at launch)
   Ragged rg;                         // ragged arrays, shifted to the box
@@ -197,6 +218,7 @@ struct Plan {
   int64_t lse_stride[3] = {0, 0, 0};
   const kvbm_paged_kv* paged = nullptr;
   bool per_sequence = false;
+  Staging staging;
   int B = 0;                         // the caller's batch (rows of a per-sequence output)
   int b0 = 0, g0 = 0;                // origin of the box
   int path = -1;                     // kernel path (-1: unknown device)
@@ -238,9 +260,34 @@ int make_plan(const kvbm_problem* p, const kvbm_options* o, int dev, Plan* out) 
       if (kv->cache_stride[i] < 0) return KVBM_ERR_SHAPE;
     sub.k = kv->k_cache;  // stands in for validate(); replaced by the gathered rows
     for (int i = 0; i < 4; ++i) sub.k_stride[i] = 0;
-    st = validate(&sub);
-    if (st != KVBM_OK) return st;
-    if ((int64_t)kv->max_pages * kv->page_size < p->N) return KVBM_ERR_SHAPE;
+  } else if (packed) {
+    sub.k_stride[0] = 0;
+  }
+  st = validate(&sub);
+  if (st != KVBM_OK) return st;
+  if (kv != nullptr && (int64_t)kv->max_pages * kv->page_size < p->N) return KVBM_ERR_SHAPE;
+  // staged execution: run ranges relative to the unit range, checked before narrowing
+  const bool staged = opt.stages != 0 || opt.run_unit_end > opt.run_unit_begin || opt.run_head_end > opt.run_head_begin;
+  if (staged) {
+    const int U = p->unit_end - p->unit_begin, G = p->Hq / p->Hkv;
+    if (opt.stages < 0 || opt.stages > 15) return KVBM_ERR_SHAPE;
+    if (kv != nullptr || opt.seq_lens != nullptr || opt.cu_seqlens != nullptr) return KVBM_ERR_SHAPE;
+    Staging& sg = pl.staging;
+    if (opt.stages != 0) sg.stages = opt.stages;
+    if (opt.run_unit_end > opt.run_unit_begin) {
+      if (opt.run_unit_begin < 0 || opt.run_unit_end > U) return KVBM_ERR_UNITS;
+      sg.rb = opt.run_unit_begin;
+      sg.re = opt.run_unit_end;
+    }
+    if (opt.run_head_end > opt.run_head_begin) {
+      if (opt.run_head_begin < 0 || opt.run_head_end > G) return KVBM_ERR_SHAPE;
+      const int nu = sg.re > sg.rb ? sg.re - sg.rb : U;
+      if (opt.run_head_end - opt.run_head_begin < G && nu != 1) return KVBM_ERR_SHAPE;
+      sg.hb = opt.run_head_begin;
+      sg.he = opt.run_head_end;
+    }
+  }
+  {
     const int G = p->Hq / p->Hkv;
     const int b0 = p->unit_begin / p->Hkv, b1 = (p->unit_end - 1) / p->Hkv;
     int g0 = 0, ng = p->Hkv;
@@ -253,10 +300,6 @@ int make_plan(const kvbm_problem* p, const kvbm_options* o, int dev, Plan* out) 
     sub.Hkv = ng;
     sub.Hq = ng * G;
     sub.q = static_cast<const char*>(p->q) + (b0 * sub.q_stride[0] + (int64_t)g0 * G * sub.q_stride[1]) * es;
-    sub.k_stride[0] = (int64_t)ng * p->N * p->D;
-    sub.k_stride[1] = (int64_t)p->N * p->D;
-    sub.k_stride[2] = p->D;
-    sub.k_stride[3] = 1;
     if (sub.key_mask != nullptr) sub.key_mask += b0 * p->key_mask_bstride;
     if (sub.query_mask != nullptr) sub.query_mask += b0 * p->query_mask_bstride;
     if (sub.pair_mask != nullptr) sub.pair_mask += b0 * p->pair_mask_bstride;
@@ -265,12 +308,18 @@ int make_plan(const kvbm_problem* p, const kvbm_options* o, int dev, Plan* out) 
     if (pl.lse != nullptr) pl.lse += b0 * pl.lse_stride[0] + (int64_t)g0 * G * pl.lse_stride[1];
     pl.b0 = b0;
     pl.g0 = g0;
-    pl.paged = kv;
-    pl.gather_bytes = align_up((size_t)sub.B * ng * p->N * p->D * es, 256);
-    // the gathered rows start on a 256-byte boundary: path selection sees an aligned k
-    sub.k = reinterpret_cast<const void*>(uintptr_t(256));
-  } else if (packed) {
-    sub.k_stride[0] = 0;
+    if (kv != nullptr) {
+      sub.k_stride[0] = (int64_t)ng * p->N * p->D;
+      sub.k_stride[1] = (int64_t)p->N * p->D;
+      sub.k_stride[2] = p->D;
+      sub.k_stride[3] = 1;
+      pl.paged = kv;
+      pl.gather_bytes = align_up((size_t)sub.B * ng * p->N * p->D * es, 256);
+      // the gathered rows start on a 256-byte boundary: path selection sees an aligned k
+      sub.k = reinterpret_cast<const void*>(uintptr_t(256));
+    } else {
+      sub.k = static_cast<const char*>(p->k) + (b0 * sub.k_stride[0] + (int64_t)g0 * sub.k_stride[1]) * es;
+    }
   }
   st = validate(&sub);
   if (st != KVBM_OK) return st;
@@ -307,7 +356,7 @@ int current_device(int* dev) {
 
 int run_plan(Plan& pl, void* mass_out, void* workspace, size_t workspace_bytes, cudaStream_t s,
              void* const* events) {
-  if (mass_out == nullptr) return KVBM_ERR_NULL;
+  if (mass_out == nullptr && (pl.staging.stages & KVBM_STAGE_REDUCE) != 0) return KVBM_ERR_NULL;
   if (workspace == nullptr || workspace_bytes < pl.total || ((uintptr_t)workspace % 256) != 0)
     return KVBM_ERR_WORKSPACE;
   kvbm_problem& sub = pl.sub;
@@ -324,7 +373,7 @@ int run_plan(Plan& pl, void* mass_out, void* workspace, size_t workspace_bytes, 
     if (st != KVBM_OK) return st;
   }
   void* out = mass_out;
-  if (pl.per_sequence && (sub.B != pl.B)) {
+  if (pl.per_sequence && (sub.B != pl.B) && (pl.staging.stages & KVBM_STAGE_REDUCE) != 0) {
     // rows of sequences outside the box are zeros; the box writes its own rows
     const size_t row = (size_t)kvbm_num_blocks(sub.N, sub.block_size) * (sub.dtype == KVBM_F64 ? 8 : 4);
     char* base = static_cast<char*>(mass_out);
@@ -335,7 +384,7 @@ int run_plan(Plan& pl, void* mass_out, void* workspace, size_t workspace_bytes, 
     out = base + row * pl.b0;
   }
   return run_passes(&sub, pl.L, pl.path, out, workspace, s, events, pl.lse, pl.lse_stride, pl.rg,
-                    pl.per_sequence, true);
+                    pl.per_sequence, true, pl.staging);
 }
 
 int plan_on_device(const kvbm_problem* p, const kvbm_options* o, Plan* pl) {
@@ -346,6 +395,14 @@ int plan_on_device(const kvbm_problem* p, const kvbm_options* o, Plan* pl) {
     return st != KVBM_OK ? st : KVBM_ERR_DEVICE;
   }
   return make_plan(p, o, dev, pl);
+}
+
+int planned_workspace_bytes(const kvbm_problem* p, size_t* bytes) {
+  Plan pl;
+  const int st = plan_on_device(p, nullptr, &pl);
+  if (st != KVBM_OK) return st;
+  *bytes = pl.total;
+  return KVBM_OK;
 }
 
 }  // namespace kvbm
@@ -387,17 +444,10 @@ int64_t kvbm_num_blocks(int32_t N, int32_t block_size) {
 }
 
 size_t kvbm_workspace_bytes(const kvbm_problem* p) {
-  if (validate(p) != KVBM_OK) return 0;
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess) {
-    cudaGetLastError();
-    dev = -1;
-  }
-  const int path = select_path(p, dev);
-  // Size for the largest layout the dtype can select when the device is
-  // unknown, so a workspace sized on the host is valid for whichever path runs.
-  if (dev < 0) return max_layout_bytes(p);
-  return layout_for(p, path).total;
+  // When the device is unknown (or not an sm_100), the size covers the
+  // largest layout the dtype can select, so a workspace sized on the host is
+  // valid for whichever path runs.
+  return kvbm_workspace_bytes_ex(p, nullptr);
 }
 
 int kvbm_kernel_path(const kvbm_problem* p) {

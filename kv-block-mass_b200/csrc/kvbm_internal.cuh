@@ -163,20 +163,45 @@ int validate(const kvbm_problem* p);
 int select_path(const kvbm_problem* p, int device);
 // `rg` sizes the tf32 split copies of a packed q/k (path 2) by their rows.
 WsLayout layout_for(const kvbm_problem* p, int path, const Ragged* rg = nullptr);
+// Workspace bytes kvbm_block_mass needs for `p` on the current device (the
+// problem narrowed to the batches x kv-heads of its unit range).
+int planned_workspace_bytes(const kvbm_problem* p, size_t* bytes);
 
 // Launchers (return a kvbm_status).
 struct LaunchOpts {
   void* mid_event = nullptr;  // cudaEvent_t recorded between pass 1 and pass 2 (or null)
-  bool run_pass1 = true;      // false: lse2 is already in the workspace (kvbm_block_mass_lse)
+  bool run_pass1 = true;      // false: lse2 is already in the workspace (LSE input), or not this stage
+  bool run_pass2 = true;
+  bool run_split = true;      // fp32 on path 2: convert the run's q/k rows to tf32 pairs
+  bool run_masks = true;      // pack a pair mask into bits (tensor-core paths)
   Ragged rg;                  // ragged batch lengths / packed layout
+  // Staged execution: the passes cover units [rb, re) of the problem's range
+  // (relative to unit_begin) and pass 1 the q-heads [hb, he) of each group.
+  int rb = 0, re = 0;         // re <= rb: every unit
+  int hb = 0, he = 0;         // he <= hb: every head
 };
+
+// The units and heads a launch covers (LaunchOpts' run ranges resolved).
+struct RunRange {
+  int rb, nu;  // units [rb, rb + nu) of the problem's range
+  int hb, nh;  // pass-1 q-heads [hb, hb + nh) of each group
+};
+inline RunRange run_range(const kvbm_problem* p, const LaunchOpts& o) {
+  const int U = p->unit_end - p->unit_begin, G = p->Hq / p->Hkv;
+  RunRange r;
+  r.rb = o.re > o.rb ? o.rb : 0;
+  r.nu = o.re > o.rb ? o.re - o.rb : U;
+  r.hb = o.he > o.hb ? o.hb : 0;
+  r.nh = o.he > o.hb ? o.he - o.hb : G;
+  return r;
+}
 int launch_simt(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws, cudaStream_t s,
                 const LaunchOpts& o);
 int launch_tc(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws, cudaStream_t s,
               const LaunchOpts& o);
 // Writes a caller's natural-log row LSE into the workspace's lse2 layout of `L.path`.
 int launch_lse_import(const kvbm_problem* p, const WsLayout& L, const float* lse, const int64_t* lse_stride,
-                      void* ws, cudaStream_t s, const Ragged& rg);
+                      void* ws, cudaStream_t s, const Ragged& rg, const RunRange& rr);
 // per_sequence: mass_out is [B, num_blocks] (row b: the units of batch b in the range).
 int launch_reduce(const kvbm_problem* p, const WsLayout& L, void* mass_out, const void* ws,
                   cudaStream_t s, bool per_sequence);

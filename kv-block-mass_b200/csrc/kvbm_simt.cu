@@ -28,6 +28,7 @@ struct Args {
   const void* k;
   long long ks0, ks1, ks2, ks3;
   int N, D, G, Hkv, ub;
+  int rb, hb, hn;  // staged calls: units [rb, ..) of the range, pass-1 q-heads [hb, hb + hn)
   const uint8_t* kmask;
   long long kmb;
   const uint8_t* qmask;
@@ -148,7 +149,7 @@ __global__ void __launch_bounds__(NT) simt_lse_kernel(Args<Acc> a) {
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int ntile = (a.N + BM - 1) / BM;
   const int r0 = (ntile - 1 - (int)blockIdx.x) * BM;  // long (late) rows first
-  const int hidx = blockIdx.y;                         // (u - ub) * G + hh
+  const int hidx = (a.rb + (int)blockIdx.y / a.hn) * a.G + a.hb + (int)blockIdx.y % a.hn;  // (u - ub) * G + hh
   const int u = a.ub + hidx / a.G, hh = hidx % a.G;
   const int b = u / a.Hkv, g = u % a.Hkv, h = g * a.G + hh;
   const SeqView sv = seq_view(a.lens, a.cu, a.kpacked != 0, b, a.N, a.total);
@@ -228,7 +229,7 @@ __global__ void __launch_bounds__(NT) simt_mass_kernel(Args<Acc> a) {
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int c0 = blockIdx.x * BN;
   const int y = blockIdx.y;
-  const int uu = blockIdx.z;
+  const int uu = a.rb + (int)blockIdx.z;
   const int u = a.ub + uu;
   const int b = u / a.Hkv, g = u % a.Hkv;
   const SeqView sv = seq_view(a.lens, a.cu, a.kpacked != 0, b, a.N, a.total);
@@ -309,7 +310,11 @@ int launch_typed(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_
   a.kpacked = o.rg.k_packed ? 1 : 0;
   a.total = o.rg.total;
 
-  const int U = p->unit_end - p->unit_begin;
+  const RunRange rr = run_range(p, o);
+  a.rb = rr.rb;
+  a.hb = rr.hb;
+  a.hn = rr.nh;
+  const int U = rr.nu;  // units this launch runs
   const size_t smem1 = size_t(2) * p->D * 64 * sizeof(Acc);
   const size_t smem2 = smem1 + (64 + 16 * 64) * sizeof(Acc);
   auto k1 = simt_lse_kernel<In, Acc>;
@@ -317,16 +322,18 @@ int launch_typed(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_
   if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1) != cudaSuccess ||
       cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2) != cudaSuccess)
     return KVBM_ERR_CUDA;
-  dim3 g1((p->N + BM - 1) / BM, U * a.G);
+  dim3 g1((p->N + BM - 1) / BM, U * a.hn);
   if (o.run_pass1) {
     k1<<<g1, NT, smem1, s>>>(a);
     if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
   }
   if (o.mid_event != nullptr && cudaEventRecord(static_cast<cudaEvent_t>(o.mid_event), s) != cudaSuccess)
     return KVBM_ERR_CUDA;
-  dim3 g2((p->N + BN - 1) / BN, L.nchunk, U);
-  k2<<<g2, NT, smem2, s>>>(a);
-  if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
+  if (o.run_pass2) {
+    dim3 g2((p->N + BN - 1) / BN, L.nchunk, U);
+    k2<<<g2, NT, smem2, s>>>(a);
+    if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
+  }
   return KVBM_OK;
 }
 
@@ -452,12 +459,14 @@ int launch_simt(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* 
 // a dropped query_mask row counts as a row that keeps no key.
 template <typename Acc, bool kNegated>
 __global__ void lse_import_kernel(const float* lse, long long s0, long long s1, long long s2, Acc* out, int N,
-                                  int Nrow, int G, int Hkv, int ub, long long rows_total, const uint8_t* qmask,
-                                  long long qmb, const int32_t* lens, const int32_t* cu, long long total) {
+                                  int Nrow, int G, int Hkv, int ub, RunRange rr, long long rows_total,
+                                  const uint8_t* qmask, long long qmb, const int32_t* lens, const int32_t* cu,
+                                  long long total) {
   const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   if (idx >= rows_total) return;
   const int i = (int)(idx % Nrow);
-  const long long hidx = idx / Nrow;  // (u - ub) * G + hh
+  const long long pr = idx / Nrow;  // (unit, head) pair of the run
+  const long long hidx = (rr.rb + pr / rr.nh) * (long long)G + rr.hb + pr % rr.nh;  // (u - ub) * G + hh
   const int u = ub + (int)(hidx / G), hh = (int)(hidx % G);
   const int b = u / Hkv, h = (u % Hkv) * G + hh;
   // a packed batch indexes its LSE like q: row cu[b] + i of [H_q, total_tokens]
@@ -472,28 +481,28 @@ __global__ void lse_import_kernel(const float* lse, long long s0, long long s1, 
   Acc r;
   if (kNegated) r = dead ? (Acc)(-INFINITY) : (Acc)(-l2);
   else r = dead ? (Acc)INFINITY : (Acc)l2;
-  out[idx] = r;
+  out[hidx * Nrow + i] = r;
 }
 
 int launch_lse_import(const kvbm_problem* p, const WsLayout& L, const float* lse, const int64_t* st, void* ws,
-                      cudaStream_t s, const Ragged& rg) {
-  const int U = p->unit_end - p->unit_begin, G = p->Hq / p->Hkv;
+                      cudaStream_t s, const Ragged& rg, const RunRange& rr) {
+  const int G = p->Hq / p->Hkv;
   const int Nrow = L.path >= 1 ? (p->N + kTcTile - 1) / kTcTile * kTcTile : p->N;
-  const long long rows = (long long)U * G * Nrow;
+  const long long rows = (long long)rr.nu * rr.nh * Nrow;
   const int threads = 256;
   const long long blocks = (rows + threads - 1) / threads;
   char* base = static_cast<char*>(ws) + L.lse_off;
   if (L.path >= 1) {
     lse_import_kernel<float, true><<<(unsigned)blocks, threads, 0, s>>>(
-        lse, st[0], st[1], st[2], reinterpret_cast<float*>(base), p->N, Nrow, G, p->Hkv, p->unit_begin, rows,
+        lse, st[0], st[1], st[2], reinterpret_cast<float*>(base), p->N, Nrow, G, p->Hkv, p->unit_begin, rr, rows,
         p->query_mask, p->query_mask_bstride, rg.lens, rg.cu, rg.total);
   } else if (p->dtype == KVBM_F64) {
     lse_import_kernel<double, false><<<(unsigned)blocks, threads, 0, s>>>(
-        lse, st[0], st[1], st[2], reinterpret_cast<double*>(base), p->N, Nrow, G, p->Hkv, p->unit_begin, rows,
+        lse, st[0], st[1], st[2], reinterpret_cast<double*>(base), p->N, Nrow, G, p->Hkv, p->unit_begin, rr, rows,
         p->query_mask, p->query_mask_bstride, rg.lens, rg.cu, rg.total);
   } else {
     lse_import_kernel<float, false><<<(unsigned)blocks, threads, 0, s>>>(
-        lse, st[0], st[1], st[2], reinterpret_cast<float*>(base), p->N, Nrow, G, p->Hkv, p->unit_begin, rows,
+        lse, st[0], st[1], st[2], reinterpret_cast<float*>(base), p->N, Nrow, G, p->Hkv, p->unit_begin, rr, rows,
         p->query_mask, p->query_mask_bstride, rg.lens, rg.cu, rg.total);
   }
   return cudaGetLastError() == cudaSuccess ? KVBM_OK : KVBM_ERR_CUDA;

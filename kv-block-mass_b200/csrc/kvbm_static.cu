@@ -47,7 +47,11 @@ extern "C" int kvbm_block_mass_static(const kvbm_problem* p, void* mass_out, voi
     return KVBM_ERR_CUDA;
   }
   if (dev < 0 || dev >= kMaxDevices) return KVBM_ERR_DEVICE;
-  const size_t need = layout_for(p, select_path(p, dev)).total;
+  // The scratch a call needs covers only the batches x kv-heads of its unit
+  // range: a range inside one batch entry needs its own units' rows.
+  size_t need = 0;
+  const int pst = planned_workspace_bytes(p, &need);
+  if (pst != KVBM_OK) return pst;
   if (need > kStaticScratchBytes) return KVBM_ERR_SCRATCH;
   void* ptr = g_scratch_addr[dev].load(std::memory_order_acquire);
   if (ptr == nullptr) {

@@ -71,7 +71,9 @@ struct TcArgs {
   int W;                   // words per bit row (Npad / 32)
   int qchunk, nchunk;
   int per_unit;            // pass-2 CTAs per unit (sum of keys_in_chunk over chunks)
-  int usel, ugroup;        // pass 1 (uniform grid): units selected, units per CTA group
+  int usel, ugroup;        // pass 1 (uniform grid): units run, units per CTA group
+  int rb;                  // first unit run (relative to ub; staged calls run a sub-range)
+  int hb, hn;              // pass 1 runs q-heads [hb, hb + hn) of each group
   const int32_t* lens;     // ragged lengths [B] or null
   const int32_t* cu;       // packed row offsets [B+1] or null
   int kpacked;             // k packed like q
@@ -326,11 +328,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     qt = item_lo(it);
   } else {
     const int nt_all = a.Npad / TILE;
-    const long long per_group = (long long)a.ugroup * a.G * nt_all;
+    const long long per_group = (long long)a.ugroup * a.hn * nt_all;
     const int grp = (int)(blockIdx.x / per_group);
     const int r = (int)(blockIdx.x - grp * per_group);
-    const int width = min(a.ugroup, a.usel - grp * a.ugroup) * a.G;  // (unit, head) pairs of this group
-    hidx = grp * a.ugroup * a.G + r % width;
+    const int width = min(a.ugroup, a.usel - grp * a.ugroup) * a.hn;  // (unit, head) pairs of this group
+    const int pr = r % width;
+    hidx = (a.rb + grp * a.ugroup + pr / a.hn) * a.G + a.hb + pr % a.hn;
     qt = nt_all - 1 - r / width;
   }
   const int u = a.ub + hidx / a.G, hh = hidx % a.G;
@@ -518,9 +521,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     y = item_mid(it);
     kt = item_lo(it);
   } else {
-    uu = (int)blockIdx.x / a.per_unit;
+    const int ul = (int)blockIdx.x / a.per_unit;
+    uu = a.rb + ul;
     y = a.nchunk - 1;
-    kt = (int)blockIdx.x - uu * a.per_unit;
+    kt = (int)blockIdx.x - ul * a.per_unit;
     while (kt >= keys_in_chunk(a, y)) {
       kt -= keys_in_chunk(a, y);
       --y;
@@ -851,13 +855,20 @@ bool make_map(CUtensorMap* map, const void* base, CUtensorMapDataType type, int 
   return r == CUDA_SUCCESS;
 }
 
-// fp32 operand -> contiguous [B, H, N, D] tf32 pair: hi = tf32(x), lo = x - hi
-// (exact in fp32).  One launch splits q (first q_elems elements; rows Nq per
-// head) and k (rows Nk per head); a packed operand is one batch entry of
-// total_tokens rows.
+// fp32 operand -> contiguous [B, H, N, D] tf32 pairs: hi = tf32(x), lo = x - hi
+// (exact in fp32).  One launch converts the rows of a box of batch entries
+// [b0, b0 + nb): q-heads [qh0, qh0 + nqh) (rows Nq per head) and kv-heads
+// [kh0, kh0 + nkh) (rows Nk), written at their places in the full
+// [B, Hq, Nq, D] / [B, Hkv, Nk, D] copies; a packed operand is one batch
+// entry of total_tokens rows.
+struct SplitBox {
+  int qb0, qnb, qh0, nqh;  // q: batch entries, heads
+  int kb0, knb, kh0, nkh;  // k: batch entries, heads
+};
+
 __global__ void split_tf32_kernel(const float* q, long long q0, long long q1, long long q2, long long q3,
                                   int Hq, const float* k, long long k0, long long k1, long long k2,
-                                  long long k3, int Hkv, int Nq, int Nk, int D, long long q_elems,
+                                  long long k3, int Hkv, int Nq, int Nk, int D, SplitBox box, long long q_elems,
                                   long long k_elems, float* q_hi, float* q_lo, float* k_hi, float* k_lo) {
   const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   if (idx >= q_elems + k_elems) return;
@@ -868,12 +879,14 @@ __global__ void split_tf32_kernel(const float* q, long long q0, long long q1, lo
   const int N = is_q ? Nq : Nk;
   const int n = (int)(r % N);
   const long long bh = r / N;
-  const int H = is_q ? Hq : Hkv;
-  const int h = (int)(bh % H), b = (int)(bh / H);
+  const int nh = is_q ? box.nqh : box.nkh;
+  const int h = (is_q ? box.qh0 : box.kh0) + (int)(bh % nh);
+  const int b = (is_q ? box.qb0 : box.kb0) + (int)(bh / nh);
   const float x = is_q ? q[b * q0 + h * q1 + n * q2 + d * q3] : k[b * k0 + h * k1 + n * k2 + d * k3];
   const float hi = to_tf32(x);
-  (is_q ? q_hi : k_hi)[e] = hi;
-  (is_q ? q_lo : k_lo)[e] = x - hi;
+  const long long o = (((long long)b * (is_q ? Hq : Hkv) + h) * N + n) * D + d;
+  (is_q ? q_hi : k_hi)[o] = hi;
+  (is_q ? q_lo : k_lo)[o] = x - hi;
 }
 
 // Pair mask (bytes, nonzero = keep) ANDed with the key and query masks ->
@@ -933,17 +946,36 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
   const Ragged& rg = o.rg;
   const int Bq = rg.cu ? 1 : p->B, Nq = rg.cu ? (int)rg.total : p->N;
   const int Bk = rg.k_packed ? 1 : p->B, Nk = rg.k_packed ? (int)rg.total : p->N;
+  const RunRange rr = run_range(p, o);
   if constexpr (kOp == Op::TF32X3) {
     // split q/k into tf32 hi/lo pairs in the workspace, then map those
     float* base = reinterpret_cast<float*>(static_cast<char*>(ws) + L.split_off);
     const long long qe = (long long)Bq * p->Hq * Nq * Dr, ke = (long long)Bk * p->Hkv * Nk * Dr;
     float *q_hi = base, *q_lo = base + qe, *k_hi = base + 2 * qe, *k_lo = base + 2 * qe + ke;
-    const long long total = qe + ke;
-    split_tf32_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(
-        static_cast<const float*>(p->q), p->q_stride[0], p->q_stride[1], p->q_stride[2], p->q_stride[3], p->Hq,
-        static_cast<const float*>(p->k), p->k_stride[0], p->k_stride[1], p->k_stride[2], p->k_stride[3], p->Hkv,
-        Nq, Nk, Dr, qe, ke, q_hi, q_lo, k_hi, k_lo);
-    if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
+    if (o.run_split) {
+      SplitBox bx;
+      if (rg.cu != nullptr || rg.lens != nullptr) {
+        // ragged calls (never staged) convert every row of q and k
+        bx = SplitBox{0, Bq, 0, p->Hq, 0, Bk, 0, p->Hkv};
+      } else {
+        // the rows passes 1 and 2 of the run units read: their batch entries x
+        // their kv-heads (whole batch entries when the run crosses one), the
+        // run's q-heads, and k unless the head range starts past 0
+        const int G = p->Hq / p->Hkv;
+        const int u0 = p->unit_begin + rr.rb, u1 = u0 + rr.nu - 1;
+        const int b0 = u0 / p->Hkv, nb = u1 / p->Hkv - b0 + 1;
+        const int g0 = nb == 1 ? u0 % p->Hkv : 0, ng = nb == 1 ? u1 % p->Hkv - g0 + 1 : p->Hkv;
+        const bool one = nb == 1 && ng == 1;
+        bx = SplitBox{b0, nb, g0 * G + (one ? rr.hb : 0), one ? rr.nh : ng * G, b0, nb, g0, rr.hb == 0 ? ng : 0};
+      }
+      const long long qn = (long long)bx.qnb * bx.nqh * Nq * Dr, kn = (long long)bx.knb * bx.nkh * Nk * Dr;
+      const long long total = qn + kn;
+      split_tf32_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(
+          static_cast<const float*>(p->q), p->q_stride[0], p->q_stride[1], p->q_stride[2], p->q_stride[3], p->Hq,
+          static_cast<const float*>(p->k), p->k_stride[0], p->k_stride[1], p->k_stride[2], p->k_stride[3],
+          p->Hkv, Nq, Nk, Dr, bx, qn, kn, q_hi, q_lo, k_hi, k_lo);
+      if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
+    }
     const int64_t qs[4] = {(int64_t)p->Hq * Nq * Dr, (int64_t)Nq * Dr, Dr, 1};
     const int64_t ks[4] = {(int64_t)p->Hkv * Nk * Dr, (int64_t)Nk * Dr, Dr, 1};
     const CUtensorMapDataType t = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
@@ -993,15 +1025,20 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
     a.prow = bits;
     a.pcol = bits + words;
     a.pb = L.bits_batches > 1 ? (long long)a.Npad * a.W : 0;
-    const long long nblk = (long long)L.bits_batches * (a.Npad / 32) * (a.Npad / 32);
-    const bool per_b = L.bits_batches > 1;
-    pack_pair_mask_kernel<<<(unsigned)((nblk * 32 + 255) / 256), 256, 0, s>>>(
-        p->pair_mask, per_b ? p->pair_mask_bstride : 0, p->pair_mask_rstride, p->key_mask,
-        per_b ? p->key_mask_bstride : 0, p->query_mask, per_b ? p->query_mask_bstride : 0, p->N, a.Npad, nblk,
-        bits, bits + words);
-    if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
+    if (o.run_masks) {
+      const long long nblk = (long long)L.bits_batches * (a.Npad / 32) * (a.Npad / 32);
+      const bool per_b = L.bits_batches > 1;
+      pack_pair_mask_kernel<<<(unsigned)((nblk * 32 + 255) / 256), 256, 0, s>>>(
+          p->pair_mask, per_b ? p->pair_mask_bstride : 0, p->pair_mask_rstride, p->key_mask,
+          per_b ? p->key_mask_bstride : 0, p->query_mask, per_b ? p->query_mask_bstride : 0, p->N, a.Npad, nblk,
+          bits, bits + words);
+      if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
+    }
   }
-  const int U = p->unit_end - p->unit_begin;
+  const int U = rr.nu;  // units this launch runs
+  a.rb = rr.rb;
+  a.hb = rr.hb;
+  a.hn = rr.nh;
   const int ntiles = a.Npad / TILE;
   // Pass-1 CTAs of a unit all stream its whole k (under causal_skip, from the
   // first tile up); running the units in groups whose k fits in L2 reads each
@@ -1011,7 +1048,7 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
   const long long k_unit_bytes = (long long)Nk * Dr * (kOp == Op::TF32X3 ? 8 : 2);
   a.usel = U;
   a.ugroup = (int)std::max(1LL, std::min<long long>(U, kPass1GroupBytes / std::max(1LL, k_unit_bytes)));
-  const long long n1 = (long long)U * a.G * ntiles, n2 = (long long)U * a.per_unit;
+  const long long n1 = (long long)U * a.hn * ntiles, n2 = (long long)U * a.per_unit;
   if (n1 > 0x7fffffffLL || n2 > 0x7fffffffLL) return KVBM_ERR_SHAPE;
   dim3 grid1((unsigned)n1), grid2((unsigned)n2);
   if constexpr (kRagged) {
@@ -1065,8 +1102,10 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
   }
   if (o.mid_event != nullptr && cudaEventRecord(static_cast<cudaEvent_t>(o.mid_event), s) != cudaSuccess)
     return KVBM_ERR_CUDA;
-  k2<<<grid2, kThreads, sm2, s>>>(tq, tq2, tk, tk2, a);
-  if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
+  if (o.run_pass2) {
+    k2<<<grid2, kThreads, sm2, s>>>(tq, tq2, tk, tk2, a);
+    if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
+  }
   return KVBM_OK;
 }
 

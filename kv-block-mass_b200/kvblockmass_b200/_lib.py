@@ -29,6 +29,14 @@ KVBM_ERR_TIMEOUT = 11
 KVBM_ERR_SCRATCH = 12
 KVBM_ERR_PAGE = 13
 
+# Stages of a staged kvbm_block_mass_ex call (kvbm_options.stages).
+KVBM_STAGE_MASKS = 1
+KVBM_STAGE_PASS1 = 2
+KVBM_STAGE_PASS2 = 4
+KVBM_STAGE_REDUCE = 8
+
+ABI_VERSION = 2
+
 # Symbols include/kvbm.h declares; tests check the library exports each one.
 EXPORTED = [
     "kvbm_abi_version",
@@ -114,6 +122,11 @@ class Options(ctypes.Structure):
         ("total_tokens", ctypes.c_int64),
         ("per_sequence", ctypes.c_int32),
         ("events", ctypes.POINTER(ctypes.c_void_p)),
+        ("stages", ctypes.c_int32),
+        ("run_unit_begin", ctypes.c_int32),
+        ("run_unit_end", ctypes.c_int32),
+        ("run_head_begin", ctypes.c_int32),
+        ("run_head_end", ctypes.c_int32),
     ]
 
 
@@ -226,8 +239,9 @@ def load() -> ctypes.CDLL:
     lib.kvbm_selftest_wait_timeout.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.POINTER(ctypes.c_int)]
     lib.kvbm_check_device_errors.restype = ctypes.c_int
     lib.kvbm_check_device_errors.argtypes = [ctypes.c_void_p]
-    if lib.kvbm_abi_version() != 1:
-        raise RuntimeError(f"libkvbm ABI {lib.kvbm_abi_version()} != 1")
+    if lib.kvbm_abi_version() != ABI_VERSION:
+        raise RuntimeError(f"libkvbm ABI {lib.kvbm_abi_version()} != {ABI_VERSION}: rebuild it with "
+                           "`python kv-block-mass_b200/build.py`")
     _lib = lib
     return lib
 

@@ -26,7 +26,7 @@ from . import _lib
 __all__ = ["block_mass_b200", "block_mass_triton", "block_mass", "kernel_path", "make_problem",
            "workspace_bytes", "launches_per_call", "block_mass_paged", "make_paged_problem",
            "paged_workspace_bytes", "run_paged", "check_device_errors", "block_mass_varlen",
-           "make_varlen_problem", "run_prepared"]
+           "make_varlen_problem", "run_prepared", "run_staged"]
 
 _DTYPES = {
     torch.float32: _lib.KVBM_F32,
@@ -355,12 +355,12 @@ def block_mass_b200(q, k, attn_mask=None, causal=False, block_size=64, scale=Non
         dev = torch.device(device)
         if dev.type != "cuda":
             raise ValueError(f"block_mass_b200 computes on CUDA devices only, got device={device}")
-        if (not q.is_cuda and not k.is_cuda and q.is_pinned() and k.is_pinned() and units is None
-                and lse is None and out is None and q.dim() == 4 and k.dim() == 4 and seq_lens is None
-                and not per_sequence):
-            return _from_pinned_host(q, k, dev, attn_mask=attn_mask, causal=causal, block_size=block_size,
-                                     scale=scale, causal_skip=causal_skip, query_mask=query_mask,
-                                     workspace=workspace)
+        if (not q.is_cuda and not k.is_cuda and units is None and lse is None and out is None
+                and q.dim() == 4 and k.dim() == 4 and q.dtype == k.dtype and seq_lens is None
+                and not per_sequence and q.numel() > 0 and k.numel() > 0):
+            return _from_host(q, k, dev, attn_mask=attn_mask, causal=causal, block_size=block_size,
+                              scale=scale, causal_skip=causal_skip, query_mask=query_mask,
+                              workspace=workspace)
         q, k = q.to(dev), k.to(dev)
     if not (q.is_cuda and k.is_cuda):
         raise ValueError("block_mass_b200 needs CUDA tensors (there is no CPU path); "
@@ -387,99 +387,137 @@ def _side_stream(dev: torch.device) -> torch.cuda.Stream:
     return _SIDE_STREAMS[dev]
 
 
-def _from_pinned_host(q, k, dev, attn_mask, causal, block_size, scale, causal_skip, query_mask, workspace,
-                      target_units: int = 1):
-    """Pinned host q/k: overlap the host-to-device copy with the kernels.
+def run_staged(prep: _Prepared, stages: int, workspace: torch.Tensor, out: torch.Tensor | None = None,
+               units: tuple[int, int] | None = None, heads: tuple[int, int] | None = None,
+               stream: torch.cuda.Stream | None = None) -> None:
+    """One staged launch of a prepared problem (``kvbm_options.stages``).
 
-    The (batch, kv-head) units are cut into contiguous segments; a copy stream
-    copies segment i + 1 while segment i runs, and the per-segment mass
-    vectors are added in segment order (deterministic; the grouping of the
-    final sum differs from one call over all units, so the bits can differ
-    from it in the last place).  Only the first segment's copy is exposed, so
-    segments are one unit each: on the Llama-3-8B N=32768 shape that measured
-    10.4-11.1 ms end to end against 11.4-11.5 ms for two-unit and 12.3-13.0 ms
-    for four-unit segments.
-
-    Consecutive segments alternate between the caller's stream and a second
-    compute stream, each with its own workspace, so that one segment's first
-    pass fills the SMs its predecessor's last CTAs leave idle.  The first unit
-    is then cut further, into its first q-head and its other q-heads (mass is
-    a sum over heads), which shortens the copy before the first kernel from a
-    whole unit's q to one head's.  A caller's explicit ``workspace`` is shared
-    by every segment, so it keeps them all on the caller's stream, in whole
-    units.
+    ``stages`` is a mask of ``_lib.KVBM_STAGE_*``; ``units`` is a range of the
+    problem's units (relative to its unit range) that passes 1 and 2 cover,
+    ``heads`` a range of q-heads of each GQA group that pass 1 covers (needs a
+    one-unit ``units``).  Every piece writes into ``workspace``, which must be
+    sized for the whole problem; the reduce stage then gives the bits of one
+    whole call.
     """
-    from .distributed import unit_segments
+    o = prep.options()
+    o.stages = int(stages)
+    o.run_unit_begin, o.run_unit_end = units if units is not None else (0, 0)
+    o.run_head_begin, o.run_head_end = heads if heads is not None else (0, 0)
+    s = stream if stream is not None else torch.cuda.current_stream(prep.keep[0].device)
+    try:
+        code = _lib.load().kvbm_block_mass_ex(ctypes.byref(prep.prob), ctypes.byref(o),
+                                              None if out is None else out.data_ptr(), workspace.data_ptr(),
+                                              workspace.numel(), s.cuda_stream)
+    finally:
+        o.stages = o.run_unit_begin = o.run_unit_end = o.run_head_begin = o.run_head_end = 0
+    if code != _lib.KVBM_OK:
+        _raise(code, prep.prob)
 
+
+def _from_host(q, k, dev, attn_mask, causal, block_size, scale, causal_skip, query_mask, workspace):
+    """Host q/k (pinned or pageable): overlap the host-to-device copies with the kernels.
+
+    The copy stream moves the inputs one piece at a time while the kernels
+    run the pieces that have arrived, as staged calls into one workspace sized
+    for the whole problem; one bucket reduce at the end sums every unit, so the
+    result has the bits of ``kvbm_block_mass`` on the same values.  The pieces:
+    q-head 0 of unit 0 (batch 0, kv-head 0) with its k, then that unit's other
+    q-heads (pass 1 only, so that only one head's q is copied before the
+    first kernel starts), then pass 2 of unit 0, then every further unit with
+    both passes.  Consecutive pieces alternate between the caller's stream and
+    a second compute stream, so one piece's pass 1 fills the SMs its
+    predecessor's last CTAs leave idle.
+
+    Pageable tensors are staged through two pinned bounce buffers of one unit
+    each: the host copies piece i + 1 into one while the copy engine reads
+    piece i from the other (and the GPU computes piece i - 1).
+    """
     B, Hq, N, D = q.shape
     Hkv = k.shape[1]
     if Hkv == 0 or Hq % Hkv != 0:
         raise ValueError(f"GQA requires H_q % H_kv == 0, got H_q={Hq}, H_kv={Hkv}")
     G = Hq // Hkv
+    pinned = q.is_pinned() and k.is_pinned()
+    S = _lib
     with torch.cuda.device(dev):
         qd = torch.empty(q.shape, dtype=q.dtype, device=dev)
         kd = torch.empty(k.shape, dtype=k.dtype, device=dev)
         compute = torch.cuda.current_stream(dev)
         copy = _copy_stream(dev)
+        side = _side_stream(dev)
         copy.wait_stream(compute)  # qd/kd may reuse memory the compute stream still reads
         am = None if attn_mask is None else attn_mask.to(dev, non_blocking=True)
         qm = None if query_mask is None else query_mask.to(dev, non_blocking=True)
-        streams = [compute] if workspace is not None else [compute, _side_stream(dev)]
-        for st in streams[1:]:
-            st.wait_stream(compute)  # the masks above, and anything the caller queued
-        U = B * Hkv
-        step = max(1, min(target_units, U))
-        # Segments: ("heads", h0, h1) is q-heads [h0, h1) of unit 0 (batch 0,
-        # kv-head 0) as a problem of its own; ("units", ub, ue) is a unit range.
-        # With two streams the first unit is cut into its first q-head and the
-        # rest, so that only one head's q (and the unit's k) is copied before
-        # the first kernel starts.
-        segs = []
-        if len(streams) > 1 and G > 1:
-            segs += [("heads", 0, 1), ("heads", 1, G)]
-            u_from = 1
+        prep = make_problem(qd, kd, attn_mask=am, causal=causal, block_size=block_size, scale=scale,
+                            causal_skip=causal_skip, query_mask=qm)
+        need = workspace_bytes(prep)
+        ws = workspace if workspace is not None and workspace.numel() >= need else \
+            torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
+        out = torch.empty(prep.out_shape, dtype=prep.out_dtype, device=dev)
+        if prep.prob.pair_mask:
+            run_staged(prep, S.KVBM_STAGE_MASKS, ws, stream=compute)
+        side.wait_stream(compute)  # the masks, their bits, and anything the caller queued
+        streams = [compute, side]
+
+        # (unit, (head0, head1), stages, host copies): q-heads of one unit, plus its k
+        # with the piece whose heads start at 0
+        def piece_copies(u, h0, h1):
+            b, g = divmod(u, Hkv)
+            cps = [(qd[b, g * G + h0:g * G + h1], q[b, g * G + h0:g * G + h1])]
+            if h0 == 0:
+                cps.insert(0, (kd[b, g:g + 1], k[b, g:g + 1]))
+            return cps
+
+        if G > 1:
+            pieces = [(0, (0, 1), S.KVBM_STAGE_PASS1), (0, (1, G), S.KVBM_STAGE_PASS1)]
         else:
-            u_from = 0
-        segs += [("units", u, min(U, u + step)) for u in range(u_from, U, step)]
-        am0 = am[0:1] if am is not None and am.dim() == 3 else am
-        qm0 = qm[0:1] if qm is not None and qm.dim() == 2 else qm
-        parts = []
-        for i, (kind, lo, hi) in enumerate(segs):
+            pieces = [(0, (0, 1), S.KVBM_STAGE_PASS1 | S.KVBM_STAGE_PASS2)]
+        pieces += [(u, (0, G), S.KVBM_STAGE_PASS1 | S.KVBM_STAGE_PASS2) for u in range(1, B * Hkv)]
+
+        bounce, bounce_ev = None, [None, None]
+        if not pinned:
+            unit_bytes = (G * N * D * q.element_size()) + N * D * k.element_size()
+            bounce = [torch.empty(unit_bytes, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+        head0_done = None
+        for i, (u, (h0, h1), stages) in enumerate(pieces):
+            cps = piece_copies(u, h0, h1)
             with torch.cuda.stream(copy):
-                if kind == "heads":
-                    if lo == 0:
-                        kd[0, 0:1].copy_(k[0, 0:1], non_blocking=True)
-                    qd[0, lo:hi].copy_(q[0, lo:hi], non_blocking=True)
+                if pinned:
+                    for dst, src in cps:
+                        dst.copy_(src, non_blocking=True)
                 else:
-                    for b, g0, g1 in unit_segments(lo, hi, Hkv):
-                        qd[b, g0 * G:g1 * G].copy_(q[b, g0 * G:g1 * G], non_blocking=True)
-                        kd[b, g0:g1].copy_(k[b, g0:g1], non_blocking=True)
+                    j = i % 2
+                    if bounce_ev[j] is not None:
+                        bounce_ev[j].synchronize()  # the copy engine has read this buffer
+                    off = 0
+                    for dst, src in cps:
+                        n = src.numel() * src.element_size()
+                        stage = bounce[j][off:off + n].view(src.dtype).view(src.shape)
+                        stage.copy_(src)
+                        dst.copy_(stage, non_blocking=True)
+                        off += n
+                    bounce_ev[j] = torch.cuda.Event()
+                    bounce_ev[j].record(copy)
                 ev = torch.cuda.Event()
                 ev.record(copy)
-            st = streams[i % len(streams)]
+            st = streams[i % 2]
             st.wait_event(ev)
-            with torch.cuda.stream(st):
-                if kind == "heads":
-                    prep = make_problem(qd[0:1, lo:hi], kd[0:1, 0:1], attn_mask=am0, causal=causal,
-                                        block_size=block_size, scale=scale, causal_skip=causal_skip,
-                                        query_mask=qm0)
-                else:
-                    prep = make_problem(qd, kd, attn_mask=am, causal=causal, block_size=block_size, scale=scale,
-                                        causal_skip=causal_skip, query_mask=qm, units=(lo, hi))
-                parts.append(run_prepared(prep, workspace=workspace))
-        for st in streams[1:]:
-            compute.wait_stream(st)
-            for t in (qd, kd) + tuple(x for x in (am, qm) if x is not None):
-                t.record_stream(st)
-        for m in parts:
-            m.record_stream(compute)
+            run_staged(prep, stages, ws, units=(u, u + 1), heads=(h0, h1), stream=st)
+            if G > 1 and i == 0:
+                head0_done = torch.cuda.Event()
+                head0_done.record(st)
+            elif G > 1 and i == 1:
+                # pass 2 of unit 0 reads pass 1 of every one of its heads
+                st.wait_event(head0_done)
+                run_staged(prep, S.KVBM_STAGE_PASS2, ws, units=(0, 1), stream=st)
+        compute.wait_stream(side)
+        run_staged(prep, S.KVBM_STAGE_REDUCE, ws, out=out, stream=compute)
+        for t in (qd, kd, ws) + tuple(x for x in (am, qm) if x is not None):
+            t.record_stream(side)
         # qd/kd were written on the copy stream: tell the allocator before they are freed
         qd.record_stream(copy)
         kd.record_stream(copy)
-        total = parts[0].clone()
-        for m in parts[1:]:
-            total += m
-        return total
+        return out
 
 
 def block_mass_triton(q, k, attn_mask=None, causal=False, block_size=64, scale=None,

@@ -27,7 +27,7 @@ def declared_functions():
 
 def test_library_loads():
     lib = _lib.load()
-    assert lib.kvbm_abi_version() == 1
+    assert lib.kvbm_abi_version() == _lib.ABI_VERSION == 2
 
 
 def test_every_declared_symbol_is_exported():
@@ -229,3 +229,58 @@ def test_validate_ex_survives_random_options():
         assert st in known
         ws = lib.kvbm_workspace_bytes_ex(ctypes.byref(p), ctypes.byref(o))
         assert (ws > 0) == (st == _lib.KVBM_OK)
+
+
+def _opts(**kw):
+    o = _lib.Options()
+    for name, v in kw.items():
+        setattr(o, name, v)
+    return o
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(stages=_lib.KVBM_STAGE_PASS1), _lib.KVBM_OK),
+    (dict(stages=16), _lib.KVBM_ERR_SHAPE),
+    (dict(stages=-1), _lib.KVBM_ERR_SHAPE),
+    (dict(stages=_lib.KVBM_STAGE_PASS2, run_unit_begin=1, run_unit_end=2), _lib.KVBM_OK),
+    (dict(run_unit_begin=1, run_unit_end=3), _lib.KVBM_ERR_UNITS),       # the problem has 2 units
+    (dict(run_unit_begin=-1, run_unit_end=1), _lib.KVBM_ERR_UNITS),
+    (dict(run_unit_begin=0, run_unit_end=1, run_head_begin=1, run_head_end=3), _lib.KVBM_OK),
+    (dict(run_head_begin=1, run_head_end=3), _lib.KVBM_ERR_SHAPE),       # narrower than G=4 over 2 units
+    (dict(run_head_begin=0, run_head_end=4), _lib.KVBM_OK),              # every head: any run range
+    (dict(run_unit_begin=0, run_unit_end=1, run_head_begin=2, run_head_end=5), _lib.KVBM_ERR_SHAPE),
+])
+def test_staged_option_checks(kw, code):
+    """Staged calls (kvbm_options.stages / run ranges) are checked on the host."""
+    lib = _lib.load()
+    p = _problem()  # B=1, H_q=8, H_kv=2: 2 units of G=4 heads
+    assert lib.kvbm_validate_ex(ctypes.byref(p), ctypes.byref(_opts(**kw))) == code
+
+
+def test_staged_calls_take_no_ragged_or_paged_inputs():
+    lib = _lib.load()
+    p = _problem()
+    lens = torch.full((1,), 100, dtype=torch.int32)
+    o = _opts(stages=_lib.KVBM_STAGE_PASS1, seq_lens=lens.data_ptr())
+    assert lib.kvbm_validate_ex(ctypes.byref(p), ctypes.byref(o)) == _lib.KVBM_ERR_SHAPE
+    o = _opts(seq_lens=lens.data_ptr())
+    assert lib.kvbm_validate_ex(ctypes.byref(p), ctypes.byref(o)) == _lib.KVBM_OK
+
+
+def test_unit_range_workspace_covers_only_its_rows():
+    """The workspace of a unit range inside one batch entry holds only those
+    units' rows: an fp32 problem's tf32 copies (path 2) shrink with the range,
+    so a one-unit slice of a problem too large for the no-allocation entry
+    point's 64 MiB fits it."""
+    lib = _lib.load()
+    shape = (1, 32, 8, 8192, 64)  # fp32 D=64 runs the 3xTF32 path
+    full = lib.kvbm_workspace_bytes(ctypes.byref(_problem(shape=shape)))
+    one = lib.kvbm_workspace_bytes(ctypes.byref(_problem(shape=shape, units=(3, 4))))
+    limit = lib.kvbm_static_scratch_bytes()
+    assert full > limit >= one
+    # lse2 + partials + tf32 hi/lo of the unit's 4 q-heads and its kv-head (a bound, all paths)
+    N, D, G = 8192, 64, 4
+    assert one <= (G * N + 64 * N) * 4 + 2 * 4 * D * N * (G + 1) + 4096
+    # a range that crosses a batch entry keeps whole batch entries
+    two_b = _problem(shape=(2, 32, 8, 8192, 64), units=(7, 9))
+    assert lib.kvbm_workspace_bytes(ctypes.byref(two_b)) > one

@@ -310,14 +310,22 @@ def test_llama3_70b_prefix_vs_oracle(cuda_device):
     assert max_rel(got.cpu().numpy(), want) < 1e-3
 
 
-@pytest.mark.parametrize("shape", [(1, 32, 8, 3000, 128), (3, 8, 2, 777, 64)])
-def test_pinned_host_inputs_pipelined(cuda_device, shape):
-    """Pinned host inputs with device='cuda' copy unit segments on a side stream
-    while earlier segments compute; the result equals the device-input call."""
+@pytest.mark.parametrize("pinned", [True, False])
+@pytest.mark.parametrize("shape,dtype", [((1, 32, 8, 3000, 128), torch.bfloat16),
+                                         ((3, 8, 2, 777, 64), torch.bfloat16),
+                                         ((2, 8, 2, 900, 64), torch.float32),    # 3xTF32: per-piece tf32 split
+                                         ((2, 4, 4, 500, 96), torch.float32)])   # SIMT
+def test_host_inputs_give_the_device_call_bits(cuda_device, shape, dtype, pinned):
+    """Host q/k with device='cuda' are copied piece by piece (q-head 0 of unit 0,
+    its other heads, then unit by unit) while earlier pieces compute, as staged
+    calls into one workspace with one reduce: the result has the bits of the
+    device-input call.  Pageable tensors go through pinned bounce buffers."""
     B, Hq, Hkv, N, D = shape
     g = torch.Generator().manual_seed(17)
-    q = torch.randn(B, Hq, N, D, generator=g).to(torch.bfloat16).pin_memory()
-    k = torch.randn(B, Hkv, N, D, generator=g).to(torch.bfloat16).pin_memory()
+    q = torch.randn(B, Hq, N, D, generator=g).to(dtype)
+    k = torch.randn(B, Hkv, N, D, generator=g).to(dtype)
+    if pinned:
+        q, k = q.pin_memory(), k.pin_memory()
     km = torch.rand(N, generator=g) > 0.1
     qm = torch.rand(B, N, generator=g) > 0.1
     a = kb.block_mass_b200(q, k, attn_mask=km, query_mask=qm, causal=True, block_size=64, device=cuda_device)
@@ -325,16 +333,15 @@ def test_pinned_host_inputs_pipelined(cuda_device, shape):
             causal=True, block_size=64)
     torch.cuda.synchronize()
     assert a.is_cuda
-    assert max_rel(a.cpu().numpy(), b.cpu().numpy()) < 1e-6
+    assert torch.equal(a, b)
     c = kb.block_mass_b200(q, k, attn_mask=km, query_mask=qm, causal=True, block_size=64, device=cuda_device)
     assert torch.equal(a, c)
 
 
 @pytest.mark.parametrize("mask_kind", ["batch_pairs", "pairs", "none"])
-def test_pinned_host_first_unit_split_by_heads(cuda_device, mask_kind):
-    """The pinned-host path cuts its first unit into q-head 0 and q-heads
-    1..G-1 (separate problems on two streams); with every mask form that the
-    cut has to slice, the result matches the device-input call."""
+def test_host_inputs_with_pair_masks(cuda_device, mask_kind):
+    """Pair masks are packed once before the pieces run (KVBM_STAGE_MASKS); every
+    mask form gives the device-input call's bits."""
     B, Hq, Hkv, N, D = 2, 8, 2, 1000, 64
     g = torch.Generator().manual_seed(29)
     q = torch.randn(B, Hq, N, D, generator=g).to(torch.bfloat16).pin_memory()
@@ -349,9 +356,58 @@ def test_pinned_host_first_unit_split_by_heads(cuda_device, mask_kind):
     a = kb.block_mass_b200(q, k, attn_mask=am, query_mask=qm, causal=True, block_size=64, device=cuda_device)
     b = run(q.to(cuda_device), k.to(cuda_device), attn_mask=None if am is None else am.to(cuda_device),
             query_mask=qm.to(cuda_device), causal=True, block_size=64)
-    assert max_rel(a.cpu().numpy(), b.cpu().numpy()) < 1e-6
-    c = kb.block_mass_b200(q, k, attn_mask=am, query_mask=qm, causal=True, block_size=64, device=cuda_device)
-    assert torch.equal(a, c)
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.float32, 64), (torch.float32, 96),
+                                     (torch.float64, 32)])
+@pytest.mark.parametrize("mask", ["none", "pairs"])
+def test_staged_pieces_on_two_streams(cuda_device, dtype, D, mask):
+    """kvbm_options.stages / run ranges through the C ABI: pass 1 per (unit,
+    head range) and pass 2 per unit, out of order on two streams, into one
+    workspace, then one reduce: the bits of one whole call, on every kernel
+    path, also with the LSE input."""
+    from kvblockmass_b200 import _lib
+    from kvblockmass_b200.ops import run_staged
+
+    S = _lib
+    B, Hq, Hkv, N = 2, 6, 2, 700
+    G = Hq // Hkv
+    g = torch.Generator().manual_seed(D)
+    q = torch.randn(B, Hq, N, D, generator=g).to(dtype).to(cuda_device)
+    k = torch.randn(B, Hkv, N, D, generator=g).to(dtype).to(cuda_device)
+    am = (torch.rand(B, N, N, generator=g) > 0.3).to(cuda_device) if mask == "pairs" else None
+    whole = run(q, k, attn_mask=am, causal=True, block_size=32)
+    prep = kb.make_problem(q, k, attn_mask=am, causal=True, block_size=32)
+    ws = torch.full((kb.workspace_bytes(prep),), 0xFF, dtype=torch.uint8, device=cuda_device)
+    out = torch.empty_like(whole)
+    s0 = torch.cuda.current_stream(cuda_device)
+    s1 = torch.cuda.Stream(device=cuda_device)
+    run_staged(prep, S.KVBM_STAGE_MASKS, ws, stream=s0)
+    s1.wait_stream(s0)
+    U = B * Hkv
+    done = {}
+    for u in reversed(range(U)):              # units in reverse, heads split in two pieces
+        for i, (h0, h1) in enumerate(((0, 1), (1, G))):
+            st = s0 if (u + i) % 2 else s1
+            run_staged(prep, S.KVBM_STAGE_PASS1, ws, units=(u, u + 1), heads=(h0, h1), stream=st)
+            e = torch.cuda.Event()
+            e.record(st)
+            done.setdefault(u, []).append(e)
+    for u in range(U):
+        st = s0 if u % 2 else s1
+        for e in done[u]:
+            st.wait_event(e)
+        run_staged(prep, S.KVBM_STAGE_PASS2, ws, units=(u, u + 1), stream=st)
+    s0.wait_stream(s1)
+    run_staged(prep, S.KVBM_STAGE_REDUCE, ws, out=out, stream=s0)
+    torch.cuda.synchronize()
+    assert torch.equal(out, whole)
+    # a staged call with every stage is the whole call
+    out2 = torch.empty_like(whole)
+    run_staged(prep, 0, ws, out=out2)
+    torch.cuda.synchronize()
+    assert torch.equal(out2, whole)
 
 
 def test_causal_skip_is_engaged(cuda_device):

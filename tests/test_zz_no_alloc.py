@@ -5,8 +5,10 @@ its KV-cache pool (so cudaMalloc fails, and a cudaMalloc/cudaFree in its step
 loop would synchronise the device) cannot hand the library a workspace.  For
 them the library keeps a fixed scratch array in device memory.  These tests
 call that entry point through the C ABI and check it against the regular
-workspace-taking entry point.  Two calls run back to back on different
-problems, so the second call finds the first one's data in the shared array.
+workspace-taking entry point and against the CPU oracle.  The calls run back
+to back on problems of different shapes and kernel paths, so each call finds
+the previous one's data in the shared array: the lse2 rows, the partials, the
+tf32 copies of fp32 inputs and the packed pair-mask bits.
 
 This file sorts last so that a run stopping at the first failure has already
 run every other test; it also passes on its own in a fresh process.
@@ -18,8 +20,11 @@ import numpy as np
 import pytest
 import torch
 
+from _helpers import max_rel
+from oracle import block_mass_np as orc
+
 from kvblockmass_b200 import _lib
-from kvblockmass_b200.ops import make_problem
+from kvblockmass_b200.ops import kernel_path, make_problem
 
 pytestmark = pytest.mark.gpu
 
@@ -28,9 +33,9 @@ TOL = {torch.float32: 2e-5, torch.bfloat16: 1e-3}
 
 def _inputs(B, Hq, Hkv, N, D, dtype, seed, dev):
     g = torch.Generator().manual_seed(seed)
-    q = torch.randn(B, Hq, N, D, generator=g).to(dtype).to(dev)
-    k = torch.randn(B, Hkv, N, D, generator=g).to(dtype).to(dev)
-    return q, k
+    q = torch.randn(B, Hq, N, D, generator=g).to(dtype)
+    k = torch.randn(B, Hkv, N, D, generator=g).to(dtype)
+    return q, k, q.to(dev), k.to(dev)
 
 
 def _regular(prep, dev):
@@ -45,44 +50,104 @@ def _regular(prep, dev):
     return out
 
 
-def test_static_matches_workspace_entry_point(cuda_device):
+def _static(prep, dev):
+    lib = _lib.load()
+    out = torch.full((prep.nb,), float("nan"), dtype=prep.out_dtype, device=dev)
+    rc = lib.kvbm_block_mass_static(ctypes.byref(prep.prob), out.data_ptr(),
+                                    torch.cuda.current_stream(dev).cuda_stream)
+    assert rc == 0, _lib.status_string(rc)
+    return out
+
+
+def _oracle(q, k, mask, kw):
+    return orc.block_mass_stream(q.float().numpy(), k.float().numpy(),
+                                 attn_mask=None if mask is None else mask.numpy(), **kw)
+
+
+# (shape, call keywords, mask kind, kernel path it must take)
+CASES = [
+    # tcgen05 path: bf16, D=128, causal, ragged N
+    (dict(B=1, Hq=8, Hkv=2, N=3000, D=128, dtype=torch.bfloat16, seed=11),
+     dict(causal=True, block_size=64), None, 1),
+    # SIMT path: fp32 with D=96 (the 3xTF32 path takes D <= 64), key mask, non-causal
+    (dict(B=2, Hq=4, Hkv=2, N=777, D=96, dtype=torch.float32, seed=12),
+     dict(causal=False, block_size=48), "keys", 0),
+    # 3xTF32 path: fp32 with D=64, its tf32 copies of q/k in the scratch array
+    (dict(B=1, Hq=4, Hkv=1, N=1000, D=64, dtype=torch.float32, seed=13),
+     dict(causal=True, block_size=64), None, 2),
+    # tcgen05 with a per-batch pair mask: its packed bits in the scratch array,
+    # after calls of other shapes left their data there
+    (dict(B=2, Hq=4, Hkv=2, N=500, D=64, dtype=torch.bfloat16, seed=14),
+     dict(causal=True, block_size=32), "batch_pairs", 1),
+]
+
+
+def test_static_matches_workspace_entry_point_and_oracle(cuda_device):
     dev = cuda_device
     lib = _lib.load()
     assert lib.kvbm_static_scratch_bytes() == 64 << 20
-    cases = [
-        # tensor-core path: bf16, D=128, causal, ragged N
-        (dict(B=1, Hq=8, Hkv=2, N=3000, D=128, dtype=torch.bfloat16, seed=11), dict(causal=True, block_size=64)),
-        # SIMT path: fp32, D=64, key mask, non-causal
-        (dict(B=2, Hq=4, Hkv=2, N=777, D=64, dtype=torch.float32, seed=12), dict(causal=False, block_size=48)),
-    ]
-    preps, outs = [], []
-    stream = torch.cuda.current_stream(dev).cuda_stream
-    for shape, kw in cases:
-        q, k = _inputs(dev=dev, **shape)
-        if shape["dtype"] == torch.float32:
-            kw = dict(kw, attn_mask=(torch.rand(shape["N"], generator=torch.Generator().manual_seed(3)) > 0.2).to(dev))
-        prep = make_problem(q, k, **kw)
-        out = torch.full((prep.nb,), float("nan"), dtype=prep.out_dtype, device=dev)
-        # two static calls in a row: the second finds the first's data in the array
-        rc = lib.kvbm_block_mass_static(ctypes.byref(prep.prob), out.data_ptr(), stream)
-        assert rc == 0, _lib.status_string(rc)
-        preps.append((prep, shape["dtype"]))
-        outs.append(out)
+    runs = []
+    for shape, kw, mkind, path in CASES:
+        q, k, qd, kd = _inputs(dev=dev, **shape)
+        N, B = shape["N"], shape["B"]
+        g = torch.Generator().manual_seed(3)
+        mask = None
+        if mkind == "keys":
+            mask = torch.rand(N, generator=g) > 0.2
+        elif mkind == "batch_pairs":
+            mask = torch.rand(B, N, N, generator=g) > 0.3
+        prep = make_problem(qd, kd, attn_mask=None if mask is None else mask.to(dev), **kw)
+        assert kernel_path(prep) == path, (shape, path)
+        runs.append((prep, shape["dtype"], q, k, mask, kw))
+    # two rounds of static calls in a row on one stream: every call finds the
+    # previous call's data in the shared array
+    firsts = [_static(prep, dev) for prep, *_ in runs]
+    seconds = [_static(prep, dev) for prep, *_ in runs]
     torch.cuda.synchronize()
-    assert lib.kvbm_check_device_errors(stream) == 0
-    for (prep, dtype), got in zip(preps, outs):
+    assert lib.kvbm_check_device_errors(torch.cuda.current_stream(dev).cuda_stream) == 0
+    for (prep, dtype, q, k, mask, kw), a, b in zip(runs, firsts, seconds):
         want = _regular(prep, dev)
         torch.cuda.synchronize()
-        g, w = got.double().cpu().numpy(), want.double().cpu().numpy()
-        assert np.isfinite(g).all()
-        rel = float(np.max(np.abs(g - w) / np.maximum(np.abs(w), 1e-6)))
-        assert rel < TOL[dtype], rel
+        ga, gb = a.double().cpu().numpy(), b.double().cpu().numpy()
+        assert np.isfinite(ga).all() and np.isfinite(gb).all()
+        assert max_rel(ga, want.double().cpu().numpy()) < TOL[dtype]
+        assert max_rel(gb, want.double().cpu().numpy()) < TOL[dtype]
+        assert max_rel(ga, _oracle(q, k, mask, kw)) < TOL[dtype]
+
+
+def test_static_unit_ranges_split_a_problem_too_large_for_the_array(cuda_device):
+    """An fp32 problem whose workspace is larger than the array is refused whole,
+    and runs as unit ranges: a range inside one batch entry needs scratch for
+    its own units' rows only.  The ranges add up to the whole."""
+    dev = cuda_device
+    lib = _lib.load()
+    q, k, qd, kd = _inputs(1, 32, 8, 8192, 64, torch.float32, 21, dev)
+    prep = make_problem(qd, kd, causal=True, block_size=64)
+    assert kernel_path(prep) == 2
+    assert lib.kvbm_workspace_bytes(ctypes.byref(prep.prob)) > lib.kvbm_static_scratch_bytes()
+    out = torch.empty(prep.nb, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    assert lib.kvbm_block_mass_static(ctypes.byref(prep.prob), out.data_ptr(), stream) == _lib.KVBM_ERR_SCRATCH
+    total = torch.zeros(prep.nb, dtype=torch.float64, device=dev)
+    parts = []
+    for u in range(8):
+        prep.prob.unit_begin, prep.prob.unit_end = u, u + 1
+        m = _static(prep, dev)
+        parts.append(m)
+        total += m.double()
+    prep.prob.unit_begin, prep.prob.unit_end = 0, 8
+    whole = _regular(prep, dev)
+    torch.cuda.synchronize()
+    assert max_rel(total.cpu().numpy(), whole.double().cpu().numpy()) < 1e-6
+    # unit 5 alone against the oracle (q-heads 20..23 with kv-head 5)
+    want = orc.block_mass_stream(q[:, 20:24].numpy(), k[:, 5:6].numpy(), causal=True, block_size=64, threads=8)
+    assert max_rel(parts[5].cpu().numpy(), want) < 2e-5
 
 
 def test_static_rejects_oversized_problem(cuda_device):
     """A problem whose scratch exceeds the fixed array is refused before any launch."""
     lib = _lib.load()
-    q, k = _inputs(1, 8, 1, 256, 128, torch.bfloat16, 5, cuda_device)
+    _, _, q, k = _inputs(1, 8, 1, 256, 128, torch.bfloat16, 5, cuda_device)
     prep = make_problem(q, k, causal=True, block_size=256)
     # Describe the Llama-3-70B N=131072 shape over the same (valid, aligned)
     # pointers: the size check fails on the host, so nothing is read.
