@@ -623,9 +623,14 @@ def b200_arm(args, w):
         ops.run_prepared(prep, out=out, workspace=ws)
         torch.cuda.synchronize()
         if path == 1:
+            # tensor-core layout: -lse2 over 128-row tiles, rows permuted inside each
+            # 64-row half (row 8m + 2p + e at p*16 + 2m + e; kvbm_internal.cuh)
             npad = (w.N + 127) // 128 * 128
             nl = ws[: q.shape[0] * q.shape[1] * npad * 4].view(torch.float32).view(q.shape[0], q.shape[1], npad)
-            lse_buf.copy_(-nl[:, :, : w.N] / 1.4426950408889634)
+            rr = torch.arange(w.N, device=dev)
+            ii = rr & 63
+            slot = (rr & ~63) | (((ii >> 1) & 3) << 4) | ((ii >> 3) << 1) | (ii & 1)
+            lse_buf.copy_(-nl[:, :, slot] / 1.4426950408889634)
         else:
             nl = ws[: q.shape[0] * q.shape[1] * w.N * 4].view(torch.float32).view(q.shape[0], q.shape[1], w.N)
             lse_buf.copy_(nl / 1.4426950408889634)
@@ -800,7 +805,37 @@ def b200_arm(args, w):
         e2e = {"value": pairs_total_per_step * Ke / (float(e_ms.item()) * 1e-3), "unit": UNIT,
                "h2d_bytes_per_step": int(q_pin.numel() * q_pin.element_size() + k_pin.numel() * k_pin.element_size()),
                "d2h_bytes_per_step": int(m_host.numel() * m_host.element_size()),
-               "steps": Ke, "api": "kvblockmass_b200.block_mass_b200(pinned host q/k, device='cuda').cpu()"}
+               "steps": Ke, "api": "kvblockmass_b200.block_mass_b200(pinned host q/k, device='cuda').cpu()",
+               "bits_equal_device_call": None}
+        # the same call on pageable host tensors (staged through pinned bounce buffers)
+        q_pg, k_pg = q_pin.clone(), k_pin.clone()
+        assert not q_pg.is_pinned()
+        kb.block_mass_b200(q_pg, k_pg, attn_mask=kmd, query_mask=qmd, causal=w.causal,
+                           block_size=w.block_size, device=dev).cpu()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        a0.record(stream)
+        for _ in range(Ke):
+            m = kb.block_mass_b200(q_pg, k_pg, attn_mask=kmd, query_mask=qmd, causal=w.causal,
+                                   block_size=w.block_size, device=dev)
+            if world > 1:
+                dist.reduce(m, dst=0, op=dist.ReduceOp.SUM)
+            m_host_pg = m.cpu()
+        a1.record(stream)
+        torch.cuda.synchronize()
+        p_ms = torch.tensor([a0.elapsed_time(a1)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(p_ms, op=dist.ReduceOp.MAX)
+        e2e["pageable"] = {"value": pairs_total_per_step * Ke / (float(p_ms.item()) * 1e-3), "unit": UNIT,
+                           "ms_per_step": float(p_ms.item()) / Ke,
+                           "api": "block_mass_b200(pageable host q/k, device='cuda'): pinned bounce buffers"}
+        del q_pg, k_pg
+        if world == 1:
+            dev_out = ops.run_prepared(prep, workspace=ws)
+            torch.cuda.synchronize()
+            e2e["bits_equal_device_call"] = bool(torch.equal(m_host.to(dev), dev_out)
+                                                 and torch.equal(m_host_pg.to(dev), dev_out))
 
     clocks = None
     if sampler:

@@ -139,8 +139,9 @@ KVBM_API size_t kvbm_workspace_bytes(const kvbm_problem* p);
  * 1 = tcgen05 tensor cores with TMA and TMEM (bf16/fp16, D <= 256 with
  *     D % 8 == 0, padded to 64/128/192/256 by the TMA's zero fill; 192 and
  *     256 run one CTA per SM and are bound by the tensor pipe),
- * 2 = tcgen05 3xTF32 for fp32 inputs (D <= 64 with D % 4 == 0): tf32 hi/lo
- *     split, three MMAs per step, fp32-grade scores,
+ * 2 = tcgen05 3xTF32 for fp32 inputs (D <= 128 with D % 4 == 0): tf32 hi/lo
+ *     split, three MMAs per step, fp32-grade scores (D > 64: one CTA per SM,
+ *     the streamed operand in 128-byte K-blocks),
  * (paths 1 and 2 take pair masks as packed bits: 2 * Npad^2 / 8 bytes of
  * workspace per mask batch entry, Npad = N rounded up to 128),
  * negative = a kvbm_status error code, negated. */

@@ -61,7 +61,7 @@ int validate(const kvbm_problem* p) {
 // Path 1 (tcgen05, bf16/fp16) needs D <= 256 with 16-byte rows (D % 8 == 0),
 // a unit-stride head dim, 16-byte aligned base pointers and row/head/batch
 // strides (TMA rules); D is padded to 64/128/192/256 by the TMA's zero fill.
-// Path 2 (tcgen05 3xTF32 for fp32 inputs) needs D <= 64 with D % 4 == 0; it
+// Path 2 (tcgen05 3xTF32 for fp32 inputs) needs D <= 128 with D % 4 == 0; it
 // reads q/k with a split kernel, so any strides work.  Both need a positive
 // scale; pair masks are packed to bits for them.  Everything else runs the
 // SIMT kernels.
@@ -69,7 +69,7 @@ int select_path(const kvbm_problem* p, int device) {
   if (device >= 0 && device_kind(device) != 1) return 0;
   if (!(p->scale > 0.0)) return 0;  // the exp/sum warps assume a positive scale
   if (!tc_path_enabled()) return 0;
-  if (p->dtype == KVBM_F32) return (p->D <= 64 && p->D % 4 == 0) ? 2 : 0;
+  if (p->dtype == KVBM_F32) return (p->D <= 128 && p->D % 4 == 0) ? 2 : 0;
   if (p->dtype != KVBM_BF16 && p->dtype != KVBM_F16) return 0;
   if (p->D > 256 || p->D % 8 != 0) return 0;
   const int64_t* qs = p->q_stride;

@@ -32,6 +32,14 @@ constexpr int kMaxQueryChunks = 64;
 // below 2^21, the width of a work-item field, and padded lengths fit int.
 constexpr int kMaxN = 1 << 28;
 
+// Stored position of row r in the tensor-core paths' lse2 array: inside each
+// 64-row half of a 128-row tile, row 8m + 2p + e goes to p*16 + 2m + e, so
+// that the 16 query rows one pass-2 thread reads are consecutive (kvbm_tc.cu).
+__host__ __device__ inline int lse_tile_slot(int r) {
+  const int i = r & 63;
+  return (r & ~63) | (((i >> 1) & 3) << 4) | ((i >> 3) << 1) | (i & 1);
+}
+
 // Where each array lives inside the caller's workspace.
 struct WsLayout {
   size_t lse_off = 0, lse_bytes = 0;     // [U_sel * G * N] lse2 (Acc)

@@ -481,7 +481,7 @@ __global__ void lse_import_kernel(const float* lse, long long s0, long long s1, 
   Acc r;
   if (kNegated) r = dead ? (Acc)(-INFINITY) : (Acc)(-l2);
   else r = dead ? (Acc)INFINITY : (Acc)l2;
-  out[hidx * Nrow + i] = r;
+  out[hidx * Nrow + (kNegated ? lse_tile_slot(i) : i)] = r;  // the tensor-core paths' row order
 }
 
 int launch_lse_import(const kvbm_problem* p, const WsLayout& L, const float* lse, const int64_t* st, void* ws,

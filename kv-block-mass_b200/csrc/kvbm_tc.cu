@@ -45,7 +45,15 @@ constexpr int kThreads = 64 + kExpThreads;  // + TMA warp + MMA warp
 #define KVBM_STAGES 2
 #endif
 constexpr int kStages = KVBM_STAGES;  // K (pass 1) / Q (pass 2) ring depth
-constexpr int kLStages = 4;         // lse2 ring depth (pass 2)
+// lse2 ring depth (pass 2).  The ring has no release barrier of its own: the
+// producer refills the slot of tile j - kLStages only after the MMA of tile
+// j - kStages completed (its Q-slot wait), that MMA waited until every exp
+// thread released the TMEM buffer of tile j - kStages - 2, and an exp thread
+// releases a buffer only after it finished computing the tile before it.  So
+// every exp thread is done with tiles <= j - kStages - 3, which covers the
+// slot's previous tile when kLStages >= kStages + 3.
+constexpr int kLStages = 8;
+static_assert(kLStages >= kStages + 3, "lse2 ring too shallow to be reused without a release barrier");
 constexpr int kTmemCols = 256;      // two 128-column fp32 accumulators
 constexpr int kMinSmem = 100 * 1024;  // caps residency at 2 CTAs/SM (TMEM: 2 x 256 columns)
 // k bytes that the units of one pass-1 CTA group may hold together (L2 is 126 MB).
@@ -125,6 +133,16 @@ struct Cfg {
   static constexpr int kSteps = kBlocks * 4;                 // 32-byte (K=16 f16 / K=8 tf32) MMA steps
   static constexpr uint32_t kFmt = kOp == Op::F16 ? 0u : kOp == Op::BF16 ? 1u : 2u;
   static_assert(kBlocks >= 1 && D * kElem % 128 == 0, "row must be whole 128-byte blocks");
+  // The streamed operand (K in pass 1, Q in pass 2) goes through ring slots of
+  // kSlotBlocks K-blocks: a whole tile per slot, except for fp32 at D = 128 on
+  // the 3xTF32 path, whose tile (hi + lo: 128 KB) streams one 128-byte K-block
+  // (32 KB) per slot, so that the resident operand and two slots fit in
+  // shared memory.  The MMAs of a tile then run block by block as they land.
+  static constexpr int kSlotBlocks = (kOp == Op::TF32X3 && kBlocks > 2) ? 1 : kBlocks;
+  static constexpr int kSlotsPerTile = kBlocks / kSlotBlocks;
+  static constexpr int kSlotPartBytes = kSlotBlocks * kBlockBytes;  // one component of a slot
+  static constexpr int kSlotBytes = kSlotPartBytes * kParts;
+  static_assert(kBlocks % kSlotBlocks == 0, "slots hold whole K-blocks");
 };
 
 __device__ __forceinline__ uint8_t* align1k(uint8_t* p) {
@@ -136,28 +154,35 @@ __device__ __forceinline__ void exp_bar_sync() {
   asm volatile("bar.sync %0, %1;" ::"n"(kExpBarrier), "n"(kExpThreads) : "memory");
 }
 
-// Issue the MMAs of one 128 x 128 tile: D[tmem] = A[128 x D] * B[128 x D]^T.
+// Issue the MMAs of the K-blocks of one ring slot of a 128 x 128 tile,
+// D[tmem] (+)= A * B^T: A is the resident operand (every K-block, component
+// tiles kTileBytes apart), B the slot holding K-blocks [kb0, kb0 + kSlotBlocks)
+// (components kSlotPartBytes apart).  The tile's first K-step overwrites D.
 template <int D, Op kOp>
-__device__ __forceinline__ void issue_tile_mma(uint32_t d_tmem, uint32_t a_smem, uint32_t b_smem,
+__device__ __forceinline__ void issue_slot_mma(uint32_t d_tmem, uint32_t a_smem, uint32_t b_smem, int kb0,
                                                uint32_t idesc) {
   using C = Cfg<D, kOp>;
 #pragma unroll
-  for (int kk = 0; kk < C::kSteps; ++kk) {
-    const uint32_t koff = (kk >> 2) * C::kBlockBytes + (kk & 3) * 32;
-    if constexpr (kOp == Op::TF32X3) {
-      // the small cross terms first, then hi.hi
-      mma_tf32(d_tmem, sw128_desc(a_smem + C::kTileBytes + koff), sw128_desc(b_smem + koff), idesc,
-               kk > 0 ? 1u : 0u);
-      mma_tf32(d_tmem, sw128_desc(a_smem + koff), sw128_desc(b_smem + C::kTileBytes + koff), idesc, 1u);
-      mma_tf32(d_tmem, sw128_desc(a_smem + koff), sw128_desc(b_smem + koff), idesc, 1u);
-    } else {
-      mma_f16(d_tmem, sw128_desc(a_smem + koff), sw128_desc(b_smem + koff), idesc, kk > 0 ? 1u : 0u);
+  for (int i = 0; i < C::kSlotBlocks; ++i) {
+#pragma unroll
+    for (int k4 = 0; k4 < 4; ++k4) {
+      const uint32_t aoff = (kb0 + i) * C::kBlockBytes + k4 * 32;
+      const uint32_t boff = i * C::kBlockBytes + k4 * 32;
+      const uint32_t acc = (kb0 + i > 0 || k4 > 0) ? 1u : 0u;
+      if constexpr (kOp == Op::TF32X3) {
+        // the small cross terms first, then hi.hi
+        mma_tf32(d_tmem, sw128_desc(a_smem + C::kTileBytes + aoff), sw128_desc(b_smem + boff), idesc, acc);
+        mma_tf32(d_tmem, sw128_desc(a_smem + aoff), sw128_desc(b_smem + C::kSlotPartBytes + boff), idesc, 1u);
+        mma_tf32(d_tmem, sw128_desc(a_smem + aoff), sw128_desc(b_smem + boff), idesc, 1u);
+      } else {
+        mma_f16(d_tmem, sw128_desc(a_smem + aoff), sw128_desc(b_smem + boff), idesc, acc);
+      }
     }
   }
 }
 
-// TMA-load one operand (all its component tiles) of rows [row, row + 128) of
-// head h of batch b into `dst`, completing on `bar`.
+// TMA-load the resident operand (every K-block of all its component tiles)
+// of rows [row, row + 128) of head h of batch b into `dst`, completing on `bar`.
 template <int D, Op kOp>
 __device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* m0, const CUtensorMap* m1,
                                              uint64_t* bar, int row, int h, int b) {
@@ -168,6 +193,20 @@ __device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* m0
     for (int kb = 0; kb < C::kBlocks; ++kb)
       tma_load_4d(dst + part * C::kTileBytes + kb * C::kBlockBytes, part == 0 ? m0 : m1, bar,
                   kb * C::kBlockElems, row, h, b);
+}
+
+// TMA-load ring slot `sb` of a streamed tile: K-blocks [sb * kSlotBlocks, ..)
+// of every component, kSlotBytes in all, completing on `bar`.
+template <int D, Op kOp>
+__device__ __forceinline__ void load_slot(uint8_t* dst, const CUtensorMap* m0, const CUtensorMap* m1,
+                                          uint64_t* bar, int sb, int row, int h, int b) {
+  using C = Cfg<D, kOp>;
+#pragma unroll
+  for (int part = 0; part < C::kParts; ++part)
+#pragma unroll
+    for (int i = 0; i < C::kSlotBlocks; ++i)
+      tma_load_4d(dst + part * C::kSlotPartBytes + i * C::kBlockBytes, part == 0 ? m0 : m1, bar,
+                  (sb * C::kSlotBlocks + i) * C::kBlockElems, row, h, b);
 }
 
 __device__ __forceinline__ void load_half(uint32_t taddr, float (&v)[HALF]) {
@@ -230,43 +269,65 @@ __device__ __forceinline__ float row_sum_exp2(const float (&v)[HALF], float C, f
   return a0.x + a0.y;
 }
 
-// acc += 2^(v[c]*C + nL[c]) over the half row, per-column nL = -lse2 (query
-// columns); with kDiag, columns c < keep_from are masked to 0; with kBits,
-// columns whose bit in `bits` (bit c of word c / 32) is clear are masked to 0.
-template <int kDeg, bool kDiag, bool kBits = false>
-__device__ __forceinline__ float2 col_sum_exp2(const float (&v)[HALF], float C, const float* nL, int keep_from,
-                                               float2 acc, uint2 bits = make_uint2(0xffffffffu, 0xffffffffu)) {
+// ---- pass 2: thread layout and the lse2 order ----
+// A pass-2 exp thread reads its warp's 32 TMEM lanes (keys) x its
+// warpgroup's 64 query columns with two tcgen05.ld.16x256b loads (lanes +0
+// and +16).  Lane l then holds the keys l/4 + {0, 8, 16, 24} of the warp's
+// 32 and, in each 8-column block m of the half, the query columns
+// 8m + 2(l%4) + {0, 1}: 4 keys x 16 columns, in
+//   v[32*ld + 4m + 2*rr + e] = (key l/4 + 16*ld + 8*rr, column 8m + 2(l%4) + e).
+// The 16 columns of lane l need 16 lse2 values, which are stored
+// consecutively (lse_tile_slot), so a thread reads them with 4 shared loads per
+// tile (a 64-column row per thread would need 16).
+
+// Of the 8 column blocks of a pass-2 thread, kEmuGroups / 2 take their exp2
+// from the FMA-pipe polynomial: the same share, kEmuGroups of 16, as pass 1.
+static_assert(kEmuGroups % 2 == 0, "pass 2 emulates whole 8-column blocks");
+__host__ __device__ constexpr bool emu_block(int m) {
+  return ((m + 1) * (kEmuGroups / 2)) / 8 != (m * (kEmuGroups / 2)) / 8;
+}
+
+// acc[i] += 2^(v*C + nL) over one thread's 4 keys (i: key l/4 + 8i) x 16
+// query columns, nL = -lse2 of the columns (16 values in lse_tile_slot order,
+// this thread's at nL[16 * (l%4) ..]).  Masks (a masked element adds 0):
+// kDiag keeps column col >= keep_from + 8i of key i (the causal diagonal tile);
+// kBits keeps column col of key i iff bit col of bits[i] is set (64 bits of
+// the half); kTail keeps columns col < keep_to (a ragged sequence's end).
+template <int kDeg, bool kDiag, bool kBits, bool kTail>
+__device__ __forceinline__ void col_sum4(const float (&v)[HALF], float C, const float* nL, int pc, int keep_from,
+                                         const uint2 (&bits)[4], int keep_to, float2 (&acc)[4]) {
   const float2 C2 = make_float2(C, C);
-  float2 a1 = make_float2(0.f, 0.f);
+  const float4* l4p = reinterpret_cast<const float4*>(nL + pc * 16);
 #pragma unroll
-  for (int g = 0; g < kGroups; ++g) {
-    const int c = 4 * g;
-    const float4 l4 = *reinterpret_cast<const float4*>(nL + c);
-    float2 v0 = make_float2(v[c], v[c + 1]), v1 = make_float2(v[c + 2], v[c + 3]);
-    if (kDiag) {
-      v0.x = (c + 0 >= keep_from) ? v0.x : -INFINITY;
-      v0.y = (c + 1 >= keep_from) ? v0.y : -INFINITY;
-      v1.x = (c + 2 >= keep_from) ? v1.x : -INFINITY;
-      v1.y = (c + 3 >= keep_from) ? v1.y : -INFINITY;
-    }
-    if (kBits) {
-      const uint32_t w = c < 32 ? bits.x : bits.y;
-      v0.x = ((w >> ((c + 0) & 31)) & 1u) ? v0.x : -INFINITY;
-      v0.y = ((w >> ((c + 1) & 31)) & 1u) ? v0.y : -INFINITY;
-      v1.x = ((w >> ((c + 2) & 31)) & 1u) ? v1.x : -INFINITY;
-      v1.y = ((w >> ((c + 3) & 31)) & 1u) ? v1.y : -INFINITY;
-    }
-    const float2 x0 = ffma2(v0, C2, make_float2(l4.x, l4.y));
-    const float2 x1 = ffma2(v1, C2, make_float2(l4.z, l4.w));
-    if (emu_group(g)) {
-      acc = fadd2_ftz(acc, exp2_fma2<kDeg>(x0));
-      a1 = fadd2_ftz(a1, exp2_fma2<kDeg>(x1));
-    } else {
-      acc = fadd2_ftz(acc, make_float2(ex2(x0.x), ex2(x0.y)));
-      a1 = fadd2_ftz(a1, make_float2(ex2(x1.x), ex2(x1.y)));
+  for (int mp = 0; mp < 4; ++mp) {
+    const float4 l4 = l4p[mp];  // -lse2 of blocks 2mp, 2mp + 1
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int m = 2 * mp + h;
+      const float2 L = h ? make_float2(l4.z, l4.w) : make_float2(l4.x, l4.y);
+      const int col = 8 * m + 2 * pc;  // this thread's first column in block m (half-local)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int o = 32 * (i >> 1) + 4 * m + 2 * (i & 1);
+        float2 x = make_float2(v[o], v[o + 1]);
+        if (kDiag) {
+          x.x = col - 8 * i >= keep_from ? x.x : -INFINITY;
+          x.y = col + 1 - 8 * i >= keep_from ? x.y : -INFINITY;
+        }
+        if (kBits) {
+          const uint32_t w = m < 4 ? bits[i].x : bits[i].y;
+          x.x = ((w >> (col & 31)) & 1u) ? x.x : -INFINITY;
+          x.y = ((w >> ((col + 1) & 31)) & 1u) ? x.y : -INFINITY;
+        }
+        if (kTail) {
+          x.x = col < keep_to ? x.x : -INFINITY;
+          x.y = col + 1 < keep_to ? x.y : -INFINITY;
+        }
+        x = ffma2(x, C2, L);
+        acc[i] = fadd2_ftz(acc[i], emu_block(m) ? exp2_fma2<kDeg>(x) : make_float2(ex2(x.x), ex2(x.y)));
+      }
     }
   }
-  return fadd2(acc, a1);
 }
 
 __device__ __forceinline__ float row_max64(const float (&v)[HALF]) {
@@ -303,10 +364,11 @@ __global__ void __launch_bounds__(kThreads, 2)
                   const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tk2, TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1k(smem_raw);
-  constexpr int TB = Cfg<D, kOp>::kOperandBytes;
+  using CF = Cfg<D, kOp>;
+  constexpr int TB = CF::kOperandBytes, SB = CF::kSlotBytes;
   uint8_t* q_tile = smem;
   uint8_t* k_ring = smem + TB;
-  float2* merge = reinterpret_cast<float2*>(smem + TB * (1 + kStages));  // [128] (m, l) of the upper halves
+  float2* merge = reinterpret_cast<float2*>(smem + TB + SB * kStages);  // [128] (m, l) of the upper halves
   uint64_t* bars = reinterpret_cast<uint64_t*>(merge + TILE);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
@@ -375,18 +437,26 @@ __global__ void __launch_bounds__(kThreads, 2)
       prefetch_tmap(&tk);
       mbar_arrive_expect_tx(q_full, TB);
       load_operand<D, kOp>(q_tile, &tq, &tq2, q_full, sv.q_row + r0, h, sv.q_b);
-      int issued = 0;
+      int issued = 0;  // ring slots (kSlotsPerTile per key tile)
       for (int j = 0; j < nkt; ++j) {
-        const int s = j % kStages, n = j / kStages;
-        if (n > 0 && !mbar_wait(&k_empty[s], (n - 1) & 1, abort_flag)) break;
-        mbar_arrive_expect_tx(&k_full[s], TB);
-        load_operand<D, kOp>(k_ring + s * TB, &tk, &tk2, &k_full[s], sv.k_row + j * TILE, g, sv.k_b);
-        issued = j + 1;
+        bool ok = true;
+        for (int sb = 0; sb < CF::kSlotsPerTile; ++sb) {
+          const int qn = j * CF::kSlotsPerTile + sb;
+          const int s = qn % kStages, n = qn / kStages;
+          if (n > 0 && !mbar_wait(&k_empty[s], (n - 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&k_full[s], SB);
+          load_slot<D, kOp>(k_ring + s * SB, &tk, &tk2, &k_full[s], sb, sv.k_row + j * TILE, g, sv.k_b);
+          issued = qn + 1;
+        }
+        if (!ok) break;
       }
       // Do not leave while our copies are in flight.
       mbar_wait(q_full, 0, abort_flag);
-      for (int j = max(0, issued - kStages); j < issued; ++j)
-        mbar_wait(&k_full[j % kStages], (j / kStages) & 1, abort_flag);
+      for (int qn = max(0, issued - kStages); qn < issued; ++qn)
+        mbar_wait(&k_full[qn % kStages], (qn / kStages) & 1, abort_flag);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -395,14 +465,21 @@ __global__ void __launch_bounds__(kThreads, 2)
       int issued = 0;
       if (mbar_wait(q_full, 0, abort_flag)) {
         for (int j = 0; j < nkt; ++j) {
-          const int s = j % kStages, buf = j & 1;
-          if (!mbar_wait(&k_full[s], (j / kStages) & 1, abort_flag)) break;
+          const int buf = j & 1;
           if (j >= 2 && !mbar_wait(&s_empty[buf], ((j >> 1) - 1) & 1, abort_flag)) break;
-          tc_fence_after();
-          issue_tile_mma<D, kOp>(tmem + buf * TILE, qs, ks + s * TB, idesc);
-          mma_commit(&k_empty[s]);
-          mma_commit(&s_full[buf]);
-          issued = j + 1;
+          int done = 0;  // slots of this tile whose MMAs were issued
+          for (; done < CF::kSlotsPerTile; ++done) {
+            const int qn = j * CF::kSlotsPerTile + done, s = qn % kStages;
+            if (!mbar_wait(&k_full[s], (qn / kStages) & 1, abort_flag)) break;
+            tc_fence_after();
+            issue_slot_mma<D, kOp>(tmem + buf * TILE, qs, ks + s * SB, done * CF::kSlotBlocks, idesc);
+            mma_commit(&k_empty[s]);
+          }
+          if (done > 0) {  // (a partial tile only after an abort: committed so that the drain waits for it)
+            mma_commit(&s_full[buf]);
+            issued = j + 1;
+          }
+          if (done < CF::kSlotsPerTile) break;
         }
       }
       if (issued > 0) mbar_wait(&s_full[(issued - 1) & 1], ((issued - 1) >> 1) & 1, abort_flag);
@@ -471,7 +548,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (!dead && a.qmask != nullptr) dead = a.qmask[b * a.qmb + row] == 0;
       // Stored negated (pass 2 adds it): rows that keep no key, and padding
       // rows, get -inf, so 2^(t - lse2) = 0 for them.
-      a.lse[(long long)(hidx) * a.Npad + row] = dead ? -INFINITY : -(m + log2f(l));
+      a.lse[(long long)(hidx) * a.Npad + lse_tile_slot(row)] = dead ? -INFINITY : -(m + log2f(l));
     }
   }
 
@@ -495,12 +572,13 @@ __global__ void __launch_bounds__(kThreads, 2)
                    const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tk2, TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1k(smem_raw);
-  constexpr int TB = Cfg<D, kOp>::kOperandBytes;
+  using CF = Cfg<D, kOp>;
+  constexpr int TB = CF::kOperandBytes, SB = CF::kSlotBytes;
   constexpr int LB = TILE * 4;  // lse2 bytes of one query tile
   uint8_t* k_tile = smem;
   uint8_t* q_ring = smem + TB;
-  float* l_ring = reinterpret_cast<float*>(smem + TB * (1 + kStages));
-  float2* merge = reinterpret_cast<float2*>(smem + TB * (1 + kStages) + LB * kLStages);  // [128]
+  float* l_ring = reinterpret_cast<float*>(smem + TB + SB * kStages);
+  float2* merge = reinterpret_cast<float2*>(smem + TB + SB * kStages + LB * kLStages);  // [128]
   uint64_t* bars = reinterpret_cast<uint64_t*>(merge + TILE);
   uint64_t* k_full = bars;
   uint64_t* q_full = bars + 1;
@@ -508,8 +586,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* s_full = q_empty + kStages;
   uint64_t* s_empty = s_full + 2;
   uint64_t* l_full = s_empty + 2;
-  uint64_t* l_empty = l_full + kLStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(l_empty + kLStages);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(l_full + kLStages);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -560,7 +637,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     for (int t = 0; t < kLStages; ++t) {
       mbar_init(&l_full[t], 1);
-      mbar_init(&l_empty[t], kExpThreads);  // every exp thread done with the tile's lse2
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -580,26 +656,36 @@ __global__ void __launch_bounds__(kThreads, 2)
       prefetch_tmap(&tk);
       mbar_arrive_expect_tx(k_full, TB);
       load_operand<D, kOp>(k_tile, &tk, &tk2, k_full, sv.k_row + c0, g, sv.k_b);
-      int issued = 0;
+      int issued = 0, issued_l = 0;  // Q ring slots (kSlotsPerTile per query tile), lse2 tiles
       for (int j = 0; j < J; ++j) {
-        const int s = j % kStages, n = j / kStages;
-        const int t = j % kLStages, nl = j / kLStages;
-        if (n > 0 && !mbar_wait(&q_empty[s], (n - 1) & 1, abort_flag)) break;
-        if (nl > 0 && !mbar_wait(&l_empty[t], (nl - 1) & 1, abort_flag)) break;
+        const int t = j % kLStages;
         const int hh = j / nqt;
         const int r = rs + (j - hh * nqt) * TILE;
         const int h = g * a.G + hh;
-        mbar_arrive_expect_tx(&q_full[s], TB);
-        load_operand<D, kOp>(q_ring + s * TB, &tq, &tq2, &q_full[s], sv.q_row + r, h, sv.q_b);
-        mbar_arrive_expect_tx(&l_full[t], LB);
-        bulk_load(l_ring + t * TILE, a.lse + (long long)(uu * a.G + hh) * a.Npad + r, LB, &l_full[t]);
-        issued = j + 1;
+        bool ok = true;
+        for (int sb = 0; sb < CF::kSlotsPerTile; ++sb) {
+          const int qn = j * CF::kSlotsPerTile + sb;
+          const int s = qn % kStages, n = qn / kStages;
+          if (n > 0 && !mbar_wait(&q_empty[s], (n - 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&q_full[s], SB);
+          load_slot<D, kOp>(q_ring + s * SB, &tq, &tq2, &q_full[s], sb, sv.q_row + r, h, sv.q_b);
+          issued = qn + 1;
+          if (sb == 0) {
+            mbar_arrive_expect_tx(&l_full[t], LB);
+            bulk_load(l_ring + t * TILE, a.lse + (long long)(uu * a.G + hh) * a.Npad + r, LB, &l_full[t]);
+            issued_l = j + 1;
+          }
+        }
+        if (!ok) break;
       }
       // Do not leave while our copies are in flight.
       mbar_wait(k_full, 0, abort_flag);
-      for (int j = max(0, issued - kStages); j < issued; ++j)
-        mbar_wait(&q_full[j % kStages], (j / kStages) & 1, abort_flag);
-      for (int j = max(0, issued - kLStages); j < issued; ++j)
+      for (int qn = max(0, issued - kStages); qn < issued; ++qn)
+        mbar_wait(&q_full[qn % kStages], (qn / kStages) & 1, abort_flag);
+      for (int j = max(0, issued_l - kLStages); j < issued_l; ++j)
         mbar_wait(&l_full[j % kLStages], (j / kLStages) & 1, abort_flag);
     }
   } else if (warp == 1) {
@@ -609,86 +695,117 @@ __global__ void __launch_bounds__(kThreads, 2)
       int issued = 0;
       if (mbar_wait(k_full, 0, abort_flag)) {
         for (int j = 0; j < J; ++j) {
-          const int s = j % kStages, buf = j & 1;
-          if (!mbar_wait(&q_full[s], (j / kStages) & 1, abort_flag)) break;
+          const int buf = j & 1;
           if (j >= 2 && !mbar_wait(&s_empty[buf], ((j >> 1) - 1) & 1, abort_flag)) break;
-          tc_fence_after();
-          issue_tile_mma<D, kOp>(tmem + buf * TILE, ks, qs + s * TB, idesc);
-          mma_commit(&q_empty[s]);
-          mma_commit(&s_full[buf]);
-          issued = j + 1;
+          int done = 0;  // slots of this tile whose MMAs were issued
+          for (; done < CF::kSlotsPerTile; ++done) {
+            const int qn = j * CF::kSlotsPerTile + done, s = qn % kStages;
+            if (!mbar_wait(&q_full[s], (qn / kStages) & 1, abort_flag)) break;
+            tc_fence_after();
+            issue_slot_mma<D, kOp>(tmem + buf * TILE, ks, qs + s * SB, done * CF::kSlotBlocks, idesc);
+            mma_commit(&q_empty[s]);  // the Q slot is free once these MMAs complete
+          }
+          if (done > 0) {  // (a partial tile only after an abort: committed so that the drain waits for it)
+            mma_commit(&s_full[buf]);
+            issued = j + 1;
+          }
+          if (done < CF::kSlotsPerTile) break;
         }
       }
       if (issued > 0) mbar_wait(&s_full[(issued - 1) & 1], ((issued - 1) >> 1) & 1, abort_flag);
     }
   } else {
-    // exp/sum warps: thread owns key c0 + rl and query columns [hf*64, hf*64 + 64) of each tile.
+    // exp/sum warps: warp w covers keys c0 + 32*(w%4) + [0, 32) and warpgroup hf
+    // the query columns [hf*64, hf*64 + 64) of each tile; lane l holds keys
+    // kr[i] = 32*(w%4) + l/4 + 8i (i < 4) and 16 of the columns (col_sum4).
     const int sub = warp & 3;
     const int hf = (warp - 2) >> 2;
-    const int rl = sub * 32 + lane;
-    const int key = c0 + rl;
+    const int pc = lane & 3;
+    const int kr0 = sub * 32 + (lane >> 2);  // local key of row i: kr0 + 8i
     const uint32_t trow = tmem + ((uint32_t)(sub * 32) << 16) + hf * HALF;
     const float C = a.C;
-    const uint32_t* pcol = kMask == kMaskPairs ? a.pcol + b * a.pb + (long long)key * a.W : nullptr;
     // kRagged: the sequence length is re-read from shared memory per tile
     // rather than held in a register across the loop (register budget).
     __shared__ int s_len;
     if (kRagged && threadIdx.x == 64) s_len = N;
     if (kRagged) exp_bar_sync();
     const volatile int* len_v = &s_len;
-    float2 acc = make_float2(0.f, 0.f);
+    float2 acc[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i] = make_float2(0.f, 0.f);
     for (int j = 0; j < J; ++j) {
       const int buf = j & 1, t = j % kLStages;
-      uint2 pw = make_uint2(0xffffffffu, 0xffffffffu);
-      if (kMask == kMaskPairs) {  // issued before the waits so the load overlaps them
-        const int hq = j / nqt;
-        const int rq = rs + (j - hq * nqt) * TILE;
-        pw = *reinterpret_cast<const uint2*>(pcol + ((rq + hf * HALF) >> 5));
+      const int hh = j / nqt;
+      const int r = rs + (j - hh * nqt) * TILE;
+      uint2 pw[4];
+      if (kMask == kMaskPairs) {  // issued before the waits so the loads overlap them
+        const uint32_t* pcol = a.pcol + b * a.pb + ((r + hf * HALF) >> 5);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          pw[i] = *reinterpret_cast<const uint2*>(pcol + (long long)(c0 + kr0 + 8 * i) * a.W);
       }
       bool ok = mbar_wait(&s_full[buf], (j >> 1) & 1, abort_flag);
       ok = ok && mbar_wait(&l_full[t], (j / kLStages) & 1, abort_flag);  // lse2 bytes landed
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
       float v[HALF];
-      load_half(trow + buf * TILE, v);
+      tmem_ld16x256_x8(trow + buf * TILE, *reinterpret_cast<float(*)[32]>(&v[0]));
+      tmem_ld16x256_x8(trow + (16u << 16) + buf * TILE, *reinterpret_cast<float(*)[32]>(&v[32]));
+      tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(&s_empty[buf]);
 
-      const int hh = j / nqt;
-      const int r = rs + (j - hh * nqt) * TILE;
-      const float* nL = l_ring + t * TILE + hf * HALF;  // -lse2 of this half's 64 query rows
+      const float* nL = l_ring + t * TILE + hf * HALF;  // -lse2 of this half's 64 query rows (lse_tile_slot order)
       constexpr bool kB = kMask == kMaskPairs;
-      // On the diagonal, query r + hf*64 + c keeps key c0 + rl iff hf*64 + c >= rl.
+      constexpr int kDeg = exp2_degree<kOp>();
+      // On the diagonal, query r + hf*64 + col keeps key c0 + kr iff hf*64 + col >= kr.
       // r < c0 (only without causal_skip): every pair is above the diagonal, adds 0.
       // kRagged: query columns at or past the sequence's end contribute 0
       // whatever their scores (their rows may hold another sequence's, or
       // undefined, values).  Otherwise those rows are the TMA's zero fill
       // past N, whose lse2 is -inf.
       if (!a.causal || r >= c0) {
-        if (kRagged) {
-          const int keep_to = *len_v - r - hf * HALF;
-          if (keep_to < HALF) {
-#pragma unroll
-            for (int c = 0; c < HALF; ++c) v[c] = c < keep_to ? v[c] : -INFINITY;
-          }
+        const int keep_from = kr0 - hf * HALF;  // key i keeps columns >= keep_from + 8i
+        const int keep_to = kRagged ? *len_v - r - hf * HALF : HALF;
+        const bool diag = a.causal && r == c0;
+        if (kRagged && keep_to < HALF) {
+          if (diag)
+            col_sum4<kDeg, true, kB, true>(v, C, nL, pc, keep_from, pw, keep_to, acc);
+          else
+            col_sum4<kDeg, false, kB, true>(v, C, nL, pc, keep_from, pw, keep_to, acc);
+        } else if (diag) {
+          col_sum4<kDeg, true, kB, false>(v, C, nL, pc, keep_from, pw, keep_to, acc);
+        } else {
+          col_sum4<kDeg, false, kB, false>(v, C, nL, pc, keep_from, pw, keep_to, acc);  // every pair kept
         }
-        constexpr int kDeg = exp2_degree<kOp>();
-        if (a.causal && r == c0)
-          acc = col_sum_exp2<kDeg, true, kB>(v, C, nL, rl - hf * HALF, acc, pw);
-        else
-          acc = col_sum_exp2<kDeg, false, kB>(v, C, nL, 0, acc, pw);  // every pair kept
       }
-      mbar_arrive(&l_empty[t]);
     }
-    // Merge the two query halves of each key (fixed order: lower half first).
-    if (hf == 1) merge[rl] = acc;
+    // Per key: the thread's 16 columns, then the 4 lanes holding the key's
+    // other columns (xor 1, 2), then the two query halves (lower half first).
+    float tot[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      tot[i] = acc[i].x + acc[i].y;
+      tot[i] += __shfl_xor_sync(0xffffffffu, tot[i], 1);
+      tot[i] += __shfl_xor_sync(0xffffffffu, tot[i], 2);
+    }
+    float* mergef = reinterpret_cast<float*>(merge);
+    if (hf == 1 && pc == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) mergef[kr0 + 8 * i] = tot[i];
+    }
     exp_bar_sync();
-    if (hf == 0 && key < a.N) {
-      const float2 o = merge[rl];
-      float total = (acc.x + acc.y) + (o.x + o.y);
-      if (kRagged && key >= *len_v) total = 0.f;  // past the sequence's end
-      else if (kMask == kMaskKeys && a.kmask[b * a.kmb + key] == 0) total = 0.f;
-      a.part[((long long)uu * a.nchunk + y) * a.N + key] = total;
+    if (hf == 0 && pc == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int key = c0 + kr0 + 8 * i;
+        if (key < a.N) {
+          float total = tot[i] + mergef[kr0 + 8 * i];
+          if (kRagged && key >= *len_v) total = 0.f;  // past the sequence's end
+          else if (kMask == kMaskKeys && a.kmask[b * a.kmb + key] == 0) total = 0.f;
+          a.part[((long long)uu * a.nchunk + y) * a.N + key] = total;
+        }
+      }
     }
   }
 
@@ -926,12 +1043,13 @@ constexpr size_t kBarBytes = 8 * (1 + 2 * kStages + 4) + 16;  // mbarriers + TME
 
 template <int D, Op kOp>
 constexpr size_t smem_lse() {
-  return 1024 + (size_t)Cfg<D, kOp>::kOperandBytes * (1 + kStages) + TILE * 8 + kBarBytes;
+  return 1024 + (size_t)Cfg<D, kOp>::kOperandBytes + (size_t)Cfg<D, kOp>::kSlotBytes * kStages + TILE * 8 +
+         kBarBytes;
 }
 template <int D, Op kOp>
 constexpr size_t smem_mass() {
-  return 1024 + (size_t)Cfg<D, kOp>::kOperandBytes * (1 + kStages) + TILE * 4 * kLStages + TILE * 8 + kBarBytes +
-         16 * kLStages;
+  return 1024 + (size_t)Cfg<D, kOp>::kOperandBytes + (size_t)Cfg<D, kOp>::kSlotBytes * kStages +
+         TILE * 4 * kLStages + TILE * 8 + kBarBytes + 8 * kLStages;
 }
 
 template <int D, Op kOp, int kMask, bool kRagged>
@@ -1163,6 +1281,7 @@ int launch_tc(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws
   if (L.path == 2) {  // fp32 inputs on tf32 tensor cores (3 MMAs per step)
     if (p->D <= 32) return launch_km<32, Op::TF32X3>(p, L, ws, s, o);
     if (p->D <= 64) return launch_km<64, Op::TF32X3>(p, L, ws, s, o);
+    if (p->D <= 128) return launch_km<128, Op::TF32X3>(p, L, ws, s, o);  // K-block slots (Cfg::kSlotBlocks)
     return KVBM_ERR_HEAD_DIM;
   }
   // Head dims run on the next whole number of 128-byte blocks (64 bf16/fp16

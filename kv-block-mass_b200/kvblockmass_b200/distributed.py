@@ -105,16 +105,25 @@ def block_mass_sharded(shards, causal=False, block_size=64, scale=None, causal_s
     if local_fn is None:
         from .ops import block_mass_b200 as local_fn  # noqa: N813
     acc = None
+    out_dtype = torch.float32
     for sh in shards:
         kw = {k: v for k, v in sh.items() if k not in ("q", "k") and v is not None}
         m = local_fn(sh["q"], sh["k"], causal=causal, block_size=block_size, scale=scale,
                      causal_skip=causal_skip, **kw)
+        if m.dtype == torch.float64:  # fp64 inputs give an fp64 mass (reference.py:77)
+            out_dtype = torch.float64
         acc = m.to(torch.float64) if acc is None else acc + m.to(torch.float64)
     if acc is None:  # a rank without units still takes part in the collective
+        if device is None and dist.get_backend(group) == "nccl":
+            device = torch.device("cuda", torch.cuda.current_device())  # NCCL needs a CUDA tensor
         acc = torch.zeros(num_blocks, dtype=torch.float64, device=device)
     if acc.numel() != num_blocks:
         raise ValueError(f"local mass has {acc.numel()} buckets, expected {num_blocks}")
-    out_dtype = torch.float32
+    # The result dtype must agree across ranks; a rank without units cannot
+    # see the inputs' dtype, so it follows the others'.
+    flag = torch.tensor([1.0 if out_dtype == torch.float64 else 0.0], dtype=torch.float64, device=acc.device)
+    dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=group)
+    out_dtype = torch.float64 if float(flag.item()) > 0 else torch.float32
     if deterministic:
         world = dist.get_world_size(group)
         parts = [torch.empty_like(acc) for _ in range(world)]

@@ -76,6 +76,8 @@ def _worker(rank, world, port, mode, out_path):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
     q, k, km, qm = _inputs()
+    if mode == "empty":  # one unit for two ranks: rank 1 has nothing to compute
+        q, k, km, qm = q[:1, :2], k[:1, :1], km[:1], qm[:1]
     nb = (q.shape[2] + 31) // 32
     try:
         if mode == "fail" and rank == 1:
@@ -83,7 +85,7 @@ def _worker(rank, world, port, mode, out_path):
         shards = shard_inputs(q, k, rank, world, attn_mask=km, query_mask=qm)
         res = block_mass_sharded(shards, causal=True, block_size=32, num_blocks=nb,
                                  local_fn=_oracle_fn, deterministic=(mode == "det"),
-                                 all_ranks=(mode == "all"))
+                                 all_ranks=(mode in ("all", "empty")))
         torch.save({"rank": rank, "mass": res}, f"{out_path}.{rank}")
     except Exception as e:  # noqa: BLE001 - the test inspects the error text
         torch.save({"rank": rank, "error": f"{type(e).__name__}: {e}"}, f"{out_path}.{rank}")
@@ -131,3 +133,18 @@ def test_rank_failure_surfaces_as_error(tmp_path):
     res = _run("fail", tmp_path)
     assert "injected rank failure" in res[1]["error"]
     assert "error" in res[0], "rank 0 should see the missing peer as an error"
+
+
+def test_rank_without_units_joins_the_collective(tmp_path):
+    """More ranks than units: the empty rank contributes zeros, and every rank
+    gets the float64 result that float64 inputs give (reference.py:77)."""
+    from oracle.block_mass_np import block_mass_stream
+
+    res = _run("empty", tmp_path)
+    q, k, km, qm = _inputs()
+    want = block_mass_stream(q[:1, :2].numpy(), k[:1, :1].numpy(), attn_mask=km[:1].numpy(),
+                             query_mask=qm[:1].numpy(), causal=True, block_size=32)
+    for r in res:
+        assert "mass" in r, r.get("error")
+        assert r["mass"].dtype == torch.float64
+        np.testing.assert_allclose(r["mass"].numpy(), want, rtol=1e-12, atol=1e-12)

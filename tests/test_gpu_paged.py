@@ -46,7 +46,8 @@ def _qk(B, Hq, Hkv, N, D, dtype, seed, device):
 
 @pytest.mark.parametrize("dtype,D,path", [
     (torch.bfloat16, 128, 1), (torch.float16, 64, 1), (torch.float32, 64, 2),
-    (torch.float64, 64, 0), (torch.bfloat16, 80, 1), (torch.bfloat16, 84, 0), (torch.float32, 128, 0),
+    (torch.float64, 64, 0), (torch.bfloat16, 80, 1), (torch.bfloat16, 84, 0), (torch.float32, 128, 2),
+    (torch.float32, 160, 0),
 ])
 @pytest.mark.parametrize("page_size", [16, 128, 7])
 def test_paged_bits_equal_dense(cuda_device, dtype, D, path, page_size):

@@ -314,7 +314,8 @@ def test_llama3_70b_prefix_vs_oracle(cuda_device):
 @pytest.mark.parametrize("shape,dtype", [((1, 32, 8, 3000, 128), torch.bfloat16),
                                          ((3, 8, 2, 777, 64), torch.bfloat16),
                                          ((2, 8, 2, 900, 64), torch.float32),    # 3xTF32: per-piece tf32 split
-                                         ((2, 4, 4, 500, 96), torch.float32)])   # SIMT
+                                         ((2, 4, 4, 500, 96), torch.float32),    # 3xTF32, K-block slots
+                                         ((2, 4, 2, 400, 160), torch.float32)])  # SIMT
 def test_host_inputs_give_the_device_call_bits(cuda_device, shape, dtype, pinned):
     """Host q/k with device='cuda' are copied piece by piece (q-head 0 of unit 0,
     its other heads, then unit by unit) while earlier pieces compute, as staged
@@ -360,7 +361,7 @@ def test_host_inputs_with_pair_masks(cuda_device, mask_kind):
 
 
 @pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.float32, 64), (torch.float32, 96),
-                                     (torch.float64, 32)])
+                                     (torch.float32, 160), (torch.float64, 32)])
 @pytest.mark.parametrize("mask", ["none", "pairs"])
 def test_staged_pieces_on_two_streams(cuda_device, dtype, D, mask):
     """kvbm_options.stages / run ranges through the C ABI: pass 1 per (unit,
@@ -477,6 +478,7 @@ def test_wide_heads_on_tensor_cores(cuda_device, dtype, D):
     (torch.bfloat16, 8, 1), (torch.bfloat16, 40, 1), (torch.float16, 80, 1), (torch.bfloat16, 96, 1),
     (torch.bfloat16, 112, 1), (torch.float16, 160, 1), (torch.bfloat16, 224, 1),
     (torch.float32, 4, 2), (torch.float32, 12, 2), (torch.float32, 48, 2), (torch.float32, 60, 2),
+    (torch.float32, 100, 2), (torch.float32, 128, 2), (torch.float32, 132, 0),
 ])
 def test_padded_head_dims_on_tensor_cores(cuda_device, dtype, D, path):
     """Head dims between the kernels' 64/128/192/256 (and 32/64 for fp32) run the
@@ -506,3 +508,38 @@ def test_head_dim_view_reads_no_padding(cuda_device):
     a = run(qv, kv, causal=True, block_size=64)
     b = run(qv.contiguous(), kv.contiguous(), causal=True, block_size=64)
     assert torch.isfinite(a).all() and torch.equal(a, b)
+
+
+@pytest.mark.parametrize("mask", [None, "keys", "pairs"])
+def test_fp32_d128_on_tensor_cores(cuda_device, mask):
+    """fp32 at D = 128 runs the 3xTF32 tensor-core kernels (kernel path 2), the
+    streamed operand one 128-byte K-block per ring slot: parity at the fp32
+    tolerance with the oracle and with the reference's own fp32 golden
+    (small case d128_n257), causal_skip on/off with the same bits."""
+    g = torch.Generator().manual_seed(128)
+    B, Hq, Hkv, N, D = 2, 8, 2, 1500, 128
+    q = torch.randn(B, Hq, N, D, generator=g)
+    k = torch.randn(B, Hkv, N, D, generator=g)
+    qd, kd = q.to(cuda_device), k.to(cuda_device)
+    assert kb.kernel_path(kb.make_problem(qd, kd, causal=True)) == 2
+    m = None
+    if mask == "keys":
+        m = torch.rand(N, generator=g) > 0.2
+    elif mask == "pairs":
+        m = torch.rand(N, N, generator=g) > 0.3
+    md = None if m is None else m.to(cuda_device)
+    for causal in (True, False):
+        got = run(qd, kd, attn_mask=md, causal=causal, block_size=64)
+        want = oracle_for(q, k, attn_mask=m, causal=causal, block_size=64)
+        assert max_rel(got.cpu().numpy(), want) < 2e-5, causal
+    a = run(qd, kd, attn_mask=md, causal=True, block_size=64)
+    assert torch.equal(a, run(qd, kd, attn_mask=md, causal=True, block_size=64, causal_skip=False))
+
+
+def test_fp32_d128_reference_golden(cuda_device, small_cases):
+    c = next(x for x in small_cases if x["name"] == "d128_n257")
+    q, k, mask = case_inputs(c)
+    qd, kd = q.float().to(cuda_device), k.float().to(cuda_device)
+    assert kb.kernel_path(kb.make_problem(qd, kd, causal=True)) == 2
+    got = run(qd, kd, causal=c["causal"], block_size=c["block_size"])
+    assert max_rel(got.cpu().numpy(), c["mass_ref_fp32"]) < 2e-5

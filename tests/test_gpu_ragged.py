@@ -54,7 +54,7 @@ LENS = [1000, 333, 128, 1, 0, 777]
 
 @pytest.mark.parametrize("dtype,D,path", [
     (torch.bfloat16, 128, 1), (torch.float16, 64, 1), (torch.float32, 64, 2),
-    (torch.float64, 64, 0), (torch.bfloat16, 80, 1), (torch.bfloat16, 84, 0),
+    (torch.float64, 64, 0), (torch.bfloat16, 80, 1), (torch.bfloat16, 84, 0), (torch.float32, 128, 2),
 ])
 @pytest.mark.parametrize("causal", [True, False])
 def test_ragged_padded_and_packed_vs_oracle(cuda_device, dtype, D, path, causal):

@@ -69,8 +69,8 @@ CASES = [
     # tcgen05 path: bf16, D=128, causal, ragged N
     (dict(B=1, Hq=8, Hkv=2, N=3000, D=128, dtype=torch.bfloat16, seed=11),
      dict(causal=True, block_size=64), None, 1),
-    # SIMT path: fp32 with D=96 (the 3xTF32 path takes D <= 64), key mask, non-causal
-    (dict(B=2, Hq=4, Hkv=2, N=777, D=96, dtype=torch.float32, seed=12),
+    # SIMT path: fp32 with D=160 (the 3xTF32 path takes D <= 128), key mask, non-causal
+    (dict(B=2, Hq=4, Hkv=2, N=777, D=160, dtype=torch.float32, seed=12),
      dict(causal=False, block_size=48), "keys", 0),
     # 3xTF32 path: fp32 with D=64, its tf32 copies of q/k in the scratch array
     (dict(B=1, Hq=4, Hkv=1, N=1000, D=64, dtype=torch.float32, seed=13),
