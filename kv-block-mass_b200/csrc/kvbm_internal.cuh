@@ -32,12 +32,20 @@ constexpr int kMaxQueryChunks = 64;
 // below 2^21, the width of a work-item field, and padded lengths fit int.
 constexpr int kMaxN = 1 << 28;
 
+// Exp/sum warpgroups of the tensor-core kernels (kvbm_tc.cu) and the columns
+// of a 128-column accumulator tile each exp thread covers.
+#ifndef KVBM_EXP_WG
+#define KVBM_EXP_WG 2
+#endif
+constexpr int kTcExpCols = kTcTile / KVBM_EXP_WG;
+
 // Stored position of row r in the tensor-core paths' lse2 array: inside each
-// 64-row half of a 128-row tile, row 8m + 2p + e goes to p*16 + 2m + e, so
-// that the 16 query rows one pass-2 thread reads are consecutive (kvbm_tc.cu).
+// kTcExpCols-row group of a 128-row tile, row 8m + 2p + e goes to
+// p * (kTcExpCols / 4) + 2m + e, so that the query rows one pass-2 thread
+// reads (p = lane % 4) are consecutive (kvbm_tc.cu).
 __host__ __device__ inline int lse_tile_slot(int r) {
-  const int i = r & 63;
-  return (r & ~63) | (((i >> 1) & 3) << 4) | ((i >> 3) << 1) | (i & 1);
+  const int i = r & (kTcExpCols - 1);
+  return (r & ~(kTcExpCols - 1)) | (((i >> 1) & 3) * (kTcExpCols / 4)) | ((i >> 3) << 1) | (i & 1);
 }
 
 // Where each array lives inside the caller's workspace.

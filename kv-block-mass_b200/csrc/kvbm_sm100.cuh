@@ -97,6 +97,12 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy reads of them (an MMA operand written by threads).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -187,6 +193,20 @@ __device__ __forceinline__ void tmem_ld16x256_x8(uint32_t taddr, float (&v)[32])
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// tmem_ld16x256_x8 over 4 blocks of 8 columns: v[4m .. 4m+3], m < 4.
+__device__ __forceinline__ void tmem_ld16x256_x4(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x4.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor for a K-major operand stored in the
@@ -199,6 +219,16 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
          | ((uint64_t)(1024 >> 4) << 32)        // stride byte offset: next 8-row group
          | ((uint64_t)1 << 46)                  // descriptor version (sm_100)
          | ((uint64_t)2 << 61);                 // swizzle mode: 128-byte
+}
+
+// Shared-memory matrix descriptor for a K-major operand of one 16-element
+// (32-byte) K step stored without swizzle: 8-row x 16-byte core matrices,
+// the two K halves 128 bytes apart, 8-row groups 256 bytes apart.
+__device__ __forceinline__ uint64_t k16_interleaved_desc(uint32_t addr) {
+  return (uint64_t)((addr & 0x3FFFFu) >> 4)  // start address
+         | ((uint64_t)(128 >> 4) << 16)        // leading byte offset: the second K half
+         | ((uint64_t)(256 >> 4) << 32)        // stride byte offset: next 8-row group
+         | ((uint64_t)1 << 46);                // descriptor version (sm_100); swizzle: none
 }
 
 // Instruction descriptor, kind::f16 / kind::tf32: fp32 accumulate, A and B of

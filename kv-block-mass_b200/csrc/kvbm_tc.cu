@@ -23,6 +23,7 @@
 // per (unit, query chunk, key) goes to the workspace; the SIMT reduce
 // (kvbm_simt.cu) adds them in a fixed order.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <math.h>
 
@@ -38,9 +39,13 @@ namespace {
 using namespace sm100;
 
 constexpr int TILE = kTcTile;       // 128
-constexpr int HALF = TILE / 2;      // columns per exp warpgroup
-constexpr int kExpThreads = 256;    // two warpgroups
+// The exp/sum warps form kExpWG warpgroups; warpgroup w covers the columns
+// [w * COLS, (w + 1) * COLS) of every accumulator tile.
+constexpr int kExpWG = KVBM_EXP_WG;
+constexpr int COLS = kTcExpCols;    // columns per exp thread and tile
+constexpr int kExpThreads = 128 * kExpWG;
 constexpr int kThreads = 64 + kExpThreads;  // + TMA warp + MMA warp
+static_assert(COLS == TILE / kExpWG && COLS % 32 == 0, "exp warpgroups split a tile's columns evenly");
 #ifndef KVBM_STAGES
 #define KVBM_STAGES 2
 #endif
@@ -54,6 +59,14 @@ constexpr int kStages = KVBM_STAGES;  // K (pass 1) / Q (pass 2) ring depth
 // slot's previous tile when kLStages >= kStages + 3.
 constexpr int kLStages = 8;
 static_assert(kLStages >= kStages + 3, "lse2 ring too shallow to be reused without a release barrier");
+// Pass 2 folds -lse2 into the accumulator (KVBM_P2_BIAS, bf16/fp16 inputs):
+// after a tile's K steps, one more 16-element K step adds ones (key side) x
+// the bf16 split hi + mid + lo of -lse2 / C (query side), so the exp threads
+// compute 2^(C * D) with no per-column lse2 load.
+#ifndef KVBM_P2_BIAS
+#define KVBM_P2_BIAS 1
+#endif
+constexpr int kBiasBytes = TILE * 32;  // a 128-row x 16-element bf16 operand
 constexpr int kTmemCols = 256;      // two 128-column fp32 accumulators
 constexpr int kMinSmem = 100 * 1024;  // caps residency at 2 CTAs/SM (TMEM: 2 x 256 columns)
 // k bytes that the units of one pass-1 CTA group may hold together (L2 is 126 MB).
@@ -61,7 +74,7 @@ constexpr int kMinSmem = 100 * 1024;  // caps residency at 2 CTAs/SM (TMEM: 2 x 
 #define KVBM_P1_GROUP_MIB 32
 #endif
 constexpr long long kPass1GroupBytes = (long long)KVBM_P1_GROUP_MIB << 20;
-constexpr int kExpBarrier = 1;      // named barrier of the 256 exp threads
+constexpr int kExpBarrier = 1;      // named barrier of the exp threads
 
 struct TcArgs {
   int N, Npad, G, Hkv, ub;
@@ -209,17 +222,18 @@ __device__ __forceinline__ void load_slot(uint8_t* dst, const CUtensorMap* m0, c
                   (sb * C::kSlotBlocks + i) * C::kBlockElems, row, h, b);
 }
 
-__device__ __forceinline__ void load_half(uint32_t taddr, float (&v)[HALF]) {
-  tmem_ld32(taddr + 0, *reinterpret_cast<float(*)[32]>(&v[0]));
-  tmem_ld32(taddr + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+// One exp thread's COLS consecutive accumulator columns of its TMEM lane.
+__device__ __forceinline__ void load_cols(uint32_t taddr, float (&v)[COLS]) {
+#pragma unroll
+  for (int i = 0; i < COLS / 32; ++i) tmem_ld32(taddr + 32 * i, *reinterpret_cast<float(*)[32]>(&v[32 * i]));
   tmem_ld_wait();
 }
 
-// Of the 16 four-column groups of a half row, kEmuGroups take their exp2 from
-// the FMA-pipe polynomial (exp2_fma2) and the rest from MUFU ex2.approx: one
-// ex2 per score element is the binding unit of both passes, and the FMA pipe
-// has room to absorb part of it.  The groups are spread evenly so that the
-// scheduler can interleave both kinds.
+// Of every 16 four-column groups of a row, KVBM_EMU_GROUPS take their exp2
+// from the FMA-pipe polynomial (exp2_fma2) and the rest from MUFU
+// ex2.approx: one ex2 per score element is the binding unit of both passes,
+// and the FMA pipe has room to absorb part of it.  The groups are spread
+// evenly so that the scheduler can interleave both kinds.
 // 4 of 16 groups, degree-4 polynomial: on the Llama-3-8B N=32768 step a
 // sweep of 2-6 groups x degree 3/4 gave 10.05 ms for this choice against
 // 10.1-10.2 ms for 2 groups.  Degree 3 (max relative error 7.5e-5) was about
@@ -234,9 +248,11 @@ __device__ __forceinline__ void load_half(uint32_t taddr, float (&v)[HALF]) {
 #ifndef KVBM_EXP2_DEGREE
 #define KVBM_EXP2_DEGREE 4
 #endif
-constexpr int kGroups = HALF / 4;
-constexpr int kEmuGroups = KVBM_EMU_GROUPS;
-static_assert(kEmuGroups >= 0 && kEmuGroups <= kGroups, "emulated groups out of range");
+constexpr int kEmuPer16 = KVBM_EMU_GROUPS;
+constexpr int kGroups = COLS / 4;                     // four-column groups of one thread's row
+constexpr int kEmuGroups = kEmuPer16 * kGroups / 16;  // of them on the FMA pipe
+static_assert(kEmuPer16 >= 0 && kEmuPer16 <= 16 && kEmuPer16 * kGroups % 16 == 0,
+              "the emulated share must be whole groups of a thread's columns");
 
 __host__ __device__ constexpr bool emu_group(int g) {
   return ((g + 1) * kEmuGroups) / kGroups != (g * kEmuGroups) / kGroups;  // Bresenham spread
@@ -247,9 +263,9 @@ constexpr int exp2_degree() {
   return kOp == Op::TF32X3 ? 4 : KVBM_EXP2_DEGREE;
 }
 
-// Sum over the half row of 2^(v*C + nm), nm = -(running max); masked entries hold -inf.
+// Sum over the thread's columns of 2^(v*C + nm), nm = -(running max); masked entries hold -inf.
 template <int kDeg>
-__device__ __forceinline__ float row_sum_exp2(const float (&v)[HALF], float C, float nm) {
+__device__ __forceinline__ float row_sum_exp2(const float (&v)[COLS], float C, float nm) {
   const float2 C2 = make_float2(C, C), N2 = make_float2(nm, nm);
   float2 a0 = make_float2(0.f, 0.f), a1 = a0;
 #pragma unroll
@@ -271,44 +287,48 @@ __device__ __forceinline__ float row_sum_exp2(const float (&v)[HALF], float C, f
 
 // ---- pass 2: thread layout and the lse2 order ----
 // A pass-2 exp thread reads its warp's 32 TMEM lanes (keys) x its
-// warpgroup's 64 query columns with two tcgen05.ld.16x256b loads (lanes +0
-// and +16).  Lane l then holds the keys l/4 + {0, 8, 16, 24} of the warp's
-// 32 and, in each 8-column block m of the half, the query columns
-// 8m + 2(l%4) + {0, 1}: 4 keys x 16 columns, in
-//   v[32*ld + 4m + 2*rr + e] = (key l/4 + 16*ld + 8*rr, column 8m + 2(l%4) + e).
-// The 16 columns of lane l need 16 lse2 values, which are stored
-// consecutively (lse_tile_slot), so a thread reads them with 4 shared loads per
-// tile (a 64-column row per thread would need 16).
+// warpgroup's COLS query columns with two tcgen05.ld.16x256b loads (lanes +0
+// and +16), each covering kBlk = COLS / 8 blocks of 8 columns.  Lane l then
+// holds the keys l/4 + {0, 8, 16, 24} of the warp's 32 and, in each block m,
+// the query columns 8m + 2(l%4) + {0, 1}: 4 keys x 2*kBlk columns, in
+//   v[(COLS/2)*ld + 4m + 2*rr + e] = (key l/4 + 16*ld + 8*rr, column 8m + 2(l%4) + e).
+// The 2*kBlk columns of lane l need as many lse2 values, which are stored
+// consecutively (lse_tile_slot), so a thread reads them with kBlk/2 shared
+// loads per tile (a full row of COLS columns per thread would need COLS/4).
+constexpr int kBlk = COLS / 8;
 
-// Of the 8 column blocks of a pass-2 thread, kEmuGroups / 2 take their exp2
-// from the FMA-pipe polynomial: the same share, kEmuGroups of 16, as pass 1.
-static_assert(kEmuGroups % 2 == 0, "pass 2 emulates whole 8-column blocks");
+// Of the kBlk column blocks of a pass-2 thread, KVBM_EMU_GROUPS/16 of them
+// take their exp2 from the FMA-pipe polynomial: the same share as pass 1.
+constexpr int kEmuBlocks = kEmuPer16 * kBlk / 16;
+static_assert(kEmuPer16 * kBlk % 16 == 0, "pass 2 emulates whole 8-column blocks");
 __host__ __device__ constexpr bool emu_block(int m) {
-  return ((m + 1) * (kEmuGroups / 2)) / 8 != (m * (kEmuGroups / 2)) / 8;
+  return ((m + 1) * kEmuBlocks) / kBlk != (m * kEmuBlocks) / kBlk;
 }
 
-// acc[i] += 2^(v*C + nL) over one thread's 4 keys (i: key l/4 + 8i) x 16
-// query columns, nL = -lse2 of the columns (16 values in lse_tile_slot order,
-// this thread's at nL[16 * (l%4) ..]).  Masks (a masked element adds 0):
-// kDiag keeps column col >= keep_from + 8i of key i (the causal diagonal tile);
-// kBits keeps column col of key i iff bit col of bits[i] is set (64 bits of
-// the half); kTail keeps columns col < keep_to (a ragged sequence's end).
-template <int kDeg, bool kDiag, bool kBits, bool kTail>
-__device__ __forceinline__ void col_sum4(const float (&v)[HALF], float C, const float* nL, int pc, int keep_from,
+// acc[i] += 2^(v*C + nL) over one thread's 4 keys (i: key l/4 + 8i) x 2*kBlk
+// query columns, nL = -lse2 of the columns (lse_tile_slot order, this
+// thread's 2*kBlk values at nL[2*kBlk * (l%4) ..]).  Masks (a masked element
+// adds 0): kDiag keeps column col >= keep_from + 8i of key i (the causal
+// diagonal tile); kBits keeps column col of key i iff bit col of bits[i] is
+// set (the thread's COLS columns); kTail keeps columns col < keep_to (a
+// ragged sequence's end).
+// kBias: the accumulator already holds s - lse2 / C (no nL reads).
+template <int kDeg, bool kDiag, bool kBits, bool kTail, bool kBias = false>
+__device__ __forceinline__ void col_sum4(const float (&v)[COLS], float C, const float* nL, int pc, int keep_from,
                                          const uint2 (&bits)[4], int keep_to, float2 (&acc)[4]) {
   const float2 C2 = make_float2(C, C);
-  const float4* l4p = reinterpret_cast<const float4*>(nL + pc * 16);
+  const float4* l4p = reinterpret_cast<const float4*>(nL + pc * 2 * kBlk);
 #pragma unroll
-  for (int mp = 0; mp < 4; ++mp) {
-    const float4 l4 = l4p[mp];  // -lse2 of blocks 2mp, 2mp + 1
+  for (int mp = 0; mp < kBlk / 2; ++mp) {
+    const float4 l4 = kBias ? make_float4(0.f, 0.f, 0.f, 0.f) : l4p[mp];  // -lse2 of blocks 2mp, 2mp + 1
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int m = 2 * mp + h;
       const float2 L = h ? make_float2(l4.z, l4.w) : make_float2(l4.x, l4.y);
-      const int col = 8 * m + 2 * pc;  // this thread's first column in block m (half-local)
+      const int col = 8 * m + 2 * pc;  // this thread's first column in block m (warpgroup-local)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int o = 32 * (i >> 1) + 4 * m + 2 * (i & 1);
+        const int o = (COLS / 2) * (i >> 1) + 4 * m + 2 * (i & 1);
         float2 x = make_float2(v[o], v[o + 1]);
         if (kDiag) {
           x.x = col - 8 * i >= keep_from ? x.x : -INFINITY;
@@ -330,12 +350,27 @@ __device__ __forceinline__ void col_sum4(const float (&v)[HALF], float C, const 
   }
 }
 
-__device__ __forceinline__ float row_max64(const float (&v)[HALF]) {
+// A pass-2 thread's 4 keys x 2*kBlk columns: lanes +0..15, then +16..31.
+__device__ __forceinline__ void load_keys16(uint32_t taddr, float (&v)[COLS]) {
+#pragma unroll
+  for (int ld = 0; ld < 2; ++ld) {
+    const uint32_t t = taddr + ((uint32_t)(16 * ld) << 16);
+    if constexpr (COLS == 64)
+      tmem_ld16x256_x8(t, *reinterpret_cast<float(*)[32]>(&v[32 * ld]));
+    else
+      tmem_ld16x256_x4(t, *reinterpret_cast<float(*)[16]>(&v[16 * ld]));
+  }
+  tmem_ld_wait();
+}
+static_assert(COLS == 64 || COLS == 32, "pass-2 loads cover 32 or 64 columns");
+
+// Max of a thread's COLS columns (3-input max tree).
+__device__ __forceinline__ float row_max(const float (&v)[COLS]) {
   float m[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) m[i] = fmaxf(v[i], v[i + 8]);
 #pragma unroll
-  for (int c = 16; c < HALF; c += 16)
+  for (int c = 16; c < COLS; c += 16)
 #pragma unroll
     for (int i = 0; i < 8; i += 2) {
       m[i] = fmax3(m[i], v[c + i], v[c + i + 8]);
@@ -368,8 +403,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   constexpr int TB = CF::kOperandBytes, SB = CF::kSlotBytes;
   uint8_t* q_tile = smem;
   uint8_t* k_ring = smem + TB;
-  float2* merge = reinterpret_cast<float2*>(smem + TB + SB * kStages);  // [128] (m, l) of the upper halves
-  uint64_t* bars = reinterpret_cast<uint64_t*>(merge + TILE);
+  float2* merge = reinterpret_cast<float2*>(smem + TB + SB * kStages);  // [kExpWG - 1][128] (m, l) of parts 1..
+  uint64_t* bars = reinterpret_cast<uint64_t*>(merge + (kExpWG - 1) * TILE);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = k_full + kStages;
@@ -485,48 +520,51 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (issued > 0) mbar_wait(&s_full[(issued - 1) & 1], ((issued - 1) >> 1) & 1, abort_flag);
     }
   } else {
-    // exp/sum warps: thread owns query row r0 + rl, columns [hf*64, hf*64 + 64) of each tile.
+    // exp/sum warps: thread owns query row r0 + rl, columns [wg*COLS, (wg + 1)*COLS) of each tile.
     const int sub = warp & 3;
-    const int hf = (warp - 2) >> 2;
+    const int wg = (warp - 2) >> 2;
     const int rl = sub * 32 + lane;
     const int row = r0 + rl;
-    const uint32_t trow = tmem + ((uint32_t)(sub * 32) << 16) + hf * HALF;
+    const uint32_t trow = tmem + ((uint32_t)(sub * 32) << 16) + wg * COLS;
     const uint8_t* kmask = kMask == kMaskKeys ? a.kmask + b * a.kmb : nullptr;
     const uint32_t* prow = kMask == kMaskPairs ? a.prow + b * a.pb + (long long)row * a.W : nullptr;
     float m = -INFINITY, l = 0.f;
     for (int j = 0; j < nkt; ++j) {
       const int buf = j & 1;
-      uint2 pw = make_uint2(0xffffffffu, 0xffffffffu);
-      if (kMask == kMaskPairs)  // issued before the wait so the load overlaps it
-        pw = *reinterpret_cast<const uint2*>(prow + ((j * TILE + hf * HALF) >> 5));
+      uint32_t kw[COLS / 32];
+#pragma unroll
+      for (int w = 0; w < COLS / 32; ++w) kw[w] = 0xffffffffu;
+      if (kMask == kMaskPairs) {  // issued before the wait so the load overlaps it
+#pragma unroll
+        for (int w = 0; w < COLS / 32; ++w) kw[w] = prow[((j * TILE + wg * COLS) >> 5) + w];
+      }
       const bool ok = mbar_wait(&s_full[buf], (j >> 1) & 1, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      float v[HALF];
-      load_half(trow + buf * TILE, v);
+      float v[COLS];
+      load_cols(trow + buf * TILE, v);
       tc_fence_before();
       mbar_arrive(&s_empty[buf]);
 
-      const int c0 = j * TILE + hf * HALF;  // first key of this thread's half
-      uint32_t kw[2] = {pw.x, pw.y};
+      const int c0 = j * TILE + wg * COLS;  // first key of this thread's columns
       if (kMask == kMaskKeys) {
 #pragma unroll
-        for (int qd = 0; qd < 2; ++qd) {
-          const int col = c0 + qd * 32 + lane;
-          kw[qd] = __ballot_sync(0xffffffffu, col < N && kmask[col] != 0);
+        for (int w = 0; w < COLS / 32; ++w) {
+          const int col = c0 + w * 32 + lane;
+          kw[w] = __ballot_sync(0xffffffffu, col < N && kmask[col] != 0);
         }
       }
-      const bool need_mask = kMask != kMaskNone || (c0 + HALF > N) || (a.causal && c0 + HALF - 1 > r0);
+      const bool need_mask = kMask != kMaskNone || (c0 + COLS > N) || (a.causal && c0 + COLS - 1 > r0);
       if (need_mask) {
-        const int lim_causal = a.causal ? row - c0 : HALF - 1;  // keep col_local <= row - c0
+        const int lim_causal = a.causal ? row - c0 : COLS - 1;  // keep col_local <= row - c0
         const int lim = min(lim_causal, N - 1 - c0);            // and col < N
 #pragma unroll
-        for (int c = 0; c < HALF; ++c) {
+        for (int c = 0; c < COLS; ++c) {
           const bool keep = (c <= lim) && ((kw[c >> 5] >> (c & 31)) & 1u);
           v[c] = keep ? v[c] : -INFINITY;
         }
       }
-      const float tmax = row_max64(v);
+      const float tmax = row_max(v);
       if (tmax != -INFINITY) {
         const float mt = tmax * a.C;
         // Rescale only when the running max grows: a fully masked tile leaves
@@ -538,12 +576,15 @@ __global__ void __launch_bounds__(kThreads, 2)
         l += row_sum_exp2<exp2_degree<kOp>()>(v, a.C, -m);
       }
     }
-    // Merge the two column halves of each row (fixed order: lower half first).
-    if (hf == 1) merge[rl] = make_float2(m, l);
+    // Merge the column parts of each row (fixed order: part 0, then 1, 2, ...).
+    if (wg > 0) merge[(wg - 1) * TILE + rl] = make_float2(m, l);
     exp_bar_sync();
-    if (hf == 0) {
-      const float2 o = merge[rl];
-      merge_ml(m, l, o.x, o.y);
+    if (wg == 0) {
+#pragma unroll
+      for (int w = 1; w < kExpWG; ++w) {
+        const float2 o = merge[(w - 1) * TILE + rl];
+        merge_ml(m, l, o.x, o.y);
+      }
       bool dead = (m == -INFINITY) || row >= N;
       if (!dead && a.qmask != nullptr) dead = a.qmask[b * a.qmb + row] == 0;
       // Stored negated (pass 2 adds it): rows that keep no key, and padding
@@ -573,13 +614,19 @@ __global__ void __launch_bounds__(kThreads, 2)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1k(smem_raw);
   using CF = Cfg<D, kOp>;
+  constexpr bool kBias = KVBM_P2_BIAS != 0 && kOp != Op::TF32X3;
+  static_assert(!kBias || CF::kSlotsPerTile == 1, "the bias step follows a whole Q tile per slot");
   constexpr int TB = CF::kOperandBytes, SB = CF::kSlotBytes;
+  constexpr int QS = SB + (kBias ? kBiasBytes : 0);  // Q ring slot: the Q operand, then its bias operand
+  static_assert(QS % 1024 == 0, "Q slots stay on 1024-byte swizzle atoms");
   constexpr int LB = TILE * 4;  // lse2 bytes of one query tile
+  constexpr int LR = kBias ? 0 : LB * kLStages;
   uint8_t* k_tile = smem;
   uint8_t* q_ring = smem + TB;
-  float* l_ring = reinterpret_cast<float*>(smem + TB + SB * kStages);
-  float2* merge = reinterpret_cast<float2*>(smem + TB + SB * kStages + LB * kLStages);  // [128]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(merge + TILE);
+  uint8_t* ones = q_ring + QS * kStages;  // kBias: the key-side operand of the bias step
+  float* l_ring = reinterpret_cast<float*>(ones + (kBias ? kBiasBytes : 0));
+  float* merge = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(l_ring) + LR);  // [kExpWG - 1][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(merge + (kExpWG - 1) * TILE);
   uint64_t* k_full = bars;
   uint64_t* q_full = bars + 1;
   uint64_t* q_empty = q_full + kStages;
@@ -628,7 +675,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (threadIdx.x == 0) {
     mbar_init(k_full, 1);
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&q_full[s], 1);
+      mbar_init(&q_full[s], kBias ? 2 : 1);  // kBias: + the producer warp's bias rows
       mbar_init(&q_empty[s], 1);  // MMA commit: the Q tile is no longer read
     }
     for (int i = 0; i < 2; ++i) {
@@ -641,6 +688,27 @@ __global__ void __launch_bounds__(kThreads, 2)
     *abort_flag = 0;
     fence_mbar_init();
   }
+  if constexpr (kBias) {
+    // The bias operands' constant parts (16-byte chunks): the key-side tile
+    // of ones ([1, 1, 1, 0, ...] in the first K half of every row, zeros in
+    // the second), and the zero second K half of every slot's query-side tile.
+    if (threadIdx.x >= 64) {
+      constexpr int kOnesChunks = kBiasBytes / 16, kZeroChunks = kBiasBytes / 32;  // per tile, per slot
+      for (int c = threadIdx.x - 64; c < kOnesChunks + kStages * kZeroChunks; c += kExpThreads) {
+        uint4 val = make_uint4(0u, 0u, 0u, 0u);
+        uint8_t* dst;
+        if (c < kOnesChunks) {
+          dst = ones + 16 * c;
+          if (((16 * c) & 128) == 0) val = make_uint4(0x3F803F80u, 0x00003F80u, 0u, 0u);  // bf16 1, 1, 1, 0
+        } else {
+          const int e = c - kOnesChunks, sl = e / kZeroChunks, r = e % kZeroChunks;  // slot, 16-byte row of its K half 2
+          dst = q_ring + sl * QS + SB + (r >> 3) * 256 + 128 + (r & 7) * 16;
+        }
+        *reinterpret_cast<uint4*>(dst) = val;
+      }
+      fence_proxy_async_smem();
+    }
+  }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
@@ -650,7 +718,55 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  if (kBias && warp == 0) {
+    // Producer warp: lane 0 issues the copies; every lane then writes the
+    // bias rows of 4 query rows of the slot's tile.
+    const float invC = 1.0f / a.C;
+    if (lane == 0) {
+      prefetch_tmap(&tq);
+      prefetch_tmap(&tk);
+      mbar_arrive_expect_tx(k_full, TB);
+      load_operand<D, kOp>(k_tile, &tk, &tk2, k_full, sv.k_row + c0, g, sv.k_b);
+    }
+    int issued = 0;
+    for (int j = 0; j < J; ++j) {
+      const int hh = j / nqt;
+      const int r = rs + (j - hh * nqt) * TILE;
+      const int h = g * a.G + hh;
+      const int s = j % kStages, n = j / kStages;
+      const bool ok = n == 0 || mbar_wait(&q_empty[s], (n - 1) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&q_full[s], SB);
+        load_slot<D, kOp>(q_ring + s * QS, &tq, &tq2, &q_full[s], 0, sv.q_row + r, h, sv.q_b);
+      }
+      issued = j + 1;
+      const float* lrow = a.lse + (long long)(uu * a.G + hh) * a.Npad + r;
+      uint8_t* bt = q_ring + s * QS + SB;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int rl = lane * 4 + e;
+        const float nl = lrow[lse_tile_slot(rl)];  // -lse2 (-inf: the row keeps no key)
+        const float v = nl == -INFINITY ? -60000.f : nl * invC;
+        const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+        const float r1 = v - __bfloat162float(hi);
+        const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+        const __nv_bfloat16 lo = __float2bfloat16_rn(r1 - __bfloat162float(mid));
+        const uint4 w = make_uint4((uint32_t)__bfloat16_as_ushort(hi) | ((uint32_t)__bfloat16_as_ushort(mid) << 16),
+                                   (uint32_t)__bfloat16_as_ushort(lo), 0u, 0u);
+        *reinterpret_cast<uint4*>(bt + (rl >> 3) * 256 + (rl & 7) * 16) = w;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&q_full[s]);
+    }
+    // Do not leave while our copies are in flight.
+    if (lane == 0) {
+      mbar_wait(k_full, 0, abort_flag);
+      for (int qn = max(0, issued - kStages); qn < issued; ++qn)
+        mbar_wait(&q_full[qn % kStages], (qn / kStages) & 1, abort_flag);
+    }
+  } else if (warp == 0) {
     if (lane == 0) {
       prefetch_tmap(&tq);
       prefetch_tmap(&tk);
@@ -671,7 +787,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             break;
           }
           mbar_arrive_expect_tx(&q_full[s], SB);
-          load_slot<D, kOp>(q_ring + s * SB, &tq, &tq2, &q_full[s], sb, sv.q_row + r, h, sv.q_b);
+          load_slot<D, kOp>(q_ring + s * QS, &tq, &tq2, &q_full[s], sb, sv.q_row + r, h, sv.q_b);
           issued = qn + 1;
           if (sb == 0) {
             mbar_arrive_expect_tx(&l_full[t], LB);
@@ -691,7 +807,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = idesc_mma(TILE, TILE, Cfg<D, kOp>::kFmt);
-      const uint32_t ks = smem_u32(k_tile), qs = smem_u32(q_ring);
+      const uint32_t ks = smem_u32(k_tile), qs = smem_u32(q_ring), os = smem_u32(ones);
+      const uint32_t idesc_b = idesc_mma(TILE, TILE, 1u);  // the bias step: bf16 operands
       int issued = 0;
       if (mbar_wait(k_full, 0, abort_flag)) {
         for (int j = 0; j < J; ++j) {
@@ -702,7 +819,10 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int qn = j * CF::kSlotsPerTile + done, s = qn % kStages;
             if (!mbar_wait(&q_full[s], (qn / kStages) & 1, abort_flag)) break;
             tc_fence_after();
-            issue_slot_mma<D, kOp>(tmem + buf * TILE, ks, qs + s * SB, done * CF::kSlotBlocks, idesc);
+            issue_slot_mma<D, kOp>(tmem + buf * TILE, ks, qs + s * QS, done * CF::kSlotBlocks, idesc);
+            if constexpr (kBias)  // D += ones x (hi + mid + lo of -lse2 / C)
+              mma_f16(tmem + buf * TILE, k16_interleaved_desc(os), k16_interleaved_desc(qs + s * QS + SB), idesc_b,
+                      1u);
             mma_commit(&q_empty[s]);  // the Q slot is free once these MMAs complete
           }
           if (done > 0) {  // (a partial tile only after an abort: committed so that the drain waits for it)
@@ -715,14 +835,14 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (issued > 0) mbar_wait(&s_full[(issued - 1) & 1], ((issued - 1) >> 1) & 1, abort_flag);
     }
   } else {
-    // exp/sum warps: warp w covers keys c0 + 32*(w%4) + [0, 32) and warpgroup hf
-    // the query columns [hf*64, hf*64 + 64) of each tile; lane l holds keys
-    // kr[i] = 32*(w%4) + l/4 + 8i (i < 4) and 16 of the columns (col_sum4).
+    // exp/sum warps: warp w covers keys c0 + 32*(w%4) + [0, 32) and warpgroup wg
+    // the query columns [wg*COLS, (wg + 1)*COLS) of each tile; lane l holds keys
+    // kr[i] = 32*(w%4) + l/4 + 8i (i < 4) and 2*kBlk of the columns (col_sum4).
     const int sub = warp & 3;
-    const int hf = (warp - 2) >> 2;
+    const int wg = (warp - 2) >> 2;
     const int pc = lane & 3;
     const int kr0 = sub * 32 + (lane >> 2);  // local key of row i: kr0 + 8i
-    const uint32_t trow = tmem + ((uint32_t)(sub * 32) << 16) + hf * HALF;
+    const uint32_t trow = tmem + ((uint32_t)(sub * 32) << 16) + wg * COLS;
     const float C = a.C;
     // kRagged: the sequence length is re-read from shared memory per tile
     // rather than held in a register across the loop (register budget).
@@ -739,49 +859,49 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int r = rs + (j - hh * nqt) * TILE;
       uint2 pw[4];
       if (kMask == kMaskPairs) {  // issued before the waits so the loads overlap them
-        const uint32_t* pcol = a.pcol + b * a.pb + ((r + hf * HALF) >> 5);
+        const uint32_t* pcol = a.pcol + b * a.pb + ((r + wg * COLS) >> 5);
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          pw[i] = *reinterpret_cast<const uint2*>(pcol + (long long)(c0 + kr0 + 8 * i) * a.W);
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t* w = pcol + (long long)(c0 + kr0 + 8 * i) * a.W;
+          pw[i] = COLS == 64 ? *reinterpret_cast<const uint2*>(w) : make_uint2(w[0], 0xffffffffu);
+        }
       }
       bool ok = mbar_wait(&s_full[buf], (j >> 1) & 1, abort_flag);
-      ok = ok && mbar_wait(&l_full[t], (j / kLStages) & 1, abort_flag);  // lse2 bytes landed
+      if (!kBias) ok = ok && mbar_wait(&l_full[t], (j / kLStages) & 1, abort_flag);  // lse2 bytes landed
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      float v[HALF];
-      tmem_ld16x256_x8(trow + buf * TILE, *reinterpret_cast<float(*)[32]>(&v[0]));
-      tmem_ld16x256_x8(trow + (16u << 16) + buf * TILE, *reinterpret_cast<float(*)[32]>(&v[32]));
-      tmem_ld_wait();
+      float v[COLS];
+      load_keys16(trow + buf * TILE, v);
       tc_fence_before();
       mbar_arrive(&s_empty[buf]);
 
-      const float* nL = l_ring + t * TILE + hf * HALF;  // -lse2 of this half's 64 query rows (lse_tile_slot order)
+      const float* nL = l_ring + t * TILE + wg * COLS;  // -lse2 of this warpgroup's query rows (lse_tile_slot order)
       constexpr bool kB = kMask == kMaskPairs;
       constexpr int kDeg = exp2_degree<kOp>();
-      // On the diagonal, query r + hf*64 + col keeps key c0 + kr iff hf*64 + col >= kr.
+      // On the diagonal, query r + wg*COLS + col keeps key c0 + kr iff wg*COLS + col >= kr.
       // r < c0 (only without causal_skip): every pair is above the diagonal, adds 0.
       // kRagged: query columns at or past the sequence's end contribute 0
       // whatever their scores (their rows may hold another sequence's, or
       // undefined, values).  Otherwise those rows are the TMA's zero fill
       // past N, whose lse2 is -inf.
       if (!a.causal || r >= c0) {
-        const int keep_from = kr0 - hf * HALF;  // key i keeps columns >= keep_from + 8i
-        const int keep_to = kRagged ? *len_v - r - hf * HALF : HALF;
+        const int keep_from = kr0 - wg * COLS;  // key i keeps columns >= keep_from + 8i
+        const int keep_to = kRagged ? *len_v - r - wg * COLS : COLS;
         const bool diag = a.causal && r == c0;
-        if (kRagged && keep_to < HALF) {
+        if (kRagged && keep_to < COLS) {
           if (diag)
-            col_sum4<kDeg, true, kB, true>(v, C, nL, pc, keep_from, pw, keep_to, acc);
+            col_sum4<kDeg, true, kB, true, kBias>(v, C, nL, pc, keep_from, pw, keep_to, acc);
           else
-            col_sum4<kDeg, false, kB, true>(v, C, nL, pc, keep_from, pw, keep_to, acc);
+            col_sum4<kDeg, false, kB, true, kBias>(v, C, nL, pc, keep_from, pw, keep_to, acc);
         } else if (diag) {
-          col_sum4<kDeg, true, kB, false>(v, C, nL, pc, keep_from, pw, keep_to, acc);
+          col_sum4<kDeg, true, kB, false, kBias>(v, C, nL, pc, keep_from, pw, keep_to, acc);
         } else {
-          col_sum4<kDeg, false, kB, false>(v, C, nL, pc, keep_from, pw, keep_to, acc);  // every pair kept
+          col_sum4<kDeg, false, kB, false, kBias>(v, C, nL, pc, keep_from, pw, keep_to, acc);  // every pair kept
         }
       }
     }
-    // Per key: the thread's 16 columns, then the 4 lanes holding the key's
-    // other columns (xor 1, 2), then the two query halves (lower half first).
+    // Per key: the thread's columns, then the 4 lanes holding the key's other
+    // columns (xor 1, 2), then the warpgroups' column parts (part 0 first).
     float tot[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -789,18 +909,19 @@ __global__ void __launch_bounds__(kThreads, 2)
       tot[i] += __shfl_xor_sync(0xffffffffu, tot[i], 1);
       tot[i] += __shfl_xor_sync(0xffffffffu, tot[i], 2);
     }
-    float* mergef = reinterpret_cast<float*>(merge);
-    if (hf == 1 && pc == 0) {
+    if (wg > 0 && pc == 0) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) mergef[kr0 + 8 * i] = tot[i];
+      for (int i = 0; i < 4; ++i) merge[(wg - 1) * TILE + kr0 + 8 * i] = tot[i];
     }
     exp_bar_sync();
-    if (hf == 0 && pc == 0) {
+    if (wg == 0 && pc == 0) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int key = c0 + kr0 + 8 * i;
         if (key < a.N) {
-          float total = tot[i] + mergef[kr0 + 8 * i];
+          float total = tot[i];
+#pragma unroll
+          for (int w = 1; w < kExpWG; ++w) total += merge[(w - 1) * TILE + kr0 + 8 * i];
           if (kRagged && key >= *len_v) total = 0.f;  // past the sequence's end
           else if (kMask == kMaskKeys && a.kmask[b * a.kmb + key] == 0) total = 0.f;
           a.part[((long long)uu * a.nchunk + y) * a.N + key] = total;
@@ -1043,13 +1164,15 @@ constexpr size_t kBarBytes = 8 * (1 + 2 * kStages + 4) + 16;  // mbarriers + TME
 
 template <int D, Op kOp>
 constexpr size_t smem_lse() {
-  return 1024 + (size_t)Cfg<D, kOp>::kOperandBytes + (size_t)Cfg<D, kOp>::kSlotBytes * kStages + TILE * 8 +
-         kBarBytes;
+  return 1024 + (size_t)Cfg<D, kOp>::kOperandBytes + (size_t)Cfg<D, kOp>::kSlotBytes * kStages +
+         (kExpWG - 1) * TILE * 8 + kBarBytes;
 }
 template <int D, Op kOp>
 constexpr size_t smem_mass() {
-  return 1024 + (size_t)Cfg<D, kOp>::kOperandBytes + (size_t)Cfg<D, kOp>::kSlotBytes * kStages +
-         TILE * 4 * kLStages + TILE * 8 + kBarBytes + 8 * kLStages;
+  constexpr bool kBias = KVBM_P2_BIAS != 0 && kOp != Op::TF32X3;
+  return 1024 + (size_t)Cfg<D, kOp>::kOperandBytes +
+         (size_t)(Cfg<D, kOp>::kSlotBytes + (kBias ? kBiasBytes : 0)) * kStages + (kBias ? kBiasBytes : 0) +
+         (kBias ? 0 : TILE * 4 * kLStages) + (kExpWG - 1) * TILE * 4 + kBarBytes + 8 * kLStages;
 }
 
 template <int D, Op kOp, int kMask, bool kRagged>
@@ -1273,7 +1396,7 @@ int selftest_wait_timeout(cudaStream_t s, unsigned long long limit_ns, int* wait
   return KVBM_OK;
 }
 
-double exp2_fma_fraction() { return (double)kEmuGroups / kGroups; }
+double exp2_fma_fraction() { return (double)kEmuPer16 / 16; }
 
 int launch_tc(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws, cudaStream_t s,
               const LaunchOpts& o) {
