@@ -297,10 +297,16 @@ __device__ __forceinline__ float row_sum_exp2(const float (&v)[COLS], float C, f
 // loads per tile (a full row of COLS columns per thread would need COLS/4).
 constexpr int kBlk = COLS / 8;
 
-// Of the kBlk column blocks of a pass-2 thread, KVBM_EMU_GROUPS/16 of them
-// take their exp2 from the FMA-pipe polynomial: the same share as pass 1.
-constexpr int kEmuBlocks = kEmuPer16 * kBlk / 16;
-static_assert(kEmuPer16 * kBlk % 16 == 0, "pass 2 emulates whole 8-column blocks");
+// Of the kBlk column blocks of a pass-2 thread, KVBM_EMU_GROUPS_P2/16 of them
+// take their exp2 from the FMA-pipe polynomial (by default the same share as
+// pass 1).
+#ifndef KVBM_EMU_GROUPS_P2
+#define KVBM_EMU_GROUPS_P2 KVBM_EMU_GROUPS
+#endif
+constexpr int kEmuPer16P2 = KVBM_EMU_GROUPS_P2;
+constexpr int kEmuBlocks = kEmuPer16P2 * kBlk / 16;
+static_assert(kEmuPer16P2 >= 0 && kEmuPer16P2 <= 16 && kEmuPer16P2 * kBlk % 16 == 0,
+              "pass 2 emulates whole 8-column blocks");
 __host__ __device__ constexpr bool emu_block(int m) {
   return ((m + 1) * kEmuBlocks) / kBlk != (m * kEmuBlocks) / kBlk;
 }
@@ -734,6 +740,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int r = rs + (j - hh * nqt) * TILE;
       const int h = g * a.G + hh;
       const int s = j % kStages, n = j / kStages;
+      // The lse2 rows of the tile, loaded before the slot wait so that their
+      // latency overlaps it (pass 1 wrote them; nothing writes them now).
+      const float* lrow = a.lse + (long long)(uu * a.G + hh) * a.Npad + r;
+      float nls[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) nls[e] = lrow[lse_tile_slot(lane * 4 + e)];
       const bool ok = n == 0 || mbar_wait(&q_empty[s], (n - 1) & 1, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
       if (lane == 0) {
@@ -741,12 +753,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         load_slot<D, kOp>(q_ring + s * QS, &tq, &tq2, &q_full[s], 0, sv.q_row + r, h, sv.q_b);
       }
       issued = j + 1;
-      const float* lrow = a.lse + (long long)(uu * a.G + hh) * a.Npad + r;
       uint8_t* bt = q_ring + s * QS + SB;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int rl = lane * 4 + e;
-        const float nl = lrow[lse_tile_slot(rl)];  // -lse2 (-inf: the row keeps no key)
+        const float nl = nls[e];  // -lse2 (-inf: the row keeps no key)
         const float v = nl == -INFINITY ? -60000.f : nl * invC;
         const __nv_bfloat16 hi = __float2bfloat16_rn(v);
         const float r1 = v - __bfloat162float(hi);
