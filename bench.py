@@ -614,6 +614,69 @@ def b200_arm(args, w):
     if lib.kvbm_check_device_errors(stream.cuda_stream) != 0:
         raise RuntimeError("a device-side wait timed out in the timed region")
 
+    # End to end through the public API: pinned host q/k in, mass back on the host.
+    # The same K steps and the same idle lead-in (0.3 s) as the device-timed
+    # steps, so that both start from the same power state.
+    e2e = None
+    if not args.no_e2e:
+        Ke = args.e2e_steps or K
+        kb.block_mass_b200(q_pin, k_pin, attn_mask=kmd, query_mask=qmd, causal=w.causal,
+                           block_size=w.block_size, device=dev).cpu()
+        torch.cuda.synchronize()
+        time.sleep(0.3)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(Ke):
+            m = kb.block_mass_b200(q_pin, k_pin, attn_mask=kmd, query_mask=qmd, causal=w.causal,
+                                   block_size=w.block_size, device=dev)
+            if world > 1:
+                dist.reduce(m, dst=0, op=dist.ReduceOp.SUM)
+            m_host = m.cpu()
+        a1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = torch.tensor([a0.elapsed_time(a1)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+        e2e = {"value": pairs_total_per_step * Ke / (float(e_ms.item()) * 1e-3), "unit": UNIT,
+               "h2d_bytes_per_step": int(q_pin.numel() * q_pin.element_size() + k_pin.numel() * k_pin.element_size()),
+               "d2h_bytes_per_step": int(m_host.numel() * m_host.element_size()),
+               "steps": Ke, "api": "kvblockmass_b200.block_mass_b200(pinned host q/k, device='cuda').cpu()",
+               "lead_in": "0.3 s idle after one untimed call, as before the device-timed steps",
+               "bits_equal_device_call": None}
+        # the same call on pageable host tensors (staged through pinned bounce buffers)
+        q_pg, k_pg = q_pin.clone(), k_pin.clone()
+        assert not q_pg.is_pinned()
+        Ke = max(3, min(Ke, 10))
+        kb.block_mass_b200(q_pg, k_pg, attn_mask=kmd, query_mask=qmd, causal=w.causal,
+                           block_size=w.block_size, device=dev).cpu()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        a0.record(stream)
+        for _ in range(Ke):
+            m = kb.block_mass_b200(q_pg, k_pg, attn_mask=kmd, query_mask=qmd, causal=w.causal,
+                                   block_size=w.block_size, device=dev)
+            if world > 1:
+                dist.reduce(m, dst=0, op=dist.ReduceOp.SUM)
+            m_host_pg = m.cpu()
+        a1.record(stream)
+        torch.cuda.synchronize()
+        p_ms = torch.tensor([a0.elapsed_time(a1)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(p_ms, op=dist.ReduceOp.MAX)
+        e2e["pageable"] = {"value": pairs_total_per_step * Ke / (float(p_ms.item()) * 1e-3), "unit": UNIT,
+                           "ms_per_step": float(p_ms.item()) / Ke,
+                           "api": "block_mass_b200(pageable host q/k, device='cuda'): pinned bounce buffers"}
+        del q_pg, k_pg
+        if world == 1:
+            dev_out = ops.run_prepared(prep, workspace=ws)
+            torch.cuda.synchronize()
+            e2e["bits_equal_device_call"] = bool(torch.equal(m_host.to(dev), dev_out)
+                                                 and torch.equal(m_host_pg.to(dev), dev_out))
+
     # Caller-provided LSE (pass 1 skipped): the path an attention forward can feed.
     lse_input = None
     if not args.no_e2e:
@@ -779,63 +842,6 @@ def b200_arm(args, w):
                   "tail_budget": Nd // 8, "top_slice": Nd // 16, "kept_tokens": int(counts[0, 0]),
                   "launches": 3, "api": "kvbm_design (expand_block_scores + design_from_scores + block retention)"}
         del mass_d, m2, outs, ws_d
-
-    # End to end through the public API: pinned host q/k in, mass back on the host.
-    e2e = None
-    if not args.no_e2e:
-        Ke = args.e2e_steps or max(3, min(K, 10))
-        kb.block_mass_b200(q_pin, k_pin, attn_mask=kmd, query_mask=qmd, causal=w.causal,
-                           block_size=w.block_size, device=dev).cpu()
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a0.record(stream)
-        for _ in range(Ke):
-            m = kb.block_mass_b200(q_pin, k_pin, attn_mask=kmd, query_mask=qmd, causal=w.causal,
-                                   block_size=w.block_size, device=dev)
-            if world > 1:
-                dist.reduce(m, dst=0, op=dist.ReduceOp.SUM)
-            m_host = m.cpu()
-        a1.record(stream)
-        torch.cuda.synchronize()
-        e_ms = torch.tensor([a0.elapsed_time(a1)], device=dev, dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
-        e2e = {"value": pairs_total_per_step * Ke / (float(e_ms.item()) * 1e-3), "unit": UNIT,
-               "h2d_bytes_per_step": int(q_pin.numel() * q_pin.element_size() + k_pin.numel() * k_pin.element_size()),
-               "d2h_bytes_per_step": int(m_host.numel() * m_host.element_size()),
-               "steps": Ke, "api": "kvblockmass_b200.block_mass_b200(pinned host q/k, device='cuda').cpu()",
-               "bits_equal_device_call": None}
-        # the same call on pageable host tensors (staged through pinned bounce buffers)
-        q_pg, k_pg = q_pin.clone(), k_pin.clone()
-        assert not q_pg.is_pinned()
-        kb.block_mass_b200(q_pg, k_pg, attn_mask=kmd, query_mask=qmd, causal=w.causal,
-                           block_size=w.block_size, device=dev).cpu()
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        a0.record(stream)
-        for _ in range(Ke):
-            m = kb.block_mass_b200(q_pg, k_pg, attn_mask=kmd, query_mask=qmd, causal=w.causal,
-                                   block_size=w.block_size, device=dev)
-            if world > 1:
-                dist.reduce(m, dst=0, op=dist.ReduceOp.SUM)
-            m_host_pg = m.cpu()
-        a1.record(stream)
-        torch.cuda.synchronize()
-        p_ms = torch.tensor([a0.elapsed_time(a1)], device=dev, dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(p_ms, op=dist.ReduceOp.MAX)
-        e2e["pageable"] = {"value": pairs_total_per_step * Ke / (float(p_ms.item()) * 1e-3), "unit": UNIT,
-                           "ms_per_step": float(p_ms.item()) / Ke,
-                           "api": "block_mass_b200(pageable host q/k, device='cuda'): pinned bounce buffers"}
-        del q_pg, k_pg
-        if world == 1:
-            dev_out = ops.run_prepared(prep, workspace=ws)
-            torch.cuda.synchronize()
-            e2e["bits_equal_device_call"] = bool(torch.equal(m_host.to(dev), dev_out)
-                                                 and torch.equal(m_host_pg.to(dev), dev_out))
 
     clocks = None
     if sampler:

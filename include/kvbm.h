@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define KVBM_ABI_VERSION 2
+#define KVBM_ABI_VERSION 3
 
 /* Only the entry points below are exported from libkvbm.so (it is built with
  * hidden default visibility). */
@@ -320,13 +320,20 @@ KVBM_API int kvbm_block_mass_paged(const kvbm_problem* p, const kvbm_paged_kv* k
  *                     run_head_begin/end: pass 1 covers q-heads [begin, end)
  *                     of each GQA group, 0 <= begin < end <= H_q/H_kv (end <=
  *                     begin: all); a head range narrower than the group needs
- *                     a run range of one unit.  Pass 2 of a unit reads pass 1
- *                     of all its heads, and (fp32 inputs on path 2) the unit's
- *                     k rows as converted by the pass-1 piece whose head range
- *                     starts at 0.  mass_out may be NULL without
- *                     KVBM_STAGE_REDUCE.  Pieces that write disjoint units or
- *                     heads may run concurrently.  Not combined with seq_lens,
- *                     cu_seqlens or paged (KVBM_ERR_SHAPE).
+ *                     a run range of one unit;
+ *                     run_row_begin/end: pass 1 covers query rows
+ *                     [begin, end) of each head it runs (end <= begin: all
+ *                     rows); begin a multiple of 128, end a multiple of 128
+ *                     or N; it reads the k rows [0, end) under causal_skip,
+ *                     all k rows otherwise.  Kernel paths 0 and 1 only, and
+ *                     not with the LSE input (KVBM_ERR_SHAPE).  Pass 2 of a
+ *                     unit reads pass 1 of all its heads and rows, and (fp32
+ *                     inputs on path 2) the unit's k rows as converted by the
+ *                     pass-1 piece whose head range starts at 0.  mass_out
+ *                     may be NULL without KVBM_STAGE_REDUCE.  Pieces that
+ *                     write disjoint units, heads or rows may run
+ *                     concurrently.  Not combined with seq_lens, cu_seqlens
+ *                     or paged (KVBM_ERR_SHAPE).
  *
  * Every ragged/per-sequence result equals the sum over sequences of the
  * reference run on each sequence alone (its first seq_lens[b] positions);
@@ -349,6 +356,8 @@ typedef struct kvbm_options {
   int32_t run_unit_end;
   int32_t run_head_begin;
   int32_t run_head_end;
+  int32_t run_row_begin;
+  int32_t run_row_end;
 } kvbm_options;
 
 /* Host-only checks of `p` with options `o` (o may be NULL). */
@@ -429,6 +438,18 @@ KVBM_API size_t kvbm_design_workspace_bytes(const kvbm_design_args* d);
  * on the host after mass.cpu(). */
 KVBM_API int kvbm_design(const kvbm_design_args* d, const kvbm_design_out* out, void* workspace,
                 size_t workspace_bytes, void* stream);
+
+/* Queue `height` copies of `width` bytes on `stream`: row i goes from
+ * src + i * src_pitch to dst + i * dst_pitch (cudaMemcpy2DAsync, direction
+ * from the pointers).  The host-input path of the Python binding moves a
+ * piece of q (the same rows of several q-heads) with one call; it stands in
+ * for the host-to-device move of reference.py:74-76 (`q.to(device)`).  The
+ * source must stay valid until the copy completes (pinned host memory:
+ * asynchronous; pageable: the call returns after staging).  KVBM_ERR_NULL for
+ * NULL pointers, KVBM_ERR_SHAPE for negative sizes or a pitch below `width`;
+ * zero sizes queue nothing. */
+KVBM_API int kvbm_copy_2d_async(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch, int64_t width,
+                       int64_t height, void* stream);
 
 /* Self-test of the failure path of the tcgen05 kernels' pipeline waits: one
  * thread waits on an mbarrier that nothing arrives at, through the same

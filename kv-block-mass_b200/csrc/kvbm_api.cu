@@ -151,7 +151,7 @@ size_t max_layout_bytes(const kvbm_problem* p, const Ragged* rg = nullptr) {
 // Stages and run ranges of a call (kvbm_options); all stages when not staged.
 struct Staging {
   int stages = KVBM_STAGE_MASKS | KVBM_STAGE_PASS1 | KVBM_STAGE_PASS2 | KVBM_STAGE_REDUCE;
-  int rb = 0, re = 0, hb = 0, he = 0;
+  int rb = 0, re = 0, hb = 0, he = 0, qb = 0, qe = 0;
 };
 
 int run_passes(const kvbm_problem* p, const WsLayout& L, int path, void* mass_out, void* ws, cudaStream_t s,
@@ -176,6 +176,8 @@ int run_passes(const kvbm_problem* p, const WsLayout& L, int path, void* mass_ou
   o.re = sg.re;
   o.hb = sg.hb;
   o.he = sg.he;
+  o.qb = sg.qb;
+  o.qe = sg.qe;
   int st = KVBM_OK;
   if (lse != nullptr && s1) {
     nvtxRangePushA("kvbm lse import");
@@ -267,7 +269,8 @@ int make_plan(const kvbm_problem* p, const kvbm_options* o, int dev, Plan* out) 
   if (st != KVBM_OK) return st;
   if (kv != nullptr && (int64_t)kv->max_pages * kv->page_size < p->N) return KVBM_ERR_SHAPE;
   // staged execution: run ranges relative to the unit range, checked before narrowing
-  const bool staged = opt.stages != 0 || opt.run_unit_end > opt.run_unit_begin || opt.run_head_end > opt.run_head_begin;
+  const bool staged = opt.stages != 0 || opt.run_unit_end > opt.run_unit_begin ||
+                      opt.run_head_end > opt.run_head_begin || opt.run_row_end > opt.run_row_begin;
   if (staged) {
     const int U = p->unit_end - p->unit_begin, G = p->Hq / p->Hkv;
     if (opt.stages < 0 || opt.stages > 15) return KVBM_ERR_SHAPE;
@@ -285,6 +288,13 @@ int make_plan(const kvbm_problem* p, const kvbm_options* o, int dev, Plan* out) 
       if (opt.run_head_end - opt.run_head_begin < G && nu != 1) return KVBM_ERR_SHAPE;
       sg.hb = opt.run_head_begin;
       sg.he = opt.run_head_end;
+    }
+    if (opt.run_row_end > opt.run_row_begin) {
+      if (opt.run_row_begin < 0 || opt.run_row_end > p->N || opt.run_row_begin % 128 != 0 ||
+          (opt.run_row_end % 128 != 0 && opt.run_row_end != p->N) || opt.lse != nullptr)
+        return KVBM_ERR_SHAPE;
+      sg.qb = opt.run_row_begin;
+      sg.qe = opt.run_row_end;
     }
   }
   {
@@ -334,6 +344,9 @@ int make_plan(const kvbm_problem* p, const kvbm_options* o, int dev, Plan* out) 
   size_t dense = 0;
   if (dev >= 0) {
     pl.path = select_path(&sub, dev);
+    // a pass-1 row range on the 3xTF32 path would leave the tf32 copies of
+    // the other rows unconverted
+    if (pl.path == 2 && pl.staging.qe > pl.staging.qb) return KVBM_ERR_SHAPE;
     pl.L = layout_for(&sub, pl.path, &pl.rg);
     dense = pl.L.total;
   } else {
@@ -557,6 +570,22 @@ int kvbm_selftest_wait_timeout(void* stream, uint64_t limit_ns, int* waited) {
   }
   if (device_kind(dev) != 1) return KVBM_ERR_DEVICE;
   return selftest_wait_timeout(static_cast<cudaStream_t>(stream), limit_ns, waited);
+}
+
+int kvbm_copy_2d_async(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch, int64_t width,
+                       int64_t height, void* stream) {
+  if (dst == nullptr || src == nullptr) return KVBM_ERR_NULL;
+  if (width < 0 || height < 0 || (height > 1 && (dst_pitch < width || src_pitch < width))) return KVBM_ERR_SHAPE;
+  if (width == 0 || height == 0) return KVBM_OK;
+  if (height == 1)
+    return cudaMemcpyAsync(dst, src, (size_t)width, cudaMemcpyDefault, static_cast<cudaStream_t>(stream)) ==
+                   cudaSuccess
+               ? KVBM_OK
+               : KVBM_ERR_CUDA;
+  return cudaMemcpy2DAsync(dst, (size_t)dst_pitch, src, (size_t)src_pitch, (size_t)width, (size_t)height,
+                           cudaMemcpyDefault, static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? KVBM_OK
+             : KVBM_ERR_CUDA;
 }
 
 int kvbm_check_device_errors(void* stream) {

@@ -192,15 +192,18 @@ struct LaunchOpts {
   bool run_masks = true;      // pack a pair mask into bits (tensor-core paths)
   Ragged rg;                  // ragged batch lengths / packed layout
   // Staged execution: the passes cover units [rb, re) of the problem's range
-  // (relative to unit_begin) and pass 1 the q-heads [hb, he) of each group.
+  // (relative to unit_begin) and pass 1 the q-heads [hb, he) of each group
+  // and the query rows [qb, qe) of each head.
   int rb = 0, re = 0;         // re <= rb: every unit
   int hb = 0, he = 0;         // he <= hb: every head
+  int qb = 0, qe = 0;         // qe <= qb: every row
 };
 
 // The units and heads a launch covers (LaunchOpts' run ranges resolved).
 struct RunRange {
   int rb, nu;  // units [rb, rb + nu) of the problem's range
   int hb, nh;  // pass-1 q-heads [hb, hb + nh) of each group
+  int qb, qe;  // pass-1 query rows [qb, qe)
 };
 inline RunRange run_range(const kvbm_problem* p, const LaunchOpts& o) {
   const int U = p->unit_end - p->unit_begin, G = p->Hq / p->Hkv;
@@ -209,6 +212,8 @@ inline RunRange run_range(const kvbm_problem* p, const LaunchOpts& o) {
   r.nu = o.re > o.rb ? o.re - o.rb : U;
   r.hb = o.he > o.hb ? o.hb : 0;
   r.nh = o.he > o.hb ? o.he - o.hb : G;
+  r.qb = o.qe > o.qb ? o.qb : 0;
+  r.qe = o.qe > o.qb ? o.qe : p->N;
   return r;
 }
 int launch_simt(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws, cudaStream_t s,

@@ -29,6 +29,7 @@ struct Args {
   long long ks0, ks1, ks2, ks3;
   int N, D, G, Hkv, ub;
   int rb, hb, hn;  // staged calls: units [rb, ..) of the range, pass-1 q-heads [hb, hb + hn)
+  int qt1;         // pass 1: row tiles below qt1, the grid's x covering the last of them
   const uint8_t* kmask;
   long long kmb;
   const uint8_t* qmask;
@@ -147,8 +148,7 @@ __global__ void __launch_bounds__(NT) simt_lse_kernel(Args<Acc> a) {
   Acc* Qs = reinterpret_cast<Acc*>(smem_raw);  // [D][64]
   Acc* Ks = Qs + a.D * 64;                      // [D][64]
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-  const int ntile = (a.N + BM - 1) / BM;
-  const int r0 = (ntile - 1 - (int)blockIdx.x) * BM;  // long (late) rows first
+  const int r0 = (a.qt1 - 1 - (int)blockIdx.x) * BM;  // long (late) rows first
   const int hidx = (a.rb + (int)blockIdx.y / a.hn) * a.G + a.hb + (int)blockIdx.y % a.hn;  // (u - ub) * G + hh
   const int u = a.ub + hidx / a.G, hh = hidx % a.G;
   const int b = u / a.Hkv, g = u % a.Hkv, h = g * a.G + hh;
@@ -314,6 +314,7 @@ int launch_typed(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_
   a.rb = rr.rb;
   a.hb = rr.hb;
   a.hn = rr.nh;
+  a.qt1 = (rr.qe + BM - 1) / BM;
   const int U = rr.nu;  // units this launch runs
   const size_t smem1 = size_t(2) * p->D * 64 * sizeof(Acc);
   const size_t smem2 = smem1 + (64 + 16 * 64) * sizeof(Acc);
@@ -322,7 +323,7 @@ int launch_typed(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStream_
   if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1) != cudaSuccess ||
       cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2) != cudaSuccess)
     return KVBM_ERR_CUDA;
-  dim3 g1((p->N + BM - 1) / BM, U * a.hn);
+  dim3 g1(a.qt1 - rr.qb / BM, U * a.hn);
   if (o.run_pass1) {
     k1<<<g1, NT, smem1, s>>>(a);
     if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;

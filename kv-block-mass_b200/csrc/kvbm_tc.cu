@@ -95,6 +95,7 @@ struct TcArgs {
   int usel, ugroup;        // pass 1 (uniform grid): units run, units per CTA group
   int rb;                  // first unit run (relative to ub; staged calls run a sub-range)
   int hb, hn;              // pass 1 runs q-heads [hb, hb + hn) of each group
+  int qt0, nqts;           // and query tiles [qt0, qt0 + nqts) of each head (uniform grid)
   const int32_t* lens;     // ragged lengths [B] or null
   const int32_t* cu;       // packed row offsets [B+1] or null
   int kpacked;             // k packed like q
@@ -430,14 +431,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     hidx = item_hi(it) * a.G + item_mid(it);
     qt = item_lo(it);
   } else {
-    const int nt_all = a.Npad / TILE;
-    const long long per_group = (long long)a.ugroup * a.hn * nt_all;
+    const long long per_group = (long long)a.ugroup * a.hn * a.nqts;
     const int grp = (int)(blockIdx.x / per_group);
     const int r = (int)(blockIdx.x - grp * per_group);
     const int width = min(a.ugroup, a.usel - grp * a.ugroup) * a.hn;  // (unit, head) pairs of this group
     const int pr = r % width;
     hidx = (a.rb + grp * a.ugroup + pr / a.hn) * a.G + a.hb + pr % a.hn;
-    qt = nt_all - 1 - r / width;
+    qt = a.qt0 + a.nqts - 1 - r / width;
   }
   const int u = a.ub + hidx / a.G, hh = hidx % a.G;
   const int b = u / a.Hkv, g = u % a.Hkv, h = g * a.G + hh;
@@ -1292,6 +1292,8 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
   a.hb = rr.hb;
   a.hn = rr.nh;
   const int ntiles = a.Npad / TILE;
+  a.qt0 = rr.qb / TILE;
+  a.nqts = std::min(ntiles, (rr.qe + TILE - 1) / TILE) - a.qt0;
   // Pass-1 CTAs of a unit all stream its whole k (under causal_skip, from the
   // first tile up); running the units in groups whose k fits in L2 reads each
   // k from DRAM about once.  On the Llama-3-8B N=32768 shape (8 MiB of k per
@@ -1300,7 +1302,7 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
   const long long k_unit_bytes = (long long)Nk * Dr * (kOp == Op::TF32X3 ? 8 : 2);
   a.usel = U;
   a.ugroup = (int)std::max(1LL, std::min<long long>(U, kPass1GroupBytes / std::max(1LL, k_unit_bytes)));
-  const long long n1 = (long long)U * a.hn * ntiles, n2 = (long long)U * a.per_unit;
+  const long long n1 = (long long)U * a.hn * a.nqts, n2 = (long long)U * a.per_unit;
   if (n1 > 0x7fffffffLL || n2 > 0x7fffffffLL) return KVBM_ERR_SHAPE;
   dim3 grid1((unsigned)n1), grid2((unsigned)n2);
   if constexpr (kRagged) {

@@ -35,7 +35,7 @@ KVBM_STAGE_PASS1 = 2
 KVBM_STAGE_PASS2 = 4
 KVBM_STAGE_REDUCE = 8
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 # Symbols include/kvbm.h declares; tests check the library exports each one.
 EXPORTED = [
@@ -63,6 +63,7 @@ EXPORTED = [
     "kvbm_block_mass_ex",
     "kvbm_design_workspace_bytes",
     "kvbm_design",
+    "kvbm_copy_2d_async",
 ]
 
 
@@ -127,6 +128,8 @@ class Options(ctypes.Structure):
         ("run_unit_end", ctypes.c_int32),
         ("run_head_begin", ctypes.c_int32),
         ("run_head_end", ctypes.c_int32),
+        ("run_row_begin", ctypes.c_int32),
+        ("run_row_end", ctypes.c_int32),
     ]
 
 
@@ -237,6 +240,9 @@ def load() -> ctypes.CDLL:
                                 ctypes.c_size_t, ctypes.c_void_p]
     lib.kvbm_selftest_wait_timeout.restype = ctypes.c_int
     lib.kvbm_selftest_wait_timeout.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.POINTER(ctypes.c_int)]
+    lib.kvbm_copy_2d_async.restype = ctypes.c_int
+    lib.kvbm_copy_2d_async.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                       ctypes.c_int64, ctypes.c_void_p]
     lib.kvbm_check_device_errors.restype = ctypes.c_int
     lib.kvbm_check_device_errors.argtypes = [ctypes.c_void_p]
     if lib.kvbm_abi_version() != ABI_VERSION:

@@ -389,13 +389,15 @@ def _side_stream(dev: torch.device) -> torch.cuda.Stream:
 
 def run_staged(prep: _Prepared, stages: int, workspace: torch.Tensor, out: torch.Tensor | None = None,
                units: tuple[int, int] | None = None, heads: tuple[int, int] | None = None,
-               stream: torch.cuda.Stream | None = None) -> None:
+               stream: torch.cuda.Stream | None = None, rows: tuple[int, int] | None = None) -> None:
     """One staged launch of a prepared problem (``kvbm_options.stages``).
 
     ``stages`` is a mask of ``_lib.KVBM_STAGE_*``; ``units`` is a range of the
     problem's units (relative to its unit range) that passes 1 and 2 cover,
     ``heads`` a range of q-heads of each GQA group that pass 1 covers (needs a
-    one-unit ``units``).  Every piece writes into ``workspace``, which must be
+    one-unit ``units``), ``rows`` a range of query rows that pass 1 covers
+    (begin a multiple of 128, end a multiple of 128 or N; kernel paths 0 and
+    1).  Every piece writes into ``workspace``, which must be
     sized for the whole problem; the reduce stage then gives the bits of one
     whole call.
     """
@@ -403,6 +405,7 @@ def run_staged(prep: _Prepared, stages: int, workspace: torch.Tensor, out: torch
     o.stages = int(stages)
     o.run_unit_begin, o.run_unit_end = units if units is not None else (0, 0)
     o.run_head_begin, o.run_head_end = heads if heads is not None else (0, 0)
+    o.run_row_begin, o.run_row_end = rows if rows is not None else (0, 0)
     s = stream if stream is not None else torch.cuda.current_stream(prep.keep[0].device)
     try:
         code = _lib.load().kvbm_block_mass_ex(ctypes.byref(prep.prob), ctypes.byref(o),
@@ -410,22 +413,47 @@ def run_staged(prep: _Prepared, stages: int, workspace: torch.Tensor, out: torch
                                               workspace.numel(), s.cuda_stream)
     finally:
         o.stages = o.run_unit_begin = o.run_unit_end = o.run_head_begin = o.run_head_end = 0
+        o.run_row_begin = o.run_row_end = 0
     if code != _lib.KVBM_OK:
         _raise(code, prep.prob)
+
+
+def _host_pieces(U: int, G: int, N: int, by_rows: bool) -> list:
+    """The pieces of a host-input call: (unit, (head0, head1), (row0, row1) or
+    None, stages, whether the unit's k travels with it).
+
+    Unit 0 comes first in small pass-1 pieces, so that little is copied before
+    the first kernel starts: with ``by_rows`` (kernel paths 0 and 1, N >= 4096)
+    in pieces of query rows, the last rows first (pass 1 of rows [r0, r1)
+    reads k rows [0, r1), all of which arrive with the first piece, and its
+    work per byte of q grows with r1 under causal masking); otherwise q-head 0,
+    then the other q-heads.  Pass 2 of unit 0 follows its last piece; every
+    further unit is one piece with both passes.
+    """
+    P1, P2 = _lib.KVBM_STAGE_PASS1, _lib.KVBM_STAGE_PASS2
+    nr = max(1, min(8, N // 2048)) if by_rows else 1
+    if nr > 1:
+        R = ((N + nr - 1) // nr + 127) // 128 * 128
+        bounds = list(range(0, N, R)) + [N]
+        chunks = list(zip(bounds[:-1], bounds[1:]))[::-1]
+        pieces = [(0, (0, G), rr, P1, i == 0) for i, rr in enumerate(chunks)]
+    elif G > 1:
+        pieces = [(0, (0, 1), None, P1, True), (0, (1, G), None, P1, False)]
+    else:
+        pieces = [(0, (0, 1), None, P1, True)]
+    return pieces + [(u, (0, G), None, P1 | P2, True) for u in range(1, U)]
 
 
 def _from_host(q, k, dev, attn_mask, causal, block_size, scale, causal_skip, query_mask, workspace):
     """Host q/k (pinned or pageable): overlap the host-to-device copies with the kernels.
 
-    The copy stream moves the inputs one piece at a time while the kernels
-    run the pieces that have arrived, as staged calls into one workspace sized
-    for the whole problem; one bucket reduce at the end sums every unit, so the
-    result has the bits of ``kvbm_block_mass`` on the same values.  The pieces:
-    q-head 0 of unit 0 (batch 0, kv-head 0) with its k, then that unit's other
-    q-heads (pass 1 only, so that only one head's q is copied before the
-    first kernel starts), then pass 2 of unit 0, then every further unit with
-    both passes.  Consecutive pieces alternate between the caller's stream and
-    a second compute stream, so one piece's pass 1 fills the SMs its
+    The copy stream moves the inputs one piece at a time (``_host_pieces``)
+    while the kernels run the pieces that have arrived, as staged calls into
+    one workspace sized for the whole problem; one bucket reduce at the end
+    sums every unit, so the result has the bits of ``kvbm_block_mass`` on the
+    same values.  The first piece's copies are queued before the problem is
+    planned.  Consecutive pieces alternate between the caller's stream and a
+    second compute stream, so one piece's pass 1 fills the SMs its
     predecessor's last CTAs leave idle.
 
     Pageable tensors are staged through two pinned bounce buffers of one unit
@@ -446,41 +474,47 @@ def _from_host(q, k, dev, attn_mask, causal, block_size, scale, causal_skip, que
         copy = _copy_stream(dev)
         side = _side_stream(dev)
         copy.wait_stream(compute)  # qd/kd may reuse memory the compute stream still reads
-        am = None if attn_mask is None else attn_mask.to(dev, non_blocking=True)
-        qm = None if query_mask is None else query_mask.to(dev, non_blocking=True)
-        prep = make_problem(qd, kd, attn_mask=am, causal=causal, block_size=block_size, scale=scale,
-                            causal_skip=causal_skip, query_mask=qm)
-        need = workspace_bytes(prep)
-        ws = workspace if workspace is not None and workspace.numel() >= need else \
-            torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
-        out = torch.empty(prep.out_shape, dtype=prep.out_dtype, device=dev)
-        if prep.prob.pair_mask:
-            run_staged(prep, S.KVBM_STAGE_MASKS, ws, stream=compute)
-        side.wait_stream(compute)  # the masks, their bits, and anything the caller queued
-        streams = [compute, side]
-
-        # (unit, (head0, head1), stages, host copies): q-heads of one unit, plus its k
-        # with the piece whose heads start at 0
-        def piece_copies(u, h0, h1):
-            b, g = divmod(u, Hkv)
-            cps = [(qd[b, g * G + h0:g * G + h1], q[b, g * G + h0:g * G + h1])]
-            if h0 == 0:
-                cps.insert(0, (kd[b, g:g + 1], k[b, g:g + 1]))
-            return cps
-
-        if G > 1:
-            pieces = [(0, (0, 1), S.KVBM_STAGE_PASS1), (0, (1, G), S.KVBM_STAGE_PASS1)]
-        else:
-            pieces = [(0, (0, 1), S.KVBM_STAGE_PASS1 | S.KVBM_STAGE_PASS2)]
-        pieces += [(u, (0, G), S.KVBM_STAGE_PASS1 | S.KVBM_STAGE_PASS2) for u in range(1, B * Hkv)]
-
+        # fp32 may run the 3xTF32 path, which takes no row pieces; pageable
+        # tensors keep whole-head pieces (the host copies into the bounce
+        # buffers run faster in large pieces)
+        pieces = _host_pieces(B * Hkv, G, N, pinned and q.dtype != torch.float32)
         bounce, bounce_ev = None, [None, None]
         if not pinned:
             unit_bytes = (G * N * D * q.element_size()) + N * D * k.element_size()
             bounce = [torch.empty(unit_bytes, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
-        head0_done = None
-        for i, (u, (h0, h1), stages) in enumerate(pieces):
-            cps = piece_copies(u, h0, h1)
+
+        # pinned q/k whose rows are contiguous: a piece is one 2-D copy of q
+        # (the same rows of its q-heads) and one of k, with no tensor views
+        direct = pinned and q.stride(3) == 1 and q.stride(2) == D and k.stride(3) == 1 and k.stride(2) == D
+        lib, es = _lib.load(), q.element_size()
+
+        def copy2d(dst, d_off, d_pitch, src, s_off, s_pitch, width, height):
+            code = lib.kvbm_copy_2d_async(dst.data_ptr() + d_off * es, d_pitch * es, src.data_ptr() + s_off * es,
+                                          s_pitch * es, width * es, height, copy.cuda_stream)
+            if code != _lib.KVBM_OK:
+                raise RuntimeError(f"kvbm error {code}: {_lib.status_string(code)}")
+
+        def copies(i):
+            """Queue piece i's host-to-device copies; the event marks their end."""
+            u, (h0, h1), rows, _, with_k = pieces[i]
+            b, g = divmod(u, Hkv)
+            if direct:
+                r0, r1 = rows if rows is not None else (0, N)
+                if with_k:
+                    copy2d(kd, b * kd.stride(0) + g * kd.stride(1), 0, k, b * k.stride(0) + g * k.stride(1), 0,
+                           N * D, 1)
+                h = g * G + h0
+                copy2d(qd, b * qd.stride(0) + h * qd.stride(1) + r0 * D, qd.stride(1),
+                       q, b * q.stride(0) + h * q.stride(1) + r0 * D, q.stride(1), (r1 - r0) * D, h1 - h0)
+                ev = torch.cuda.Event()
+                ev.record(copy)
+                return ev
+            cps = [(kd[b, g], k[b, g])] if with_k else []
+            qu, qdu = q[b, g * G:(g + 1) * G], qd[b, g * G:(g + 1) * G]
+            if rows is None:  # whole heads: one contiguous copy
+                cps.append((qdu[h0:h1], qu[h0:h1]))
+            else:
+                cps += [(qdu[h, rows[0]:rows[1]], qu[h, rows[0]:rows[1]]) for h in range(h0, h1)]
             with torch.cuda.stream(copy):
                 if pinned:
                     for dst, src in cps:
@@ -500,16 +534,43 @@ def _from_host(q, k, dev, attn_mask, causal, block_size, scale, causal_skip, que
                     bounce_ev[j].record(copy)
                 ev = torch.cuda.Event()
                 ev.record(copy)
+            return ev
+
+        first = copies(0)
+        am = None if attn_mask is None else attn_mask.to(dev, non_blocking=True)
+        qm = None if query_mask is None else query_mask.to(dev, non_blocking=True)
+        prep = make_problem(qd, kd, attn_mask=am, causal=causal, block_size=block_size, scale=scale,
+                            causal_skip=causal_skip, query_mask=qm)
+        need = workspace_bytes(prep)
+        ws = workspace if workspace is not None and workspace.numel() >= need else \
+            torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
+        out = torch.empty(prep.out_shape, dtype=prep.out_dtype, device=dev)
+        if prep.prob.pair_mask:
+            run_staged(prep, S.KVBM_STAGE_MASKS, ws, stream=compute)
+        side.wait_stream(compute)  # the masks, their bits, and anything the caller queued
+        streams = [compute, side]
+        n0 = sum(1 for pc in pieces if pc[0] == 0)  # unit 0's pieces; its pass 2 follows the last
+        last = [None, None]  # the latest unit-0 piece on each compute stream
+        for i, (u, heads, rows, stages, _) in enumerate(pieces):
+            ev = first if i == 0 else copies(i)
             st = streams[i % 2]
             st.wait_event(ev)
-            run_staged(prep, stages, ws, units=(u, u + 1), heads=(h0, h1), stream=st)
-            if G > 1 and i == 0:
-                head0_done = torch.cuda.Event()
-                head0_done.record(st)
-            elif G > 1 and i == 1:
-                # pass 2 of unit 0 reads pass 1 of every one of its heads
-                st.wait_event(head0_done)
+            run_staged(prep, stages, ws, units=(u, u + 1), heads=heads, rows=rows, stream=st)
+            if i < n0 - 1:
+                last[i % 2] = torch.cuda.Event()
+                last[i % 2].record(st)
+            elif i == n0 - 1:
+                # pass 2 of unit 0 reads pass 1 of every one of its heads and rows
+                if last[(i + 1) % 2] is not None:
+                    st.wait_event(last[(i + 1) % 2])
                 run_staged(prep, S.KVBM_STAGE_PASS2, ws, units=(0, 1), stream=st)
+        if direct:
+            # one element of each through torch on the copy stream, after every
+            # piece: the host allocator then keeps the pinned blocks of q and k
+            # until the copies end, as it does for its own asynchronous copies
+            with torch.cuda.stream(copy):
+                qd[-1, -1, -1, -1:].copy_(q[-1, -1, -1, -1:], non_blocking=True)
+                kd[-1, -1, -1, -1:].copy_(k[-1, -1, -1, -1:], non_blocking=True)
         compute.wait_stream(side)
         run_staged(prep, S.KVBM_STAGE_REDUCE, ws, out=out, stream=compute)
         for t in (qd, kd, ws) + tuple(x for x in (am, qm) if x is not None):

@@ -27,7 +27,7 @@ def declared_functions():
 
 def test_library_loads():
     lib = _lib.load()
-    assert lib.kvbm_abi_version() == _lib.ABI_VERSION == 2
+    assert lib.kvbm_abi_version() == _lib.ABI_VERSION == 3
 
 
 def test_every_declared_symbol_is_exported():
@@ -255,6 +255,51 @@ def test_staged_option_checks(kw, code):
     lib = _lib.load()
     p = _problem()  # B=1, H_q=8, H_kv=2: 2 units of G=4 heads
     assert lib.kvbm_validate_ex(ctypes.byref(p), ctypes.byref(_opts(**kw))) == code
+
+
+@pytest.mark.parametrize("rows,code", [
+    ((0, 128), _lib.KVBM_OK),
+    ((128, 256), _lib.KVBM_OK),
+    ((256, 300), _lib.KVBM_OK),       # the end may be N
+    ((128, 300), _lib.KVBM_OK),
+    ((64, 128), _lib.KVBM_ERR_SHAPE),  # begin not a multiple of 128
+    ((0, 200), _lib.KVBM_ERR_SHAPE),   # end neither a multiple of 128 nor N
+    ((256, 384), _lib.KVBM_ERR_SHAPE),  # past N
+    ((-128, 128), _lib.KVBM_ERR_SHAPE),
+    ((128, 128), _lib.KVBM_OK),       # empty: every row
+])
+def test_staged_row_range_checks(rows, code):
+    """A pass-1 query-row range (kvbm_options.run_row_begin/end) is checked on the host."""
+    lib = _lib.load()
+    p = _problem(shape=(1, 8, 2, 300, 64), dtype=_lib.KVBM_BF16)
+    o = _opts(stages=_lib.KVBM_STAGE_PASS1, run_row_begin=rows[0], run_row_end=rows[1])
+    assert lib.kvbm_validate_ex(ctypes.byref(p), ctypes.byref(o)) == code
+
+
+def test_staged_row_range_excludes_the_lse_input():
+    lib = _lib.load()
+    p = _problem(shape=(1, 8, 2, 300, 64), dtype=_lib.KVBM_BF16)
+    lse = torch.zeros(1, 8, 300)
+    o = _opts(stages=_lib.KVBM_STAGE_PASS1, run_row_begin=0, run_row_end=128, lse=lse.data_ptr())
+    for i, s in enumerate(lse.stride()):
+        o.lse_stride[i] = s
+    assert lib.kvbm_validate_ex(ctypes.byref(p), ctypes.byref(o)) == _lib.KVBM_ERR_SHAPE
+    o.run_row_begin = o.run_row_end = 0
+    assert lib.kvbm_validate_ex(ctypes.byref(p), ctypes.byref(o)) == _lib.KVBM_OK
+
+
+def test_copy_2d_argument_checks():
+    """kvbm_copy_2d_async checks its arguments on the host; zero sizes queue nothing."""
+    lib = _lib.load()
+    buf = ctypes.create_string_buffer(64)
+    ptr = ctypes.addressof(buf)
+    assert lib.kvbm_copy_2d_async(None, 8, ptr, 8, 8, 2, None) == _lib.KVBM_ERR_NULL
+    assert lib.kvbm_copy_2d_async(ptr, 8, None, 8, 8, 2, None) == _lib.KVBM_ERR_NULL
+    assert lib.kvbm_copy_2d_async(ptr, 8, ptr, 8, -1, 2, None) == _lib.KVBM_ERR_SHAPE
+    assert lib.kvbm_copy_2d_async(ptr, 8, ptr, 8, 8, -2, None) == _lib.KVBM_ERR_SHAPE
+    assert lib.kvbm_copy_2d_async(ptr, 4, ptr, 8, 8, 2, None) == _lib.KVBM_ERR_SHAPE  # pitch below width
+    assert lib.kvbm_copy_2d_async(ptr, 8, ptr, 8, 0, 2, None) == _lib.KVBM_OK
+    assert lib.kvbm_copy_2d_async(ptr, 8, ptr, 8, 8, 0, None) == _lib.KVBM_OK
 
 
 def test_staged_calls_take_no_ragged_or_paged_inputs():

@@ -312,13 +312,15 @@ def test_llama3_70b_prefix_vs_oracle(cuda_device):
 
 @pytest.mark.parametrize("pinned", [True, False])
 @pytest.mark.parametrize("shape,dtype", [((1, 32, 8, 3000, 128), torch.bfloat16),
+                                         ((1, 8, 2, 9000, 128), torch.bfloat16),  # unit 0 by query rows
+                                         ((2, 4, 2, 4200, 32), torch.float64),    # SIMT, rows
                                          ((3, 8, 2, 777, 64), torch.bfloat16),
                                          ((2, 8, 2, 900, 64), torch.float32),    # 3xTF32: per-piece tf32 split
                                          ((2, 4, 4, 500, 96), torch.float32),    # 3xTF32, K-block slots
                                          ((2, 4, 2, 400, 160), torch.float32)])  # SIMT
 def test_host_inputs_give_the_device_call_bits(cuda_device, shape, dtype, pinned):
-    """Host q/k with device='cuda' are copied piece by piece (q-head 0 of unit 0,
-    its other heads, then unit by unit) while earlier pieces compute, as staged
+    """Host q/k with device='cuda' are copied piece by piece (unit 0 by query
+    rows or by heads, then unit by unit) while earlier pieces compute, as staged
     calls into one workspace with one reduce: the result has the bits of the
     device-input call.  Pageable tensors go through pinned bounce buffers."""
     B, Hq, Hkv, N, D = shape
@@ -337,6 +339,21 @@ def test_host_inputs_give_the_device_call_bits(cuda_device, shape, dtype, pinned
     assert torch.equal(a, b)
     c = kb.block_mass_b200(q, k, attn_mask=km, query_mask=qm, causal=True, block_size=64, device=cuda_device)
     assert torch.equal(a, c)
+
+
+@pytest.mark.parametrize("N", [700, 5000])
+def test_host_inputs_with_strided_rows(cuda_device, N):
+    """Pinned q/k whose rows are not contiguous per head (a [B, N, H, D] buffer
+    viewed as [B, H, N, D]) take the per-piece tensor copies instead of the
+    2-D copies; the result is still the device-input call's bits."""
+    B, Hq, Hkv, D = 1, 8, 2, 128
+    g = torch.Generator().manual_seed(N)
+    q = torch.randn(B, N, Hq, D, generator=g).to(torch.bfloat16).pin_memory().transpose(1, 2)
+    k = torch.randn(B, N, Hkv, D, generator=g).to(torch.bfloat16).pin_memory().transpose(1, 2)
+    assert q.is_pinned() and q.stride(2) != D
+    a = kb.block_mass_b200(q, k, causal=True, block_size=64, device=cuda_device)
+    b = run(q.to(cuda_device), k.to(cuda_device), causal=True, block_size=64)
+    assert torch.equal(a, b)
 
 
 @pytest.mark.parametrize("mask_kind", ["batch_pairs", "pairs", "none"])
@@ -409,6 +426,57 @@ def test_staged_pieces_on_two_streams(cuda_device, dtype, D, mask):
     run_staged(prep, 0, ws, out=out2)
     torch.cuda.synchronize()
     assert torch.equal(out2, whole)
+
+
+@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.float16, 64), (torch.float64, 32),
+                                     (torch.float32, 160)])
+@pytest.mark.parametrize("causal,skip", [(True, True), (True, False), (False, True)])
+def test_staged_row_pieces(cuda_device, dtype, D, causal, skip):
+    """kvbm_options.run_row_begin/end: pass 1 in pieces of query rows (in any
+    order, on two streams, rows of one piece ending at N or on a 128-row
+    boundary), then pass 2 and the reduce: the bits of one whole call."""
+    from kvblockmass_b200 import _lib
+    from kvblockmass_b200.ops import run_staged
+
+    B, Hq, Hkv, N = 2, 4, 2, 1000
+    g = torch.Generator().manual_seed(D + 7)
+    q = torch.randn(B, Hq, N, D, generator=g).to(dtype).to(cuda_device)
+    k = torch.randn(B, Hkv, N, D, generator=g).to(dtype).to(cuda_device)
+    km = (torch.rand(N, generator=g) > 0.1).to(cuda_device)
+    kw = dict(attn_mask=km, causal=causal, causal_skip=skip, block_size=48)
+    whole = run(q, k, **kw)
+    prep = kb.make_problem(q, k, **kw)
+    assert kb.kernel_path(prep) in (0, 1)
+    ws = torch.full((kb.workspace_bytes(prep),), 0xFF, dtype=torch.uint8, device=cuda_device)
+    out = torch.empty_like(whole)
+    s0 = torch.cuda.current_stream(cuda_device)
+    s1 = torch.cuda.Stream(device=cuda_device)
+    s1.wait_stream(s0)
+    chunks = [(768, 1000), (0, 256), (256, 768)]
+    for u in range(B * Hkv):
+        for i, rows in enumerate(chunks):
+            st = s0 if (u + i) % 2 else s1
+            run_staged(prep, _lib.KVBM_STAGE_PASS1, ws, units=(u, u + 1), rows=rows, stream=st)
+    s0.wait_stream(s1)
+    run_staged(prep, _lib.KVBM_STAGE_PASS2, ws, stream=s0)
+    run_staged(prep, _lib.KVBM_STAGE_REDUCE, ws, out=out, stream=s0)
+    torch.cuda.synchronize()
+    assert torch.equal(out, whole)
+
+
+def test_staged_row_range_is_refused_on_the_tf32_path(cuda_device):
+    """The 3xTF32 path converts whole rows of q/k to tf32 pairs in pass 1, so a
+    row range there is refused before any launch."""
+    from kvblockmass_b200 import _lib
+    from kvblockmass_b200.ops import run_staged
+
+    q = torch.randn(1, 4, 512, 64, device=cuda_device)
+    k = torch.randn(1, 2, 512, 64, device=cuda_device)
+    prep = kb.make_problem(q, k, causal=True, block_size=64)
+    assert kb.kernel_path(prep) == 2
+    ws = torch.empty(kb.workspace_bytes(prep), dtype=torch.uint8, device=cuda_device)
+    with pytest.raises(ValueError, match="sizes"):
+        run_staged(prep, _lib.KVBM_STAGE_PASS1, ws, units=(0, 1), rows=(0, 256))
 
 
 def test_causal_skip_is_engaged(cuda_device):
