@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define KVBM_ABI_VERSION 3
+#define KVBM_ABI_VERSION 4
 
 /* Only the entry points below are exported from libkvbm.so (it is built with
  * hidden default visibility). */
@@ -304,6 +304,20 @@ KVBM_API int kvbm_block_mass_paged(const kvbm_problem* p, const kvbm_paged_kv* k
  *                     row b the mass of sequence b alone (rows of sequences
  *                     outside the unit range are written as zeros)
  *   events            4 cudaEvent_t as kvbm_block_mass_events (or NULL)
+ *   method            KVBM_METHOD_* (0: automatic), how the mass is formed:
+ *                     TWO_PASS: pass 1 writes each row's lse2, pass 2
+ *                     recomputes the scores and sums 2^(s - lse2) per key
+ *                     (the reference's scheme, triton_kernel.py:69-145);
+ *                     ONE_PASS (tensor-core paths 1 and 2, block_size a
+ *                     multiple of 64, no LSE input): pass 1 also keeps, for
+ *                     each row, the log2-sum of 2^s over every 64-key segment
+ *                     it visits, and once the row's lse2 is final turns them
+ *                     into bucket partials, sum_i 2^(segment sum - lse2_i):
+ *                     the same mass from half the MMAs and exponentials.
+ *                     AUTO takes ONE_PASS where it applies and its workspace
+ *                     stays within 2x the two-pass one + 256 MiB, else
+ *                     TWO_PASS.  ONE_PASS on a problem it does not apply to
+ *                     is KVBM_ERR_SHAPE.
  *   stages, run_unit_begin/end, run_head_begin/end
  *                     staged execution (all zero: the whole call).  A caller
  *                     that receives a problem in pieces, e.g. copying it from
@@ -342,6 +356,9 @@ KVBM_API int kvbm_block_mass_paged(const kvbm_problem* p, const kvbm_paged_kv* k
 #define KVBM_STAGE_PASS1 2   /* row lse2, or the LSE import; fp32 path 2: tf32 split first */
 #define KVBM_STAGE_PASS2 4   /* per-key partials                                          */
 #define KVBM_STAGE_REDUCE 8  /* bucket reduce into mass_out                                */
+#define KVBM_METHOD_AUTO 0
+#define KVBM_METHOD_TWO_PASS 1
+#define KVBM_METHOD_ONE_PASS 2
 typedef struct kvbm_options {
   const float* lse;
   int64_t lse_stride[3];
@@ -358,6 +375,7 @@ typedef struct kvbm_options {
   int32_t run_head_end;
   int32_t run_row_begin;
   int32_t run_row_end;
+  int32_t method;
 } kvbm_options;
 
 /* Host-only checks of `p` with options `o` (o may be NULL). */
@@ -365,6 +383,12 @@ KVBM_API int kvbm_validate_ex(const kvbm_problem* p, const kvbm_options* o);
 
 /* Workspace bytes kvbm_block_mass_ex needs (0 on invalid input). */
 KVBM_API size_t kvbm_workspace_bytes_ex(const kvbm_problem* p, const kvbm_options* o);
+
+/* The method (KVBM_METHOD_TWO_PASS or KVBM_METHOD_ONE_PASS) a
+ * kvbm_block_mass_ex call of `p` with options `o` (may be NULL) takes on the
+ * current device, or a kvbm_status error code, negated.  Host-only.  No
+ * counterpart in the reference (it has only the two-pass scheme). */
+KVBM_API int kvbm_method(const kvbm_problem* p, const kvbm_options* o);
 
 /* Every option combined: dense, paged, padded-ragged or packed-varlen k/q,
  * optional LSE input, summed or per-sequence output.  `o` may be NULL (then

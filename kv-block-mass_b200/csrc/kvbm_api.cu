@@ -81,7 +81,38 @@ int select_path(const kvbm_problem* p, int device) {
   return 1;
 }
 
-WsLayout layout_for(const kvbm_problem* p, int path, const Ragged* rg) {
+// SM count of a device, cached like device_kind (0 when unknown).
+std::atomic<int> g_dev_sms[kMaxDevices] = {};
+
+int device_sms(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return 0;
+  int n = g_dev_sms[dev].load(std::memory_order_acquire);
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1) {
+      cudaGetLastError();
+      return 0;
+    }
+    g_dev_sms[dev].store(n, std::memory_order_release);
+  }
+  return n;
+}
+
+// SM count assumed when the device is unknown (sizes a workspace that fits
+// any sm_100 part).
+constexpr int kMaxSms = 160;
+
+bool one_pass_eligible(const kvbm_problem* p, int path, bool lse_input) {
+  return (path == 1 || path == 2) && !lse_input && p->block_size % kTcExpCols == 0;
+}
+
+WsLayout layout_for(const kvbm_problem* p, int path, const Ragged* rg, int method, int sms, bool lse_input,
+                    bool per_sequence) {
+  if (method == KVBM_METHOD_AUTO) {
+    if (!one_pass_eligible(p, path, lse_input)) return layout_for(p, path, rg, KVBM_METHOD_TWO_PASS, sms);
+    const WsLayout two = layout_for(p, path, rg, KVBM_METHOD_TWO_PASS, sms);
+    const WsLayout one = layout_for(p, path, rg, KVBM_METHOD_ONE_PASS, sms, false, per_sequence);
+    return one.total <= 2 * two.total + (size_t(256) << 20) ? one : two;
+  }
   WsLayout L;
   L.path = path;
   L.acc_bytes = (p->dtype == KVBM_F64) ? 8 : 4;
@@ -103,7 +134,30 @@ WsLayout layout_for(const kvbm_problem* p, int path, const Ragged* rg) {
   L.lse_bytes = U * G * n_lse * L.acc_bytes;
   L.part_off = align_up(L.lse_off + L.lse_bytes, 256);
   L.part_bytes = U * (size_t)L.nchunk * (size_t)p->N * L.acc_bytes;
-  L.split_off = align_up(L.part_off + L.part_bytes, 256);
+  L.one_pass = method == KVBM_METHOD_ONE_PASS && one_pass_eligible(p, path, lse_input);
+  if (L.one_pass) {
+    // partials per (head, query tile, bucket); segment sums per resident CTA
+    const size_t ntiles = n_lse / kTcTile;
+    const size_t nb = (size_t)kvbm_num_blocks(p->N, p->block_size);
+    L.part_bytes = U * G * ntiles * nb * 4;
+    L.seg_tiles = p->block_size % kTcTile == 0 ? p->block_size / kTcTile : 1;
+    L.seg_per_bucket = L.seg_tiles > 1 ? kTcTile / kTcExpCols : p->block_size / kTcExpCols;
+    L.slot_cols = (int)((ntiles + L.seg_tiles - 1) / L.seg_tiles) * (kTcTile / kTcExpCols);
+    L.slot_count = 2 * (sms > 0 ? sms : kMaxSms);
+    L.slot_off = align_up(L.part_off + L.part_bytes, 256);
+    L.slot_bytes = (size_t)L.slot_count * L.slot_cols * kTcTile * 4;
+    // first reduce step: enough (bucket group, split) CTAs to cover the SMs
+    const size_t b_out = per_sequence ? (size_t)p->B : 1;
+    const size_t groups = (nb + 31) / 32 * b_out;
+    const size_t items = U * G * ntiles;
+    size_t splits = (296 + groups - 1) / groups;
+    splits = splits < 1 ? 1 : (splits > 64 ? 64 : splits);
+    if (splits > items) splits = items;
+    L.red_splits = (int)splits;
+    L.red_off = align_up(L.slot_off + L.slot_bytes, 256);
+    L.red_bytes = splits * b_out * nb * 8;
+  }
+  L.split_off = align_up((L.one_pass ? L.red_off + L.red_bytes : L.part_off + L.part_bytes), 256);
   // path 2: tf32 hi/lo copies of every q and k row (packed operands: total_tokens rows per head)
   const bool q_packed = rg != nullptr && rg->cu != nullptr, k_packed = rg != nullptr && rg->k_packed;
   const size_t q_rows = q_packed ? (size_t)rg->total : (size_t)p->B * p->N;
@@ -136,11 +190,11 @@ WsLayout layout_for(const kvbm_problem* p, int path, const Ragged* rg) {
 
 // Largest workspace over the kernel paths `p`'s dtype can take: SIMT, plus
 // tcgen05 for bf16/fp16 (path 1) or 3xTF32 for fp32 (path 2).
-size_t max_layout_bytes(const kvbm_problem* p, const Ragged* rg = nullptr) {
+size_t max_layout_bytes(const kvbm_problem* p, const Ragged* rg, int method, bool lse_input, bool per_sequence) {
   size_t m = layout_for(p, 0, rg).total;
   const int tc = p->dtype == KVBM_F32 ? 2 : (p->dtype == KVBM_F64 ? 0 : 1);
   if (tc != 0) {
-    const size_t t = layout_for(p, tc, rg).total;
+    const size_t t = layout_for(p, tc, rg, method, 0, lse_input, per_sequence).total;
     m = t > m ? t : m;
   }
   return m;
@@ -341,16 +395,22 @@ int make_plan(const kvbm_problem* p, const kvbm_options* o, int dev, Plan* out) 
   pl.rg.k_packed = packed && kv == nullptr;
   pl.per_sequence = opt.per_sequence != 0;
   pl.B = p->B;
+  if (opt.method < KVBM_METHOD_AUTO || opt.method > KVBM_METHOD_ONE_PASS) return KVBM_ERR_SHAPE;
+  const bool lse_in = pl.lse != nullptr;
   size_t dense = 0;
   if (dev >= 0) {
     pl.path = select_path(&sub, dev);
     // a pass-1 row range on the 3xTF32 path would leave the tf32 copies of
     // the other rows unconverted
     if (pl.path == 2 && pl.staging.qe > pl.staging.qb) return KVBM_ERR_SHAPE;
-    pl.L = layout_for(&sub, pl.path, &pl.rg);
+    if (opt.method == KVBM_METHOD_ONE_PASS && !one_pass_eligible(&sub, pl.path, lse_in)) return KVBM_ERR_SHAPE;
+    pl.L = layout_for(&sub, pl.path, &pl.rg, opt.method, device_sms(dev), lse_in, pl.per_sequence);
     dense = pl.L.total;
   } else {
-    dense = max_layout_bytes(&sub, &pl.rg);
+    if (opt.method == KVBM_METHOD_ONE_PASS && !one_pass_eligible(&sub, sub.dtype == KVBM_F32 ? 2 : 1, lse_in))
+      return KVBM_ERR_SHAPE;
+    if (opt.method == KVBM_METHOD_ONE_PASS && sub.dtype == KVBM_F64) return KVBM_ERR_SHAPE;
+    dense = max_layout_bytes(&sub, &pl.rg, opt.method, lse_in, pl.per_sequence);
   }
   pl.gather_off = align_up(dense, 256);
   pl.total = pl.gather_off + pl.gather_bytes;
@@ -410,9 +470,9 @@ int plan_on_device(const kvbm_problem* p, const kvbm_options* o, Plan* pl) {
   return make_plan(p, o, dev, pl);
 }
 
-int planned_workspace_bytes(const kvbm_problem* p, size_t* bytes) {
+int planned_workspace_bytes(const kvbm_problem* p, size_t* bytes, const kvbm_options* o) {
   Plan pl;
-  const int st = plan_on_device(p, nullptr, &pl);
+  const int st = plan_on_device(p, o, &pl);
   if (st != KVBM_OK) return st;
   *bytes = pl.total;
   return KVBM_OK;
@@ -482,7 +542,8 @@ int kvbm_launches_per_call(const kvbm_problem* p) {
     dev = -1;
   }
   // pass 1 (lse2) or the lse import, pass 2 (per-key partials), bucket reduce,
-  // for 3xTF32 the split of q/k into tf32 pairs, for a pair mask its packing
+  // for 3xTF32 the split of q/k into tf32 pairs, for a pair mask its packing;
+  // the one-pass method has no pass 2 but reduces in two steps (same count)
   const int path = select_path(p, dev);
   return 3 + (path == 2 ? 1 : 0) + (path >= 1 && p->pair_mask != nullptr ? 1 : 0);
 }
@@ -549,6 +610,13 @@ size_t kvbm_workspace_bytes_ex(const kvbm_problem* p, const kvbm_options* o) {
   Plan pl;
   if (make_plan(p, o, dev, &pl) != KVBM_OK) return 0;
   return pl.total;
+}
+
+int kvbm_method(const kvbm_problem* p, const kvbm_options* o) {
+  Plan pl;
+  const int st = plan_on_device(p, o, &pl);
+  if (st != KVBM_OK) return -st;
+  return pl.L.one_pass ? KVBM_METHOD_ONE_PASS : KVBM_METHOD_TWO_PASS;
 }
 
 int kvbm_block_mass_ex(const kvbm_problem* p, const kvbm_options* o, void* mass_out, void* workspace,

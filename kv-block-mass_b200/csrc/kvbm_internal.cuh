@@ -59,6 +59,20 @@ struct WsLayout {
   size_t plan_off = 0, plan_bytes = 0;
   long long work1_cap = 0;               // pass-1 items: U * G * ceil(N / 128)
   long long work2_cap = 0;               // pass-2 items: U * (pass-2 CTAs of a full-length unit)
+  // One-pass method (tensor-core paths): pass 1 also turns its row sums into
+  // per-(head, query tile, bucket) partials, so there is no pass 2.
+  //   part region: [U_sel * G, ntiles, nb] fp32 partials (in place of the per-key ones)
+  //   slot region: [slot_count, slot_cols, 128] fp32 segment log-sums, one
+  //                slot per CTA resident at a time (2 per SM)
+  //   red region:  [red_splits, B_out, nb] fp64 sums of the first reduce step
+  bool one_pass = false;
+  size_t slot_off = 0, slot_bytes = 0;
+  size_t red_off = 0, red_bytes = 0;
+  int slot_count = 0;  // slots: 2 per SM of the device
+  int slot_cols = 0;   // segment sums per row of one slot
+  int seg_tiles = 1;   // key tiles one segment sum covers (F)
+  int seg_per_bucket = 0;
+  int red_splits = 0;  // item ranges of the first reduce step
   size_t total = 0;
   int path = 0;        // 0 SIMT, 1 tcgen05 (bf16/fp16), 2 tcgen05 3xTF32 (fp32)
   int qchunk = 0;      // query rows per mass-pass CTA
@@ -178,10 +192,15 @@ double exp2_fma_fraction();  // kvbm_tc.cu: share of exp2 evaluated on the FMA p
 int validate(const kvbm_problem* p);
 int select_path(const kvbm_problem* p, int device);
 // `rg` sizes the tf32 split copies of a packed q/k (path 2) by their rows.
-WsLayout layout_for(const kvbm_problem* p, int path, const Ragged* rg = nullptr);
+// `method` is a KVBM_METHOD_*; `sms` the device's SM count (0: unknown, the
+// largest supported count).
+WsLayout layout_for(const kvbm_problem* p, int path, const Ragged* rg = nullptr, int method = KVBM_METHOD_TWO_PASS,
+                    int sms = 0, bool lse_input = false, bool per_sequence = false);
+// Whether `p` can run the one-pass method on kernel path `path`.
+bool one_pass_eligible(const kvbm_problem* p, int path, bool lse_input);
 // Workspace bytes kvbm_block_mass needs for `p` on the current device (the
 // problem narrowed to the batches x kv-heads of its unit range).
-int planned_workspace_bytes(const kvbm_problem* p, size_t* bytes);
+int planned_workspace_bytes(const kvbm_problem* p, size_t* bytes, const kvbm_options* o = nullptr);
 
 // Launchers (return a kvbm_status).
 struct LaunchOpts {
@@ -224,7 +243,7 @@ int launch_tc(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws
 int launch_lse_import(const kvbm_problem* p, const WsLayout& L, const float* lse, const int64_t* lse_stride,
                       void* ws, cudaStream_t s, const Ragged& rg, const RunRange& rr);
 // per_sequence: mass_out is [B, num_blocks] (row b: the units of batch b in the range).
-int launch_reduce(const kvbm_problem* p, const WsLayout& L, void* mass_out, const void* ws,
+int launch_reduce(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws,
                   cudaStream_t s, bool per_sequence);
 
 // Device error word: set when a bounded wait in a tcgen05 kernel gives up.

@@ -438,6 +438,71 @@ __global__ void __launch_bounds__(256) reduce_seq_kernel(const Acc* part, Out* m
   if (threadIdx.x == 0) mass[(long long)b * nb + j] = static_cast<Out>(t);
 }
 
+// ---------------------------------------------------------------- one-pass reduce
+// The one-pass method leaves one partial per (head, query tile, bucket):
+// part1[item][j], item = hidx * ntiles + qt over the problem's (unit, q-head)
+// pairs hidx.  Step 1: CTA (bucket group, split, batch) sums the items of its
+// split for 32 consecutive buckets (a lane per bucket, coalesced rows); warp
+// w takes items i0 + w, i0 + w + 8, ... in order, kBatch loads in flight per
+// thread, and the 8 warps' sums add in warp order.  Under causal an item
+// whose last query row lies before the bucket's first key is not read (qt <
+// floor(j * bs / 128)): its pass-1 CTA wrote nothing there.  Step 2 adds the
+// splits in order.  Both steps accumulate in fp64: deterministic.
+__global__ void __launch_bounds__(256) tile_reduce_kernel(const float* part1, double* red, int nb, int bs,
+                                                          int ntiles, int G, int Hkv, int ub, int U, int causal,
+                                                          int splits, int per_seq) {
+  __shared__ double wsum[8][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int j = blockIdx.x * 32 + lane;
+  const int split = blockIdx.y, b = blockIdx.z;
+  long long h0 = 0, h1 = (long long)U * G;  // (unit, q-head) pairs of this output row
+  if (per_seq) {
+    const int u0 = max(ub, b * Hkv), u1 = min(ub + U, (b + 1) * Hkv);
+    h0 = (long long)(u0 - ub) * G;
+    h1 = u1 > u0 ? (long long)(u1 - ub) * G : h0;
+  }
+  const long long items = (h1 - h0) * ntiles;
+  const long long i0 = items * split / splits, i1 = items * (split + 1) / splits;
+  const int qmin = causal ? (int)(((long long)j * bs) / kTcTile) : 0;
+  double acc = 0.0;
+  if (i0 + w < i1) {
+    long long hid = h0 + (i0 + w) / ntiles;
+    int qt = (int)((i0 + w) % ntiles);
+    constexpr int kBatch = 8;
+    for (long long i = i0 + w; i < i1; i += 8 * kBatch) {
+      float v[kBatch];
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) {
+        const bool keep = i + 8LL * k < i1 && j < nb && qt >= qmin;
+        v[k] = keep ? part1[(hid * ntiles + qt) * nb + j] : 0.f;
+        qt += 8;
+        while (qt >= ntiles) {
+          qt -= ntiles;
+          ++hid;
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) acc += (double)v[k];
+    }
+  }
+  wsum[w][lane] = acc;
+  __syncthreads();
+  if (w == 0 && j < nb) {
+    double t = 0.0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += wsum[k][lane];
+    red[((long long)split * gridDim.z + b) * nb + j] = t;
+  }
+}
+
+__global__ void tile_reduce_final_kernel(const double* red, float* mass, int nb, int splits, int b_out) {
+  const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (idx >= (long long)b_out * nb) return;
+  double t = 0.0;
+  for (int sp = 0; sp < splits; ++sp) t += red[(long long)sp * b_out * nb + idx];
+  mass[idx] = (float)t;
+}
+
 }  // namespace
 
 int launch_simt(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws,
@@ -509,12 +574,26 @@ int launch_lse_import(const kvbm_problem* p, const WsLayout& L, const float* lse
   return cudaGetLastError() == cudaSuccess ? KVBM_OK : KVBM_ERR_CUDA;
 }
 
-int launch_reduce(const kvbm_problem* p, const WsLayout& L, void* mass_out, const void* ws,
+int launch_reduce(const kvbm_problem* p, const WsLayout& L, void* mass_out, void* ws,
                   cudaStream_t s, bool per_sequence) {
   if (L.key_tile <= 0 || (L.key_tile & (L.key_tile - 1)) != 0) return KVBM_ERR_SHAPE;  // power of two
   const int nb = (int)kvbm_num_blocks(p->N, p->block_size);
   const int U = p->unit_end - p->unit_begin;
   const char* base = static_cast<const char*>(ws) + L.part_off;
+  if (L.one_pass) {
+    const int b_out = per_sequence ? p->B : 1;
+    const int ntiles = (p->N + kTcTile - 1) / kTcTile;
+    double* red = reinterpret_cast<double*>(static_cast<char*>(ws) + L.red_off);
+    const dim3 grid((nb + 31) / 32, L.red_splits, b_out);
+    tile_reduce_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const float*>(base), red, nb, p->block_size, ntiles,
+                                            p->Hq / p->Hkv, p->Hkv, p->unit_begin, U, p->causal != 0,
+                                            L.red_splits, per_sequence ? 1 : 0);
+    if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
+    const long long n = (long long)b_out * nb;
+    tile_reduce_final_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(red, static_cast<float*>(mass_out), nb,
+                                                                       L.red_splits, b_out);
+    return cudaGetLastError() == cudaSuccess ? KVBM_OK : KVBM_ERR_CUDA;
+  }
   if (per_sequence) {
     const dim3 grid(nb, p->B);
     if (p->dtype == KVBM_F64)

@@ -254,6 +254,13 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// MUFU log2 (lg2.approx: 0 -> -inf; subnormal inputs flush to zero)
+__device__ __forceinline__ float lg2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // ---- packed fp32 pairs (sm_100 f32x2 instructions) ----
 __device__ __forceinline__ unsigned long long pk(float2 v) { return *reinterpret_cast<unsigned long long*>(&v); }
 __device__ __forceinline__ float2 upk(unsigned long long u) { return *reinterpret_cast<float2*>(&u); }

@@ -50,8 +50,16 @@ extern "C" int kvbm_block_mass_static(const kvbm_problem* p, void* mass_out, voi
   // The scratch a call needs covers only the batches x kv-heads of its unit
   // range: a range inside one batch entry needs its own units' rows.
   size_t need = 0;
-  const int pst = planned_workspace_bytes(p, &need);
+  int pst = planned_workspace_bytes(p, &need);
   if (pst != KVBM_OK) return pst;
+  // The one-pass method's segment slots and per-tile partials take more
+  // scratch than the two-pass method; the array may fit only the latter.
+  kvbm_options o{};
+  if (need > kStaticScratchBytes) {
+    o.method = KVBM_METHOD_TWO_PASS;
+    pst = planned_workspace_bytes(p, &need, &o);
+    if (pst != KVBM_OK) return pst;
+  }
   if (need > kStaticScratchBytes) return KVBM_ERR_SCRATCH;
   void* ptr = g_scratch_addr[dev].load(std::memory_order_acquire);
   if (ptr == nullptr) {
@@ -63,5 +71,5 @@ extern "C" int kvbm_block_mass_static(const kvbm_problem* p, void* mass_out, voi
     }
     g_scratch_addr[dev].store(ptr, std::memory_order_release);
   }
-  return kvbm_block_mass(p, mass_out, ptr, kStaticScratchBytes, stream);
+  return kvbm_block_mass_ex(p, &o, mass_out, ptr, kStaticScratchBytes, stream);
 }

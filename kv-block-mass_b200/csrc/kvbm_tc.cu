@@ -104,6 +104,17 @@ struct TcArgs {
   const unsigned long long* work1;  // pass 1: (unit, head, query tile), longest tiles first
   const unsigned long long* work2;  // pass 2: (unit, chunk, key tile), unit-major
   const long long* work_count;      // items in work1, work2
+  // One-pass method: pass 1 keeps, per row, the log2-sum of 2^(s*C) over each
+  // segment of seg_tiles key tiles x one exp thread's COLS columns in a slot
+  // of `slots`, and at the end turns them into the bucket partials `part1`.
+  int one_pass;
+  int nb, bs;              // buckets of the mass vector, block size
+  int seg_tiles;           // key tiles one segment covers (block_size / 128, or 1)
+  int seg_per_bucket;      // segments of one bucket
+  int slot_cols;           // segments per row of one slot
+  int slot_count;          // slots: 2 per SM (index 2 * %smid + TMEM half)
+  float* slots;            // [slot_count][slot_cols][128]
+  float* part1;            // [U_sel * G][Npad / 128][nb]
 };
 
 // A work item: three fields of 21 bits (units, heads, chunks and tiles all
@@ -411,7 +422,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint8_t* q_tile = smem;
   uint8_t* k_ring = smem + TB;
   float2* merge = reinterpret_cast<float2*>(smem + TB + SB * kStages);  // [kExpWG - 1][128] (m, l) of parts 1..
-  uint64_t* bars = reinterpret_cast<uint64_t*>(merge + (kExpWG - 1) * TILE);
+  float* lse_s = reinterpret_cast<float*>(merge + (kExpWG - 1) * TILE);  // [128] -lse2 (one pass)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(lse_s + TILE);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = k_full + kStages;
@@ -471,6 +483,21 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // One pass: this CTA's slot of segment sums.  At most two pass-1 CTAs are
+  // resident on an SM (each holds 256 of the 512 TMEM columns), and two
+  // disjoint 256-column allocations are exactly the two halves, so
+  // (SM, TMEM half) names one resident CTA.  A CTA reuses a slot only after
+  // the previous holder freed its TMEM, i.e. after its last read of the slot.
+  int slot = 0;
+  if (a.one_pass) {
+    uint32_t smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    slot = 2 * (int)smid + ((tmem & 0xFFFFu) >= 256u ? 1 : 0);
+    if (slot >= a.slot_count) {  // an SM id past the device's SM count: no slot (recorded, no work)
+      if (threadIdx.x == 0) atomicOr(&g_kvbm_device_error, 1u);
+      goto done;
+    }
+  }
 
   if (warp == 0) {
     if (lane == 0) {
@@ -535,6 +562,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint8_t* kmask = kMask == kMaskKeys ? a.kmask + b * a.kmb : nullptr;
     const uint32_t* prow = kMask == kMaskPairs ? a.prow + b * a.pb + (long long)row * a.W : nullptr;
     float m = -INFINITY, l = 0.f;
+    // one pass: the current segment's sum (relative to m), its index and the
+    // tile that starts the next segment
+    float* seg = a.one_pass ? a.slots + (size_t)slot * a.slot_cols * TILE + rl : nullptr;
+    float bacc = 0.f;
+    int cur = wg, seg_end = a.seg_tiles;
     for (int j = 0; j < nkt; ++j) {
       const int buf = j & 1;
       uint32_t kw[COLS / 32];
@@ -570,18 +602,30 @@ __global__ void __launch_bounds__(kThreads, 2)
           v[c] = keep ? v[c] : -INFINITY;
         }
       }
+      if (seg != nullptr && j == seg_end) {  // a new segment: store the finished one
+        __stcg(seg + (size_t)cur * TILE, m + lg2(bacc));
+        cur += kExpWG;
+        seg_end += a.seg_tiles;
+        bacc = 0.f;
+      }
       const float tmax = row_max(v);
       if (tmax != -INFINITY) {
         const float mt = tmax * a.C;
         // Rescale only when the running max grows: a fully masked tile leaves
         // (m, l) bit-identical, which keeps causal_skip on/off identical.
         if (mt > m) {
-          l = l * ex2(m - mt);
+          const float al = ex2(m - mt);
+          l = l * al;
+          bacc = bacc * al;
           m = mt;
         }
-        l += row_sum_exp2<exp2_degree<kOp>()>(v, a.C, -m);
+        const float t = row_sum_exp2<exp2_degree<kOp>()>(v, a.C, -m);
+        l += t;
+        bacc += t;
       }
     }
+    // log2 of the segment's sum of 2^(s*C): -inf when it kept no key
+    if (seg != nullptr) __stcg(seg + (size_t)cur * TILE, m + lg2(bacc));
     // Merge the column parts of each row (fixed order: part 0, then 1, 2, ...).
     if (wg > 0) merge[(wg - 1) * TILE + rl] = make_float2(m, l);
     exp_bar_sync();
@@ -595,10 +639,48 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (!dead && a.qmask != nullptr) dead = a.qmask[b * a.qmb + row] == 0;
       // Stored negated (pass 2 adds it): rows that keep no key, and padding
       // rows, get -inf, so 2^(t - lse2) = 0 for them.
-      a.lse[(long long)(hidx) * a.Npad + lse_tile_slot(row)] = dead ? -INFINITY : -(m + log2f(l));
+      const float nl = dead ? -INFINITY : -(m + log2f(l));
+      a.lse[(long long)(hidx) * a.Npad + lse_tile_slot(row)] = nl;
+      lse_s[rl] = nl;
+    }
+    if (a.one_pass) {
+      // Bucket partials of this query tile: part1[j] = sum over the 128 rows r
+      // and the segments sg of bucket j of 2^(seg[sg][r] - lse2[r]).  Warp w
+      // takes buckets w, w + 8, ...; lane l rows 4l .. 4l + 3 (one float4 of
+      // each segment), then a fixed xor tree over the lanes.  The buckets are
+      // those the reduce reads: under causal, every bucket whose first key is
+      // at most the tile's last row; a segment this CTA did not visit (past
+      // its causal bound) adds nothing, as a visited one past the diagonal
+      // adds exact zeros.
+      __threadfence_block();
+      exp_bar_sync();
+      const int ew = (warp - 2);
+      const float4 nl4 = reinterpret_cast<const float4*>(lse_s)[lane];
+      // rows that keep no key, and rows past the sequence (whose scores may
+      // come from padding of any value, NaN included), add exact zeros
+      const bool d0 = nl4.x == -INFINITY, d1 = nl4.y == -INFINITY, d2 = nl4.z == -INFINITY,
+                 d3 = nl4.w == -INFINITY;
+      const int nseg = ((nkt - 1) / a.seg_tiles + 1) * kExpWG;
+      const int nbw = a.causal ? min(a.nb, (r0 + TILE - 1) / a.bs + 1) : a.nb;
+      const float4* sbase = reinterpret_cast<const float4*>(a.slots + (size_t)slot * a.slot_cols * TILE) + lane;
+      float* dst = a.part1 + ((long long)hidx * (a.Npad / TILE) + qt) * a.nb;
+      for (int jb = ew; jb < nbw; jb += kExpThreads / 32) {
+        const int s0 = jb * a.seg_per_bucket, s1 = min(s0 + a.seg_per_bucket, nseg);
+        float acc = 0.f;
+        for (int sg = s0; sg < s1; ++sg) {
+          const float4 L = __ldcg(sbase + (size_t)sg * (TILE / 4));
+          const float e0 = d0 ? 0.f : ex2(L.x + nl4.x), e1 = d1 ? 0.f : ex2(L.y + nl4.y);
+          const float e2 = d2 ? 0.f : ex2(L.z + nl4.z), e3 = d3 ? 0.f : ex2(L.w + nl4.w);
+          acc += (e0 + e1) + (e2 + e3);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) dst[jb] = acc;
+      }
     }
   }
 
+done:
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
@@ -1176,7 +1258,7 @@ constexpr size_t kBarBytes = 8 * (1 + 2 * kStages + 4) + 16;  // mbarriers + TME
 template <int D, Op kOp>
 constexpr size_t smem_lse() {
   return 1024 + (size_t)Cfg<D, kOp>::kOperandBytes + (size_t)Cfg<D, kOp>::kSlotBytes * kStages +
-         (kExpWG - 1) * TILE * 8 + kBarBytes;
+         (kExpWG - 1) * TILE * 8 + TILE * 4 + kBarBytes;
 }
 template <int D, Op kOp>
 constexpr size_t smem_mass() {
@@ -1271,6 +1353,15 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
   a.total = rg.total;
   a.work1 = a.work2 = nullptr;
   a.work_count = nullptr;
+  a.one_pass = L.one_pass ? 1 : 0;
+  a.nb = (int)kvbm_num_blocks(p->N, p->block_size);
+  a.bs = p->block_size;
+  a.seg_tiles = L.seg_tiles;
+  a.seg_per_bucket = L.seg_per_bucket;
+  a.slot_cols = L.slot_cols;
+  a.slot_count = L.slot_count;
+  a.slots = L.one_pass ? reinterpret_cast<float*>(static_cast<char*>(ws) + L.slot_off) : nullptr;
+  a.part1 = L.one_pass ? a.part : nullptr;
   if (kMask == kMaskPairs) {
     uint32_t* bits = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + L.bits_off);
     const long long words = (long long)L.bits_batches * a.Npad * a.W;
@@ -1356,7 +1447,7 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
   }
   if (o.mid_event != nullptr && cudaEventRecord(static_cast<cudaEvent_t>(o.mid_event), s) != cudaSuccess)
     return KVBM_ERR_CUDA;
-  if (o.run_pass2) {
+  if (o.run_pass2 && !L.one_pass) {
     k2<<<grid2, kThreads, sm2, s>>>(tq, tq2, tk, tk2, a);
     if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
   }

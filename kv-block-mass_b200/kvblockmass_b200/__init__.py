@@ -26,6 +26,7 @@ from .ops import (  # noqa: F401
     block_mass_varlen,
     check_device_errors,
     kernel_path,
+    method_of,
     launches_per_call,
     make_paged_problem,
     make_problem,
@@ -53,6 +54,7 @@ __all__ = [
     "design_from_mass",
     "DeviceDesign",
     "kernel_path",
+    "method_of",
     "make_problem",
     "workspace_bytes",
     "launches_per_call",

@@ -34,8 +34,11 @@ KVBM_STAGE_MASKS = 1
 KVBM_STAGE_PASS1 = 2
 KVBM_STAGE_PASS2 = 4
 KVBM_STAGE_REDUCE = 8
+KVBM_METHOD_AUTO = 0
+KVBM_METHOD_TWO_PASS = 1
+KVBM_METHOD_ONE_PASS = 2
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 # Symbols include/kvbm.h declares; tests check the library exports each one.
 EXPORTED = [
@@ -64,6 +67,7 @@ EXPORTED = [
     "kvbm_design_workspace_bytes",
     "kvbm_design",
     "kvbm_copy_2d_async",
+    "kvbm_method",
 ]
 
 
@@ -130,6 +134,7 @@ class Options(ctypes.Structure):
         ("run_head_end", ctypes.c_int32),
         ("run_row_begin", ctypes.c_int32),
         ("run_row_end", ctypes.c_int32),
+        ("method", ctypes.c_int32),
     ]
 
 
@@ -243,6 +248,8 @@ def load() -> ctypes.CDLL:
     lib.kvbm_copy_2d_async.restype = ctypes.c_int
     lib.kvbm_copy_2d_async.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                        ctypes.c_int64, ctypes.c_void_p]
+    lib.kvbm_method.restype = ctypes.c_int
+    lib.kvbm_method.argtypes = [P, O]
     lib.kvbm_check_device_errors.restype = ctypes.c_int
     lib.kvbm_check_device_errors.argtypes = [ctypes.c_void_p]
     if lib.kvbm_abi_version() != ABI_VERSION:

@@ -26,7 +26,7 @@ from . import _lib
 __all__ = ["block_mass_b200", "block_mass_triton", "block_mass", "kernel_path", "make_problem",
            "workspace_bytes", "launches_per_call", "block_mass_paged", "make_paged_problem",
            "paged_workspace_bytes", "run_paged", "check_device_errors", "block_mass_varlen",
-           "make_varlen_problem", "run_prepared", "run_staged"]
+           "make_varlen_problem", "run_prepared", "run_staged", "method_of"]
 
 _DTYPES = {
     torch.float32: _lib.KVBM_F32,
@@ -195,9 +195,19 @@ def _validate_ex(prep: _Prepared):
         _raise(code, prep.prob)
 
 
+_METHODS = {None: 0, "auto": 0, "two_pass": 1, "one_pass": 2}
+
+
+def _set_method(prep: _Prepared, method) -> None:
+    if method not in _METHODS:
+        raise ValueError(f"method must be one of 'auto', 'two_pass', 'one_pass', got {method!r}")
+    if _METHODS[method]:
+        prep.options().method = _METHODS[method]
+
+
 def make_problem(q, k, attn_mask=None, causal=False, block_size=64, scale=None,
                  causal_skip=True, query_mask=None, units=None, seq_lens=None,
-                 per_sequence=False) -> _Prepared:
+                 per_sequence=False, method=None) -> _Prepared:
     """Validate arguments and build the C ``kvbm_problem`` for ``q``/``k``.
 
     Mask shapes (True = keep; combined with ``causal`` by AND):
@@ -207,7 +217,11 @@ def make_problem(q, k, attn_mask=None, causal=False, block_size=64, scale=None,
     contributes exactly 0, as a pair-mask row that keeps nothing would).
     ``seq_lens`` ``[B]``: sequence ``b`` is its first ``seq_lens[b] <= N``
     positions (ragged batch in the padded layout); ``per_sequence``: the
-    output is ``[B, num_blocks]``, one row per sequence.
+    output is ``[B, num_blocks]``, one row per sequence.  ``method``:
+    ``"two_pass"`` (row statistics, then a second pass over the scores),
+    ``"one_pass"`` (pass 1 keeps per-segment log-sums and forms the mass
+    itself; tensor-core paths, block_size a multiple of 64) or ``"auto"``
+    (None: one pass where it applies).
     """
     if not (isinstance(q, torch.Tensor) and isinstance(k, torch.Tensor)):
         raise TypeError("q and k must be torch tensors")
@@ -227,13 +241,14 @@ def make_problem(q, k, attn_mask=None, causal=False, block_size=64, scale=None,
     prep = _fill_problem(q.data_ptr(), q.stride(), k.data_ptr(), k.stride(), q.dtype, B, Hq, Hkv, N, D,
                          q.device, [q, k], attn_mask, causal, block_size, scale, causal_skip, query_mask, units)
     _set_ragged(prep, q.device, seq_lens=seq_lens, per_sequence=per_sequence)
+    _set_method(prep, method)
     _validate_ex(prep)
     return prep
 
 
 def make_varlen_problem(q, k, cu_seqlens, max_seqlen=None, attn_mask=None, causal=False, block_size=64,
                         scale=None, causal_skip=True, query_mask=None, units=None,
-                        per_sequence=False) -> _Prepared:
+                        per_sequence=False, method=None) -> _Prepared:
     """Packed (varlen) batch: ``q [T, H_q, D]``, ``k [T, H_kv, D]``, sequence ``b``
     is rows ``[cu_seqlens[b], cu_seqlens[b + 1])``.  ``max_seqlen`` (host int,
     read from ``cu_seqlens`` when omitted) is the bucket extent ``N``; masks
@@ -260,6 +275,7 @@ def make_varlen_problem(q, k, cu_seqlens, max_seqlen=None, attn_mask=None, causa
     prep = _fill_problem(q.data_ptr(), qs, k.data_ptr(), ks, q.dtype, B, Hq, Hkv, int(max_seqlen), D, q.device,
                          [q, k], attn_mask, causal, block_size, scale, causal_skip, query_mask, units)
     _set_ragged(prep, q.device, cu_seqlens=cu_seqlens, total=T, per_sequence=per_sequence)
+    _set_method(prep, method)
     _validate_ex(prep)
     return prep
 
@@ -274,6 +290,15 @@ def workspace_bytes(prep: _Prepared) -> int:
 def kernel_path(prep: _Prepared) -> int:
     """0 = SIMT kernels, 1 = tcgen05 tensor-core kernels, 2 = tcgen05 3xTF32 (current device)."""
     return int(_lib.load().kvbm_kernel_path(ctypes.byref(prep.prob)))
+
+
+def method_of(prep: _Prepared) -> str:
+    """``"one_pass"`` or ``"two_pass"``: how the current device runs ``prep``."""
+    opts = ctypes.byref(prep.opts) if prep.opts is not None else None
+    code = int(_lib.load().kvbm_method(ctypes.byref(prep.prob), opts))
+    if code < 0:
+        _raise(-code, prep.prob)
+    return "one_pass" if code == _lib.KVBM_METHOD_ONE_PASS else "two_pass"
 
 
 def launches_per_call(prep: _Prepared) -> int:
@@ -337,7 +362,7 @@ def run_prepared(prep: _Prepared, out: torch.Tensor | None = None,
 def block_mass_b200(q, k, attn_mask=None, causal=False, block_size=64, scale=None,
                     causal_skip=True, query_mask=None, *, BLOCK_M=None, BLOCK_N=None,
                     query_chunk=None, device=None, units=None, out=None, workspace=None, lse=None,
-                    seq_lens=None, per_sequence=False):
+                    seq_lens=None, per_sequence=False, method=None):
     """Block-pooled column sums of the softmax attention matrix on a B200.
 
     Returns ``mass [ceil(N / block_size)]`` (float32; float64 for float64
@@ -349,6 +374,7 @@ def block_mass_b200(q, k, attn_mask=None, causal=False, block_size=64, scale=Non
     statistics pass: about half the work.  ``seq_lens [B]`` makes the batch
     ragged (sequence ``b`` is its first ``seq_lens[b]`` positions; the padding
     is never read into a pair); ``per_sequence`` returns ``[B, num_blocks]``.
+    ``method`` as for ``make_problem``.
     """
     del BLOCK_M, BLOCK_N, query_chunk  # tiling is fixed by the kernels
     if device is not None:
@@ -360,14 +386,14 @@ def block_mass_b200(q, k, attn_mask=None, causal=False, block_size=64, scale=Non
                 and not per_sequence and q.numel() > 0 and k.numel() > 0):
             return _from_host(q, k, dev, attn_mask=attn_mask, causal=causal, block_size=block_size,
                               scale=scale, causal_skip=causal_skip, query_mask=query_mask,
-                              workspace=workspace)
+                              workspace=workspace, method=method)
         q, k = q.to(dev), k.to(dev)
     if not (q.is_cuda and k.is_cuda):
         raise ValueError("block_mass_b200 needs CUDA tensors (there is no CPU path); "
                          "pass device='cuda' or use the reference's block_mass_reference")
     prep = make_problem(q, k, attn_mask=attn_mask, causal=causal, block_size=block_size,
                         scale=scale, causal_skip=causal_skip, query_mask=query_mask, units=units,
-                        seq_lens=seq_lens, per_sequence=per_sequence)
+                        seq_lens=seq_lens, per_sequence=per_sequence, method=method)
     return run_prepared(prep, out=out, workspace=workspace, lse=lse)
 
 
@@ -444,7 +470,7 @@ def _host_pieces(U: int, G: int, N: int, by_rows: bool) -> list:
     return pieces + [(u, (0, G), None, P1 | P2, True) for u in range(1, U)]
 
 
-def _from_host(q, k, dev, attn_mask, causal, block_size, scale, causal_skip, query_mask, workspace):
+def _from_host(q, k, dev, attn_mask, causal, block_size, scale, causal_skip, query_mask, workspace, method=None):
     """Host q/k (pinned or pageable): overlap the host-to-device copies with the kernels.
 
     The copy stream moves the inputs one piece at a time (``_host_pieces``)
@@ -540,7 +566,7 @@ def _from_host(q, k, dev, attn_mask, causal, block_size, scale, causal_skip, que
         am = None if attn_mask is None else attn_mask.to(dev, non_blocking=True)
         qm = None if query_mask is None else query_mask.to(dev, non_blocking=True)
         prep = make_problem(qd, kd, attn_mask=am, causal=causal, block_size=block_size, scale=scale,
-                            causal_skip=causal_skip, query_mask=qm)
+                            causal_skip=causal_skip, query_mask=qm, method=method)
         need = workspace_bytes(prep)
         ws = workspace if workspace is not None and workspace.numel() >= need else \
             torch.empty(max(need, 256), dtype=torch.uint8, device=dev)

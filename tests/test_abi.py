@@ -27,7 +27,7 @@ def declared_functions():
 
 def test_library_loads():
     lib = _lib.load()
-    assert lib.kvbm_abi_version() == _lib.ABI_VERSION == 3
+    assert lib.kvbm_abi_version() == _lib.ABI_VERSION == 4
 
 
 def test_every_declared_symbol_is_exported():
@@ -257,6 +257,54 @@ def test_staged_option_checks(kw, code):
     assert lib.kvbm_validate_ex(ctypes.byref(p), ctypes.byref(_opts(**kw))) == code
 
 
+@pytest.mark.parametrize("pkw,okw,code", [
+    (dict(dtype=_lib.KVBM_BF16), dict(method=_lib.KVBM_METHOD_ONE_PASS), _lib.KVBM_OK),
+    (dict(dtype=_lib.KVBM_F32), dict(method=_lib.KVBM_METHOD_ONE_PASS), _lib.KVBM_OK),
+    (dict(dtype=_lib.KVBM_BF16, block_size=256), dict(method=_lib.KVBM_METHOD_ONE_PASS), _lib.KVBM_OK),
+    (dict(dtype=_lib.KVBM_BF16, block_size=192), dict(method=_lib.KVBM_METHOD_ONE_PASS), _lib.KVBM_OK),
+    # one pass needs block_size % 64 == 0, tensor-core dtypes and no LSE input
+    (dict(dtype=_lib.KVBM_BF16, block_size=48), dict(method=_lib.KVBM_METHOD_ONE_PASS), _lib.KVBM_ERR_SHAPE),
+    (dict(dtype=_lib.KVBM_F64), dict(method=_lib.KVBM_METHOD_ONE_PASS), _lib.KVBM_ERR_SHAPE),
+    (dict(dtype=_lib.KVBM_BF16), dict(method=_lib.KVBM_METHOD_ONE_PASS, lse=0x10000), _lib.KVBM_ERR_SHAPE),
+    (dict(dtype=_lib.KVBM_BF16, block_size=48), dict(method=_lib.KVBM_METHOD_AUTO), _lib.KVBM_OK),
+    (dict(dtype=_lib.KVBM_BF16), dict(method=_lib.KVBM_METHOD_TWO_PASS), _lib.KVBM_OK),
+    (dict(dtype=_lib.KVBM_BF16), dict(method=3), _lib.KVBM_ERR_SHAPE),
+    (dict(dtype=_lib.KVBM_BF16), dict(method=-1), _lib.KVBM_ERR_SHAPE),
+])
+def test_method_option_checks(pkw, okw, code):
+    """kvbm_options.method is checked on the host: the one-pass method needs a
+    tensor-core dtype, a block size that is a multiple of 64 and no LSE input."""
+    lib = _lib.load()
+    o = _lib.Options()
+    for name, v in okw.items():
+        setattr(o, name, v)
+    p = _problem(**pkw)
+    assert lib.kvbm_validate_ex(ctypes.byref(p), ctypes.byref(o)) == code
+
+
+def test_one_pass_workspace_holds_slots_and_tile_partials():
+    """With the device unknown the workspace covers the one-pass layout: its
+    per-tile partials [U*G, ceil(N/128), nb] fp32 and 2 x 160 slots of
+    [ceil(N/128) / F * 2, 128] fp32 segment sums, where F = block_size / 128
+    (or 1)."""
+    lib = _lib.load()
+    for bs in (64, 256):
+        N, Hq, Hkv = 32768, 32, 8
+        p = _problem(shape=(1, Hq, Hkv, N, 128), dtype=_lib.KVBM_BF16, block_size=bs)
+        one = lib.kvbm_workspace_bytes_ex(ctypes.byref(p), ctypes.byref(_opts(method=_lib.KVBM_METHOD_ONE_PASS)))
+        two = lib.kvbm_workspace_bytes_ex(ctypes.byref(p), ctypes.byref(_opts(method=_lib.KVBM_METHOD_TWO_PASS)))
+        auto = lib.kvbm_workspace_bytes_ex(ctypes.byref(p), ctypes.byref(_opts()))
+        nt, nb = N // 128, N // bs
+        F = max(1, bs // 128)
+        part1 = Hq * nt * nb * 4
+        slots = 2 * 160 * (nt // F * 2) * 128 * 4
+        assert one >= part1 + slots + Hq * N * 4
+        assert auto == one and two <= one
+        if bs == 64:  # larger than every SIMT layout (which an unknown device could also take)
+            assert one < part1 + slots + Hq * N * 4 + (8 << 20)
+            assert two < one
+
+
 @pytest.mark.parametrize("rows,code", [
     ((0, 128), _lib.KVBM_OK),
     ((128, 256), _lib.KVBM_OK),
@@ -316,11 +364,17 @@ def test_unit_range_workspace_covers_only_its_rows():
     """The workspace of a unit range inside one batch entry holds only those
     units' rows: an fp32 problem's tf32 copies (path 2) shrink with the range,
     so a one-unit slice of a problem too large for the no-allocation entry
-    point's 64 MiB fits it."""
+    point's 64 MiB fits it (with the two-pass method, which that entry point
+    falls back to when the one-pass slots do not fit)."""
     lib = _lib.load()
+    two_pass = _opts(method=_lib.KVBM_METHOD_TWO_PASS)
+
+    def ws(p):
+        return lib.kvbm_workspace_bytes_ex(ctypes.byref(p), ctypes.byref(two_pass))
+
     shape = (1, 32, 8, 8192, 64)  # fp32 D=64 runs the 3xTF32 path
-    full = lib.kvbm_workspace_bytes(ctypes.byref(_problem(shape=shape)))
-    one = lib.kvbm_workspace_bytes(ctypes.byref(_problem(shape=shape, units=(3, 4))))
+    full = ws(_problem(shape=shape))
+    one = ws(_problem(shape=shape, units=(3, 4)))
     limit = lib.kvbm_static_scratch_bytes()
     assert full > limit >= one
     # lse2 + partials + tf32 hi/lo of the unit's 4 q-heads and its kv-head (a bound, all paths)
@@ -328,4 +382,4 @@ def test_unit_range_workspace_covers_only_its_rows():
     assert one <= (G * N + 64 * N) * 4 + 2 * 4 * D * N * (G + 1) + 4096
     # a range that crosses a batch entry keeps whole batch entries
     two_b = _problem(shape=(2, 32, 8, 8192, 64), units=(7, 9))
-    assert lib.kvbm_workspace_bytes(ctypes.byref(two_b)) > one
+    assert ws(two_b) > one
