@@ -175,7 +175,8 @@ KVBM_API int kvbm_block_mass_lse(const kvbm_problem* p, const float* lse, const 
 /* kvbm_block_mass that also records up to four CUDA events (cudaEvent_t,
  * each may be NULL) on `stream`: events[0] before pass 1, events[1] between
  * pass 1 and pass 2, events[2] between pass 2 and the bucket reduce,
- * events[3] after the reduce.  Per-kernel timing for benchmarks; it replaces
+ * events[3] after the reduce (with the one-pass method events[1] and [2] mark
+ * the same point).  Per-kernel timing for benchmarks; it replaces
  * the CUDA-event timing of the reference's bench (bench/bench_block_mass.py:37-54)
  * at kernel rather than call granularity. */
 KVBM_API int kvbm_block_mass_events(const kvbm_problem* p, void* mass_out, void* workspace,
@@ -201,9 +202,10 @@ KVBM_API double kvbm_exp2_fma_fraction(void);
  * afford cudaMalloc/cudaFree in its step loop because they synchronise the
  * device and stall its other streams.  A C/FFI host may hold only the input and
  * output pointers another framework gave it.  Such callers still pass q, k, the
- * masks and `mass_out`; the scratch the two passes need (the per-row lse2 values
- * and per-key partial sums) comes from a fixed device array inside this
- * library instead of a caller workspace.
+ * masks and `mass_out`; the scratch the passes need (the per-row lse2 values
+ * and the partial sums) comes from a fixed device array inside this library
+ * instead of a caller workspace.  The call takes the two-pass method
+ * (KVBM_METHOD_TWO_PASS) when the one-pass method's scratch does not fit.
  *
  * Limit: the array holds kvbm_static_scratch_bytes() bytes (64 MiB).  Every
  * GPU that loads the library holds it until the process exits.  A problem
@@ -353,8 +355,9 @@ KVBM_API int kvbm_block_mass_paged(const kvbm_problem* p, const kvbm_paged_kv* k
  * reference run on each sequence alone (its first seq_lens[b] positions);
  * buckets j >= ceil(len / block_size) of a sequence get 0 from it. */
 #define KVBM_STAGE_MASKS 1   /* pack a pair mask into bits (tensor-core paths)             */
-#define KVBM_STAGE_PASS1 2   /* row lse2, or the LSE import; fp32 path 2: tf32 split first */
-#define KVBM_STAGE_PASS2 4   /* per-key partials                                          */
+#define KVBM_STAGE_PASS1 2   /* row lse2, or the LSE import; fp32 path 2: tf32 split first;
+                                one pass: also the bucket partials                       */
+#define KVBM_STAGE_PASS2 4   /* per-key partials (two passes; launches nothing with one)   */
 #define KVBM_STAGE_REDUCE 8  /* bucket reduce into mass_out                                */
 #define KVBM_METHOD_AUTO 0
 #define KVBM_METHOD_TWO_PASS 1

@@ -664,18 +664,36 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int nbw = a.causal ? min(a.nb, (r0 + TILE - 1) / a.bs + 1) : a.nb;
       const float4* sbase = reinterpret_cast<const float4*>(a.slots + (size_t)slot * a.slot_cols * TILE) + lane;
       float* dst = a.part1 + ((long long)hidx * (a.Npad / TILE) + qt) * a.nb;
-      for (int jb = ew; jb < nbw; jb += kExpThreads / 32) {
-        const int s0 = jb * a.seg_per_bucket, s1 = min(s0 + a.seg_per_bucket, nseg);
-        float acc = 0.f;
-        for (int sg = s0; sg < s1; ++sg) {
-          const float4 L = __ldcg(sbase + (size_t)sg * (TILE / 4));
-          const float e0 = d0 ? 0.f : ex2(L.x + nl4.x), e1 = d1 ? 0.f : ex2(L.y + nl4.y);
-          const float e2 = d2 ? 0.f : ex2(L.z + nl4.z), e3 = d3 ? 0.f : ex2(L.w + nl4.w);
-          acc += (e0 + e1) + (e2 + e3);
+      // kEpiU buckets per warp at a time, their loads issued together (one
+      // L2 round trip per group instead of per bucket); a segment past the
+      // CTA's last adds +0, as if it had not been read
+      constexpr int kEpiU = 8, kEw = kExpThreads / 32;
+      for (int base = ew; base < nbw; base += kEw * kEpiU) {
+        float acc[kEpiU];
+#pragma unroll
+        for (int u = 0; u < kEpiU; ++u) acc[u] = 0.f;
+        for (int so = 0; so < a.seg_per_bucket; ++so) {
+          float4 L[kEpiU];
+#pragma unroll
+          for (int u = 0; u < kEpiU; ++u) {
+            const int jb = base + kEw * u, sg = jb * a.seg_per_bucket + so;
+            L[u] = (jb < nbw && sg < nseg) ? __ldcg(sbase + (size_t)sg * (TILE / 4))
+                                           : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+          }
+#pragma unroll
+          for (int u = 0; u < kEpiU; ++u) {
+            const float e0 = d0 ? 0.f : ex2(L[u].x + nl4.x), e1 = d1 ? 0.f : ex2(L[u].y + nl4.y);
+            const float e2 = d2 ? 0.f : ex2(L[u].z + nl4.z), e3 = d3 ? 0.f : ex2(L[u].w + nl4.w);
+            acc[u] += (e0 + e1) + (e2 + e3);
+          }
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (lane == 0) dst[jb] = acc;
+        for (int u = 0; u < kEpiU; ++u) {
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], o);
+          const int jb = base + kEw * u;
+          if (lane == 0 && jb < nbw) dst[jb] = acc[u];
+        }
       }
     }
   }

@@ -453,8 +453,11 @@ def _host_pieces(U: int, G: int, N: int, by_rows: bool) -> list:
     in pieces of query rows, the last rows first (pass 1 of rows [r0, r1)
     reads k rows [0, r1), all of which arrive with the first piece, and its
     work per byte of q grows with r1 under causal masking); otherwise q-head 0,
-    then the other q-heads.  Pass 2 of unit 0 follows its last piece; every
-    further unit is one piece with both passes.
+    then the other q-heads.  With ``by_rows`` the last unit is cut the same
+    way, so the piece copied last is its first rows, whose kernels are short:
+    little work is left once the last copy lands.  A unit cut into pieces runs
+    pass 2 after its last piece; every other unit is one piece with both
+    passes.
     """
     P1, P2 = _lib.KVBM_STAGE_PASS1, _lib.KVBM_STAGE_PASS2
     nr = max(1, min(8, N // 2048)) if by_rows else 1
@@ -462,8 +465,13 @@ def _host_pieces(U: int, G: int, N: int, by_rows: bool) -> list:
         R = ((N + nr - 1) // nr + 127) // 128 * 128
         bounds = list(range(0, N, R)) + [N]
         chunks = list(zip(bounds[:-1], bounds[1:]))[::-1]
-        pieces = [(0, (0, G), rr, P1, i == 0) for i, rr in enumerate(chunks)]
-    elif G > 1:
+
+        def by_row(u):
+            return [(u, (0, G), rr, P1, i == 0) for i, rr in enumerate(chunks)]
+
+        return by_row(0) + [(u, (0, G), None, P1 | P2, True) for u in range(1, U - 1)] + \
+            (by_row(U - 1) if U > 1 else [])
+    if G > 1:
         pieces = [(0, (0, 1), None, P1, True), (0, (1, G), None, P1, False)]
     else:
         pieces = [(0, (0, 1), None, P1, True)]
@@ -575,21 +583,25 @@ def _from_host(q, k, dev, attn_mask, causal, block_size, scale, causal_skip, que
             run_staged(prep, S.KVBM_STAGE_MASKS, ws, stream=compute)
         side.wait_stream(compute)  # the masks, their bits, and anything the caller queued
         streams = [compute, side]
-        n0 = sum(1 for pc in pieces if pc[0] == 0)  # unit 0's pieces; its pass 2 follows the last
-        last = [None, None]  # the latest unit-0 piece on each compute stream
+        # units cut into pass-1 pieces: their pass 2 follows their last piece
+        last_piece = {pc[0]: i for i, pc in enumerate(pieces) if not pc[3] & S.KVBM_STAGE_PASS2}
+        latest = {}  # (unit, stream index) -> event after that unit's latest piece there
         for i, (u, heads, rows, stages, _) in enumerate(pieces):
             ev = first if i == 0 else copies(i)
             st = streams[i % 2]
             st.wait_event(ev)
             run_staged(prep, stages, ws, units=(u, u + 1), heads=heads, rows=rows, stream=st)
-            if i < n0 - 1:
-                last[i % 2] = torch.cuda.Event()
-                last[i % 2].record(st)
-            elif i == n0 - 1:
-                # pass 2 of unit 0 reads pass 1 of every one of its heads and rows
-                if last[(i + 1) % 2] is not None:
-                    st.wait_event(last[(i + 1) % 2])
-                run_staged(prep, S.KVBM_STAGE_PASS2, ws, units=(0, 1), stream=st)
+            if u not in last_piece:
+                continue
+            if i < last_piece[u]:
+                latest[(u, i % 2)] = torch.cuda.Event()
+                latest[(u, i % 2)].record(st)
+            else:
+                # pass 2 of the unit reads pass 1 of every one of its heads and rows
+                other = latest.get((u, (i + 1) % 2))
+                if other is not None:
+                    st.wait_event(other)
+                run_staged(prep, S.KVBM_STAGE_PASS2, ws, units=(u, u + 1), stream=st)
         if direct:
             # one element of each through torch on the copy stream, after every
             # piece: the host allocator then keeps the pinned blocks of q and k

@@ -13,29 +13,35 @@ P1, P2 = _lib.KVBM_STAGE_PASS1, _lib.KVBM_STAGE_PASS2
                                             (4, 1, 700, False), (1, 2, 5000, True)])
 def test_pieces_cover_every_head_and_row_once(U, G, N, by_rows):
     pieces = _host_pieces(U, G, N, by_rows)
-    # unit 0 first, in pass-1 pieces; every further unit is one piece with both passes
-    u0 = [pc for pc in pieces if pc[0] == 0]
-    assert pieces[:len(u0)] == u0
-    assert [pc[0] for pc in pieces[len(u0):]] == list(range(1, U))
-    assert all(pc[3] == P1 | P2 and pc[1] == (0, G) and pc[2] is None and pc[4] for pc in pieces[len(u0):])
-    assert all(pc[3] == P1 for pc in u0)
-    # k travels with the first piece of unit 0 only
-    assert [pc[4] for pc in u0] == [True] + [False] * (len(u0) - 1)
-    # every (head, row) of unit 0 exactly once
-    cover = {}
-    for _, (h0, h1), rows, _, _ in u0:
-        r0, r1 = rows if rows is not None else (0, N)
-        assert 0 <= r0 < r1 <= N and r0 % 128 == 0 and (r1 % 128 == 0 or r1 == N)
-        for h in range(h0, h1):
-            cover.setdefault(h, []).append((r0, r1))
-    assert sorted(cover) == list(range(G))
-    for h, rr in cover.items():
-        rr.sort()
-        assert rr[0][0] == 0 and rr[-1][1] == N
-        assert all(a[1] == b[0] for a, b in zip(rr, rr[1:]))
-    # row pieces only where asked for and long enough; the last rows come first
-    rowed = any(pc[2] is not None for pc in u0)
-    assert rowed == (by_rows and N >= 4096)
-    if rowed:
-        assert 2 <= len(u0) <= 8
-        assert [pc[2] for pc in u0] == sorted((pc[2] for pc in u0), reverse=True)
+    rowed = by_rows and N >= 4096  # row pieces only where asked for and long enough
+    # unit 0 first, in pass-1 pieces; with row pieces the last unit comes last,
+    # cut the same way; every other unit is one piece with both passes
+    split = {0} | ({U - 1} if rowed else set())
+    order = [pc[0] for pc in pieces]
+    assert order == sorted(order)
+    for u in range(U):
+        mine = [pc for pc in pieces if pc[0] == u]
+        if u not in split:
+            assert len(mine) == 1
+            pc = mine[0]
+            assert pc[3] == P1 | P2 and pc[1] == (0, G) and pc[2] is None and pc[4]
+            continue
+        assert all(pc[3] == P1 for pc in mine)
+        # k travels with the unit's first piece only
+        assert [pc[4] for pc in mine] == [True] + [False] * (len(mine) - 1)
+        # every (head, row) of the unit exactly once
+        cover = {}
+        for _, (h0, h1), rows, _, _ in mine:
+            r0, r1 = rows if rows is not None else (0, N)
+            assert 0 <= r0 < r1 <= N and r0 % 128 == 0 and (r1 % 128 == 0 or r1 == N)
+            for h in range(h0, h1):
+                cover.setdefault(h, []).append((r0, r1))
+        assert sorted(cover) == list(range(G))
+        for h, rr in cover.items():
+            rr.sort()
+            assert rr[0][0] == 0 and rr[-1][1] == N
+            assert all(a[1] == b[0] for a, b in zip(rr, rr[1:]))
+        assert any(pc[2] is not None for pc in mine) == rowed
+        if rowed:  # the last rows come first
+            assert 2 <= len(mine) <= 8
+            assert [pc[2] for pc in mine] == sorted((pc[2] for pc in mine), reverse=True)
