@@ -49,7 +49,8 @@ from concurrent.futures import ThreadPoolExecutor
 
 import numpy as np
 
-__all__ = ["block_mass_stream", "normalize_masks", "num_blocks", "dense_keys_from_pages", "block_mass_ragged"]
+__all__ = ["block_mass_stream", "normalize_masks", "num_blocks", "dense_keys_from_pages", "block_mass_ragged",
+           "block_mass_segment_lse"]
 
 
 def num_blocks(n: int, block_size: int) -> int:
@@ -352,3 +353,66 @@ def block_mass_ragged(q, k, lens, attn_mask=None, causal=False, block_size=64, s
                               causal=causal, block_size=block_size, scale=scale)
         out[b, :m.shape[0]] = m
     return out if per_sequence else out.sum(axis=0, dtype=np.float64).astype(acc)
+
+
+def block_mass_segment_lse(q, k, attn_mask=None, causal=False, block_size=64, scale=None, query_mask=None,
+                           seg=64, tile=128):
+    """The mass from per-row segment log-sums: the identity the library's
+    one-pass method computes, checked here against the reference's outputs.
+
+    For query row ``i`` the reference's softmax summed over the keys of bucket
+    ``j`` (``reference.py:113-124``) is ``2^(L_ij - lse2_i)``, where
+    ``L_ij = log2 sum_{c in j} 2^(t_ic)`` over the kept keys (``t`` the scores
+    times ``log2 e``) and ``lse2_i`` the row's log2-sum-exp2 over all kept
+    keys.  This walks each row's keys in tiles of ``tile`` keys, as the kernel
+    does: it keeps a running max ``m`` and, for every piece of ``seg`` keys
+    (cut at bucket edges too), the sum of ``2^(t - m)`` rescaled when ``m``
+    grows, and records ``L = m + log2(sum)`` when the piece ends.  The mass is
+    ``sum_i sum_pieces 2^(L - lse2_i)``.  Float64; small shapes only.
+    """
+    q = np.asarray(q, dtype=np.float64)
+    k = np.asarray(k, dtype=np.float64)
+    B, Hq, N, D = q.shape
+    Hkv = k.shape[1]
+    if Hq % Hkv != 0:
+        raise ValueError(f"GQA requires H_q % H_kv == 0, got H_q={Hq}, H_kv={Hkv}")
+    G = Hq // Hkv
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    key, pair, qm = normalize_masks(attn_mask, query_mask, B, N)
+    nb = num_blocks(N, block_size)
+    out = np.zeros(nb, dtype=np.float64)
+    log2e = 1.0 / math.log(2.0)
+    # piece boundaries: every multiple of seg and of block_size
+    edges = sorted(set(range(0, N, seg)) | set(range(0, N, block_size)) | {N})
+    for b in range(B):
+        keep = _keep_rows(b, 0, N, N, causal, key, pair, qm)
+        for h in range(Hq):
+            t = (q[b, h] @ k[b, h // G].T) * (scale * log2e)
+            t = np.where(keep, t, -np.inf)
+            for i in range(N):
+                m, l = -np.inf, 0.0
+                pieces = []  # (bucket, L)
+                for c0 in range(0, N, tile):
+                    row = t[i, c0:c0 + tile]
+                    tmax = row.max()
+                    if tmax > m:  # rescale only when the running max grows
+                        if pieces:
+                            pass  # recorded pieces are absolute (m + log2 sum): nothing to rescale
+                        l = l * (2.0 ** (m - tmax)) if np.isfinite(m) else 0.0
+                        m = tmax
+                    for p0, p1 in zip(edges[:-1], edges[1:]):
+                        if p0 < c0 or p1 > c0 + tile:
+                            continue
+                        sub = row[p0 - c0:p1 - c0]
+                        ssum = float(np.exp2(sub - m).sum()) if np.isfinite(m) else 0.0
+                        l += ssum
+                        with np.errstate(divide="ignore"):
+                            pieces.append((p0 // block_size, m + math.log2(ssum) if ssum > 0 else -np.inf))
+                if not np.isfinite(m) or l == 0.0:
+                    continue  # a row that keeps no key contributes 0 (reference.py:117-119)
+                lse2 = m + math.log2(l)
+                for j, L in pieces:
+                    if np.isfinite(L):
+                        out[j] += 2.0 ** (L - lse2)
+    return out
