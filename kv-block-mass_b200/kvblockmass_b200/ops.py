@@ -448,29 +448,26 @@ def _host_pieces(U: int, G: int, N: int, by_rows: bool) -> list:
     """The pieces of a host-input call: (unit, (head0, head1), (row0, row1) or
     None, stages, whether the unit's k travels with it).
 
-    Unit 0 comes first in small pass-1 pieces, so that little is copied before
-    the first kernel starts: with ``by_rows`` (kernel paths 0 and 1, N >= 4096)
-    in pieces of query rows, the last rows first (pass 1 of rows [r0, r1)
-    reads k rows [0, r1), all of which arrive with the first piece, and its
-    work per byte of q grows with r1 under causal masking); otherwise q-head 0,
-    then the other q-heads.  With ``by_rows`` the last unit is cut the same
-    way, so the piece copied last is its first rows, whose kernels are short:
-    little work is left once the last copy lands.  A unit cut into pieces runs
-    pass 2 after its last piece; every other unit is one piece with both
-    passes.
+    With ``by_rows`` (kernel paths 0 and 1, N >= 4096) every unit is cut into
+    three pieces of query rows, and the pieces go in order of work per byte:
+    first rows [N/2, N) of every unit with its k, then rows [N/4, N/2) of
+    every unit, then rows [0, N/4).  Under causal masking pass 1 of rows
+    [r0, r1) reads k rows [0, r1), and its work per byte of q grows with r1:
+    the last half of the rows carries three quarters of a unit's work in 60 %
+    of its bytes (with k), the first quarter 1/16 of the work in 20 %.  So the
+    kernels run ahead of the copies while the earlier rows still stream in,
+    and the pieces copied last are short.
+    Otherwise unit 0 goes first as q-head 0 (with the k), then its other
+    q-heads, and every further unit is one piece with both passes.  A unit cut
+    into pieces runs pass 2 after its last piece.
     """
     P1, P2 = _lib.KVBM_STAGE_PASS1, _lib.KVBM_STAGE_PASS2
-    nr = max(1, min(8, N // 2048)) if by_rows else 1
-    if nr > 1:
-        R = ((N + nr - 1) // nr + 127) // 128 * 128
-        bounds = list(range(0, N, R)) + [N]
-        chunks = list(zip(bounds[:-1], bounds[1:]))[::-1]
-
-        def by_row(u):
-            return [(u, (0, G), rr, P1, i == 0) for i, rr in enumerate(chunks)]
-
-        return by_row(0) + [(u, (0, G), None, P1 | P2, True) for u in range(1, U - 1)] + \
-            (by_row(U - 1) if U > 1 else [])
+    if by_rows and N >= 4096:
+        half = (N // 2 + 127) // 128 * 128
+        quarter = (N // 4 + 127) // 128 * 128
+        return [(u, (0, G), (half, N), P1, True) for u in range(U)] + \
+            [(u, (0, G), (quarter, half), P1, False) for u in range(U)] + \
+            [(u, (0, G), (0, quarter), P1, False) for u in range(U)]
     if G > 1:
         pieces = [(0, (0, 1), None, P1, True), (0, (1, G), None, P1, False)]
     else:
