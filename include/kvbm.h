@@ -354,7 +354,8 @@ KVBM_API int kvbm_block_mass_paged(const kvbm_problem* p, const kvbm_paged_kv* k
  * Every ragged/per-sequence result equals the sum over sequences of the
  * reference run on each sequence alone (its first seq_lens[b] positions);
  * buckets j >= ceil(len / block_size) of a sequence get 0 from it. */
-#define KVBM_STAGE_MASKS 1   /* pack a pair mask into bits (tensor-core paths)             */
+#define KVBM_STAGE_MASKS 1   /* pack a pair mask into bits; check a key mask's dropped keys
+                                (tensor-core paths; run it before any pass-1 piece)      */
 #define KVBM_STAGE_PASS1 2   /* row lse2, or the LSE import; fp32 path 2: tf32 split first;
                                 one pass: also the bucket partials                       */
 #define KVBM_STAGE_PASS2 4   /* per-key partials (two passes; launches nothing with one)   */

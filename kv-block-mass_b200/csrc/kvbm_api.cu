@@ -184,7 +184,8 @@ WsLayout layout_for(const kvbm_problem* p, int path, const Ragged* rg, int metho
     L.work2_cap = (long long)U * per_unit;
     L.plan_bytes = ragged_plan_layout((long long)U, ntmax, L.work1_cap, L.work2_cap).total;
   }
-  L.total = align_up(L.plan_off + L.plan_bytes, 256);
+  L.flag_off = align_up(L.plan_off + L.plan_bytes, 256);
+  L.total = L.flag_off + (tc ? 256 : 0);
   return L;
 }
 
@@ -542,10 +543,12 @@ int kvbm_launches_per_call(const kvbm_problem* p) {
     dev = -1;
   }
   // pass 1 (lse2) or the lse import, pass 2 (per-key partials), bucket reduce,
-  // for 3xTF32 the split of q/k into tf32 pairs, for a pair mask its packing;
-  // the one-pass method has no pass 2 but reduces in two steps (same count)
+  // for 3xTF32 the split of q/k into tf32 pairs, for a pair mask its packing,
+  // for a key mask on path 1 its pre-pass over the masked keys' rows; the
+  // one-pass method has no pass 2 but reduces in two steps (same count)
   const int path = select_path(p, dev);
-  return 3 + (path == 2 ? 1 : 0) + (path >= 1 && p->pair_mask != nullptr ? 1 : 0);
+  return 3 + (path == 2 ? 1 : 0) + (path >= 1 && p->pair_mask != nullptr ? 1 : 0) +
+         (path == 1 && p->key_mask != nullptr && p->pair_mask == nullptr ? 1 : 0);
 }
 
 int kvbm_block_mass(const kvbm_problem* p, void* mass_out, void* workspace,

@@ -57,6 +57,7 @@ struct WsLayout {
   int bits_batches = 0;                  // batch entries of the packed bits (1 or B)
   // tensor-core paths with ragged lengths: the CTA work lists and their plan
   size_t plan_off = 0, plan_bytes = 0;
+  size_t flag_off = 0;                   // tensor-core paths: a word of the key-mask pre-pass
   long long work1_cap = 0;               // pass-1 items: U * G * ceil(N / 128)
   long long work2_cap = 0;               // pass-2 items: U * (pass-2 CTAs of a full-length unit)
   // One-pass method (tensor-core paths): pass 1 also turns its row sums into

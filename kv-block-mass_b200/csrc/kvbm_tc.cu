@@ -75,6 +75,9 @@ constexpr int kMinSmem = 100 * 1024;  // caps residency at 2 CTAs/SM (TMEM: 2 x 
 #endif
 constexpr long long kPass1GroupBytes = (long long)KVBM_P1_GROUP_MIB << 20;
 constexpr int kExpBarrier = 1;      // named barrier of the exp threads
+#ifndef KVBM_P1_KEY_BIAS
+#define KVBM_P1_KEY_BIAS 1
+#endif
 
 struct TcArgs {
   int N, Npad, G, Hkv, ub;
@@ -115,7 +118,13 @@ struct TcArgs {
   int slot_count;          // slots: 2 per SM (index 2 * %smid + TMEM half)
   float* slots;            // [slot_count][slot_cols][128]
   float* part1;            // [U_sel * G][Npad / 128][nb]
+  const unsigned* keys_finite;  // kKeysFiniteMark: every key the key mask drops has a finite k row
 };
+
+// Written over the key-mask check word (byte-wise 0x5A) before the pre-pass;
+// the pre-pass clears it on a non-finite element, and pass 1 trusts the bias
+// alone only on this exact value (an unset workspace takes the select).
+constexpr unsigned kKeysFiniteMark = 0x5A5A5A5Au;
 
 // A work item: three fields of 21 bits (units, heads, chunks and tiles all
 // stay below 2^21).
@@ -418,10 +427,22 @@ __global__ void __launch_bounds__(kThreads, 2)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1k(smem_raw);
   using CF = Cfg<D, kOp>;
+  // A key mask is folded into the accumulator: after a tile's K steps, one
+  // more bf16 MMA adds ones (query side) x [0 or -inf, 0, ...] (key side:
+  // -inf for a masked key or one past the sequence), which the producer warp
+  // writes per K slot from the mask bytes.  Kept scores gain exact zeros, so
+  // the bits are those of a select; the exp threads then mask only the
+  // causal diagonal.  (fp32 on the 3xTF32 path has no shared memory left for
+  // the operand and keeps the select.)
+  constexpr bool kKeyBias = KVBM_P1_KEY_BIAS != 0 && kMask == kMaskKeys && kOp != Op::TF32X3;
+  static_assert(!kKeyBias || CF::kSlotsPerTile == 1, "the key bias step follows a whole K tile per slot");
   constexpr int TB = CF::kOperandBytes, SB = CF::kSlotBytes;
+  constexpr int KS = SB + (kKeyBias ? kBiasBytes : 0);  // K ring slot: the K operand, then its key-bias operand
+  static_assert(KS % 1024 == 0, "K slots stay on 1024-byte swizzle atoms");
   uint8_t* q_tile = smem;
   uint8_t* k_ring = smem + TB;
-  float2* merge = reinterpret_cast<float2*>(smem + TB + SB * kStages);  // [kExpWG - 1][128] (m, l) of parts 1..
+  uint8_t* ones = k_ring + KS * kStages;  // kKeyBias: the query-side operand of the bias step
+  float2* merge = reinterpret_cast<float2*>(ones + (kKeyBias ? kBiasBytes : 0));  // [kExpWG - 1][128] (m, l) of parts 1..
   float* lse_s = reinterpret_cast<float*>(merge + (kExpWG - 1) * TILE);  // [128] -lse2 (one pass)
   uint64_t* bars = reinterpret_cast<uint64_t*>(lse_s + TILE);
   uint64_t* q_full = bars;
@@ -465,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&k_full[s], 1);
+      mbar_init(&k_full[s], kKeyBias ? 2 : 1);  // kKeyBias: + the producer warp's bias rows
       mbar_init(&k_empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -474,6 +495,27 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     *abort_flag = 0;
     fence_mbar_init();
+  }
+  if constexpr (kKeyBias) {
+    // The bias operands' constant parts (16-byte chunks): the query-side tile
+    // of ones ([1, 0, ...] in the first K half of every row, zeros in the
+    // second), and the zero second K half of every slot's key-side tile.
+    if (threadIdx.x >= 64) {
+      constexpr int kOnesChunks = kBiasBytes / 16, kZeroChunks = kBiasBytes / 32;  // per tile, per slot
+      for (int c = threadIdx.x - 64; c < kOnesChunks + kStages * kZeroChunks; c += kExpThreads) {
+        uint4 val = make_uint4(0u, 0u, 0u, 0u);
+        uint8_t* dst;
+        if (c < kOnesChunks) {
+          dst = ones + 16 * c;
+          if (((16 * c) & 128) == 0) val = make_uint4(0x00003F80u, 0u, 0u, 0u);  // bf16 1, 0, ...
+        } else {
+          const int e = c - kOnesChunks, sl = e / kZeroChunks, r = e % kZeroChunks;  // slot, 16-byte row of its K half 2
+          dst = k_ring + sl * KS + SB + (r >> 3) * 256 + 128 + (r & 7) * 16;
+        }
+        *reinterpret_cast<uint4*>(dst) = val;
+      }
+      fence_proxy_async_smem();
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -499,7 +541,51 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   }
 
-  if (warp == 0) {
+  if (kKeyBias && warp == 0) {
+    // Producer warp: lane 0 issues the copies; every lane then writes the
+    // key-bias rows of 4 keys of the slot's tile.
+    const uint8_t* km = a.kmask + b * a.kmb;
+    if (lane == 0) {
+      prefetch_tmap(&tq);
+      prefetch_tmap(&tk);
+      mbar_arrive_expect_tx(q_full, TB);
+      load_operand<D, kOp>(q_tile, &tq, &tq2, q_full, sv.q_row + r0, h, sv.q_b);
+    }
+    int issued = 0;
+    for (int j = 0; j < nkt; ++j) {
+      const int s = j % kStages, n = j / kStages;
+      // this lane's keys, read before the slot wait so that the loads overlap it
+      bool keep[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int c = j * TILE + lane * 4 + e;
+        keep[e] = c < N && km[c] != 0;
+      }
+      const bool ok = n == 0 || mbar_wait(&k_empty[s], (n - 1) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&k_full[s], SB);
+        load_slot<D, kOp>(k_ring + s * KS, &tk, &tk2, &k_full[s], 0, sv.k_row + j * TILE, g, sv.k_b);
+      }
+      issued = j + 1;
+      uint8_t* bt = k_ring + s * KS + SB;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int rl = lane * 4 + e;
+        const uint4 w = make_uint4(keep[e] ? 0u : 0x0000FF80u, 0u, 0u, 0u);  // bf16 0 or -inf, then zeros
+        *reinterpret_cast<uint4*>(bt + (rl >> 3) * 256 + (rl & 7) * 16) = w;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&k_full[s]);
+    }
+    // Do not leave while our copies are in flight.
+    if (lane == 0) {
+      mbar_wait(q_full, 0, abort_flag);
+      for (int qn = max(0, issued - kStages); qn < issued; ++qn)
+        mbar_wait(&k_full[qn % kStages], (qn / kStages) & 1, abort_flag);
+    }
+  } else if (warp == 0) {
     if (lane == 0) {
       prefetch_tmap(&tq);
       prefetch_tmap(&tk);
@@ -516,7 +602,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             break;
           }
           mbar_arrive_expect_tx(&k_full[s], SB);
-          load_slot<D, kOp>(k_ring + s * SB, &tk, &tk2, &k_full[s], sb, sv.k_row + j * TILE, g, sv.k_b);
+          load_slot<D, kOp>(k_ring + s * KS, &tk, &tk2, &k_full[s], sb, sv.k_row + j * TILE, g, sv.k_b);
           issued = qn + 1;
         }
         if (!ok) break;
@@ -529,7 +615,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = idesc_mma(TILE, TILE, Cfg<D, kOp>::kFmt);
-      const uint32_t qs = smem_u32(q_tile), ks = smem_u32(k_ring);
+      const uint32_t qs = smem_u32(q_tile), ks = smem_u32(k_ring), os = smem_u32(ones);
+      const uint32_t idesc_b = idesc_mma(TILE, TILE, 1u);  // the key bias step: bf16 operands
       int issued = 0;
       if (mbar_wait(q_full, 0, abort_flag)) {
         for (int j = 0; j < nkt; ++j) {
@@ -540,7 +627,10 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int qn = j * CF::kSlotsPerTile + done, s = qn % kStages;
             if (!mbar_wait(&k_full[s], (qn / kStages) & 1, abort_flag)) break;
             tc_fence_after();
-            issue_slot_mma<D, kOp>(tmem + buf * TILE, qs, ks + s * SB, done * CF::kSlotBlocks, idesc);
+            issue_slot_mma<D, kOp>(tmem + buf * TILE, qs, ks + s * KS, done * CF::kSlotBlocks, idesc);
+            if constexpr (kKeyBias)  // D += ones x (0 or -inf per key)
+              mma_f16(tmem + buf * TILE, k16_interleaved_desc(os), k16_interleaved_desc(ks + s * KS + SB), idesc_b,
+                      1u);
             mma_commit(&k_empty[s]);
           }
           if (done > 0) {  // (a partial tile only after an abort: committed so that the drain waits for it)
@@ -560,6 +650,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int row = r0 + rl;
     const uint32_t trow = tmem + ((uint32_t)(sub * 32) << 16) + wg * COLS;
     const uint8_t* kmask = kMask == kMaskKeys ? a.kmask + b * a.kmb : nullptr;
+    // With the key bias, the mask is also applied as a select unless the
+    // pre-pass found every masked key's k row finite (a NaN or an infinity
+    // there scores NaN despite the -inf bias; the reference's masked_fill
+    // drops any value).
+    const bool key_select = kMask == kMaskKeys && (!kKeyBias || *a.keys_finite != kKeysFiniteMark);
     const uint32_t* prow = kMask == kMaskPairs ? a.prow + b * a.pb + (long long)row * a.W : nullptr;
     float m = -INFINITY, l = 0.f;
     // one pass: the current segment's sum (relative to m), its index and the
@@ -576,6 +671,14 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int w = 0; w < COLS / 32; ++w) kw[w] = prow[((j * TILE + wg * COLS) >> 5) + w];
       }
+      bool kkeep[COLS / 32];  // key mask bytes of this lane's columns, also loaded before the wait
+      if (key_select) {
+#pragma unroll
+        for (int w = 0; w < COLS / 32; ++w) {
+          const int col = j * TILE + wg * COLS + w * 32 + lane;
+          kkeep[w] = col < N && kmask[col] != 0;
+        }
+      }
       const bool ok = mbar_wait(&s_full[buf], (j >> 1) & 1, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
@@ -585,14 +688,14 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_arrive(&s_empty[buf]);
 
       const int c0 = j * TILE + wg * COLS;  // first key of this thread's columns
-      if (kMask == kMaskKeys) {
+      if (key_select) {
 #pragma unroll
-        for (int w = 0; w < COLS / 32; ++w) {
-          const int col = c0 + w * 32 + lane;
-          kw[w] = __ballot_sync(0xffffffffu, col < N && kmask[col] != 0);
-        }
+        for (int w = 0; w < COLS / 32; ++w) kw[w] = __ballot_sync(0xffffffffu, kkeep[w]);
       }
-      const bool need_mask = kMask != kMaskNone || (c0 + COLS > N) || (a.causal && c0 + COLS - 1 > r0);
+      // (with the key bias alone, masked keys already hold -inf; the keys
+      // past N are still selected away, since their rows may hold any value)
+      const bool need_mask = (kMask != kMaskNone && (kMask != kMaskKeys || key_select)) || (c0 + COLS > N) ||
+                             (a.causal && c0 + COLS - 1 > r0);
       if (need_mask) {
         const int lim_causal = a.causal ? row - c0 : COLS - 1;  // keep col_local <= row - c0
         const int lim = min(lim_causal, N - 1 - c0);            // and col < N
@@ -1271,11 +1374,41 @@ __global__ void pack_pair_mask_kernel(const uint8_t* pm, long long pbs, long lon
   pcol[((long long)bm * Npad + cb * 32 + lane) * Wl + ib] = mycol;
 }
 
+// Key-mask pre-pass of the tensor-core pass 1 (bf16/fp16): clears *finite
+// when a key the mask drops holds a NaN or an infinity in any head's k row.
+// One thread per (batch, key, kv-head); rows the mask keeps, and keys past the
+// sequence (selected away in pass 1), are not read.  16-bit elements, 16-byte
+// rows chunks (path 1 guarantees 16-byte aligned rows).
+__global__ void masked_keys_finite_kernel(const uint16_t* k, long long s0, long long s1, long long s2, int B,
+                                          int Hkv, int N, int D, const uint8_t* km, long long kmb,
+                                          const int32_t* lens, const int32_t* cu, int kpacked, long long total,
+                                          uint32_t exp_mask, unsigned* finite) {
+  const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (idx >= (long long)B * N * Hkv) return;
+  const int g = (int)(idx % Hkv);
+  const long long bc = idx / Hkv;
+  const int c = (int)(bc % N), b = (int)(bc / N);
+  const SeqView sv = seq_view(lens, cu, kpacked != 0, b, N, total);
+  if (c >= sv.n || km[b * kmb + c] != 0) return;
+  const uint4* row = reinterpret_cast<const uint4*>(k + sv.k_b * s0 + g * s1 + (long long)(sv.k_row + c) * s2);
+  bool bad = false;
+  for (int i = 0; i < D / 8; ++i) {
+    const uint4 w = row[i];
+    const uint32_t x[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      bad |= ((x[e] & exp_mask) == exp_mask) || ((x[e] & (exp_mask << 16)) == (exp_mask << 16));
+  }
+  if (bad) *finite = 0u;
+}
+
 constexpr size_t kBarBytes = 8 * (1 + 2 * kStages + 4) + 16;  // mbarriers + TMEM slot + abort flag
 
-template <int D, Op kOp>
+template <int D, Op kOp, int kMask>
 constexpr size_t smem_lse() {
-  return 1024 + (size_t)Cfg<D, kOp>::kOperandBytes + (size_t)Cfg<D, kOp>::kSlotBytes * kStages +
+  constexpr bool kKeyBias = KVBM_P1_KEY_BIAS != 0 && kMask == kMaskKeys && kOp != Op::TF32X3;
+  return 1024 + (size_t)Cfg<D, kOp>::kOperandBytes +
+         (size_t)(Cfg<D, kOp>::kSlotBytes + (kKeyBias ? kBiasBytes : 0)) * kStages + (kKeyBias ? kBiasBytes : 0) +
          (kExpWG - 1) * TILE * 8 + TILE * 4 + kBarBytes;
 }
 template <int D, Op kOp>
@@ -1380,6 +1513,18 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
   a.slot_count = L.slot_count;
   a.slots = L.one_pass ? reinterpret_cast<float*>(static_cast<char*>(ws) + L.slot_off) : nullptr;
   a.part1 = L.one_pass ? a.part : nullptr;
+  unsigned* finite_word = reinterpret_cast<unsigned*>(static_cast<char*>(ws) + L.flag_off);
+  a.keys_finite = finite_word;
+  constexpr bool kKeyBias = KVBM_P1_KEY_BIAS != 0 && kMask == kMaskKeys && kOp != Op::TF32X3;
+  if (kKeyBias && o.run_masks) {
+    if (cudaMemsetAsync(finite_word, 0x5A, sizeof(unsigned), s) != cudaSuccess) return KVBM_ERR_CUDA;
+    const long long n = (long long)p->B * p->N * p->Hkv;
+    masked_keys_finite_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
+        static_cast<const uint16_t*>(p->k), p->k_stride[0], p->k_stride[1], p->k_stride[2], p->B, p->Hkv, p->N,
+        Dr, p->key_mask, p->key_mask_bstride, rg.lens, rg.cu, rg.k_packed ? 1 : 0, rg.total,
+        kOp == Op::BF16 ? 0x7F80u : 0x7C00u, finite_word);
+    if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
+  }
   if (kMask == kMaskPairs) {
     uint32_t* bits = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + L.bits_off);
     const long long words = (long long)L.bits_batches * a.Npad * a.W;
@@ -1452,7 +1597,7 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
     grid2 = dim3((unsigned)L.work2_cap);
   }
 
-  const size_t sm1 = smem_lse<D, kOp>() > (size_t)kMinSmem ? smem_lse<D, kOp>() : (size_t)kMinSmem;
+  const size_t sm1 = smem_lse<D, kOp, kMask>() > (size_t)kMinSmem ? smem_lse<D, kOp, kMask>() : (size_t)kMinSmem;
   const size_t sm2 = smem_mass<D, kOp>() > (size_t)kMinSmem ? smem_mass<D, kOp>() : (size_t)kMinSmem;
   auto k1 = tc_lse_kernel<D, kOp, kMask, kRagged>;
   auto k2 = tc_mass_kernel<D, kOp, kMask, kRagged>;

@@ -576,7 +576,7 @@ def _from_host(q, k, dev, attn_mask, causal, block_size, scale, causal_skip, que
         ws = workspace if workspace is not None and workspace.numel() >= need else \
             torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
         out = torch.empty(prep.out_shape, dtype=prep.out_dtype, device=dev)
-        if prep.prob.pair_mask:
+        if prep.prob.pair_mask or prep.prob.key_mask:
             run_staged(prep, S.KVBM_STAGE_MASKS, ws, stream=compute)
         side.wait_stream(compute)  # the masks, their bits, and anything the caller queued
         streams = [compute, side]

@@ -73,3 +73,34 @@ def test_pair_mask_matches_query_mask_form(cuda_device):
     a = run(q.to(cuda_device), k.to(cuda_device), query_mask=qm.to(cuda_device), causal=True, block_size=64)
     b = run(q.to(cuda_device), k.to(cuda_device), attn_mask=pm.to(cuda_device), causal=True, block_size=64)
     assert max_rel(a.cpu().numpy(), b.cpu().numpy()) < 1e-5
+
+
+@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.float16, 64), (torch.float32, 64)])
+@pytest.mark.parametrize("per_batch", [False, True])
+def test_key_mask_drops_non_finite_keys(cuda_device, dtype, D, per_batch):
+    """Keys dropped by a key mask add nothing, whatever their rows of k hold:
+    the reference's masked_fill (reference.py:113-114) discards NaN and
+    infinite scores too.  The tensor-core kernels fold a key mask into the
+    accumulator as a -inf bias; a masked key holding NaN or inf makes the
+    tile take the select instead.  Same bits as with those rows zeroed."""
+    B, N = 2, 1000
+    q, k, g = _qk(B, 8, 2, N, D, dtype, 35)
+    km = torch.rand(B, 1, N, generator=g) > 0.3 if per_batch else torch.rand(N, generator=g) > 0.3
+    dropped = (~km[:, 0] if per_batch else ~km[None].expand(B, N))
+    bad = k.clone()
+    zero = k.clone()
+    for b in range(B):
+        idx = torch.nonzero(dropped[b]).flatten()
+        bad[b, :, idx[::3]] = float("nan")
+        bad[b, :, idx[1::3]] = float("inf")
+        bad[b, :, idx[2::3]] = -float("inf")
+        zero[b, :, idx] = 0
+    kmd = km.to(cuda_device)
+    got = run(q.to(cuda_device), bad.to(cuda_device), attn_mask=kmd, causal=True, block_size=64)
+    clean = run(q.to(cuda_device), zero.to(cuda_device), attn_mask=kmd, causal=True, block_size=64)
+    assert torch.isfinite(got).all()
+    assert torch.equal(got, clean)
+    if not per_batch:
+        want = oracle_for(q, zero, attn_mask=km, causal=True, block_size=64)
+        assert max_rel(got.cpu().numpy(), want) < TOL[dtype]
+    kb.check_device_errors(cuda_device)
