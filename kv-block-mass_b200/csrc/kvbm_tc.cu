@@ -78,6 +78,9 @@ constexpr int kExpBarrier = 1;      // named barrier of the exp threads
 #ifndef KVBM_P1_KEY_BIAS
 #define KVBM_P1_KEY_BIAS 1
 #endif
+#ifndef KVBM_L2_HINTS
+#define KVBM_L2_HINTS 1
+#endif
 
 struct TcArgs {
   int N, Npad, G, Hkv, ub;
@@ -227,6 +230,19 @@ __device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* m0
     for (int kb = 0; kb < C::kBlocks; ++kb)
       tma_load_4d(dst + part * C::kTileBytes + kb * C::kBlockBytes, part == 0 ? m0 : m1, bar,
                   kb * C::kBlockElems, row, h, b);
+}
+
+// load_operand with an L2 eviction policy on every copy.
+template <int D, Op kOp>
+__device__ __forceinline__ void load_operand_hint(uint8_t* dst, const CUtensorMap* m0, const CUtensorMap* m1,
+                                                  uint64_t* bar, int row, int h, int b, uint64_t policy) {
+  using C = Cfg<D, kOp>;
+#pragma unroll
+  for (int part = 0; part < C::kParts; ++part)
+#pragma unroll
+    for (int kb = 0; kb < C::kBlocks; ++kb)
+      tma_load_4d_hint(dst + part * C::kTileBytes + kb * C::kBlockBytes, part == 0 ? m0 : m1, bar,
+                       kb * C::kBlockElems, row, h, b, policy);
 }
 
 // TMA-load ring slot `sb` of a streamed tile: K-blocks [sb * kSlotBlocks, ..)
@@ -549,7 +565,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       prefetch_tmap(&tq);
       prefetch_tmap(&tk);
       mbar_arrive_expect_tx(q_full, TB);
-      load_operand<D, kOp>(q_tile, &tq, &tq2, q_full, sv.q_row + r0, h, sv.q_b);
+      // the Q tile is read once: first out of L2, so that k and the slots stay
+      if (KVBM_L2_HINTS)
+        load_operand_hint<D, kOp>(q_tile, &tq, &tq2, q_full, sv.q_row + r0, h, sv.q_b, l2_policy_evict_first());
+      else
+        load_operand<D, kOp>(q_tile, &tq, &tq2, q_full, sv.q_row + r0, h, sv.q_b);
     }
     int issued = 0;
     for (int j = 0; j < nkt; ++j) {
@@ -590,7 +610,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       prefetch_tmap(&tq);
       prefetch_tmap(&tk);
       mbar_arrive_expect_tx(q_full, TB);
-      load_operand<D, kOp>(q_tile, &tq, &tq2, q_full, sv.q_row + r0, h, sv.q_b);
+      // the Q tile is read once: first out of L2, so that k and the slots stay
+      if (KVBM_L2_HINTS)
+        load_operand_hint<D, kOp>(q_tile, &tq, &tq2, q_full, sv.q_row + r0, h, sv.q_b, l2_policy_evict_first());
+      else
+        load_operand<D, kOp>(q_tile, &tq, &tq2, q_full, sv.q_row + r0, h, sv.q_b);
       int issued = 0;  // ring slots (kSlotsPerTile per key tile)
       for (int j = 0; j < nkt; ++j) {
         bool ok = true;
@@ -660,6 +684,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // one pass: the current segment's sum (relative to m), its index and the
     // tile that starts the next segment
     float* seg = a.one_pass ? a.slots + (size_t)slot * a.slot_cols * TILE + rl : nullptr;
+    const uint64_t keep_pol = l2_policy_evict_last();  // segment sums: kept in L2 for the epilogue
     float bacc = 0.f;
     int cur = wg, seg_end = a.seg_tiles;
     for (int j = 0; j < nkt; ++j) {
@@ -706,7 +731,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
       if (seg != nullptr && j == seg_end) {  // a new segment: store the finished one
-        __stcg(seg + (size_t)cur * TILE, m + lg2(bacc));
+        if (KVBM_L2_HINTS)
+          st_cg_hint(seg + (size_t)cur * TILE, m + lg2(bacc), keep_pol);
+        else
+          __stcg(seg + (size_t)cur * TILE, m + lg2(bacc));
         cur += kExpWG;
         seg_end += a.seg_tiles;
         bacc = 0.f;
@@ -728,7 +756,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
     // log2 of the segment's sum of 2^(s*C): -inf when it kept no key
-    if (seg != nullptr) __stcg(seg + (size_t)cur * TILE, m + lg2(bacc));
+    if (seg != nullptr) {
+      if (KVBM_L2_HINTS)
+        st_cg_hint(seg + (size_t)cur * TILE, m + lg2(bacc), keep_pol);
+      else
+        __stcg(seg + (size_t)cur * TILE, m + lg2(bacc));
+    }
     // Merge the column parts of each row (fixed order: part 0, then 1, 2, ...).
     if (wg > 0) merge[(wg - 1) * TILE + rl] = make_float2(m, l);
     exp_bar_sync();
@@ -771,6 +804,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       // L2 round trip per group instead of per bucket); a segment past the
       // CTA's last adds +0, as if it had not been read
       constexpr int kEpiU = 8, kEw = kExpThreads / 32;
+      const uint64_t drop_pol = l2_policy_evict_first();  // read once: first out of L2
       for (int base = ew; base < nbw; base += kEw * kEpiU) {
         float acc[kEpiU];
 #pragma unroll
@@ -780,8 +814,10 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
           for (int u = 0; u < kEpiU; ++u) {
             const int jb = base + kEw * u, sg = jb * a.seg_per_bucket + so;
-            L[u] = (jb < nbw && sg < nseg) ? __ldcg(sbase + (size_t)sg * (TILE / 4))
-                                           : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+            L[u] = (jb < nbw && sg < nseg)
+                       ? (KVBM_L2_HINTS ? ld_cg_hint(sbase + (size_t)sg * (TILE / 4), drop_pol)
+                                        : __ldcg(sbase + (size_t)sg * (TILE / 4)))
+                       : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
           }
 #pragma unroll
           for (int u = 0; u < kEpiU; ++u) {
