@@ -490,10 +490,11 @@ KVBM_API int kvbm_copy_2d_async(void* dst, int64_t dst_pitch, const void* src, i
 KVBM_API int kvbm_selftest_wait_timeout(void* stream, uint64_t limit_ns, int* waited);
 
 /* Reads and clears the device-side error words of the current device (set
- * when a bounded wait inside a tcgen05 kernel gave up, or when a page gather
- * met a block-table entry out of range).  Synchronises `stream`.  Returns
- * KVBM_OK, KVBM_ERR_TIMEOUT (takes precedence), KVBM_ERR_PAGE or
- * KVBM_ERR_CUDA. */
+ * when a bounded wait inside a tcgen05 kernel gave up, when a tcgen05 kernel
+ * found no work slot or more work items than its launch covers (cu_seqlens
+ * that decrease), or when a page gather met a block-table entry out of
+ * range).  Synchronises `stream`.  Returns KVBM_OK, KVBM_ERR_TIMEOUT (the
+ * first three; takes precedence), KVBM_ERR_PAGE or KVBM_ERR_CUDA. */
 KVBM_API int kvbm_check_device_errors(void* stream);
 
 #ifdef __cplusplus

@@ -1214,6 +1214,7 @@ struct PlanArgs {
   int* fill;
   long long* lvl_off;
   long long* unit_off;
+  long long grid1;  // CTAs of the pass-1 launch (the items past it would not run)
 };
 
 // pass-2 key tiles of chunk y for a unit of nt tiles (keys_in_chunk, per unit)
@@ -1297,6 +1298,9 @@ __global__ void __launch_bounds__(kPlanThreads) ragged_plan_kernel(PlanArgs p) {
   if (t == 0) {
     p.counts[0] = total1;
     p.counts[1] = total2;
+    // more pass-1 items than the launch has CTAs: only cu_seqlens that
+    // decrease somewhere give more tiles than total_tokens allows
+    if (total1 > p.grid1) atomicOr(&g_kvbm_device_error, 1u);
   }
 }
 
@@ -1622,6 +1626,15 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
     pa.fill = reinterpret_cast<int*>(plan + pl.fill);
     pa.lvl_off = reinterpret_cast<long long*>(plan + pl.lvl_off);
     pa.unit_off = reinterpret_cast<long long*>(plan + pl.unit_off);
+    // Pass 1 launches one CTA per item, and the CTAs past the item count
+    // return at once; they still cost a launch each.  A packed batch of
+    // total_tokens rows has at most ceil(T / 128) + B query tiles per
+    // kv-head, far fewer than B * ceil(N / 128) when the lengths are uneven.
+    pa.grid1 = L.work1_cap;
+    if (rg.cu != nullptr) {
+      const long long tiles = (rg.total + TILE - 1) / TILE + p->B;
+      pa.grid1 = std::min(pa.grid1, (long long)a.G * p->Hkv * tiles);
+    }
     ragged_plan_kernel<<<1, kPlanThreads, 0, s>>>(pa);
     if (cudaGetLastError() != cudaSuccess) return KVBM_ERR_CUDA;
     if (cudaMemsetAsync(static_cast<char*>(ws) + L.part_off, 0, L.part_bytes, s) != cudaSuccess)
@@ -1629,7 +1642,7 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
     a.work1 = pa.work1;
     a.work2 = pa.work2;
     a.work_count = pa.counts;
-    grid1 = dim3((unsigned)L.work1_cap);
+    grid1 = dim3((unsigned)pa.grid1);
     grid2 = dim3((unsigned)L.work2_cap);
   }
 

@@ -197,6 +197,28 @@ def test_cu_seqlens_past_total_are_clamped(cuda_device, dtype, D):
     torch.cuda.synchronize()
 
 
+def test_decreasing_cu_seqlens_are_reported(cuda_device):
+    """The tensor-core pass 1 of a packed batch launches at most
+    ceil(total_tokens / 128) + B query tiles per kv-head.  cu_seqlens that
+    decrease (so that the clamped sequences overlap and hold more rows than
+    total_tokens) exceed that: the call reads nothing out of range and reports
+    it through the device error word."""
+    g = torch.Generator().manual_seed(70)
+    T = 500
+    qp = torch.randn(T, 8, 128, generator=g).to(torch.bfloat16).to(cuda_device)
+    kp = torch.randn(T, 2, 128, generator=g).to(torch.bfloat16).to(cuda_device)
+    kb.check_device_errors(cuda_device)
+    good = torch.tensor([0, 250, 500], dtype=torch.int32, device=cuda_device)
+    kb.block_mass_varlen(qp, kp, good, max_seqlen=500, causal=True, block_size=64)
+    kb.check_device_errors(cuda_device)  # monotone offsets: no report
+    bad = torch.tensor([0, 500, 0, 500], dtype=torch.int32, device=cuda_device)  # 500 + 0 + 500 rows
+    kb.block_mass_varlen(qp, kp, bad, max_seqlen=500, causal=True, block_size=64)
+    with pytest.raises(RuntimeError):
+        kb.check_device_errors(cuda_device)
+    kb.check_device_errors(cuda_device)  # the read cleared it
+    assert torch.isfinite(kb.block_mass_varlen(qp, kp, good, max_seqlen=500, causal=True, block_size=64)).all()
+
+
 @pytest.mark.slow
 @pytest.mark.parametrize("dtype,D,N,short", [(torch.bfloat16, 128, 262144, 100000), (torch.float64, 32, 40000, 20000)])
 def test_wide_query_chunks_past_64_chunks(cuda_device, dtype, D, N, short):
