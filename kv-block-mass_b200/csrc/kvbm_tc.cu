@@ -546,6 +546,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   // disjoint 256-column allocations are exactly the two halves, so
   // (SM, TMEM half) names one resident CTA.  A CTA reuses a slot only after
   // the previous holder freed its TMEM, i.e. after its last read of the slot.
+  static_assert(2 * kTmemCols == 512, "two pass-1 CTAs per SM take the two TMEM halves");
   int slot = 0;
   if (a.one_pass) {
     uint32_t smid;

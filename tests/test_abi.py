@@ -95,6 +95,13 @@ def test_num_blocks_and_workspace():
     assert ws % 256 == 0
     assert lib.kvbm_workspace_bytes(ctypes.byref(_problem(shape=(1, 6, 4, 8, 4)))) == 0
     assert lib.kvbm_launches_per_call(ctypes.byref(p)) == 3
+    # bf16 with a key mask: + the pre-pass over the dropped keys' rows on tensor-core path 1
+    # (without a GPU and its driver the path here is the SIMT one)
+    pk = _problem(dtype=_lib.KVBM_BF16)
+    km = (ctypes.c_uint8 * 128)()
+    pk.key_mask = ctypes.cast(km, ctypes.c_void_p).value
+    tc = lib.kvbm_kernel_path(ctypes.byref(pk)) == 1
+    assert lib.kvbm_launches_per_call(ctypes.byref(pk)) == 3 + (1 if tc else 0)
 
 
 def test_block_mass_without_device_fails_cleanly():
