@@ -714,9 +714,13 @@ def b200_arm(args, w):
                                     ws.data_ptr(), ws.numel(), stream.cuda_stream)
         l1.record(stream)
         torch.cuda.synchronize()
+        lse_ms = l0.elapsed_time(l1) / K
         lse_input = {"value": pairs_rank * K / (l0.elapsed_time(l1) * 1e-3), "unit": UNIT,
-                     "ms_per_step": l0.elapsed_time(l1) / K, "per_gpu": True,
-                     "api": "kvbm_block_mass_lse (row LSE supplied, as an attention forward returns it)"}
+                     "ms_per_step": lse_ms, "per_gpu": True,
+                     "api": "kvbm_block_mass_lse (row LSE supplied, as an attention forward returns it)",
+                     # the two-pass method's pass 2 alone (plus the LSE import and the reduce):
+                     # one exp2 per pair against the live-measured MUFU rate
+                     "pass2_mufu_frac_of_bound": (pairs_rank / ex2.value) / (lse_ms * 1e-3)}
         del lse_buf
 
     # Paged key cache (16-key pages, shuffled page ids): page gather + both passes.

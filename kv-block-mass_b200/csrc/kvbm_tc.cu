@@ -547,6 +547,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   // (SM, TMEM half) names one resident CTA.  A CTA reuses a slot only after
   // the previous holder freed its TMEM, i.e. after its last read of the slot.
   static_assert(2 * kTmemCols == 512, "two pass-1 CTAs per SM take the two TMEM halves");
+  static_assert(2 * kTmemCols == 512, "two pass-1 CTAs per SM take the two TMEM halves");
   int slot = 0;
   if (a.one_pass) {
     uint32_t smid;
