@@ -319,7 +319,12 @@ KVBM_API int kvbm_block_mass_paged(const kvbm_problem* p, const kvbm_paged_kv* k
  *                     AUTO takes ONE_PASS where it applies and its workspace
  *                     stays within 2x the two-pass one + 256 MiB, else
  *                     TWO_PASS.  ONE_PASS on a problem it does not apply to
- *                     is KVBM_ERR_SHAPE.
+ *                     is KVBM_ERR_SHAPE.  One pass keeps its segment sums
+ *                     in 2 slots per SM indexed by %smid; on a device whose
+ *                     SM ids reach past its SM count (not so on a whole
+ *                     B200) a CTA there finds no slot, does no work and
+ *                     kvbm_check_device_errors reports KVBM_ERR_TIMEOUT:
+ *                     use TWO_PASS there.
  *   stages, run_unit_begin/end, run_head_begin/end
  *                     staged execution (all zero: the whole call).  A caller
  *                     that receives a problem in pieces, e.g. copying it from
