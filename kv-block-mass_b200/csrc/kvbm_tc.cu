@@ -285,6 +285,16 @@ __device__ __forceinline__ void load_cols(uint32_t taddr, float (&v)[COLS]) {
 #ifndef KVBM_EXP2_DEGREE
 #define KVBM_EXP2_DEGREE 4
 #endif
+// The same for the one-pass kernel.  There each row's bucket masses and its
+// normaliser are sums of the same exponentials (segment sums over sum of all
+// of them), so a polynomial's bias cancels in the sum rule, and degree 3
+// (max relative error 7.5e-5 per emulated element, one FFMA2 fewer) stays
+// far inside the 1e-3 of bf16/fp16 inputs: on the Llama-3-8B N=32768 step it
+// measured 4.82-4.90 ms against 4.95-5.01 ms for degree 4 (three interleaved
+// rounds of 20 steps; 5.235 against 5.299 ms sustained).
+#ifndef KVBM_EXP2_DEGREE_ONE_PASS
+#define KVBM_EXP2_DEGREE_ONE_PASS 3
+#endif
 constexpr int kEmuPer16 = KVBM_EMU_GROUPS;
 constexpr int kGroups = COLS / 4;                     // four-column groups of one thread's row
 constexpr int kEmuGroups = kEmuPer16 * kGroups / 16;  // of them on the FMA pipe
@@ -298,6 +308,10 @@ __host__ __device__ constexpr bool emu_group(int g) {
 template <Op kOp>
 constexpr int exp2_degree() {
   return kOp == Op::TF32X3 ? 4 : KVBM_EXP2_DEGREE;
+}
+template <Op kOp>
+constexpr int exp2_degree_one_pass() {
+  return kOp == Op::TF32X3 ? 4 : KVBM_EXP2_DEGREE_ONE_PASS;
 }
 
 // Sum over the thread's columns of 2^(v*C + nm), nm = -(running max); masked entries hold -inf.
@@ -752,7 +766,9 @@ __global__ void __launch_bounds__(kThreads, 2)
           bacc = bacc * al;
           m = mt;
         }
-        const float t = row_sum_exp2<exp2_degree<kOp>()>(v, a.C, -m);
+        // (pass 1 of the two-pass method keeps the degree of pass 2)
+        const float t = a.one_pass ? row_sum_exp2<exp2_degree_one_pass<kOp>()>(v, a.C, -m)
+                                   : row_sum_exp2<exp2_degree<kOp>()>(v, a.C, -m);
         l += t;
         bacc += t;
       }

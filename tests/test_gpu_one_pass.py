@@ -9,9 +9,12 @@ sum_i 2^(segment sum - lse2_i).  It is the mass of the reference
 from the row statistics alone, so the scores are computed once.
 
 Tolerances as in test_gpu_parity.py (max relative error per bucket): 1e-3 for
-bf16/fp16 against the fp32-upcast oracle, 2e-5 for fp32; the two methods
-agree within 2e-5 on every dtype (both are fp32 arithmetic on the same
-scores).  causal_skip on/off gives the same bits on either method.
+bf16/fp16 against the fp32-upcast oracle, 2e-5 for fp32.  The two methods are
+fp32 arithmetic on the same scores and agree within 2e-5 for fp32 inputs and
+1e-4 for bf16/fp16, where the one-pass kernel takes a quarter of its
+exponentials from a degree-3 polynomial (7.5e-5 max relative error per
+element) and the two-pass kernels from a degree-4 one.  causal_skip on/off
+gives the same bits on either method.
 """
 
 import numpy as np
@@ -26,6 +29,7 @@ import kvblockmass_b200 as kb
 pytestmark = pytest.mark.gpu
 
 TOL = {torch.float32: 2e-5, torch.bfloat16: 1e-3, torch.float16: 1e-3}
+AGREE = {torch.float32: 2e-5, torch.bfloat16: 1e-4, torch.float16: 1e-4}  # one pass vs two passes
 
 
 def _qk(B, Hq, Hkv, N, D, dtype, seed):
@@ -54,7 +58,7 @@ def test_one_pass_matches_oracle_and_two_pass(cuda_device, dtype, D, bs, causal)
     one, two = _both(qd, kd, causal=causal, block_size=bs)
     want = oracle_for(q, k, causal=causal, block_size=bs)
     assert max_rel(one.cpu().numpy(), want) < TOL[dtype]
-    assert max_rel(one.double().cpu().numpy(), two.double().cpu().numpy()) < 2e-5
+    assert max_rel(one.double().cpu().numpy(), two.double().cpu().numpy()) < AGREE[dtype]
     rows = 2 * 8 * N
     assert abs(float(one.double().sum()) - rows) < 1e-5 * rows  # sum rule
     skip_off = run(qd, kd, causal=causal, block_size=bs, causal_skip=False, method="one_pass")
@@ -81,13 +85,13 @@ def test_one_pass_masks(cuda_device, mask):
     one, two = _both(qd, kd, **dev_kw)
     want = oracle_for(q, k, **kw)
     assert max_rel(one.cpu().numpy(), want) < 1e-3
-    assert max_rel(one.cpu().numpy(), two.cpu().numpy()) < 2e-5
+    assert max_rel(one.cpu().numpy(), two.cpu().numpy()) < AGREE[torch.bfloat16]
     assert torch.equal(one, run(qd, kd, causal_skip=False, method="one_pass", **dev_kw))
 
 
 def test_one_pass_ragged_and_per_sequence(cuda_device):
     """Padded ragged lengths with a per-sequence output: one pass equals the
-    two-pass method within 2e-5 and the oracle run on each sequence alone."""
+    two-pass method within 1e-4 and the oracle run on each sequence alone."""
     B, N = 4, 1100
     q, k, _ = _qk(B, 8, 2, N, 128, torch.bfloat16, 63)
     lens = torch.tensor([1100, 1, 517, 0], dtype=torch.int32)
@@ -97,7 +101,7 @@ def test_one_pass_ragged_and_per_sequence(cuda_device):
     qd, kd, ld = q.to(cuda_device), k.to(cuda_device), lens.to(cuda_device)
     one, two = _both(qd, kd, causal=True, block_size=64, seq_lens=ld, per_sequence=True)
     assert one.shape == (B, (N + 63) // 64)
-    assert max_rel(one.cpu().numpy(), two.cpu().numpy()) < 2e-5
+    assert max_rel(one.cpu().numpy(), two.cpu().numpy()) < AGREE[torch.bfloat16]
     for b in range(B):
         n = int(lens[b])
         want = np.zeros(one.shape[1])
@@ -142,11 +146,11 @@ def test_method_choice(cuda_device):
 
 def test_one_pass_llama3_8b_shape_against_two_pass(cuda_device):
     """Llama-3-8B attention shape at N=8192 (B1 Hq32 Hkv8 D128, bf16, per-head
-    scale): the two methods agree within 2e-5 per bucket and the sum rule holds."""
+    scale): the two methods agree within 1e-4 per bucket and the sum rule holds."""
     from kvblockmass_b200.workloads import WORKLOADS, make_inputs
 
     q, k, _, _ = make_inputs(WORKLOADS["llama3_8b_n32k"], N=8192)
     qd, kd = q.to(cuda_device), k.to(cuda_device)
     one, two = _both(qd, kd, causal=True, block_size=64)
-    assert max_rel(one.cpu().numpy(), two.cpu().numpy()) < 2e-5
+    assert max_rel(one.cpu().numpy(), two.cpu().numpy()) < AGREE[torch.bfloat16]
     assert abs(float(one.double().sum()) - 32 * 8192) < 1e-5 * 32 * 8192
