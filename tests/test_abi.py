@@ -289,6 +289,20 @@ def test_method_option_checks(pkw, okw, code):
     assert lib.kvbm_validate_ex(ctypes.byref(p), ctypes.byref(o)) == code
 
 
+def test_auto_method_falls_back_to_two_passes_for_long_sequences():
+    """The one-pass partials grow as (N/128) * (N/block_size) per head: at
+    N = 2^20 with 64-key blocks they would be 17 GiB, so the automatic choice
+    takes two passes (the workspace equals the two-pass one), while a forced
+    one-pass call still sizes its own."""
+    lib = _lib.load()
+    p = _problem(shape=(1, 32, 8, 1 << 20, 128), dtype=_lib.KVBM_BF16, block_size=64)
+    auto = lib.kvbm_workspace_bytes_ex(ctypes.byref(p), ctypes.byref(_opts()))
+    two = lib.kvbm_workspace_bytes_ex(ctypes.byref(p), ctypes.byref(_opts(method=_lib.KVBM_METHOD_TWO_PASS)))
+    one = lib.kvbm_workspace_bytes_ex(ctypes.byref(p), ctypes.byref(_opts(method=_lib.KVBM_METHOD_ONE_PASS)))
+    assert auto == two and one > 4 * two
+    assert one >= 32 * 8192 * 16384 * 4  # the per-tile partials alone
+
+
 def test_one_pass_workspace_holds_slots_and_tile_partials():
     """With the device unknown the workspace covers the one-pass layout: its
     per-tile partials [U*G, ceil(N/128), nb] fp32 and 2 x 160 slots of
