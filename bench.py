@@ -16,8 +16,9 @@ Reported beside the device-timed value:
   e2e           the same metric through the public API (block_mass_b200 on
                 pinned host tensors, device="cuda"), H2D of q/k and D2H of the
                 mass inside the timed region;
-  lse_input     the device-resident step with the row LSE supplied (pass 2
-                and the reduce only);
+  lse_input     the device-resident step with the row LSE supplied (one pass
+                that needs no running max, and the two-pass method's pass 2
+                alone beside it);
   paged         the device-resident step with k read from a paged cache
                 (16-key pages in shuffled order + block table): page gather,
                 both passes, reduce;
@@ -703,24 +704,40 @@ def b200_arm(args, w):
             nl = ws[: q.shape[0] * q.shape[1] * w.N * 4].view(torch.float32).view(q.shape[0], q.shape[1], w.N)
             lse_buf.copy_(nl / 1.4426950408889634)
         st3 = (ctypes.c_int64 * 3)(*lse_buf.stride())
-        for _ in range(2):
-            lib.kvbm_block_mass_lse(ctypes.byref(prep.prob), lse_buf.data_ptr(), st3, out.data_ptr(),
-                                    ws.data_ptr(), ws.numel(), stream.cuda_stream)
-        torch.cuda.synchronize()
-        l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        l0.record(stream)
-        for _ in range(K):
-            lib.kvbm_block_mass_lse(ctypes.byref(prep.prob), lse_buf.data_ptr(), st3, out.data_ptr(),
-                                    ws.data_ptr(), ws.numel(), stream.cuda_stream)
-        l1.record(stream)
-        torch.cuda.synchronize()
-        lse_ms = l0.elapsed_time(l1) / K
-        lse_input = {"value": pairs_rank * K / (l0.elapsed_time(l1) * 1e-3), "unit": UNIT,
-                     "ms_per_step": lse_ms, "per_gpu": True,
-                     "api": "kvbm_block_mass_lse (row LSE supplied, as an attention forward returns it)",
-                     # the two-pass method's pass 2 alone (plus the LSE import and the reduce):
+
+        def lse_call(method):
+            o = _lib.Options()
+            o.lse = lse_buf.data_ptr()
+            for i in range(3):
+                o.lse_stride[i] = st3[i]
+            o.method = method
+            return lambda: lib.kvbm_block_mass_ex(ctypes.byref(prep.prob), ctypes.byref(o), out.data_ptr(),
+                                                  ws.data_ptr(), ws.numel(), stream.cuda_stream)
+
+        def lse_ms_of(call):
+            for _ in range(2):
+                if call() != 0:
+                    raise RuntimeError("kvbm_block_mass_ex with an LSE failed")
+            torch.cuda.synchronize()
+            l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            l0.record(stream)
+            for _ in range(K):
+                call()
+            l1.record(stream)
+            torch.cuda.synchronize()
+            return l0.elapsed_time(l1) / K
+
+        lse_ms = lse_ms_of(lse_call(_lib.KVBM_METHOD_AUTO))
+        lse2_ms = lse_ms_of(lse_call(_lib.KVBM_METHOD_TWO_PASS))
+        lse_input = {"value": pairs_rank / (lse_ms * 1e-3), "unit": UNIT,
+                     "ms_per_step": lse_ms, "per_gpu": True, "method": ops.method_of(prep),
+                     "api": "kvbm_block_mass_ex with kvbm_options.lse (row LSE supplied, as an attention "
+                            "forward returns it; the same as kvbm_block_mass_lse)",
                      # one exp2 per pair against the live-measured MUFU rate
-                     "pass2_mufu_frac_of_bound": (pairs_rank / ex2.value) / (lse_ms * 1e-3)}
+                     "mufu_frac_of_bound": (pairs_rank / ex2.value) / (lse_ms * 1e-3),
+                     "two_pass": {"value": pairs_rank / (lse2_ms * 1e-3), "ms_per_step": lse2_ms,
+                                  "note": "the two-pass method's pass 2 alone (plus the LSE import and the reduce)",
+                                  "pass2_mufu_frac_of_bound": (pairs_rank / ex2.value) / (lse2_ms * 1e-3)}}
         del lse_buf
 
     # Paged key cache (16-key pages, shuffled page ids): page gather + both passes.

@@ -163,9 +163,11 @@ KVBM_API int kvbm_block_mass(const kvbm_problem* p, void* mass_out, void* worksp
  * log-sum-exp, as an attention forward pass returns it (for example the
  * softmax LSE of a FlashAttention forward): lse[b*s0 + h*s1 + i*s2] =
  * log(sum over kept keys c of exp(scale * q[b,h,i] . k[b,h/G,c])), natural
- * log, fp32, with the same scale and masks as `p`.  Pass 1 is skipped: the
- * LSE is copied into the workspace and only pass 2 and the bucket reduce run,
- * about half the work.  A non-finite LSE marks a row that keeps no key (it
+ * log, fp32, with the same scale and masks as `p`.  The row statistics are
+ * not recomputed: the LSE is copied into the workspace, and then (one-pass
+ * method, the default where it applies) pass 1 sums 2^(s - lse2) per segment
+ * with no running max, or (two-pass method) only pass 2 and the bucket
+ * reduce run; about half the work either way.  A non-finite LSE marks a row that keeps no key (it
  * contributes 0).  lse_stride = {s0, s1, s2} in elements.  It extends the
  * reference's entry points (there the row statistics are always recomputed,
  * triton_kernel.py:69-104); workspace and output as kvbm_block_mass. */
@@ -311,11 +313,14 @@ KVBM_API int kvbm_block_mass_paged(const kvbm_problem* p, const kvbm_paged_kv* k
  *                     recomputes the scores and sums 2^(s - lse2) per key
  *                     (the reference's scheme, triton_kernel.py:69-145);
  *                     ONE_PASS (tensor-core paths 1 and 2, block_size a
- *                     multiple of 64, no LSE input): pass 1 also keeps, for
+ *                     multiple of 64): pass 1 also keeps, for
  *                     each row, the log2-sum of 2^s over every 64-key segment
  *                     it visits, and once the row's lse2 is final turns them
  *                     into bucket partials, sum_i 2^(segment sum - lse2_i):
  *                     the same mass from half the MMAs and exponentials.
+ *                     With an LSE input pass 1 takes the caller's lse2 and
+ *                     sums 2^(s - lse2) per segment directly (no running
+ *                     max, no lg2, no exponentials in the epilogue).
  *                     AUTO takes ONE_PASS where it applies and its workspace
  *                     stays within 2x the two-pass one + 256 MiB, else
  *                     TWO_PASS.  ONE_PASS on a problem it does not apply to

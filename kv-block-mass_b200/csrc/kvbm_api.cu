@@ -102,7 +102,8 @@ int device_sms(int dev) {
 constexpr int kMaxSms = 160;
 
 bool one_pass_eligible(const kvbm_problem* p, int path, bool lse_input) {
-  return (path == 1 || path == 2) && !lse_input && p->block_size % kTcExpCols == 0;
+  (void)lse_input;  // with the caller's LSE pass 1 forms the masses directly
+  return (path == 1 || path == 2) && p->block_size % kTcExpCols == 0;
 }
 
 WsLayout layout_for(const kvbm_problem* p, int path, const Ragged* rg, int method, int sms, bool lse_input,
@@ -222,7 +223,8 @@ int run_passes(const kvbm_problem* p, const WsLayout& L, int path, void* mass_ou
   const bool sm = (sg.stages & KVBM_STAGE_MASKS) != 0, sr = (sg.stages & KVBM_STAGE_REDUCE) != 0;
   LaunchOpts o;
   o.mid_event = events != nullptr ? events[1] : nullptr;
-  o.run_pass1 = s1 && lse == nullptr;
+  o.run_pass1 = s1 && (lse == nullptr || L.one_pass);
+  o.lse_known = lse != nullptr && L.one_pass;
   o.run_pass2 = s2;
   o.run_split = s1;
   o.run_masks = sm;
@@ -243,7 +245,8 @@ int run_passes(const kvbm_problem* p, const WsLayout& L, int path, void* mass_ou
   if (s1 || s2 || sm) {
     // NVTX ranges mark the host-side enqueue of each pass (a profiler pairs
     // them with the kernels they launch)
-    nvtxRangePushA(o.run_pass1 ? "kvbm pass 1 (lse) + pass 2 (mass)" : "kvbm pass 2 (mass)");
+    nvtxRangePushA(L.one_pass ? "kvbm pass 1 (lse + mass)"
+                              : (o.run_pass1 ? "kvbm pass 1 (lse) + pass 2 (mass)" : "kvbm pass 2 (mass)"));
     st = (path >= 1) ? launch_tc(p, L, mass_out, ws, s, o) : launch_simt(p, L, mass_out, ws, s, o);
     nvtxRangePop();
     if (st != KVBM_OK) return st;

@@ -206,7 +206,8 @@ int planned_workspace_bytes(const kvbm_problem* p, size_t* bytes, const kvbm_opt
 // Launchers (return a kvbm_status).
 struct LaunchOpts {
   void* mid_event = nullptr;  // cudaEvent_t recorded between pass 1 and pass 2 (or null)
-  bool run_pass1 = true;      // false: lse2 is already in the workspace (LSE input), or not this stage
+  bool run_pass1 = true;      // false: lse2 is already in the workspace (LSE input, two passes), or not this stage
+  bool lse_known = false;     // one pass with the caller's LSE in the workspace (pass 1 forms the masses directly)
   bool run_pass2 = true;
   bool run_split = true;      // fp32 on path 2: convert the run's q/k rows to tf32 pairs
   bool run_masks = true;      // pack a pair mask into bits (tensor-core paths)

@@ -114,6 +114,7 @@ struct TcArgs {
   // segment of seg_tiles key tiles x one exp thread's COLS columns in a slot
   // of `slots`, and at the end turns them into the bucket partials `part1`.
   int one_pass;
+  int lse_known;           // one pass with the caller's row LSE (already in `lse`): no running max
   int nb, bs;              // buckets of the mass vector, block size
   int seg_tiles;           // key tiles one segment covers (block_size / 128, or 1)
   int seg_per_bucket;      // segments of one bucket
@@ -702,6 +703,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     float* seg = a.one_pass ? a.slots + (size_t)slot * a.slot_cols * TILE + rl : nullptr;
     const uint64_t keep_pol = l2_policy_evict_last();  // segment sums: kept in L2 for the epilogue
     float bacc = 0.f;
+    // With the caller's LSE (imported as -lse2, -inf for rows that keep no
+    // key and rows past the sequence) each score's share is 2^(s*C - lse2)
+    // at once: the segment sums are the masses themselves, with no running
+    // max, no rescale and no lg2.
+    const float nlk = a.lse_known ? a.lse[(long long)hidx * a.Npad + lse_tile_slot(row)] : 0.f;
     int cur = wg, seg_end = a.seg_tiles;
     for (int j = 0; j < nkt; ++j) {
       const int buf = j & 1;
@@ -747,13 +753,18 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
       if (seg != nullptr && j == seg_end) {  // a new segment: store the finished one
+        const float sv_ = a.lse_known ? bacc : m + lg2(bacc);
         if (KVBM_L2_HINTS)
-          st_cg_hint(seg + (size_t)cur * TILE, m + lg2(bacc), keep_pol);
+          st_cg_hint(seg + (size_t)cur * TILE, sv_, keep_pol);
         else
-          __stcg(seg + (size_t)cur * TILE, m + lg2(bacc));
+          __stcg(seg + (size_t)cur * TILE, sv_);
         cur += kExpWG;
         seg_end += a.seg_tiles;
         bacc = 0.f;
+      }
+      if (a.lse_known) {
+        bacc += row_sum_exp2<exp2_degree<kOp>()>(v, a.C, nlk);
+        continue;
       }
       const float tmax = row_max(v);
       if (tmax != -INFINITY) {
@@ -773,13 +784,18 @@ __global__ void __launch_bounds__(kThreads, 2)
         bacc += t;
       }
     }
-    // log2 of the segment's sum of 2^(s*C): -inf when it kept no key
+    // log2 of the segment's sum of 2^(s*C): -inf when it kept no key (with
+    // the caller's LSE: the segment's mass itself)
     if (seg != nullptr) {
+      const float sv_ = a.lse_known ? bacc : m + lg2(bacc);
       if (KVBM_L2_HINTS)
-        st_cg_hint(seg + (size_t)cur * TILE, m + lg2(bacc), keep_pol);
+        st_cg_hint(seg + (size_t)cur * TILE, sv_, keep_pol);
       else
-        __stcg(seg + (size_t)cur * TILE, m + lg2(bacc));
+        __stcg(seg + (size_t)cur * TILE, sv_);
     }
+    if (a.lse_known) {
+      if (wg == 0) lse_s[rl] = nlk;
+    } else {
     // Merge the column parts of each row (fixed order: part 0, then 1, 2, ...).
     if (wg > 0) merge[(wg - 1) * TILE + rl] = make_float2(m, l);
     exp_bar_sync();
@@ -796,6 +812,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const float nl = dead ? -INFINITY : -(m + log2f(l));
       a.lse[(long long)(hidx) * a.Npad + lse_tile_slot(row)] = nl;
       lse_s[rl] = nl;
+    }
     }
     if (a.one_pass) {
       // Bucket partials of this query tile: part1[j] = sum over the 128 rows r
@@ -839,8 +856,11 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
 #pragma unroll
           for (int u = 0; u < kEpiU; ++u) {
-            const float e0 = d0 ? 0.f : ex2(L[u].x + nl4.x), e1 = d1 ? 0.f : ex2(L[u].y + nl4.y);
-            const float e2 = d2 ? 0.f : ex2(L[u].z + nl4.z), e3 = d3 ? 0.f : ex2(L[u].w + nl4.w);
+            float4 e = L[u];  // with the caller's LSE: the masses themselves
+            if (!a.lse_known)
+              e = make_float4(ex2(L[u].x + nl4.x), ex2(L[u].y + nl4.y), ex2(L[u].z + nl4.z), ex2(L[u].w + nl4.w));
+            const float e0 = d0 ? 0.f : e.x, e1 = d1 ? 0.f : e.y;
+            const float e2 = d2 ? 0.f : e.z, e3 = d3 ? 0.f : e.w;
             acc[u] += (e0 + e1) + (e2 + e3);
           }
         }
@@ -1563,6 +1583,7 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
   a.work1 = a.work2 = nullptr;
   a.work_count = nullptr;
   a.one_pass = L.one_pass ? 1 : 0;
+  a.lse_known = (L.one_pass && o.lse_known) ? 1 : 0;
   a.nb = (int)kvbm_num_blocks(p->N, p->block_size);
   a.bs = p->block_size;
   a.seg_tiles = L.seg_tiles;

@@ -269,10 +269,10 @@ def test_staged_option_checks(kw, code):
     (dict(dtype=_lib.KVBM_F32), dict(method=_lib.KVBM_METHOD_ONE_PASS), _lib.KVBM_OK),
     (dict(dtype=_lib.KVBM_BF16, block_size=256), dict(method=_lib.KVBM_METHOD_ONE_PASS), _lib.KVBM_OK),
     (dict(dtype=_lib.KVBM_BF16, block_size=192), dict(method=_lib.KVBM_METHOD_ONE_PASS), _lib.KVBM_OK),
-    # one pass needs block_size % 64 == 0, tensor-core dtypes and no LSE input
+    # one pass needs block_size % 64 == 0 and tensor-core dtypes
     (dict(dtype=_lib.KVBM_BF16, block_size=48), dict(method=_lib.KVBM_METHOD_ONE_PASS), _lib.KVBM_ERR_SHAPE),
     (dict(dtype=_lib.KVBM_F64), dict(method=_lib.KVBM_METHOD_ONE_PASS), _lib.KVBM_ERR_SHAPE),
-    (dict(dtype=_lib.KVBM_BF16), dict(method=_lib.KVBM_METHOD_ONE_PASS, lse=0x10000), _lib.KVBM_ERR_SHAPE),
+    (dict(dtype=_lib.KVBM_BF16), dict(method=_lib.KVBM_METHOD_ONE_PASS, lse=0x10000), _lib.KVBM_OK),
     (dict(dtype=_lib.KVBM_BF16, block_size=48), dict(method=_lib.KVBM_METHOD_AUTO), _lib.KVBM_OK),
     (dict(dtype=_lib.KVBM_BF16), dict(method=_lib.KVBM_METHOD_TWO_PASS), _lib.KVBM_OK),
     (dict(dtype=_lib.KVBM_BF16), dict(method=3), _lib.KVBM_ERR_SHAPE),
@@ -280,7 +280,8 @@ def test_staged_option_checks(kw, code):
 ])
 def test_method_option_checks(pkw, okw, code):
     """kvbm_options.method is checked on the host: the one-pass method needs a
-    tensor-core dtype, a block size that is a multiple of 64 and no LSE input."""
+    tensor-core dtype and a block size that is a multiple of 64 (with an LSE
+    input its pass 1 takes the caller's row statistics)."""
     lib = _lib.load()
     o = _lib.Options()
     for name, v in okw.items():

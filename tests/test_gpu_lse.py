@@ -1,4 +1,4 @@
-"""Block mass from a caller-provided row log-sum-exp (pass 1 skipped).
+"""Block mass from a caller-provided row log-sum-exp (no row statistics pass).
 
 An attention forward already knows each query row's LSE; handing it to
 ``block_mass_b200(..., lse=...)`` (C ABI ``kvbm_block_mass_lse``) must give
@@ -47,7 +47,12 @@ def test_lse_input_matches_two_pass(cuda_device, dtype, causal):
     lse = torch_lse(q, k, causal).float()
     a = run(q, k, causal=causal, block_size=64)
     b = run(q, k, causal=causal, block_size=64, lse=lse)
-    assert max_rel(b.cpu().numpy(), a.cpu().numpy()) < 2e-5
+    # (the one-pass call without an LSE takes a quarter of its bf16 exponentials
+    # from a degree-3 polynomial: 1e-4; fp32 runs degree 4 throughout)
+    assert max_rel(b.cpu().numpy(), a.cpu().numpy()) < (1e-4 if dtype == torch.bfloat16 else 2e-5)
+    # the same LSE through the two-pass method (pass 2 alone): same mass
+    c = run(q, k, causal=causal, block_size=64, lse=lse, method="two_pass")
+    assert max_rel(b.cpu().numpy(), c.cpu().numpy()) < 2e-5
     want = oracle_for(q, k, causal=causal, block_size=64)
     assert max_rel(b.cpu().numpy(), want) < (1e-3 if dtype == torch.bfloat16 else 2e-5)
 
