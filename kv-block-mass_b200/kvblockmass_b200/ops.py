@@ -323,7 +323,7 @@ def run_prepared(prep: _Prepared, out: torch.Tensor | None = None,
     """Launch the kernels of a prepared problem on ``stream`` (default: current).
 
     With ``lse`` (``[B, H_q, N]`` natural-log row log-sum-exp; ``[H_q, T]`` for
-    a packed batch) pass 1 is skipped.
+    a packed batch) the row statistics are not recomputed.
     """
     q = prep.keep[0]
     dev = q.device
