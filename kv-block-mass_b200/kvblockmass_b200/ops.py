@@ -370,8 +370,8 @@ def block_mass_b200(q, k, attn_mask=None, causal=False, block_size=64, scale=Non
     sum to the (batch, kv-head) units ``[begin, end)`` of ``B * H_kv`` (used by
     the multi-GPU shards); ``out``/``workspace`` let callers reuse buffers.
     ``lse`` ([B, H_q, N], natural log of sum_c exp(scale * q.k_c) over the kept
-    keys, e.g. the softmax LSE an attention forward returns) skips the row
-    statistics pass: about half the work.  ``seq_lens [B]`` makes the batch
+    keys, e.g. the softmax LSE an attention forward returns) spares the row
+    statistics (one pass: no running max; two passes: no pass 1).  ``seq_lens [B]`` makes the batch
     ragged (sequence ``b`` is its first ``seq_lens[b]`` positions; the padding
     is never read into a pair); ``per_sequence`` returns ``[B, num_blocks]``.
     ``method`` as for ``make_problem``.
