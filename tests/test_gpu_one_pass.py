@@ -154,3 +154,44 @@ def test_one_pass_llama3_8b_shape_against_two_pass(cuda_device):
     one, two = _both(qd, kd, causal=True, block_size=64)
     assert max_rel(one.cpu().numpy(), two.cpu().numpy()) < AGREE[torch.bfloat16]
     assert abs(float(one.double().sum()) - 32 * 8192) < 1e-5 * 32 * 8192
+
+
+@pytest.mark.parametrize("with_lse", [False, True])
+def test_one_pass_with_paged_keys_key_mask_ragged_and_lse(cuda_device, with_lse):
+    """The extensions together on the one-pass kernel: padded ragged lengths
+    (NaN past each length), a per-batch key mask (the key bias step and its
+    pre-pass), per-sequence output, the caller's LSE or not, and k read from a
+    paged cache.  Against the two-pass method, the paged call (same bits as
+    the dense one) and the oracle run on each sequence alone."""
+    from test_gpu_lse import torch_lse
+    from test_gpu_paged import paginate
+
+    B, N, bs = 3, 1000, 128
+    q, k, g = _qk(B, 8, 2, N, 128, torch.bfloat16, 66)
+    lens_l = [1000, 640, 77]
+    km = torch.rand(B, 1, N, generator=g) > 0.25
+    for b, L in enumerate(lens_l):
+        q[b, :, L:] = float("nan")
+        k[b, :, L:] = float("nan")
+    qd, kd, kmd = q.to(cuda_device), k.to(cuda_device), km.to(cuda_device)
+    lens = torch.tensor(lens_l, dtype=torch.int32, device=cuda_device)
+    lse = None
+    if with_lse:
+        lse = torch.full((B, 8, N), float("-inf"), device=cuda_device)
+        for b, L in enumerate(lens_l):
+            lse[b, :, :L] = torch_lse(qd[b:b + 1, :, :L], kd[b:b + 1, :, :L], True, attn_mask=kmd[b, 0, :L])[0].float()
+    kw = dict(attn_mask=kmd, causal=True, block_size=bs, seq_lens=lens, per_sequence=True, lse=lse)
+    one, two = _both(qd, kd, **kw)
+    # with the caller's LSE both methods take the degree-4 polynomial
+    assert max_rel(one.cpu().numpy(), two.cpu().numpy()) < (2e-5 if with_lse else AGREE[torch.bfloat16])
+    for b, L in enumerate(lens_l):
+        w = oracle_for(q[b:b + 1, :, :L], k[b:b + 1, :, :L], attn_mask=km[b, 0, :L], causal=True, block_size=bs)
+        want = np.zeros(one.shape[1])
+        want[:len(w)] = w
+        assert max_rel(one[b].cpu().numpy(), want) < 1e-3
+    cache, table = paginate(kd, 16)
+    paged = kb.block_mass_paged(qd, cache, table.to(cuda_device), attn_mask=kmd, causal=True, block_size=bs,
+                                seq_lens=lens, per_sequence=True, lse=lse)
+    torch.cuda.synchronize()
+    assert torch.equal(paged, one)
+    kb.check_device_errors(cuda_device)
