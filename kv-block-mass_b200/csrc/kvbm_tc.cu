@@ -1598,6 +1598,7 @@ int launch_variant(const kvbm_problem* p, const WsLayout& L, void* ws, cudaStrea
   if (kKeyBias && o.run_masks) {
     if (cudaMemsetAsync(finite_word, 0x5A, sizeof(unsigned), s) != cudaSuccess) return KVBM_ERR_CUDA;
     const long long n = (long long)p->B * p->N * p->Hkv;
+    if ((n + 255) / 256 > 0x7fffffffLL) return KVBM_ERR_SHAPE;
     masked_keys_finite_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
         static_cast<const uint16_t*>(p->k), p->k_stride[0], p->k_stride[1], p->k_stride[2], p->B, p->Hkv, p->N,
         Dr, p->key_mask, p->key_mask_bstride, rg.lens, rg.cu, rg.k_packed ? 1 : 0, rg.total,
