@@ -642,7 +642,7 @@ class _PagedPrepared:
 
 def make_paged_problem(q, k_cache, block_table, attn_mask=None, causal=False, block_size=64, scale=None,
                        causal_skip=True, query_mask=None, units=None, seq_lens=None, cu_seqlens=None,
-                       max_seqlen=None, per_sequence=False) -> _PagedPrepared:
+                       max_seqlen=None, per_sequence=False, method=None) -> _PagedPrepared:
     """Validate a paged call and build its C structs.
 
     ``k_cache`` is ``[num_pages, page_size, H_kv, D]`` (any strides, the dtype
@@ -702,6 +702,7 @@ def make_paged_problem(q, k_cache, block_table, attn_mask=None, causal=False, bl
     prep.options().paged = ctypes.pointer(kv)
     _set_ragged(prep, q.device, seq_lens=seq_lens, cu_seqlens=cu_seqlens, total=q.shape[0] if packed else 0,
                 per_sequence=per_sequence)
+    _set_method(prep, method)
     _validate_ex(prep)
     return _PagedPrepared(prep, kv, [k_cache, table])
 
@@ -718,7 +719,7 @@ def run_paged(pp: _PagedPrepared, out: torch.Tensor | None = None, workspace: to
 
 def block_mass_paged(q, k_cache, block_table, attn_mask=None, causal=False, block_size=64, scale=None,
                      causal_skip=True, query_mask=None, *, seq_lens=None, cu_seqlens=None, max_seqlen=None,
-                     per_sequence=False, units=None, out=None, workspace=None, lse=None):
+                     per_sequence=False, units=None, out=None, workspace=None, lse=None, method=None):
     """``block_mass_b200`` with keys read from a paged KV cache.
 
     ``k_cache [num_pages, page_size, H_kv, D]`` and ``block_table [B,
@@ -729,20 +730,20 @@ def block_mass_paged(q, k_cache, block_table, attn_mask=None, causal=False, bloc
     same bits as the dense call on the keys the table names.  A page id
     outside ``[0, num_pages)`` is not read (its keys count as zero vectors);
     ``check_device_errors()`` reports it.  Table entries past a sequence's
-    length are never read.
+    length are never read.  ``method`` as for ``make_problem``.
     """
     if not (q.is_cuda and k_cache.is_cuda):
         raise ValueError("block_mass_paged needs CUDA tensors (there is no CPU path)")
     pp = make_paged_problem(q, k_cache, block_table, attn_mask=attn_mask, causal=causal, block_size=block_size,
                             scale=scale, causal_skip=causal_skip, query_mask=query_mask, units=units,
                             seq_lens=seq_lens, cu_seqlens=cu_seqlens, max_seqlen=max_seqlen,
-                            per_sequence=per_sequence)
+                            per_sequence=per_sequence, method=method)
     return run_paged(pp, out=out, workspace=workspace, lse=lse)
 
 
 def block_mass_varlen(q, k, cu_seqlens, max_seqlen=None, attn_mask=None, causal=False, block_size=64,
                       scale=None, causal_skip=True, query_mask=None, *, per_sequence=False, units=None, out=None,
-                      workspace=None, lse=None):
+                      workspace=None, lse=None, method=None):
     """Block mass of a packed (varlen) batch, as FlashAttention's varlen layout.
 
     ``q [T, H_q, D]``, ``k [T, H_kv, D]``; sequence ``b`` is rows
@@ -751,13 +752,14 @@ def block_mass_varlen(q, k, cu_seqlens, max_seqlen=None, attn_mask=None, causal=
     which synchronises) sets ``N``: the output is ``[ceil(N / block_size)]``
     summed over sequences, or ``[B, ceil(N / block_size)]`` with
     ``per_sequence``.  Each sequence contributes exactly what the reference
-    computes for it alone.  ``lse`` is ``[H_q, T]``.
+    computes for it alone.  ``lse`` is ``[H_q, T]``; ``method`` as for
+    ``make_problem``.
     """
     if not (q.is_cuda and k.is_cuda):
         raise ValueError("block_mass_varlen needs CUDA tensors (there is no CPU path)")
     prep = make_varlen_problem(q, k, cu_seqlens, max_seqlen=max_seqlen, attn_mask=attn_mask, causal=causal,
                                block_size=block_size, scale=scale, causal_skip=causal_skip,
-                               query_mask=query_mask, units=units, per_sequence=per_sequence)
+                               query_mask=query_mask, units=units, per_sequence=per_sequence, method=method)
     return run_prepared(prep, out=out, workspace=workspace, lse=lse)
 
 

@@ -192,6 +192,8 @@ def test_one_pass_with_paged_keys_key_mask_ragged_and_lse(cuda_device, with_lse)
     cache, table = paginate(kd, 16)
     paged = kb.block_mass_paged(qd, cache, table.to(cuda_device), attn_mask=kmd, causal=True, block_size=bs,
                                 seq_lens=lens, per_sequence=True, lse=lse)
+    paged2 = kb.block_mass_paged(qd, cache, table.to(cuda_device), attn_mask=kmd, causal=True, block_size=bs,
+                                 seq_lens=lens, per_sequence=True, lse=lse, method="two_pass")
     torch.cuda.synchronize()
-    assert torch.equal(paged, one)
+    assert torch.equal(paged, one) and torch.equal(paged2, two)
     kb.check_device_errors(cuda_device)
